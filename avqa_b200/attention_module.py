@@ -1,0 +1,227 @@
+"""``AVQAttention``: the AVQ-attention nn.Module on B200 kernels.
+
+Constructor, attribute names and forward signature follow the reference
+(``src/avqa/attention_module.py:70-316``); parameters are created in the same
+order, so under the same RNG seed the projections and the default codebook
+equal the reference's.  The forward pass runs the reference pipeline
+(``pipeline.py:276-399``) with every stage from VQ precompute to the final
+reduction executed by the CUDA library:
+
+    validate -> project -> split heads -> codebook cast -> KV cache ->
+    quantize (or incremental append) -> parent attention -> routing ->
+    [HVAQ] -> child correction (1..passes) -> merge heads -> out_proj
+
+The output is fp32 for every input dtype, as in the reference (its online
+softmax state is fp32, ``attention.py:37-68``).  Features the reference
+offers but no benchmark configuration uses -- user or causal masks, BCAR
+codebook adaptation, the threshold router, the adaptive budget scheduler,
+learnable HVAQ parameters and the dense "reference" execution mode -- raise
+:class:`BackendError` instead of silently running elsewhere.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+from torch import nn
+
+from avqa_b200 import ops
+from avqa_b200.backend import Backend, CUDABackend
+from avqa_b200.cache import KVCache, PagedKVCache
+from avqa_b200.codebook import HierarchicalCodebook
+from avqa_b200.config import AVQConfig
+from avqa_b200.exceptions import BackendError, DeviceError, DtypeError, RoutingError, ShapeError
+
+SUPPORTED_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
+
+
+class AVQAttention(nn.Module):
+    """AVQ attention (hierarchical VQ keys, parent attention, routed child correction)."""
+
+    def __init__(self, config: AVQConfig, *, in_proj: bool = True, out_proj: bool = True) -> None:
+        super().__init__()
+        self.config = config
+        self.backend = Backend.create(config.backend.name)
+        E = config.attention.embed_dim
+        if in_proj:
+            self.q_proj = nn.Linear(E, E, bias=False)
+            self.k_proj = nn.Linear(E, E, bias=False)
+            self.v_proj = nn.Linear(E, E, bias=False)
+        else:
+            self.q_proj = nn.Identity()
+            self.k_proj = nn.Identity()
+            self.v_proj = nn.Identity()
+        self.out_proj = nn.Linear(E, E, bias=False) if out_proj else nn.Identity()
+        self.codebook = HierarchicalCodebook(
+            num_heads=config.attention.num_heads, num_parents=config.codebook.num_codewords,
+            children_per_parent=config.codebook.children_per_codeword, head_dim=E // config.attention.num_heads,
+            perturbation_scale=config.codebook.perturbation_scale, device="cpu", dtype=torch.float32)
+        self.codebook.initialize_children_around_parents()
+        self.dropout = nn.Dropout(config.dropout) if config.dropout > 0 else nn.Identity()
+        self.last_keys: torch.Tensor | None = None
+        self.last_parent_assignments: torch.Tensor | None = None
+        self.process_group = None  # set by avqa_b200.parallel for head sharding
+        self._check_supported()
+
+    # -- configuration -----------------------------------------------------------
+
+    def _check_supported(self) -> None:
+        c = self.config
+        unsupported = []
+        if c.codebook.bcar_enabled:
+            unsupported.append("codebook.bcar_enabled")
+        if c.routing.strategy == "threshold":
+            unsupported.append("routing.strategy='threshold'")
+        if c.refinement.adaptive_budget:
+            unsupported.append("refinement.adaptive_budget")
+        if c.hopfield.learnable_parent_beta or c.hopfield.learnable_alpha:
+            unsupported.append("hopfield.learnable_*")
+        if not c.refinement.enabled or c.execution.mode == "reference":
+            unsupported.append("dense (naive) attention path")
+        if c.execution.compile_enabled:
+            unsupported.append("execution.compile_enabled")
+        if unsupported:
+            raise BackendError("not supported by the cuda backend: " + ", ".join(unsupported))
+        if c.refinement.passes <= 0:
+            raise RoutingError(f"passes must be positive, got {c.refinement.passes}")
+        if c.refinement.passes > 1 and not 0.0 < c.refinement.pass_decay <= 1.0:
+            raise RoutingError(f"decay must be in (0, 1], got {c.refinement.pass_decay}")
+        if c.refinement.passes > 8:
+            raise BackendError("at most 8 refinement passes are supported", {"passes": c.refinement.passes})
+
+    @property
+    def hvaq_mode(self) -> int:
+        c = self.config
+        if not (c.backend.hopfield and c.hopfield.adaptive != "none"):
+            return 0
+        return {"entropy": 1, "linear": 2}[c.hopfield.adaptive]
+
+    # -- helpers -----------------------------------------------------------------
+
+    @staticmethod
+    def split_heads(tensor: torch.Tensor, num_heads: int) -> torch.Tensor:
+        """``[B, T, E]`` -> ``[B, H, T, D]`` (a view)."""
+        B, T, E = tensor.shape
+        return tensor.view(B, T, num_heads, E // num_heads).transpose(1, 2)
+
+    @staticmethod
+    def merge_heads(tensor: torch.Tensor) -> torch.Tensor:
+        B, H, T, D = tensor.shape
+        return tensor.transpose(1, 2).contiguous().view(B, T, H * D)
+
+    def maybe_project(self, query, key, value):
+        return self.q_proj(query), self.k_proj(key), self.v_proj(value)
+
+    def validate_inputs(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor) -> None:
+        """Same checks as the reference (attention_module.py:321-342)."""
+        if self.config.backend.skip_validation:
+            return
+        E = self.config.attention.embed_dim
+        for name, t in (("query", query), ("key", key), ("value", value)):
+            if t.ndim != 3:
+                raise ShapeError(f"{name} must have rank 3", expected=3, actual=t.ndim)
+            if t.dtype not in SUPPORTED_DTYPES:
+                raise DtypeError(f"{name} has unsupported dtype", expected=[str(d) for d in SUPPORTED_DTYPES],
+                                 actual=str(t.dtype))
+            if t.shape[-1] != E:
+                raise ShapeError(f"{name} embed dim mismatch", expected=E, actual=t.shape[-1])
+        devs = {t.device for t in (query, key, value)}
+        if len(devs) > 1:
+            raise DeviceError("query/key/value are on different devices", actual=[str(d) for d in devs])
+        if key.shape != value.shape:
+            raise ShapeError("value shape mismatch", expected=tuple(key.shape), actual=tuple(value.shape))
+
+    def sync_codebook_device(self, q: torch.Tensor) -> None:
+        """Cast the codebook to the input's device and dtype (attention_module.py:344-348)."""
+        if self.codebook.parents.device != q.device or self.codebook.parents.dtype != q.dtype:
+            self.codebook.parents = self.codebook.parents.to(device=q.device, dtype=q.dtype)
+            self.codebook.children = self.codebook.children.to(device=q.device, dtype=q.dtype)
+
+    # -- forward -----------------------------------------------------------------
+
+    def forward(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, mask: torch.Tensor | None = None,
+                kv_cache: KVCache | None = None) -> torch.Tensor:
+        c = self.config
+        if c.precision.autocast:
+            with torch.autocast(device_type=query.device.type, dtype=getattr(torch, c.precision.dtype)):
+                return self.forward_impl(query, key, value, mask, kv_cache)
+        return self.forward_impl(query, key, value, mask, kv_cache)
+
+    def forward_impl(self, query, key, value, mask=None, kv_cache=None) -> torch.Tensor:
+        if mask is not None or self.config.causal:
+            raise BackendError("attention masks (user or causal) are not supported by the cuda backend")
+        self.validate_inputs(query, key, value)
+        if not query.is_cuda:
+            raise DeviceError("the cuda backend needs CUDA tensors", expected="cuda", actual=str(query.device))
+        qp, kp, vp = self.maybe_project(query, key, value)
+        H = self.config.attention.num_heads
+        q = self.split_heads(qp, H)
+        k = self.split_heads(kp, H)
+        v = self.split_heads(vp, H)
+        self.sync_codebook_device(q)
+        backend: CUDABackend = self.backend  # type: ignore[assignment]
+        cb = backend.prepared_codebook(self.codebook.parents, self.codebook.children, q.dtype, q.device)
+        state = self.resolve_quantization(k, v, cb, kv_cache)
+        B, _, T, D = q.shape
+        if state.S == 0:
+            # pipeline.py:344-345: budget 0 -> naive attention over zero keys
+            attn = backend.naive_attention(q, k, v)
+            return self.dropout(self.out_proj(self.merge_heads(attn)))
+        min_valid = self.global_min_valid(state)
+        out = torch.empty(B, T, H * D, dtype=torch.float32, device=q.device)
+        out4 = out.view(B, T, H, D).transpose(1, 2)
+        c = self.config
+        beta0 = c.hopfield.beta_init if c.hopfield.beta_init > 0 else 1.0 / math.sqrt(D)
+        backend.forward(q, cb, state, min(c.routing.refinement_budget, cb.dims[1]), c.refinement.passes,
+                        c.refinement.pass_decay, self.hvaq_mode, beta0, c.hopfield.alpha, out=out4,
+                        min_valid=min_valid)
+        return self.dropout(self.out_proj(out))
+
+    def global_min_valid(self, state: ops.QuantState) -> torch.Tensor:
+        """The budget floor: min over every (b,h) of the call -- and of every
+        rank when heads are sharded across a process group."""
+        if self.process_group is None:
+            return state.gmin
+        import torch.distributed as dist
+        g = state.gmin.clone()
+        dist.all_reduce(g, op=dist.ReduceOp.MIN, group=self.process_group)
+        return g
+
+    def resolve_quantization(self, k: torch.Tensor, v: torch.Tensor, cb: ops.PreparedCodebook,
+                             kv_cache: KVCache | None) -> ops.QuantState:
+        """Quantize ``k``/``v`` -- or, with a cache, extend the cache's state."""
+        if kv_cache is None:
+            st = ops.quantize(k, v, cb)
+            self.last_keys = k.detach()
+            self.last_parent_assignments = st.passign.view(k.shape[:3]).long()
+            return st
+        skey = (id(self), id(cb), k.dtype)
+        st = kv_cache.quant_states.get(skey)
+        if st is not None and (st.B != k.shape[0] or st.H != k.shape[1]):
+            st = None
+        if st is None:
+            ck, cv = kv_cache.lookup()
+            if ck.shape[-2] > 0:
+                ck = ck.to(device=k.device, dtype=k.dtype)
+                cv = cv.to(device=v.device, dtype=v.dtype)
+                kf, vf = torch.cat([ck, k], dim=-2), torch.cat([cv, v], dim=-2)
+            else:
+                kf, vf = k, v
+            st = ops.quantize(kf, vf, cb, keep_sums=True)
+            kv_cache.append(k, v)
+            kv_cache.quant_states.clear()
+            kv_cache.quant_states[skey] = st
+            return st
+        if isinstance(kv_cache, PagedKVCache) and str(kv_cache.device) == str(k.device) and kv_cache.dtype == k.dtype:
+            cursor = 0
+            for page, slot0, take in kv_cache.reserve(k.shape[0], k.shape[2]):
+                ops.append(st, k[:, :, cursor:cursor + take], v[:, :, cursor:cursor + take], cb,
+                           kv_cache.key_pages[page], kv_cache.value_pages[page], slot0)
+                cursor += take
+        else:
+            ops.append(st, k, v, cb)
+            kv_cache.append(k, v)
+        return st
+
+
+__all__ = ["AVQAttention"]

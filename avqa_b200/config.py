@@ -102,9 +102,11 @@ class MergeConfig:
 
 @dataclass(frozen=True, slots=True)
 class BackendConfig:
-    """Backend selection; ``"cuda"`` selects the B200 kernels."""
+    """Backend selection.  This package implements ``"cuda"`` (the default
+    here); ``"torch"`` is accepted so that the reference's JSON configs load,
+    but constructing a module with it raises :class:`BackendError`."""
 
-    name: str = "torch"
+    name: str = "cuda"
     enable_autotune: bool = False
     skip_validation: bool = False
     hopfield: bool = False

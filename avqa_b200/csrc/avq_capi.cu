@@ -1,0 +1,177 @@
+// extern "C" entry points (include/avqa_b200.h): argument checks, dtype
+// dispatch and error reporting around the kernel launchers.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/avqa_b200.h"
+#include "avq_kernels.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int finish(int rc, const char* what) {
+  if (rc == AVQ_OK) {
+    const cudaError_t e = cudaPeekAtLastError();
+    if (e != cudaSuccess) return fail(AVQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return AVQ_OK;
+  }
+  if (rc == AVQ_ERR_UNSUPPORTED) return fail(rc, "%s: unsupported size (D <= 256, C <= 8, M0 <= 8192, passes <= 8)", what);
+  if (rc == AVQ_ERR_WORKSPACE) return fail(rc, "%s: workspace too small", what);
+  const cudaError_t e = cudaGetLastError();
+  return fail(rc, "%s: %s", what, cudaGetErrorString(e));
+}
+
+avq::Strides3 st3(const long long* s) { return avq::Strides3{(long)s[0], (long)s[1], (long)s[2]}; }
+
+bool bad_dtype(int dt) { return dt < 0 || dt > 2; }
+
+}  // namespace
+
+extern "C" {
+
+const char* avq_version(void) { return "avqa_b200 0.1.0 (sm_100a)"; }
+
+int avq_last_error(char* buf, int len) {
+  if (buf && len > 0) {
+    std::strncpy(buf, g_last_error.c_str(), (size_t)len - 1);
+    buf[len - 1] = 0;
+  }
+  return (int)g_last_error.size();
+}
+
+int avq_prepare_codebook(int dtype, const float* parents32, const float* children32, int H, int M0, int C, int D,
+                         void* parents_dt, void* children_dt, float* p_sq, float* c_sq, void* stream) {
+  if (bad_dtype(dtype)) return fail(AVQ_ERR_ARG, "avq_prepare_codebook: bad dtype %d", dtype);
+  if (H <= 0 || M0 <= 0 || C <= 0 || D <= 0) return fail(AVQ_ERR_ARG, "avq_prepare_codebook: sizes must be > 0");
+  if (!parents32 || !children32 || !parents_dt || !children_dt || !p_sq || !c_sq)
+    return fail(AVQ_ERR_ARG, "avq_prepare_codebook: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc;
+  switch (dtype) {
+    case 0: rc = avq::launch_prep_codebook<avq::DT_F32>(parents32, children32, H, M0, C, D, parents_dt, children_dt, p_sq, c_sq, st); break;
+    case 1: rc = avq::launch_prep_codebook<avq::DT_BF16>(parents32, children32, H, M0, C, D, parents_dt, children_dt, p_sq, c_sq, st); break;
+    default: rc = avq::launch_prep_codebook<avq::DT_F16>(parents32, children32, H, M0, C, D, parents_dt, children_dt, p_sq, c_sq, st); break;
+  }
+  return finish(rc, "avq_prepare_codebook");
+}
+
+size_t avq_quantize_workspace_size(int B, int H, int S, int M0) {
+  return avq::quantize_workspace_bytes(B * H, S, M0);
+}
+
+int avq_quantize(int dtype, const void* keys, const long long* key_strides, const void* values,
+                 const long long* value_strides, int B, int H, int S, int D, int M0, int C, const void* parents_dt,
+                 const float* p_sq, const void* children_dt, const float* c_sq, int* passign, int* cassign,
+                 void* pagg, void* cagg, float* pacc, float* cacc, int* pcnt, int* ccnt, int* nvalid,
+                 int* gmin_valid, void* workspace, size_t workspace_bytes, void* stream) {
+  if (bad_dtype(dtype)) return fail(AVQ_ERR_ARG, "avq_quantize: bad dtype %d", dtype);
+  if (B < 0 || H <= 0 || S < 0 || D <= 0 || M0 <= 0 || C <= 0) return fail(AVQ_ERR_ARG, "avq_quantize: bad sizes");
+  if (!key_strides || !value_strides || !parents_dt || !p_sq || !children_dt || !c_sq || !pagg || !cagg || !pcnt ||
+      !ccnt || !nvalid)
+    return fail(AVQ_ERR_ARG, "avq_quantize: null pointer");
+  if (S > 0 && (!keys || !values || !passign || !cassign)) return fail(AVQ_ERR_ARG, "avq_quantize: null key pointer");
+  if ((pacc == nullptr) != (cacc == nullptr)) return fail(AVQ_ERR_ARG, "avq_quantize: pacc and cacc go together");
+  const size_t need = avq::quantize_workspace_bytes(B * H, S, M0);
+  if (workspace_bytes < need || (need && !workspace))
+    return fail(AVQ_ERR_WORKSPACE, "avq_quantize: workspace %zu < %zu bytes", workspace_bytes, need);
+  if (B == 0) return AVQ_OK;
+  avq::QuantizeArgs a{keys, st3(key_strides), values, st3(value_strides), B, H, S, D, M0, C, parents_dt, p_sq,
+                      children_dt, c_sq, passign, cassign, pagg, cagg, pacc, cacc, pcnt, ccnt, nvalid, gmin_valid,
+                      workspace, workspace_bytes};
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc;
+  switch (dtype) {
+    case 0: rc = avq::launch_quantize<avq::DT_F32>(a, st); break;
+    case 1: rc = avq::launch_quantize<avq::DT_BF16>(a, st); break;
+    default: rc = avq::launch_quantize<avq::DT_F16>(a, st); break;
+  }
+  return finish(rc, "avq_quantize");
+}
+
+int avq_selection_stride(int P, int passes, float pass_decay) {
+  if (P <= 0 || passes <= 0 || passes > 8) return fail(AVQ_ERR_ARG, "avq_selection_stride: bad P/passes"), -1;
+  return avq::selection_stride(P, passes, pass_decay);
+}
+
+size_t avq_forward_workspace_size(int B, int H, int T, int D, int M0, int P, int passes, float pass_decay) {
+  if (P <= 0 || passes <= 0 || passes > 8) return 0;
+  return avq::forward_workspace_bytes(B * H, T, D, M0, P, passes, pass_decay);
+}
+
+int avq_forward(int dtype, const void* q, const long long* q_strides, int B, int H, int T, int D, int M0, int C,
+                const void* parents_dt, const void* children_dt, const void* pagg, const void* cagg, const int* pcnt,
+                const int* ccnt, const int* min_valid, int P, int passes, float pass_decay, int hvaq, float beta0,
+                float alpha, float* out, const long long* out_strides, float* importance_out, int* selected_out,
+                int* pass_counts_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (bad_dtype(dtype)) return fail(AVQ_ERR_ARG, "avq_forward: bad dtype %d", dtype);
+  if (B < 0 || H <= 0 || T < 0 || D <= 0 || M0 <= 0 || C <= 0) return fail(AVQ_ERR_ARG, "avq_forward: bad sizes");
+  if (P <= 0) return fail(AVQ_ERR_ARG, "avq_forward: budget must be > 0, got %d", P);
+  if (P > M0) return fail(AVQ_ERR_ARG, "avq_forward: budget (%d) exceeds number of parents (%d)", P, M0);
+  if (passes <= 0 || passes > 8) return fail(AVQ_ERR_ARG, "avq_forward: passes must be in [1, 8], got %d", passes);
+  if (passes > 1 && !(pass_decay > 0.f && pass_decay <= 1.f))
+    return fail(AVQ_ERR_ARG, "avq_forward: decay must be in (0, 1], got %g", (double)pass_decay);
+  if (hvaq < 0 || hvaq > 2) return fail(AVQ_ERR_ARG, "avq_forward: hvaq must be 0, 1 or 2");
+  if (hvaq && !(beta0 > 0.f)) return fail(AVQ_ERR_ARG, "avq_forward: beta_init must be > 0");
+  if (!q_strides || !out_strides || !parents_dt || !children_dt || !pagg || !cagg || !pcnt || !ccnt || !min_valid)
+    return fail(AVQ_ERR_ARG, "avq_forward: null pointer");
+  if (B * T > 0 && (!q || !out)) return fail(AVQ_ERR_ARG, "avq_forward: null q/out");
+  const size_t need = avq::forward_workspace_bytes(B * H, T, D, M0, P, passes, pass_decay);
+  if (workspace_bytes < need || !workspace)
+    return fail(AVQ_ERR_WORKSPACE, "avq_forward: workspace %zu < %zu bytes", workspace_bytes, need);
+  avq::ForwardArgs a{q, st3(q_strides), B, H, T, D, M0, C, parents_dt, children_dt, pagg, cagg, pcnt, ccnt, min_valid,
+                     P, passes, pass_decay, hvaq, beta0, alpha, out, st3(out_strides), importance_out, selected_out,
+                     pass_counts_out, workspace, workspace_bytes};
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc;
+  switch (dtype) {
+    case 0: rc = avq::launch_forward<avq::DT_F32>(a, st); break;
+    case 1: rc = avq::launch_forward<avq::DT_BF16>(a, st); break;
+    default: rc = avq::launch_forward<avq::DT_F16>(a, st); break;
+  }
+  return finish(rc, "avq_forward");
+}
+
+int avq_append(int dtype, const void* k, const long long* k_strides, const void* v, const long long* v_strides,
+               int B, int H, int Tn, int D, int M0, int C, const void* parents_dt, const float* p_sq,
+               const void* children_dt, const float* c_sq, float* pacc, float* cacc, void* pagg, void* cagg,
+               int* pcnt, int* ccnt, int* nvalid, void* kpage, void* vpage, const long long* page_strides, int slot0,
+               void* stream) {
+  if (bad_dtype(dtype)) return fail(AVQ_ERR_ARG, "avq_append: bad dtype %d", dtype);
+  if (B < 0 || H <= 0 || Tn < 0 || D <= 0 || M0 <= 0 || C <= 0) return fail(AVQ_ERR_ARG, "avq_append: bad sizes");
+  if (!k || !v || !k_strides || !v_strides || !parents_dt || !p_sq || !children_dt || !c_sq || !pacc || !cacc ||
+      !pagg || !cagg || !pcnt || !ccnt || !nvalid)
+    return fail(AVQ_ERR_ARG, "avq_append: null pointer");
+  if ((kpage == nullptr) != (vpage == nullptr) || (kpage && !page_strides))
+    return fail(AVQ_ERR_ARG, "avq_append: kpage, vpage and page_strides go together");
+  avq::AppendArgs a{k, st3(k_strides), v, st3(v_strides), B, H, Tn, D, M0, C, parents_dt, p_sq, children_dt, c_sq,
+                    pacc, cacc, pagg, cagg, pcnt, ccnt, nvalid, kpage, vpage,
+                    kpage ? st3(page_strides) : avq::Strides3{0, 0, 0}, slot0};
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc;
+  switch (dtype) {
+    case 0: rc = avq::launch_append<avq::DT_F32>(a, st); break;
+    case 1: rc = avq::launch_append<avq::DT_BF16>(a, st); break;
+    default: rc = avq::launch_append<avq::DT_F16>(a, st); break;
+  }
+  return finish(rc, "avq_append");
+}
+
+int avq_reduce_min(const int* v, int n, int* out, void* stream) {
+  if (!v || !out || n <= 0) return fail(AVQ_ERR_ARG, "avq_reduce_min: bad arguments");
+  return finish(avq::launch_reduce_min(v, n, out, (cudaStream_t)stream), "avq_reduce_min");
+}
+
+}  // extern "C"

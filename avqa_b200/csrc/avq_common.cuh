@@ -1,0 +1,102 @@
+// Shared numerics for the AVQ-attention kernels (sm_100a).
+//
+// Every kernel reproduces the reference's rounding points: a torch CPU op
+// computes in fp32 and narrows its result to the tensor dtype once.  Here a
+// value "in dtype DT" is carried as a float that holds a DT-representable
+// number; rnd<DT>() performs the narrowing (round-to-nearest-even).
+// Reductions that the reference performs in fp32 are accumulated in double
+// and narrowed fp64 -> fp32 -> DT, i.e. the exactly rounded sum.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace avq {
+
+enum DType : int { DT_F32 = 0, DT_BF16 = 1, DT_F16 = 2 };
+
+template <int DT> struct Storage;
+template <> struct Storage<DT_F32> { using T = float; };
+template <> struct Storage<DT_BF16> { using T = __nv_bfloat16; };
+template <> struct Storage<DT_F16> { using T = __half; };
+
+__device__ __forceinline__ float to_f(float x) { return x; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+
+template <int DT> __device__ __forceinline__ typename Storage<DT>::T from_f(float x);
+template <> __device__ __forceinline__ float from_f<DT_F32>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<DT_BF16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ __half from_f<DT_F16>(float x) { return __float2half_rn(x); }
+
+// Narrow an fp32 value to DT and widen it back (RNE; NaN stays NaN, fp16
+// overflow becomes inf).
+template <int DT> __device__ __forceinline__ float rnd(float x) { return to_f(from_f<DT>(x)); }
+
+// fp64 -> fp32 -> DT (the narrowing of an fp32-accumulated reduction).
+template <int DT> __device__ __forceinline__ float rnd64(double x) { return rnd<DT>(__double2float_rn(x)); }
+
+// A Python scalar bound (clamp_min(1e-12)) cast to DT: 1e-12 in bf16, 0 in fp16.
+template <int DT> __device__ __forceinline__ float eps_dt() { return rnd<DT>(1e-12f); }
+
+// Saturating count: index_add_ of ones in DT stops growing at 2^(mantissa+1).
+template <int DT> __device__ __forceinline__ float count_dt(int n) {
+  const int sat = DT == DT_BF16 ? 256 : (DT == DT_F16 ? 2048 : (1 << 24));
+  return (float)(n < sat ? n : sat);
+}
+
+__device__ __forceinline__ float step_down(float y, int k) {
+  for (int i = 0; i < k; ++i) y = nextafterf(y, -INFINITY);
+  return y;
+}
+__device__ __forceinline__ float step_up(float y, int k) {
+  for (int i = 0; i < k; ++i) y = nextafterf(y, INFINITY);
+  return y;
+}
+
+// rnd<DT>(correctly rounded fp32 exp(x)).  CUDA's expf is within 2 ulp; when
+// every fp32 value in that window narrows to the same DT value the answer is
+// known, otherwise the exponential is recomputed in double.
+template <int DT> __device__ __forceinline__ float exp_rn(float x) {
+  if (DT != DT_F32) {
+    const float y = expf(x);
+    if (isfinite(y) && y > 0.f) {
+      const float a = rnd<DT>(step_down(y, 3)), b = rnd<DT>(step_up(y, 3));
+      if (a == b) return a;
+    }
+  }
+  return rnd<DT>(__double2float_rn(exp((double)x)));
+}
+
+// Same for the natural logarithm (HVAQ entropy), x > 0.
+template <int DT> __device__ __forceinline__ float log_rn(float x) {
+  if (DT != DT_F32) {
+    const float y = logf(x);
+    if (isfinite(y)) {
+      const float a = rnd<DT>(step_down(y, 3)), b = rnd<DT>(step_up(y, 3));
+      if (a == b) return a;
+    }
+  }
+  return rnd<DT>(__double2float_rn(log((double)x)));
+}
+
+// Order-preserving map of a float onto uint32 (ascending); NaN maps above +inf.
+__device__ __forceinline__ uint32_t float_order_key(float f) {
+  if (isnan(f)) return 0xFFFFFFFFu;
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Load a DT row element as float.
+template <typename T> __device__ __forceinline__ float ld(const T* p, long i) { return to_f(p[i]); }
+
+}  // namespace avq
+
+// Status codes shared with the host wrapper.
+#define AVQ_OK 0
+#define AVQ_ERR_ARG 1
+#define AVQ_ERR_CUDA 2
+#define AVQ_ERR_UNSUPPORTED 3
+#define AVQ_ERR_WORKSPACE 4

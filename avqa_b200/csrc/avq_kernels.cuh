@@ -1,0 +1,105 @@
+// Internal declarations shared by the kernel translation units and the C-ABI.
+#pragma once
+
+#include "avq_common.cuh"
+
+namespace avq {
+
+// Element (b, h, s, d) of a 4-D tensor lives at b*b_ + h*h_ + s*s_ + d.
+struct Strides3 {
+  long b, h, s;
+};
+
+inline size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
+
+struct QuantizeArgs {
+  const void* keys;
+  Strides3 ks;
+  const void* values;
+  Strides3 vs;
+  int B, H, S, D, M0, C;
+  const void* parents_dt;
+  const float* p_sq;
+  const void* children_dt;
+  const float* c_sq;
+  int* passign;
+  int* cassign;
+  void* pagg;
+  void* cagg;
+  float* pacc;  // optional fp32 accumulators (needed for incremental decode)
+  float* cacc;
+  int* pcnt;
+  int* ccnt;
+  int* nvalid;
+  int* gmin_valid;  // optional: atomicMin of nvalid (caller initialises it)
+  void* workspace;
+  size_t workspace_bytes;
+};
+
+struct ForwardArgs {
+  const void* q;
+  Strides3 qs;
+  int B, H, T, D, M0, C;
+  const void* parents_dt;
+  const void* children_dt;
+  const void* pagg;
+  const void* cagg;
+  const int* pcnt;
+  const int* ccnt;
+  const int* min_valid;  // device scalar: min over all (b,h) of non-empty parents
+  int P;
+  int passes;
+  float pass_decay;
+  int hvaq;  // 0 off, 1 entropy, 2 linear
+  float beta0;
+  float alpha;
+  float* out;  // fp32
+  Strides3 os;
+  float* importance_out;  // optional [G, M0] pre-HVAQ importance (dtype values)
+  int* selected_out;      // optional [G, sel_stride] selections of every pass
+  int* pass_counts_out;   // optional [passes]
+  void* workspace;
+  size_t workspace_bytes;
+};
+
+struct AppendArgs {
+  const void* k;
+  Strides3 ks;
+  const void* v;
+  Strides3 vs;
+  int B, H, Tn, D, M0, C;
+  const void* parents_dt;
+  const float* p_sq;
+  const void* children_dt;
+  const float* c_sq;
+  float* pacc;
+  float* cacc;
+  void* pagg;
+  void* cagg;
+  int* pcnt;
+  int* ccnt;
+  int* nvalid;
+  void* kpage;  // optional paged K/V destination
+  void* vpage;
+  Strides3 pgs;
+  int slot0;
+};
+
+template <int DT>
+int launch_append(const AppendArgs& a, cudaStream_t st);
+int launch_reduce_min(const int* v, int n, int* out, cudaStream_t st);
+
+template <int DT>
+int launch_prep_codebook(const float* parents32, const float* children32, int H, int M0, int C, int D,
+                         void* parents_dt, void* children_dt, float* p_sq, float* c_sq, cudaStream_t st);
+template <int DT>
+int launch_quantize(const QuantizeArgs& a, cudaStream_t st);
+size_t quantize_workspace_bytes(int G, int S, int M0);
+
+template <int DT>
+int launch_forward(const ForwardArgs& a, cudaStream_t st);
+size_t forward_workspace_bytes(int G, int T, int D, int M0, int P, int passes, float decay);
+int selection_stride(int P, int passes, float decay);
+void pass_budget_caps(int P, int passes, float decay, int* caps);
+
+}  // namespace avq

@@ -1,0 +1,401 @@
+// Hierarchical vector quantization of keys (reference quantizer.py:166-278).
+//
+//   prep_codebook   : cast the fp32 master codebook to the dtype, squared norms
+//   assign          : parent distance + first-argmin, then child distance +
+//                     first-argmin inside the assigned parent
+//   bucket_hist / bucket_scan / bucket_scatter
+//                   : stable counting sort of keys by parent (key order kept
+//                     inside every bucket) -> per-parent member lists
+//   aggregate       : per parent, fp32 sum of member values in key order,
+//                     narrowed once (the reference's 2-D index_add_), plus
+//                     the child sums and counts in the same pass
+//
+// Index work is exact.  Dot products here accumulate in double, so every
+// distance equals the exactly rounded reference value.
+#include "avq_kernels.cuh"
+
+namespace avq {
+
+// ---------------------------------------------------------------------------
+// Codebook preparation (attention_module.py:344-348 cast + quantizer.py:208,224 norms)
+// ---------------------------------------------------------------------------
+template <int DT>
+__global__ void prep_codebook_kernel(const float* __restrict__ src, typename Storage<DT>::T* __restrict__ dst,
+                                     float* __restrict__ sq, long rows, int D) {
+  const int lane = threadIdx.x & 31;
+  const long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  double acc = 0.0;
+  for (int d = lane; d < D; d += 32) {
+    const float x = rnd<DT>(src[row * D + d]);
+    dst[row * D + d] = from_f<DT>(x);
+    acc += (double)rnd<DT>(__fmul_rn(x, x));
+  }
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) sq[row] = rnd64<DT>(acc);
+}
+
+// ---------------------------------------------------------------------------
+// Assignment
+// ---------------------------------------------------------------------------
+struct ArgMin {
+  float v;
+  int i;
+};
+
+// torch.argmin: the first minimum; a NaN wins over every number.
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+  if (bi < 0) return true;
+  const bool n = isnan(v), bn = isnan(bv);
+  if (n || bn) return n && (!bn || i < bi);
+  return v < bv || (v == bv && i < bi);
+}
+
+__device__ __forceinline__ ArgMin shfl_best(ArgMin a, int width_mask) {
+  for (int o = 1; o <= width_mask; o <<= 1) {
+    const float v = __shfl_xor_sync(0xffffffffu, a.v, o);
+    const int i = __shfl_xor_sync(0xffffffffu, a.i, o);
+    if (i >= 0 && better(v, i, a.v, a.i)) a = {v, i};
+  }
+  return a;
+}
+
+constexpr int AS_ROWS = 64;  // keys per CTA
+constexpr int AS_COLS = 32;  // parents per smem tile
+
+template <int DT>
+__global__ void __launch_bounds__(256) assign_kernel(const typename Storage<DT>::T* __restrict__ keys, Strides3 ks,
+                                                     int H, int S, int D, int M0, int C,
+                                                     const typename Storage<DT>::T* __restrict__ parents,
+                                                     const float* __restrict__ p_sq,
+                                                     const typename Storage<DT>::T* __restrict__ children,
+                                                     const float* __restrict__ c_sq, int* __restrict__ passign,
+                                                     int* __restrict__ cassign) {
+  extern __shared__ float smem[];
+  const int ld = D + 1;
+  float* kk = smem;                      // [AS_ROWS][ld]
+  float* pp = kk + AS_ROWS * ld;         // [AS_COLS][ld]
+  float* ksq = pp + AS_COLS * ld;        // [AS_ROWS]
+  const int g = blockIdx.y, b = g / H, h = g % H;
+  const int s0 = blockIdx.x * AS_ROWS;
+  const int tid = threadIdx.x, r = tid >> 2, l4 = tid & 3;
+  const long kbase = (long)b * ks.b + (long)h * ks.h;
+
+  for (int e = tid; e < AS_ROWS * D; e += blockDim.x) {
+    const int rr = e / D, d = e % D;
+    const int s = s0 + rr;
+    kk[rr * ld + d] = s < S ? to_f(keys[kbase + (long)s * ks.s + d]) : 0.f;
+  }
+  __syncthreads();
+  if (tid < AS_ROWS) {
+    double acc = 0.0;
+    for (int d = 0; d < D; ++d) {
+      const float x = kk[tid * ld + d];
+      acc += (double)rnd<DT>(__fmul_rn(x, x));
+    }
+    ksq[tid] = rnd64<DT>(acc);
+  }
+  __syncthreads();
+  const float my_ksq = ksq[r];
+  ArgMin best = {0.f, -1};
+  const long pbase = (long)h * M0;
+  for (int p0 = 0; p0 < M0; p0 += AS_COLS) {
+    for (int e = tid; e < AS_COLS * D; e += blockDim.x) {
+      const int j = e / D, d = e % D;
+      pp[j * ld + d] = (p0 + j < M0) ? to_f(parents[(pbase + p0 + j) * D + d]) : 0.f;
+    }
+    __syncthreads();
+    double acc[AS_COLS / 4];
+#pragma unroll
+    for (int i = 0; i < AS_COLS / 4; ++i) acc[i] = 0.0;
+    for (int d = 0; d < D; ++d) {
+      const double kv = (double)kk[r * ld + d];
+#pragma unroll
+      for (int i = 0; i < AS_COLS / 4; ++i) acc[i] = fma(kv, (double)pp[(l4 + 4 * i) * ld + d], acc[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < AS_COLS / 4; ++i) {
+      const int p = p0 + l4 + 4 * i;
+      if (p < M0) {
+        const float cross = rnd64<DT>(acc[i]);
+        const float two = rnd<DT>(__fmul_rn(2.f, cross));
+        const float t1 = rnd<DT>(__fadd_rn(my_ksq, p_sq[pbase + p]));
+        const float dd = rnd<DT>(__fsub_rn(t1, two));
+        if (better(dd, p, best.v, best.i)) best = {dd, p};
+      }
+    }
+    __syncthreads();
+  }
+  best = shfl_best(best, 2);
+  const int s = s0 + r;
+  // Child stage: children of the assigned parent; the cross term is a sum of
+  // dtype-rounded elementwise products (quantizer.py:223-226).
+  ArgMin cb = {0.f, -1};
+  const int p = best.i;
+  for (int c = l4; c < C; c += 4) {
+    const long crow = ((pbase + p) * C + c);
+    double acc = 0.0;
+    for (int d = 0; d < D; ++d) acc += (double)rnd<DT>(__fmul_rn(kk[r * ld + d], to_f(children[crow * D + d])));
+    const float cross = rnd64<DT>(acc);
+    const float two = rnd<DT>(__fmul_rn(2.f, cross));
+    const float t1 = rnd<DT>(__fadd_rn(my_ksq, c_sq[crow]));
+    const float dd = rnd<DT>(__fsub_rn(t1, two));
+    if (better(dd, c, cb.v, cb.i)) cb = {dd, c};
+  }
+  cb = shfl_best(cb, 2);
+  if (l4 == 0 && s < S) {
+    passign[(long)g * S + s] = p;
+    cassign[(long)g * S + s] = cb.i;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Stable counting sort by parent
+// ---------------------------------------------------------------------------
+// hist[g][seg][p] = number of keys of segment seg assigned to parent p.
+__global__ void bucket_hist_kernel(const int* __restrict__ passign, int S, int M0, int nseg, int seg_len,
+                                   int* __restrict__ hist) {
+  extern __shared__ int sh[];
+  const int g = blockIdx.y, seg = blockIdx.x;
+  for (int p = threadIdx.x; p < M0; p += blockDim.x) sh[p] = 0;
+  __syncthreads();
+  const int s_end = min(S, (seg + 1) * seg_len);
+  for (int s = seg * seg_len + threadIdx.x; s < s_end; s += blockDim.x) atomicAdd(&sh[passign[(long)g * S + s]], 1);
+  __syncthreads();
+  int* out = hist + ((long)g * nseg + seg) * M0;
+  for (int p = threadIdx.x; p < M0; p += blockDim.x) out[p] = sh[p];
+}
+
+// Per g: bucket totals -> exclusive offsets; hist rewritten in place as each
+// segment's first slot per bucket.  Writes parent offsets/counts, the number
+// of non-empty parents and folds it into the global minimum.
+__global__ void bucket_scan_kernel(int* __restrict__ hist, int M0, int nseg, int* __restrict__ poff,
+                                   int* __restrict__ pcnt, int* __restrict__ nvalid, int* __restrict__ gmin_valid) {
+  extern __shared__ int sh[];  // [M0] totals, then scan scratch
+  const int g = blockIdx.x;
+  int* base = hist + (long)g * nseg * M0;
+  for (int p = threadIdx.x; p < M0; p += blockDim.x) {
+    int run = 0;
+    for (int seg = 0; seg < nseg; ++seg) {
+      const int c = base[(long)seg * M0 + p];
+      base[(long)seg * M0 + p] = run;
+      run += c;
+    }
+    sh[p] = run;
+  }
+  __syncthreads();
+  // exclusive scan of the totals (M0 <= 8192), sequential per thread chunk
+  __shared__ int chunk_sum[1024];
+  const int nt = blockDim.x, per = (M0 + nt - 1) / nt;
+  const int lo = threadIdx.x * per, hi = min(M0, lo + per);
+  int acc = 0, nz = 0;
+  for (int p = lo; p < hi; ++p) {
+    acc += sh[p];
+    nz += sh[p] > 0;
+  }
+  chunk_sum[threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int t = 0; t < nt; ++t) {
+      const int c = chunk_sum[t];
+      chunk_sum[t] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  int run = chunk_sum[threadIdx.x];
+  for (int p = lo; p < hi; ++p) {
+    const int c = sh[p];
+    poff[(long)g * M0 + p] = run;
+    pcnt[(long)g * M0 + p] = c;
+    for (int seg = 0; seg < nseg; ++seg) base[(long)seg * M0 + p] += run;
+    run += c;
+  }
+  // number of valid parents
+  for (int o = 16; o > 0; o >>= 1) nz += __shfl_xor_sync(0xffffffffu, nz, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) chunk_sum[threadIdx.x >> 5] = nz;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int tot = 0;
+    for (int w = 0; w < (nt + 31) / 32; ++w) tot += chunk_sum[w];
+    nvalid[g] = tot;
+    if (gmin_valid) atomicMin(gmin_valid, tot);
+  }
+}
+
+// One warp per segment walks its keys in order; ranks inside a 32-key group
+// come from __match_any_sync, so the order inside every bucket is key order.
+__global__ void bucket_scatter_kernel(const int* __restrict__ passign, const int* __restrict__ hist, int S, int M0,
+                                      int nseg, int seg_len, int* __restrict__ order) {
+  extern __shared__ int run[];  // [M0]
+  const int g = blockIdx.y, seg = blockIdx.x, lane = threadIdx.x;
+  const int* off = hist + ((long)g * nseg + seg) * M0;
+  for (int p = lane; p < M0; p += 32) run[p] = off[p];
+  __syncwarp();
+  const int s_begin = seg * seg_len, s_end = min(S, s_begin + seg_len);
+  for (int s0 = s_begin; s0 < s_end; s0 += 32) {
+    const int s = s0 + lane;
+    const bool act = s < s_end;
+    const int p = act ? passign[(long)g * S + s] : -1 - lane;  // inactive lanes never match
+    const unsigned peers = __match_any_sync(0xffffffffu, p);
+    const unsigned lower = peers & ((1u << lane) - 1u);
+    if (act) {
+      const int pos = run[p] + __popc(lower);
+      order[(long)g * S + pos] = s;
+    }
+    __syncwarp();
+    if (act && (peers >> lane) == 1u) run[p] += __popc(peers);  // highest lane of the group
+    __syncwarp();
+  }
+}
+
+// One warp per parent: members in key order; lane owns dims lane, lane+32, ...
+template <int DT, int CMAX, int DMAX>
+__global__ void __launch_bounds__(256) aggregate_kernel(
+    const typename Storage<DT>::T* __restrict__ values, Strides3 vs, int H, int S, int D, int M0, int C,
+    const int* __restrict__ order, const int* __restrict__ poff, const int* __restrict__ pcnt,
+    const int* __restrict__ cassign, typename Storage<DT>::T* __restrict__ pagg,
+    typename Storage<DT>::T* __restrict__ cagg, float* __restrict__ pacc, float* __restrict__ cacc,
+    int* __restrict__ ccnt, long rows) {
+  constexpr int NJ = DMAX / 32;
+  const int lane = threadIdx.x & 31;
+  const long gp = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gp >= rows) return;
+  const int g = (int)(gp / M0);
+  const int b = g / H, h = g % H;
+  const long vbase = (long)b * vs.b + (long)h * vs.h;
+  float ap[NJ];
+  float ac[CMAX][NJ];
+  int cn[CMAX];
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    ap[j] = 0.f;
+#pragma unroll
+    for (int c = 0; c < CMAX; ++c) ac[c][j] = 0.f;
+  }
+#pragma unroll
+  for (int c = 0; c < CMAX; ++c) cn[c] = 0;
+  const int beg = poff[gp], n = pcnt[gp];
+  for (int i = 0; i < n; ++i) {
+    const int s = order[(long)g * S + beg + i];
+    const int cc = cassign[(long)g * S + s];
+#pragma unroll
+    for (int c = 0; c < CMAX; ++c) cn[c] += (c == cc);
+    const typename Storage<DT>::T* row = values + vbase + (long)s * vs.s;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int d = lane + 32 * j;
+      if (d < D) {
+        const float v = to_f(row[d]);
+        ap[j] = __fadd_rn(ap[j], v);
+#pragma unroll
+        for (int c = 0; c < CMAX; ++c)
+          if (c == cc) ac[c][j] = __fadd_rn(ac[c][j], v);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const int d = lane + 32 * j;
+    if (d < D) {
+      pagg[gp * D + d] = from_f<DT>(ap[j]);
+      if (pacc) pacc[gp * D + d] = ap[j];
+#pragma unroll
+      for (int c = 0; c < CMAX; ++c)
+        if (c < C) {
+          cagg[(gp * C + c) * D + d] = from_f<DT>(ac[c][j]);
+          if (cacc) cacc[(gp * C + c) * D + d] = ac[c][j];
+        }
+    }
+  }
+  if (lane == 0)
+#pragma unroll
+    for (int c = 0; c < CMAX; ++c)
+      if (c < C) ccnt[gp * C + c] = cn[c];
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers
+// ---------------------------------------------------------------------------
+template <int DT>
+int launch_prep_codebook(const float* parents32, const float* children32, int H, int M0, int C, int D,
+                         void* parents_dt, void* children_dt, float* p_sq, float* c_sq, cudaStream_t st) {
+  using T = typename Storage<DT>::T;
+  const long rp = (long)H * M0, rc = rp * C;
+  prep_codebook_kernel<DT><<<(unsigned)((rp + 7) / 8), 256, 0, st>>>(parents32, (T*)parents_dt, p_sq, rp, D);
+  prep_codebook_kernel<DT><<<(unsigned)((rc + 7) / 8), 256, 0, st>>>(children32, (T*)children_dt, c_sq, rc, D);
+  return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
+}
+
+int bucket_segments(int S, int M0, int* seg_len) {
+  int nseg = S / 256;
+  if (nseg < 1) nseg = 1;
+  if (nseg > 64) nseg = 64;
+  *seg_len = (S + nseg - 1) / nseg;
+  if (*seg_len < 1) *seg_len = 1;
+  return nseg;
+}
+
+size_t quantize_workspace_bytes(int G, int S, int M0) {
+  int seg_len;
+  const int nseg = bucket_segments(S, M0, &seg_len);
+  return align_up((size_t)G * nseg * M0 * sizeof(int)) + align_up((size_t)G * (S > 0 ? S : 1) * sizeof(int)) +
+         align_up((size_t)G * M0 * sizeof(int));
+}
+
+template <int DT>
+int launch_quantize(const QuantizeArgs& a, cudaStream_t st) {
+  using T = typename Storage<DT>::T;
+  const int G = a.B * a.H;
+  if (a.D > 256 || a.C > 8 || a.M0 > 8192) return AVQ_ERR_UNSUPPORTED;
+  int seg_len;
+  const int nseg = bucket_segments(a.S, a.M0, &seg_len);
+  char* ws = (char*)a.workspace;
+  int* hist = (int*)ws;
+  ws += align_up((size_t)G * nseg * a.M0 * sizeof(int));
+  int* order = (int*)ws;
+  ws += align_up((size_t)G * (a.S > 0 ? a.S : 1) * sizeof(int));
+  int* poff = (int*)ws;
+  if (a.S > 0) {
+    const size_t smem = (size_t)((AS_ROWS + AS_COLS) * (a.D + 1) + AS_ROWS) * sizeof(float);
+    auto kfn = assign_kernel<DT>;
+    cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dim3 grid((a.S + AS_ROWS - 1) / AS_ROWS, G);
+    kfn<<<grid, 256, smem, st>>>((const T*)a.keys, a.ks, a.H, a.S, a.D, a.M0, a.C, (const T*)a.parents_dt, a.p_sq,
+                                 (const T*)a.children_dt, a.c_sq, a.passign, a.cassign);
+    bucket_hist_kernel<<<dim3(nseg, G), 256, a.M0 * sizeof(int), st>>>(a.passign, a.S, a.M0, nseg, seg_len, hist);
+  } else {
+    cudaMemsetAsync(hist, 0, (size_t)G * nseg * a.M0 * sizeof(int), st);
+  }
+  bucket_scan_kernel<<<G, 1024, a.M0 * sizeof(int), st>>>(hist, a.M0, nseg, poff, a.pcnt, a.nvalid, a.gmin_valid);
+  if (a.S > 0)
+    bucket_scatter_kernel<<<dim3(nseg, G), 32, a.M0 * sizeof(int), st>>>(a.passign, hist, a.S, a.M0, nseg, seg_len,
+                                                                         order);
+  const long rows = (long)G * a.M0;
+  const unsigned blocks = (unsigned)((rows + 7) / 8);
+#define AVQ_AGG(CM, DM)                                                                                          \
+  aggregate_kernel<DT, CM, DM><<<blocks, 256, 0, st>>>((const T*)a.values, a.vs, a.H, a.S, a.D, a.M0, a.C, order, \
+                                                       poff, a.pcnt, a.cassign, (T*)a.pagg, (T*)a.cagg, a.pacc,  \
+                                                       a.cacc, a.ccnt, rows)
+  if (a.C <= 4) {
+    if (a.D <= 64) AVQ_AGG(4, 64); else if (a.D <= 128) AVQ_AGG(4, 128); else AVQ_AGG(4, 256);
+  } else {
+    if (a.D <= 64) AVQ_AGG(8, 64); else if (a.D <= 128) AVQ_AGG(8, 128); else AVQ_AGG(8, 256);
+  }
+#undef AVQ_AGG
+  return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
+}
+
+template int launch_prep_codebook<DT_F32>(const float*, const float*, int, int, int, int, void*, void*, float*, float*,
+                                          cudaStream_t);
+template int launch_prep_codebook<DT_BF16>(const float*, const float*, int, int, int, int, void*, void*, float*,
+                                           float*, cudaStream_t);
+template int launch_prep_codebook<DT_F16>(const float*, const float*, int, int, int, int, void*, void*, float*, float*,
+                                          cudaStream_t);
+template int launch_quantize<DT_F32>(const QuantizeArgs&, cudaStream_t);
+template int launch_quantize<DT_BF16>(const QuantizeArgs&, cudaStream_t);
+template int launch_quantize<DT_F16>(const QuantizeArgs&, cudaStream_t);
+
+}  // namespace avq

@@ -1,0 +1,111 @@
+/*
+ * avqa_b200 -- C ABI of the B200 AVQ-attention kernels.
+ *
+ * Every entry point takes raw device pointers, plain integer sizes and a
+ * CUDA stream (as void*), enqueues its kernels on that stream and returns an
+ * int status: 0 = AVQ_OK, otherwise an error code; avq_last_error() returns
+ * the message of the calling thread's last failure.  Nothing here allocates
+ * device memory: scratch space is the caller's `workspace`, sized by the
+ * matching *_workspace_size() query.
+ *
+ * dtype: 0 = fp32, 1 = bf16, 2 = fp16.  Tensors in "dtype" hold elements of
+ * that type; counts and indices are int32.  Strides are in elements: element
+ * (b, h, s, d) of a 4-D operand is at b*stride[0] + h*stride[1] + s*stride[2] + d
+ * (so module layout [B, S, H*D] is {S*H*D, D, H*D} and head layout
+ * [B, H, S, D] is {H*S*D, S*D, D}).
+ *
+ * Reference interfaces replaced (paths in sachncs/avqa):
+ *   avq_prepare_codebook  attention_module.py:344-348 (codebook cast to the
+ *                         input dtype) + the squared norms of quantizer.py:208,224
+ *   avq_quantize          Backend.quantize / TorchBackend.quantize, backend.py:216-237
+ *                         -> EuclideanHierarchicalQuantizer.precompute, quantizer.py:166-278
+ *   avq_forward           run_pipeline stages 6-11, pipeline.py:322-393, with
+ *                         AVQAttention.refine_and_output, attention_module.py:471-544
+ *   avq_append            resolve_kv_cache + KVCache.append, attention_module.py:350-367,
+ *                         cache.py:246-260, plus the re-quantization of the grown key
+ *                         set (quantizer.py:166-278) done incrementally
+ *   avq_reduce_min        the budget's min over (b,h) of valid parents, pipeline.py:341-342
+ */
+#ifndef AVQA_B200_H
+#define AVQA_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AVQ_OK 0
+#define AVQ_ERR_ARG 1
+#define AVQ_ERR_CUDA 2
+#define AVQ_ERR_UNSUPPORTED 3
+#define AVQ_ERR_WORKSPACE 4
+
+/* Library version string. */
+const char* avq_version(void);
+
+/* Copy the calling thread's last error message into buf (NUL-terminated);
+ * returns its full length. */
+int avq_last_error(char* buf, int len);
+
+/* Cast the fp32 master codebook to `dtype` and compute the dtype-rounded
+ * squared norms.  parents32 [H,M0,D], children32 [H,M0,C,D] (fp32);
+ * outputs parents_dt [H,M0,D], children_dt [H,M0,C,D] (dtype),
+ * p_sq [H,M0], c_sq [H,M0,C] (fp32 holding dtype values). */
+int avq_prepare_codebook(int dtype, const float* parents32, const float* children32, int H, int M0, int C, int D,
+                         void* parents_dt, void* children_dt, float* p_sq, float* c_sq, void* stream);
+
+size_t avq_quantize_workspace_size(int B, int H, int S, int M0);
+
+/* Hierarchical VQ of S keys per (b,h) against the (b,h)'s head codebook.
+ * keys/values: dtype with strides key_strides/value_strides (3 longs each).
+ * Outputs (G = B*H): passign, cassign [G,S]; pagg [G,M0,D] and cagg
+ * [G,M0,C,D] in dtype; pacc/cacc the fp32 sums before narrowing (may be
+ * NULL); pcnt [G,M0], ccnt [G,M0,C] exact counts; nvalid [G] non-empty
+ * parents; gmin_valid (may be NULL) receives atomicMin(nvalid) -- the caller
+ * initialises it (e.g. to INT_MAX). */
+int avq_quantize(int dtype, const void* keys, const long long* key_strides, const void* values,
+                 const long long* value_strides, int B, int H, int S, int D, int M0, int C, const void* parents_dt,
+                 const float* p_sq, const void* children_dt, const float* c_sq, int* passign, int* cassign,
+                 void* pagg, void* cagg, float* pacc, float* cacc, int* pcnt, int* ccnt, int* nvalid,
+                 int* gmin_valid, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Number of int32 slots per (b,h) in the `selected` output of avq_forward:
+ * the sum of the per-pass budget caps for base budget P. */
+int avq_selection_stride(int P, int passes, float pass_decay);
+
+size_t avq_forward_workspace_size(int B, int H, int T, int D, int M0, int P, int passes, float pass_decay);
+
+/* AVQ attention of T queries per (b,h) over a quantized key set.
+ * q: dtype with q_strides; out: fp32 with out_strides (module layout
+ * [B,T,H*D] -> {T*H*D, D, H*D}).  min_valid: device int, the minimum over
+ * every (b,h) of the call (or of all ranks) of non-empty parents; the
+ * routing budget is min(P, *min_valid).  hvaq: 0 off, 1 entropy schedule,
+ * 2 linear schedule; beta0 the base temperature (1/sqrt(D) when the config
+ * says 0), alpha the linear slope.  importance_out [G,M0] fp32, selected_out
+ * [G, avq_selection_stride()] int32 and pass_counts_out [passes] int32 are
+ * optional diagnostics (NULL to skip). */
+int avq_forward(int dtype, const void* q, const long long* q_strides, int B, int H, int T, int D, int M0, int C,
+                const void* parents_dt, const void* children_dt, const void* pagg, const void* cagg, const int* pcnt,
+                const int* ccnt, const int* min_valid, int P, int passes, float pass_decay, int hvaq, float beta0,
+                float alpha, float* out, const long long* out_strides, float* importance_out, int* selected_out,
+                int* pass_counts_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Append Tn new tokens per (b,h) to a quantized key set, in order:
+ * assign each new key, add its value to the fp32 bucket sums pacc/cacc,
+ * refresh pagg/cagg, bump pcnt/ccnt/nvalid.  When kpage/vpage are not NULL
+ * the raw k/v are also written to page slots slot0.. (page_strides). */
+int avq_append(int dtype, const void* k, const long long* k_strides, const void* v, const long long* v_strides,
+               int B, int H, int Tn, int D, int M0, int C, const void* parents_dt, const float* p_sq,
+               const void* children_dt, const float* c_sq, float* pacc, float* cacc, void* pagg, void* cagg,
+               int* pcnt, int* ccnt, int* nvalid, void* kpage, void* vpage, const long long* page_strides, int slot0,
+               void* stream);
+
+/* *out = min(v[0..n)). */
+int avq_reduce_min(const int* v, int n, int* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AVQA_B200_H */

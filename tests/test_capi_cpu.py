@@ -1,0 +1,61 @@
+"""The C-ABI library loads and exports every declared symbol; host-side
+argument checks work without a GPU (no kernel is launched)."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from avqa_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "avqa_b200.h"
+
+
+def declared() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(avq_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_binding() -> None:
+    assert set(declared()) == set(_lib.exported_symbols())
+
+
+def test_library_exports_every_declared_symbol() -> None:
+    lib = _lib.load()
+    for name in declared():
+        assert hasattr(lib, name), name
+    assert lib.avq_version().startswith(b"avqa_b200")
+
+
+def test_selection_stride_matches_pass_caps() -> None:
+    from avqa_b200.ops import pass_caps
+    lib = _lib.load()
+    assert lib.avq_selection_stride(48, 3, 0.5) == 48 + 24 + 12 == sum(pass_caps(48, 3, 0.5))
+    assert lib.avq_selection_stride(8, 1, 1.0) == 8
+    assert lib.avq_selection_stride(5, 3, 0.3) == sum(pass_caps(5, 3, 0.3))
+
+
+@pytest.mark.parametrize("call", ["bad_dtype", "bad_budget", "null"])
+def test_forward_rejects_bad_arguments(call: str) -> None:
+    lib = _lib.load()
+    s = (ctypes.c_longlong * 3)(1, 1, 1)
+    args = dict(dtype=1, P=4, M0=8, q=None)
+    if call == "bad_dtype":
+        args["dtype"] = 7
+    if call == "bad_budget":
+        args["P"] = 9
+    rc = lib.avq_forward(args["dtype"], args["q"], s, 1, 1, 1, 8, args["M0"], 2, None, None, None, None, None, None,
+                         None, args["P"], 1, 1.0, 0, 0.0, 1.0, None, s, None, None, None, None, 0, None)
+    assert rc == 1
+    msg = _lib.last_error()
+    assert msg.startswith("avq_forward")
+    if call == "bad_budget":
+        assert "exceeds number of parents" in msg
+
+
+def test_workspace_queries() -> None:
+    lib = _lib.load()
+    assert lib.avq_quantize_workspace_size(4, 32, 8192, 512) > 4 * 32 * 8192 * 4
+    assert lib.avq_forward_workspace_size(1, 1, 1, 8, 4, 2, 1, 1.0) > 0

@@ -1,0 +1,98 @@
+"""CUDA path vs the reference's recorded outputs (tests/golden) and the oracle.
+
+Every golden case is replayed through the C ABI (quantize, forward, append):
+assignments, counts, aggregates and routed indices must equal the reference
+bit for bit; outputs must be within 2e-5 (fp32) / 1e-2 (bf16, fp16)
+normwise of the reference, and match the oracle.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import golden_io as G
+from oracle import avq_oracle as O
+from parity import (OUT_TOL, assert_quant_equal, assert_routing_equal, cuda_forward_heads, heads_view, normrel,
+                    oracle_config, quant_arrays, to_dev)
+
+pytestmark = pytest.mark.gpu
+
+
+def _golden_quant(g: G.Golden, i: int, shape_g: tuple) -> dict:
+    return {
+        "passign": g.get(f"quant{i}_passign").reshape(shape_g[0], -1).astype(np.int64),
+        "cassign": g.get(f"quant{i}_cassign").reshape(shape_g[0], -1).astype(np.int64),
+        "pagg": g.f(f"quant{i}_pagg").reshape(shape_g[0], -1, shape_g[2]),
+        "cagg": g.f(f"quant{i}_cagg").reshape(shape_g[0], -1, shape_g[1], shape_g[2]),
+        "pcnt": g.get(f"quant{i}_pcnt").reshape(shape_g[0], -1),
+        "ccnt": g.get(f"quant{i}_ccnt").reshape(shape_g[0], -1, shape_g[1]),
+    }
+
+
+def _cfg(g: G.Golden) -> O.ForwardConfig:
+    hc = g.meta["config"]["hopfield"]
+    return oracle_config(g.w, hc["adaptive"], hc["alpha"], hc["beta_init"])
+
+
+@pytest.mark.parametrize("name", G.case_names())
+def test_golden_case(name: str) -> None:
+    from avqa_b200 import ops
+    g = G.load(name)
+    w, dt = g.w, g.dt
+    cfg = _cfg(g)
+    B, H, D, M0, C = w["B"], w["H"], w["D"], w["M0"], w["C"]
+    q, k, v = g.inputs()
+    P32, C32 = g.get("parents32"), g.get("children32")
+    cb = ops.prepare_codebook(torch.from_numpy(P32), torch.from_numpy(C32), G.TD[dt], torch.device("cuda"))
+    pd, cd = O.cast_codebook(P32, C32, dt)
+    # the cast codebook equals the oracle's
+    np.testing.assert_array_equal(cb.parents.float().cpu().numpy(), pd)
+    np.testing.assert_array_equal(cb.children.float().cpu().numpy(), cd)
+    qd, kd, vd = to_dev(q, dt), to_dev(k, dt), to_dev(v, dt)
+    tol = OUT_TOL[dt]
+    if w["decode_steps"]:
+        from avqa_b200.workloads import Workload, make_decode_tokens
+        st = ops.quantize(heads_view(kd, H), heads_view(vd, H), cb, keep_sums=True)
+        toks = [tuple(O.rnd(x.numpy(), dt) for x in tok) for tok in make_decode_tokens(Workload(**w), w["decode_steps"])]
+
+        def calls():
+            kk, vv = k, v
+            for (qt, kt, vt) in toks:
+                ops.append(st, heads_view(to_dev(kt, dt), H), heads_view(to_dev(vt, dt), H), cb)
+                kk, vv = np.concatenate([kk, kt], 1), np.concatenate([vv, vt], 1)
+                yield to_dev(qt, dt), kk, vv, st, qt
+    elif w["q_chunk"]:
+        st = ops.quantize(heads_view(kd, H), heads_view(vd, H), cb)
+
+        def calls():
+            for c0 in range(0, w["T"], w["q_chunk"]):
+                yield qd[:, c0:c0 + w["q_chunk"]], k, v, st, q[:, c0:c0 + w["q_chunk"]]
+    else:
+        st = ops.quantize(heads_view(kd, H), heads_view(vd, H), cb)
+
+        def calls():
+            yield qd, k, v, st, q
+    sel_i = 0
+    for ci, (qdev, kfull, vfull, st, qnp) in enumerate(calls()):
+        res = O.forward(qnp, kfull, vfull, pd, cd, cfg)
+        got_q = quant_arrays(st, B, H)
+        assert_quant_equal(got_q, res["quant"], tag=f"{name} call{ci} vs oracle")
+        want = _golden_quant(g, ci, (B * H, C, D))
+        if got_q["passign"] is not None:
+            np.testing.assert_array_equal(got_q["passign"], want["passign"])
+            np.testing.assert_array_equal(got_q["cassign"], want["cassign"])
+        for key in ("pagg", "cagg", "pcnt", "ccnt"):
+            np.testing.assert_array_equal(got_q[key], want[key], err_msg=f"{name} call{ci} {key} vs reference")
+        if res.get("naive"):
+            continue
+        out, diag = cuda_forward_heads(heads_view(qdev, H), st, cb, cfg)
+        assert_routing_equal(diag, res, tag=f"{name} call{ci}")
+        for s in diag.selections():
+            gs = g.get(f"sel{sel_i}").reshape(B * H, -1)
+            np.testing.assert_array_equal(s.long().cpu().numpy(), gs, err_msg=f"{name} sel{sel_i} vs reference")
+            sel_i += 1
+        out_bte = out.transpose(0, 2, 1, 3).reshape(B, -1, H * D)
+        ref_out = g.get(f"out{ci}").reshape(out_bte.shape)
+        assert normrel(out_bte, ref_out) <= tol, f"{name} call{ci}: {normrel(out_bte, ref_out)} vs reference"
+        assert normrel(out_bte, res["out_bte"]) <= tol
