@@ -29,13 +29,31 @@ _SIGS = {
     "avq_quantize": ([_I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                       _P, _P, _P, _Z, _P], _I),
     "avq_selection_stride": ([_I, _I, _F], _I),
-    "avq_forward_workspace_size": ([_I, _I, _I, _I, _I, _I, _I, _F], _Z),
+    "avq_forward_workspace_size": ([_I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I], _Z),
     "avq_forward": ([_I, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _I, _F, _F, _P, _P,
                      _P, _P, _P, _P, _Z, _P], _I),
     "avq_append": ([_I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                     _P, _I, _P], _I),
     "avq_reduce_min": ([_P, _I, _P, _P], _I),
+    "avq_profile_begin": ([], _I),
+    "avq_profile_end": ([ctypes.c_char_p, _I, _P, _P, _I], _I),
 }
+
+
+def profile_begin() -> None:
+    load().avq_profile_begin()
+
+
+def profile_end() -> dict[str, tuple[float, int]]:
+    """Per-kernel (total ms, launches) recorded since :func:`profile_begin`."""
+    names = ctypes.create_string_buffer(4096)
+    ms = (ctypes.c_float * 64)()
+    cnt = (ctypes.c_int * 64)()
+    n = load().avq_profile_end(names, len(names), ctypes.addressof(ms), ctypes.addressof(cnt), 64)
+    if n < 0:
+        raise BackendError(f"avq_profile_end failed: {last_error()}")
+    keys = names.value.decode().split("\n")[:n]
+    return {k: (float(ms[i]), int(cnt[i])) for i, k in enumerate(keys)}
 
 _lib: ctypes.CDLL | None = None
 

@@ -494,12 +494,23 @@ struct FwdWorkspace {
   float *sbuf, *m, *l, *z, *a, *beta, *imp;
   double *part0, *part1;
   int *sel, *pass_cnt;
+  void* slog;  // tensor-core path: logits scratch when not in shared memory (or kept for HVAQ)
   size_t bytes;
 };
 
-static FwdWorkspace carve(void* base, int G, int T, int D, int M0, int sel_stride) {
-  const int nqt = (T + PA_ROWS - 1) / PA_ROWS;
+bool forward_uses_mma(int dtype, int D, int M0, int C) {
+  return parent_attn_mma_ok(dtype, D, M0) && (C == 4 || C == 8);
+}
+
+// Layout of the caller's workspace.  The exact path keeps fp32 logits
+// [G,T,M0]; the tensor-core path keeps dtype logits only when they do not fit
+// in shared memory or must survive for the HVAQ pass.
+static FwdWorkspace carve(void* base, int dtype, int G, int T, int D, int M0, int C, int sel_stride, int hvaq) {
+  const bool mma = forward_uses_mma(dtype, D, M0, C);
+  const int rows = mma ? PM_ROWS_PUBLIC : PA_ROWS;
+  const int nqt = (T + rows - 1) / rows;
   const long GT = (long)G * (T > 0 ? T : 1);
+  const int dtb = dtype == DT_F32 ? 4 : 2;
   char* p = (char*)base;
   FwdWorkspace w;
   auto take = [&](size_t n) {
@@ -507,23 +518,25 @@ static FwdWorkspace carve(void* base, int G, int T, int D, int M0, int sel_strid
     p += align_up(n);
     return (void*)r;
   };
-  w.sbuf = (float*)take(sizeof(float) * GT * M0);
+  w.sbuf = mma ? nullptr : (float*)take(sizeof(float) * GT * M0);
+  w.slog = (mma && (hvaq || !parent_attn_mma_smem_mode(D, M0))) ? take(parent_attn_mma_scratch(G, T, M0, dtb)) : nullptr;
   w.m = (float*)take(sizeof(float) * GT);
   w.l = (float*)take(sizeof(float) * GT);
   w.z = (float*)take(sizeof(float) * GT);
   w.beta = (float*)take(sizeof(float) * GT);
-  w.a = (float*)take(sizeof(float) * GT * D);
+  w.a = (float*)take((size_t)(mma ? dtb : 4) * GT * D);
   w.imp = (float*)take(sizeof(float) * (long)G * M0);
   w.part0 = (double*)take(sizeof(double) * (long)G * (nqt > 0 ? nqt : 1) * M0);
-  w.part1 = (double*)take(sizeof(double) * (long)G * (nqt > 0 ? nqt : 1) * M0);
+  w.part1 = hvaq ? (double*)take(sizeof(double) * (long)G * (nqt > 0 ? nqt : 1) * M0) : nullptr;
   w.sel = (int*)take(sizeof(int) * (long)G * sel_stride);
   w.pass_cnt = (int*)take(sizeof(int) * MAX_PASSES);
   w.bytes = (size_t)(p - (char*)base);
   return w;
 }
 
-size_t forward_workspace_bytes(int G, int T, int D, int M0, int P, int passes, float decay) {
-  return carve(nullptr, G, T, D, M0, selection_stride(P, passes, decay)).bytes;
+size_t forward_workspace_bytes(int dtype, int G, int T, int D, int M0, int C, int P, int passes, float decay,
+                               int hvaq) {
+  return carve(nullptr, dtype, G, T, D, M0, C, selection_stride(P, passes, decay), hvaq).bytes;
 }
 
 template <int DT, int DMAX, int CMAX>
@@ -536,6 +549,7 @@ static void launch_correct(const ForwardArgs& a, const FwdWorkspace& w, float sq
   const size_t smem = sizeof(float) * ((size_t)PA_ROWS * (a.D + 1) + (size_t)NCH * (a.D + 1) + (size_t)NCH * a.D +
                                        (size_t)CJ * a.D + PA_ROWS * CJ + PA_ROWS * NCH + 2 * NCH + CJ) +
                       sizeof(int) * CJ;
+  AVQ_TIMED("correct_exact", st);
   auto k = correct_kernel<DT, DMAX, CMAX>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   k<<<dim3(nqt, G), 256, smem, st>>>((const T*)a.q, a.qs, a.H, a.T, a.D, a.M0, a.C, sqrtD, (const T*)a.children_dt,
@@ -552,7 +566,10 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
   const int G = a.B * a.H;
   if (G == 0 || a.T == 0) return AVQ_OK;
   const int sel_stride = selection_stride(a.P, a.passes, a.pass_decay);
-  FwdWorkspace w = carve(a.workspace, G, a.T, a.D, a.M0, sel_stride);
+  const bool qaligned = ((uintptr_t)a.q % 16 == 0) && a.qs.s % 8 == 0 && a.qs.h % 8 == 0 && a.qs.b % 8 == 0;
+  const bool mma = forward_uses_mma(DT, a.D, a.M0, a.C);
+  if (mma && !qaligned) return AVQ_ERR_UNSUPPORTED;
+  FwdWorkspace w = carve(a.workspace, DT, G, a.T, a.D, a.M0, a.C, sel_stride, a.hvaq);
   if (a.workspace_bytes < w.bytes) return AVQ_ERR_WORKSPACE;
   PassLayout lay;
   lay.n = a.passes;
@@ -564,14 +581,53 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
   int* sel = a.selected_out ? a.selected_out : w.sel;
   int* pcnt_out = a.pass_counts_out ? a.pass_counts_out : w.pass_cnt;
   const float sqrtD = (float)std::sqrt((double)a.D);
-  const int nqt = (a.T + PA_ROWS - 1) / PA_ROWS;
-  const size_t pa_smem = sizeof(float) * ((size_t)(PA_ROWS + PA_COLS) * (a.D + 1) + PA_ROWS * (PA_COLS + 1) + PA_COLS);
   int npow2 = 1;
   while (npow2 < a.M0) npow2 <<= 1;
   const size_t rt_smem = sizeof(unsigned long long) * npow2 + a.M0;
+  auto rk = route_kernel<DT>;
+  cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rt_smem);
+  auto route = [&](auto... args) {
+    AVQ_TIMED("route", st);
+    rk<<<G, 1024, rt_smem, st>>>(args...);
+  };
+  const bool hv = a.hvaq != 0;
+  float* imp_out = a.importance_out ? a.importance_out : w.imp;
 
+  if constexpr (DT != DT_F32) {
+    if (mma) {
+      const int nqt = (a.T + PM_ROWS_PUBLIC - 1) / PM_ROWS_PUBLIC;
+      PAArgs pa{a.q, a.qs, a.B, a.H, a.T, a.D, a.M0, sqrtD, a.parents_dt, a.pagg, a.pcnt, 0, hv ? 1 : 0, w.slog,
+                !hv && parent_attn_mma_smem_mode(a.D, a.M0), w.m, w.l, w.z, w.a, w.part0, sel, sel_stride, pcnt_out,
+                a.hvaq, a.beta0, a.alpha, w.beta};
+      int rc = launch_parent_attn_mma<DT>(pa, st);
+      if (rc != AVQ_OK) return rc;
+      route(w.part0, nqt, a.pcnt, a.M0, a.min_valid, a.P, a.passes, a.pass_decay, 0,
+                                   (!hv && a.passes > 1) ? 1 : 0, lay, sel, sel_stride, pcnt_out, imp_out);
+      if (hv) {
+        pa.mode = 1;
+        pa.keep_logits = 0;
+        pa.imp_part = w.part1;
+        rc = launch_parent_attn_mma<DT>(pa, st);
+        if (rc != AVQ_OK) return rc;
+        if (a.passes > 1)
+          route(w.part1, nqt, a.pcnt, a.M0, a.min_valid, a.P, a.passes, a.pass_decay, 1, 1,
+                                       lay, sel, sel_stride, pcnt_out, w.imp);
+      }
+      CorrArgs ca{a.q, a.qs, a.B, a.H, a.T, a.D, a.M0, a.C, sqrtD, a.parents_dt, a.children_dt, a.pagg, a.cagg,
+                  a.pcnt, a.ccnt, w.m, w.l, w.z, hv ? w.beta : nullptr, w.a, sel, sel_stride, pcnt_out, a.passes,
+                  {0, 0, 0, 0, 0, 0, 0, 0}, a.passes > 1 ? 1 : 0, a.out, a.os};
+      for (int k = 0; k < a.passes; ++k) ca.pass_off[k] = lay.off[k];
+      rc = launch_correct_mma<DT>(ca, st);
+      if (rc != AVQ_OK) return rc;
+      return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
+    }
+  }
+
+  const int nqt = (a.T + PA_ROWS - 1) / PA_ROWS;
+  const size_t pa_smem = sizeof(float) * ((size_t)(PA_ROWS + PA_COLS) * (a.D + 1) + PA_ROWS * (PA_COLS + 1) + PA_COLS);
 #define AVQ_PA(DM, MODE, PART)                                                                                       \
   do {                                                                                                               \
+    AVQ_TIMED(MODE ? "parent_attn_hvaq_exact" : "parent_attn_exact", st);                                            \
     auto k = parent_attn_kernel<DT, DM>;                                                                             \
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pa_smem);                              \
     k<<<dim3(nqt, G), 256, pa_smem, st>>>((const T*)a.q, a.qs, a.H, a.T, a.D, a.M0, sqrtD, (const T*)a.parents_dt,   \
@@ -584,18 +640,13 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
     else if (a.D <= 128) AVQ_PA(128, MODE, PART);              \
     else AVQ_PA(256, MODE, PART);                              \
   } while (0)
-
-  auto rk = route_kernel<DT>;
-  cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rt_smem);
   AVQ_PA_D(0, w.part0);
-  const bool hv = a.hvaq != 0;
-  rk<<<G, 1024, rt_smem, st>>>(w.part0, nqt, a.pcnt, a.M0, a.min_valid, a.P, a.passes, a.pass_decay, 0,
-                               (!hv && a.passes > 1) ? 1 : 0, lay, sel, sel_stride, pcnt_out,
-                               a.importance_out ? a.importance_out : w.imp);
+  route(w.part0, nqt, a.pcnt, a.M0, a.min_valid, a.P, a.passes, a.pass_decay, 0,
+                               (!hv && a.passes > 1) ? 1 : 0, lay, sel, sel_stride, pcnt_out, imp_out);
   if (hv) {
     AVQ_PA_D(1, w.part1);
     if (a.passes > 1)
-      rk<<<G, 1024, rt_smem, st>>>(w.part1, nqt, a.pcnt, a.M0, a.min_valid, a.P, a.passes, a.pass_decay, 1, 1, lay,
+      route(w.part1, nqt, a.pcnt, a.M0, a.min_valid, a.P, a.passes, a.pass_decay, 1, 1, lay,
                                    sel, sel_stride, pcnt_out, w.imp);
   }
 #undef AVQ_PA_D

@@ -3,7 +3,10 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/avqa_b200.h"
 #include "avq_kernels.cuh"
@@ -35,6 +38,39 @@ int finish(int rc, const char* what) {
 }
 
 avq::Strides3 st3(const long long* s) { return avq::Strides3{(long)s[0], (long)s[1], (long)s[2]}; }
+
+struct ProfRecord {
+  const char* name;
+  cudaEvent_t e0, e1;
+};
+std::mutex g_prof_mu;
+std::vector<ProfRecord> g_prof;
+bool g_prof_on = false;
+
+}  // namespace
+
+namespace avq {
+
+ProfileScope::ProfileScope(const char* n, cudaStream_t s) : name(n), st(s), e0(nullptr), on(false) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  if (!g_prof_on) return;
+  if (cudaEventCreate(&e0) != cudaSuccess) return;
+  cudaEventRecord(e0, st);
+  on = true;
+}
+
+ProfileScope::~ProfileScope() {
+  if (!on) return;
+  cudaEvent_t e1;
+  if (cudaEventCreate(&e1) != cudaSuccess) return;
+  cudaEventRecord(e1, st);
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  g_prof.push_back({name, e0, e1});
+}
+
+}  // namespace avq
+
+namespace {
 
 bool bad_dtype(int dt) { return dt < 0 || dt > 2; }
 
@@ -106,9 +142,10 @@ int avq_selection_stride(int P, int passes, float pass_decay) {
   return avq::selection_stride(P, passes, pass_decay);
 }
 
-size_t avq_forward_workspace_size(int B, int H, int T, int D, int M0, int P, int passes, float pass_decay) {
-  if (P <= 0 || passes <= 0 || passes > 8) return 0;
-  return avq::forward_workspace_bytes(B * H, T, D, M0, P, passes, pass_decay);
+size_t avq_forward_workspace_size(int dtype, int B, int H, int T, int D, int M0, int C, int P, int passes,
+                                  float pass_decay, int hvaq) {
+  if (bad_dtype(dtype) || P <= 0 || passes <= 0 || passes > 8) return 0;
+  return avq::forward_workspace_bytes(dtype, B * H, T, D, M0, C, P, passes, pass_decay, hvaq);
 }
 
 int avq_forward(int dtype, const void* q, const long long* q_strides, int B, int H, int T, int D, int M0, int C,
@@ -128,7 +165,7 @@ int avq_forward(int dtype, const void* q, const long long* q_strides, int B, int
   if (!q_strides || !out_strides || !parents_dt || !children_dt || !pagg || !cagg || !pcnt || !ccnt || !min_valid)
     return fail(AVQ_ERR_ARG, "avq_forward: null pointer");
   if (B * T > 0 && (!q || !out)) return fail(AVQ_ERR_ARG, "avq_forward: null q/out");
-  const size_t need = avq::forward_workspace_bytes(B * H, T, D, M0, P, passes, pass_decay);
+  const size_t need = avq::forward_workspace_bytes(dtype, B * H, T, D, M0, C, P, passes, pass_decay, hvaq);
   if (workspace_bytes < need || !workspace)
     return fail(AVQ_ERR_WORKSPACE, "avq_forward: workspace %zu < %zu bytes", workspace_bytes, need);
   avq::ForwardArgs a{q, st3(q_strides), B, H, T, D, M0, C, parents_dt, children_dt, pagg, cagg, pcnt, ccnt, min_valid,
@@ -167,6 +204,52 @@ int avq_append(int dtype, const void* k, const long long* k_strides, const void*
     default: rc = avq::launch_append<avq::DT_F16>(a, st); break;
   }
   return finish(rc, "avq_append");
+}
+
+int avq_profile_begin(void) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  for (auto& r : g_prof) {
+    cudaEventDestroy(r.e0);
+    cudaEventDestroy(r.e1);
+  }
+  g_prof.clear();
+  g_prof_on = true;
+  return AVQ_OK;
+}
+
+int avq_profile_end(char* names, int names_len, float* total_ms, int* launches, int max_kernels) {
+  std::vector<ProfRecord> recs;
+  {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    g_prof_on = false;
+    recs.swap(g_prof);
+  }
+  std::map<std::string, std::pair<double, int>> agg;
+  int rc = AVQ_OK;
+  for (auto& r : recs) {
+    float ms = 0.f;
+    if (cudaEventSynchronize(r.e1) != cudaSuccess || cudaEventElapsedTime(&ms, r.e0, r.e1) != cudaSuccess)
+      rc = fail(AVQ_ERR_CUDA, "avq_profile_end: %s", cudaGetErrorString(cudaGetLastError()));
+    auto& a = agg[r.name];
+    a.first += ms;
+    a.second += 1;
+    cudaEventDestroy(r.e0);
+    cudaEventDestroy(r.e1);
+  }
+  std::string joined;
+  int k = 0;
+  for (auto& kv : agg) {
+    if (k >= max_kernels) break;
+    if (total_ms) total_ms[k] = (float)kv.second.first;
+    if (launches) launches[k] = kv.second.second;
+    joined += kv.first + "\n";
+    ++k;
+  }
+  if (names && names_len > 0) {
+    std::strncpy(names, joined.c_str(), (size_t)names_len - 1);
+    names[names_len - 1] = 0;
+  }
+  return rc == AVQ_OK ? k : -1;
 }
 
 int avq_reduce_min(const int* v, int n, int* out, void* stream) {

@@ -146,6 +146,7 @@ int launch_append(const AppendArgs& a, cudaStream_t st) {
   const int G = a.B * a.H;
   if (G == 0 || a.Tn == 0) return AVQ_OK;
   const size_t smem = sizeof(float) * (a.D + 128) + sizeof(int) * 128;
+  AVQ_TIMED("append", st);
   append_kernel<DT><<<G, 128, smem, st>>>((const T*)a.k, a.ks, (const T*)a.v, a.vs, a.H, a.Tn, a.D, a.M0, a.C,
                                           (const T*)a.parents_dt, a.p_sq, (const T*)a.children_dt, a.c_sq, a.pacc,
                                           a.cacc, (T*)a.pagg, (T*)a.cagg, a.pcnt, a.ccnt, a.nvalid, (T*)a.kpage,

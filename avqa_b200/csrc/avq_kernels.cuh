@@ -2,6 +2,7 @@
 #pragma once
 
 #include "avq_common.cuh"
+#include "avq_profile.cuh"
 
 namespace avq {
 
@@ -85,6 +86,67 @@ struct AppendArgs {
   int slot0;
 };
 
+// Parent-attention pass of the tensor-core path (avq_attention_mma.cu).
+struct PAArgs {
+  const void* q;
+  Strides3 qs;
+  int B, H, T, D, M0;
+  float sqrtD;
+  const void* parents;
+  const void* pagg;
+  const int* pcnt;
+  int mode;            // 0 plain, 1 HVAQ rescale of the stored logits
+  int keep_logits;     // mode 0 only: leave the logits in sglobal for a later HVAQ pass
+  void* sglobal;       // logits scratch when they do not fit in shared memory
+  bool s_in_smem;
+  float *m, *l, *z;    // [G,T]
+  void* a;             // [G,T,D] dtype
+  double* imp_part;    // [G, nqt, M0]
+  const int* sel0;
+  int sel_stride;
+  const int* pass_cnt;
+  int hvaq;
+  float beta0, alpha;
+  float* beta;         // [G,T]
+};
+
+struct PassOffsets {
+  int off[8];
+};
+
+struct CorrArgs {
+  const void* q;
+  Strides3 qs;
+  int B, H, T, D, M0, C;
+  float sqrtD;
+  const void* parents;
+  const void* children;
+  const void* pagg;
+  const void* cagg;
+  const int* pcnt;
+  const int* ccnt;
+  const float *m, *l, *z, *beta;  // beta: HVAQ temperatures or nullptr
+  const void* a;                  // [G,T,D] dtype
+  const int* sel;
+  int sel_stride;
+  const int* pass_cnt;
+  int npass;
+  int pass_off[8];
+  int multipass;
+  float* out;
+  Strides3 os;
+};
+
+template <int DT>
+int launch_parent_attn_mma(const PAArgs& a, cudaStream_t st);
+template <int DT>
+int launch_correct_mma(const CorrArgs& a, cudaStream_t st);
+size_t parent_attn_mma_smem(int D, int M0, bool s_in_smem, int dt_bytes);
+bool parent_attn_mma_ok(int dt, int D, int M0);
+bool parent_attn_mma_smem_mode(int D, int M0);
+size_t parent_attn_mma_scratch(int G, int T, int M0, int dt_bytes);
+constexpr int PM_ROWS_PUBLIC = 64;
+
 template <int DT>
 int launch_append(const AppendArgs& a, cudaStream_t st);
 int launch_reduce_min(const int* v, int n, int* out, cudaStream_t st);
@@ -98,7 +160,8 @@ size_t quantize_workspace_bytes(int G, int S, int M0);
 
 template <int DT>
 int launch_forward(const ForwardArgs& a, cudaStream_t st);
-size_t forward_workspace_bytes(int G, int T, int D, int M0, int P, int passes, float decay);
+size_t forward_workspace_bytes(int dtype, int G, int T, int D, int M0, int C, int P, int passes, float decay, int hvaq);
+bool forward_uses_mma(int dtype, int D, int M0, int C);
 int selection_stride(int P, int passes, float decay);
 void pass_budget_caps(int P, int passes, float decay, int* caps);
 

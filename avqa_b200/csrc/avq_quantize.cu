@@ -13,6 +13,7 @@
 // Index work is exact.  Dot products here accumulate in double, so every
 // distance equals the exactly rounded reference value.
 #include "avq_kernels.cuh"
+#include "avq_mma.cuh"
 
 namespace avq {
 
@@ -146,6 +147,161 @@ __global__ void __launch_bounds__(256) assign_kernel(const typename Storage<DT>:
   if (l4 == 0 && s < S) {
     passign[(long)g * S + s] = p;
     cassign[(long)g * S + s] = cb.i;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core assignment (bf16 / fp16).  CTA = 128 keys x all parents in
+// chunks of 64; warp w owns keys [16w, 16w+16) and every parent, so each
+// key's argmin stays inside one warp (quad shuffles).  The cross term k.p is
+// an m16n8k16 MMA with fp32 accumulation, narrowed like the reference's
+// bf16/fp16 matmul output; norms and the child stage accumulate in double.
+// ---------------------------------------------------------------------------
+constexpr int AM_ROWS = 128;
+constexpr int AM_CH = 64;
+
+template <int DT, int D>
+__global__ void __launch_bounds__(256) assign_mma_kernel(const typename Storage<DT>::T* __restrict__ keys, Strides3 ks,
+                                                         int H, int S, int M0, int C,
+                                                         const typename Storage<DT>::T* __restrict__ parents,
+                                                         const float* __restrict__ p_sq,
+                                                         const typename Storage<DT>::T* __restrict__ children,
+                                                         const float* __restrict__ c_sq, int* __restrict__ passign,
+                                                         int* __restrict__ cassign) {
+  using T = typename Storage<DT>::T;
+  constexpr int LDS = D + 8, KS = D / 16, CPR = D / 8;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  T* sk = (T*)smem_raw;                        // [AM_ROWS][LDS]
+  T* sp = sk + AM_ROWS * LDS;                  // [2][AM_CH][LDS]
+  float* sksq = (float*)(sp + 2 * AM_CH * LDS);  // [AM_ROWS]
+  float* spsq = sksq + AM_ROWS;                  // [2][AM_CH]
+  int* sbest = (int*)(spsq + 2 * AM_CH);         // [AM_ROWS]
+  const int g = blockIdx.y, b = g / H, h = g % H, s0 = blockIdx.x * AM_ROWS;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const T* kb = keys + (long)b * ks.b + (long)h * ks.h;
+  const T* pb = parents + (long)h * M0 * D;
+
+  for (int i = tid; i < AM_ROWS * CPR; i += blockDim.x) {
+    const int r = i / CPR, c = i % CPR, s = s0 + r;
+    cp_async16(sk + r * LDS + c * 8, kb + (long)(s < S ? s : 0) * ks.s + c * 8, s < S);
+  }
+  auto load_chunk = [&](int buf, int p0) {
+    for (int i = tid; i < AM_CH * CPR; i += blockDim.x) {
+      const int r = i / CPR, c = i % CPR, p = p0 + r;
+      cp_async16(sp + (buf * AM_CH + r) * LDS + c * 8, pb + (long)(p < M0 ? p : 0) * D + c * 8, p < M0);
+    }
+    if (tid < AM_CH) {
+      const int p = p0 + tid;
+      if (p < M0) {
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(spsq + buf * AM_CH + tid)),
+                     "l"(p_sq + (long)h * M0 + p));
+      } else {
+        spsq[buf * AM_CH + tid] = INFINITY;
+      }
+    }
+  };
+  load_chunk(0, 0);
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  if (tid < AM_ROWS) {
+    double acc = 0.0;
+#pragma unroll 8
+    for (int d = 0; d < D; ++d) {
+      const float x = to_f(sk[tid * LDS + d]);
+      acc += (double)rnd<DT>(__fmul_rn(x, x));
+    }
+    sksq[tid] = rnd64<DT>(acc);
+  }
+  uint32_t af[KS][4];
+#pragma unroll
+  for (int k = 0; k < KS; ++k)
+    ldsm_x4(af[k][0], af[k][1], af[k][2], af[k][3], sk + (warp * 16 + (lane & 15)) * LDS + k * 16 + (lane >> 4) * 8);
+  __syncthreads();
+  const int rA = warp * 16 + (lane >> 2), rB = rA + 8;
+  const float ksqA = sksq[rA], ksqB = sksq[rB];
+  float bvA = 0.f, bvB = 0.f;
+  int biA = -1, biB = -1;
+  const int nch = (M0 + AM_CH - 1) / AM_CH;
+  for (int ci = 0; ci < nch; ++ci) {
+    const int buf = ci & 1, p0 = ci * AM_CH;
+    if (ci + 1 < nch) load_chunk(buf ^ 1, p0 + AM_CH);
+    cp_async_commit();
+    float acc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    const T* spb = sp + buf * AM_CH * LDS;
+#pragma unroll
+    for (int k = 0; k < KS; ++k) {
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        uint32_t b0, b1, b2, b3;
+        const int q = lane >> 3;
+        ldsm_x4(b0, b1, b2, b3, spb + (jj * 16 + (q >> 1) * 8 + (lane & 7)) * LDS + k * 16 + (q & 1) * 8);
+        mma16816<DT>(acc[2 * jj], af[k], b0, b1);
+        mma16816<DT>(acc[2 * jj + 1], af[k], b2, b3);
+      }
+    }
+    const float* psq = spsq + buf * AM_CH;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int cl = j * 8 + (lane & 3) * 2 + e, p = p0 + cl;
+        if (p < M0) {
+          const float ps = psq[cl];
+          {
+            const float cross = rnd<DT>(acc[j][e]);
+            const float dd = rnd<DT>(__fsub_rn(rnd<DT>(__fadd_rn(ksqA, ps)), rnd<DT>(__fmul_rn(2.f, cross))));
+            if (better(dd, p, bvA, biA)) { bvA = dd; biA = p; }
+          }
+          {
+            const float cross = rnd<DT>(acc[j][2 + e]);
+            const float dd = rnd<DT>(__fsub_rn(rnd<DT>(__fadd_rn(ksqB, ps)), rnd<DT>(__fmul_rn(2.f, cross))));
+            if (better(dd, p, bvB, biB)) { bvB = dd; biB = p; }
+          }
+        }
+      }
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+  }
+  ArgMin A = shfl_best({bvA, biA}, 2), Bm = shfl_best({bvB, biB}, 2);
+  if ((lane & 3) == 0) {
+    sbest[rA] = A.i;
+    sbest[rB] = Bm.i;
+  }
+  __syncwarp();
+  // child stage: lane -> key warp*16 + lane/2, children lane&1, +2, ...
+  const int r = warp * 16 + (lane >> 1), half = lane & 1, s = s0 + r;
+  const int p = sbest[r];
+  const float ksq = sksq[r];
+  ArgMin cb = {0.f, -1};
+  for (int c = half; c < C; c += 2) {
+    const long crow = ((long)h * M0 + p) * C + c;
+    const uint4* cr = reinterpret_cast<const uint4*>(children + crow * D);
+    const uint4* kr = reinterpret_cast<const uint4*>(sk + r * LDS);
+    double acc = 0.0;
+#pragma unroll 4
+    for (int v = 0; v < D / 8; ++v) {
+      const uint4 cv = __ldg(cr + v), kv = kr[v];
+      const T* ce = reinterpret_cast<const T*>(&cv);
+      const T* ke = reinterpret_cast<const T*>(&kv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc += (double)rnd<DT>(__fmul_rn(to_f(ke[e]), to_f(ce[e])));
+    }
+    const float cross = rnd64<DT>(acc);
+    const float dd = rnd<DT>(__fsub_rn(rnd<DT>(__fadd_rn(ksq, c_sq[crow])), rnd<DT>(__fmul_rn(2.f, cross))));
+    if (better(dd, c, cb.v, cb.i)) cb = {dd, c};
+  }
+  {
+    const float v = __shfl_xor_sync(0xffffffffu, cb.v, 1);
+    const int i = __shfl_xor_sync(0xffffffffu, cb.i, 1);
+    if (i >= 0 && better(v, i, cb.v, cb.i)) cb = {v, i};
+  }
+  if (half == 0 && s < S) {
+    passign[(long)(blockIdx.y) * S + s] = p;
+    cassign[(long)(blockIdx.y) * S + s] = cb.i;
   }
 }
 
@@ -316,6 +472,122 @@ __global__ void __launch_bounds__(256) aggregate_kernel(
       if (c < C) ccnt[gp * C + c] = cn[c];
 }
 
+template <int DT>
+__device__ __forceinline__ float half_bits_to_f(uint32_t u) {
+  if (DT == DT_BF16) return __uint_as_float(u << 16);
+  return __half2float(__ushort_as_half((unsigned short)u));
+}
+
+// VPL consecutive dtype elements with one 4/8/16-byte load.
+template <int DT, int VPL>
+__device__ __forceinline__ void load_row_elems(const typename Storage<DT>::T* p, float* out) {
+  if constexpr (DT == DT_F32) {
+    if constexpr (VPL == 4) {
+      const float4 w = *reinterpret_cast<const float4*>(p);
+      out[0] = w.x; out[1] = w.y; out[2] = w.z; out[3] = w.w;
+    } else {
+      const float2 w = *reinterpret_cast<const float2*>(p);
+      out[0] = w.x; out[1] = w.y;
+    }
+  } else if constexpr (VPL == 4) {
+    const uint2 w = *reinterpret_cast<const uint2*>(p);
+    out[0] = half_bits_to_f<DT>(w.x & 0xffffu); out[1] = half_bits_to_f<DT>(w.x >> 16);
+    out[2] = half_bits_to_f<DT>(w.y & 0xffffu); out[3] = half_bits_to_f<DT>(w.y >> 16);
+  } else {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(p);
+    out[0] = half_bits_to_f<DT>(w & 0xffffu); out[1] = half_bits_to_f<DT>(w >> 16);
+  }
+}
+
+// Vectorised aggregation for D = 32 * VPL (VPL = 2 or 4 dtype elements per
+// lane, one 4- or 8-byte load per member).  The warp fetches 32 member ids
+// (and their child ids) at once and keeps 8 value rows in flight; the fp32
+// additions stay in key order.
+template <int DT, int CMAX, int VPL>
+__global__ void __launch_bounds__(256, 2) aggregate_vec_kernel(
+    const typename Storage<DT>::T* __restrict__ values, Strides3 vs, int H, int S, int M0, int C,
+    const int* __restrict__ order, const int* __restrict__ poff, const int* __restrict__ pcnt,
+    const int* __restrict__ cassign, typename Storage<DT>::T* __restrict__ pagg,
+    typename Storage<DT>::T* __restrict__ cagg, float* __restrict__ pacc, float* __restrict__ cacc,
+    int* __restrict__ ccnt, long rows) {
+  using T = typename Storage<DT>::T;
+  struct alignas(VPL * sizeof(T)) V {
+    T e[VPL];
+  };
+  constexpr int D = 32 * VPL, U = 8;
+  const int lane = threadIdx.x & 31;
+  const long gp = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gp >= rows) return;
+  const int g = (int)(gp / M0), b = g / H, h = g % H;
+  const T* vbase = values + (long)b * vs.b + (long)h * vs.h + lane * VPL;
+  float ap[VPL], ac[CMAX][VPL];
+  int cn = 0;  // lane c < CMAX counts child c
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    ap[j] = 0.f;
+#pragma unroll
+    for (int c = 0; c < CMAX; ++c) ac[c][j] = 0.f;
+  }
+  const int beg = poff[gp], n = pcnt[gp];
+  const int* ord = order + (long)g * S + beg;
+  const int* cas = cassign + (long)g * S;
+  for (int i0 = 0; i0 < n; i0 += 32) {
+    const int m = min(32, n - i0);
+    const int my_s = lane < m ? ord[i0 + lane] : 0;
+    const int my_c = lane < m ? cas[my_s] : -1;
+#pragma unroll
+    for (int c = 0; c < CMAX; ++c) {
+      const int k = __popc(__ballot_sync(0xffffffffu, my_c == c));
+      if (lane == c) cn += k;
+    }
+    for (int j0 = 0; j0 < m; j0 += U) {
+      float buf[U][VPL];
+      int cc[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = j0 + u;
+        const int s = __shfl_sync(0xffffffffu, my_s, j & 31);
+        cc[u] = __shfl_sync(0xffffffffu, my_c, j & 31);
+        load_row_elems<DT, VPL>(vbase + (long)(j < m ? s : my_s) * vs.s, buf[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (j0 + u < m) {
+#pragma unroll
+          for (int q = 0; q < VPL; ++q) {
+            const float v = buf[u][q];
+            ap[q] = __fadd_rn(ap[q], v);
+#pragma unroll
+            for (int c = 0; c < CMAX; ++c)
+              if (c == cc[u]) ac[c][q] = __fadd_rn(ac[c][q], v);
+          }
+        }
+      }
+    }
+  }
+  const long o = gp * D + lane * VPL;
+  V pv;
+#pragma unroll
+  for (int q = 0; q < VPL; ++q) pv.e[q] = from_f<DT>(ap[q]);
+  *reinterpret_cast<V*>(pagg + o) = pv;
+  if (pacc)
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) pacc[o + q] = ap[q];
+#pragma unroll
+  for (int c = 0; c < CMAX; ++c) {
+    if (c < C) {
+      const long oc = (gp * C + c) * D + lane * VPL;
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) pv.e[q] = from_f<DT>(ac[c][q]);
+      *reinterpret_cast<V*>(cagg + oc) = pv;
+      if (cacc)
+#pragma unroll
+        for (int q = 0; q < VPL; ++q) cacc[oc + q] = ac[c][q];
+    }
+  }
+  if (lane < C) ccnt[gp * C + lane] = cn;
+}
+
 // ---------------------------------------------------------------------------
 // Host launchers
 // ---------------------------------------------------------------------------
@@ -359,23 +631,63 @@ int launch_quantize(const QuantizeArgs& a, cudaStream_t st) {
   ws += align_up((size_t)G * (a.S > 0 ? a.S : 1) * sizeof(int));
   int* poff = (int*)ws;
   if (a.S > 0) {
-    const size_t smem = (size_t)((AS_ROWS + AS_COLS) * (a.D + 1) + AS_ROWS) * sizeof(float);
-    auto kfn = assign_kernel<DT>;
-    cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    dim3 grid((a.S + AS_ROWS - 1) / AS_ROWS, G);
-    kfn<<<grid, 256, smem, st>>>((const T*)a.keys, a.ks, a.H, a.S, a.D, a.M0, a.C, (const T*)a.parents_dt, a.p_sq,
-                                 (const T*)a.children_dt, a.c_sq, a.passign, a.cassign);
-    bucket_hist_kernel<<<dim3(nseg, G), 256, a.M0 * sizeof(int), st>>>(a.passign, a.S, a.M0, nseg, seg_len, hist);
-  } else {
-    cudaMemsetAsync(hist, 0, (size_t)G * nseg * a.M0 * sizeof(int), st);
+    const bool aligned = ((uintptr_t)a.keys % 16 == 0) && a.ks.s % 8 == 0 && a.ks.h % 8 == 0 && a.ks.b % 8 == 0;
+    bool done = false;
+    if constexpr (DT != DT_F32) {
+      if (aligned && (a.D == 64 || a.D == 128)) {
+        done = true;
+      auto launch_mma = [&](auto kfn, int D) {
+        AVQ_TIMED("assign", st);
+        const size_t smem = (size_t)(AM_ROWS + 2 * AM_CH) * (D + 8) * sizeof(T) +
+                            (AM_ROWS + 2 * AM_CH) * sizeof(float) + AM_ROWS * sizeof(int);
+        cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kfn<<<dim3((a.S + AM_ROWS - 1) / AM_ROWS, G), 256, smem, st>>>(
+            (const T*)a.keys, a.ks, a.H, a.S, a.M0, a.C, (const T*)a.parents_dt, a.p_sq, (const T*)a.children_dt,
+            a.c_sq, a.passign, a.cassign);
+      };
+        if (a.D == 64) launch_mma(assign_mma_kernel<DT, 64>, 64);
+        else launch_mma(assign_mma_kernel<DT, 128>, 128);
+      }
+    }
+    if (!done) {
+      AVQ_TIMED("assign_exact", st);
+      const size_t smem = (size_t)((AS_ROWS + AS_COLS) * (a.D + 1) + AS_ROWS) * sizeof(float);
+      auto kfn = assign_kernel<DT>;
+      cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      dim3 grid((a.S + AS_ROWS - 1) / AS_ROWS, G);
+      kfn<<<grid, 256, smem, st>>>((const T*)a.keys, a.ks, a.H, a.S, a.D, a.M0, a.C, (const T*)a.parents_dt, a.p_sq,
+                                   (const T*)a.children_dt, a.c_sq, a.passign, a.cassign);
+    }
   }
-  bucket_scan_kernel<<<G, 1024, a.M0 * sizeof(int), st>>>(hist, a.M0, nseg, poff, a.pcnt, a.nvalid, a.gmin_valid);
-  if (a.S > 0)
-    bucket_scatter_kernel<<<dim3(nseg, G), 32, a.M0 * sizeof(int), st>>>(a.passign, hist, a.S, a.M0, nseg, seg_len,
-                                                                         order);
+  {
+    AVQ_TIMED("bucket_sort", st);
+    if (a.S > 0)
+      bucket_hist_kernel<<<dim3(nseg, G), 256, a.M0 * sizeof(int), st>>>(a.passign, a.S, a.M0, nseg, seg_len, hist);
+    else
+      cudaMemsetAsync(hist, 0, (size_t)G * nseg * a.M0 * sizeof(int), st);
+    bucket_scan_kernel<<<G, 1024, a.M0 * sizeof(int), st>>>(hist, a.M0, nseg, poff, a.pcnt, a.nvalid, a.gmin_valid);
+    if (a.S > 0)
+      bucket_scatter_kernel<<<dim3(nseg, G), 32, a.M0 * sizeof(int), st>>>(a.passign, hist, a.S, a.M0, nseg, seg_len,
+                                                                           order);
+  }
+  AVQ_TIMED("aggregate", st);
   const long rows = (long)G * a.M0;
   const unsigned blocks = (unsigned)((rows + 7) / 8);
-#define AVQ_AGG(CM, DM)                                                                                          \
+  const bool valigned = ((uintptr_t)a.values % 16 == 0) && a.vs.s % 8 == 0 && a.vs.h % 8 == 0 && a.vs.b % 8 == 0;
+  if (valigned && (a.D == 64 || a.D == 128)) {
+#define AVQ_AGGV(CM, VP)                                                                                              \
+  aggregate_vec_kernel<DT, CM, VP><<<blocks, 256, 0, st>>>((const T*)a.values, a.vs, a.H, a.S, a.M0, a.C, order, poff, \
+                                                           a.pcnt, a.cassign, (T*)a.pagg, (T*)a.cagg, a.pacc, a.cacc,  \
+                                                           a.ccnt, rows)
+    if (a.C <= 4) {
+      if (a.D == 64) AVQ_AGGV(4, 2); else AVQ_AGGV(4, 4);
+    } else {
+      if (a.D == 64) AVQ_AGGV(8, 2); else AVQ_AGGV(8, 4);
+    }
+#undef AVQ_AGGV
+    return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
+  }
+#define AVQ_AGG(CM, DM)                                                                                         \
   aggregate_kernel<DT, CM, DM><<<blocks, 256, 0, st>>>((const T*)a.values, a.vs, a.H, a.S, a.D, a.M0, a.C, order, \
                                                        poff, a.pcnt, a.cassign, (T*)a.pagg, (T*)a.cagg, a.pacc,  \
                                                        a.cacc, a.ccnt, rows)

@@ -183,7 +183,7 @@ def forward(q: torch.Tensor, cb: PreparedCodebook, st: QuantState, P: int, passe
     dev = q.device
     if out is None:
         out = torch.empty(B, T, H, D, dtype=torch.float32, device=dev).permute(0, 2, 1, 3)
-    ws_bytes = lib.avq_forward_workspace_size(B, H, T, D, M0, P, passes, pass_decay)
+    ws_bytes = lib.avq_forward_workspace_size(_lib.dtype_code(q.dtype), B, H, T, D, M0, C, P, passes, pass_decay, hvaq)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     diag = None
     imp = sel = pc = None

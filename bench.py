@@ -1,0 +1,368 @@
+"""Benchmark of the AVQ-attention forward on B200.
+
+Workload (N=1): the prefill configuration -- B=4, Tq=S=8192, 32 heads x
+d=128 (E=4096), 512 parents x 4 children, budget 32, single pass, bf16,
+Gaussian-mixture keys (512 centres, sigma 0.3), q/v ~ N(0,1), seed 1; codebook
+initialised from the keys with the fixed key-based recipe
+(``avqa_b200.codebook.codebook_from_keys``).  Inputs are synthetic.
+
+A step is one ``AVQAttention.forward`` of that batch through the public API:
+quantize all S keys of every (b,h), parent attention, global budget routing,
+child correction, fp32 output.  The inputs (0.8 GB) exceed the 126 MB L2,
+so no flush is needed between steps.
+
+Multi-GPU (torchrun, one rank per GPU): weak scaling -- every rank processes
+its own batch of 4 (different seeds); the ranks form one global batch, so the
+routing budget min(P, min over all (b,h) of non-empty parents) is an
+all-reduce(MIN) over NCCL each step, exactly as one reference call over the
+concatenated batch would compute it.
+
+``--impl reference`` times the CPU restatement of the reference algorithm
+(oracle/, numpy with all host threads) on a bounded sample (one (b,h) slice of
+the workload per step) and reports the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "query tokens/s/GPU at 1/2/4/8 B200; % of HBM/tensor roofline per kernel"
+UNIT = "query tokens/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c2")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-slices", type=int, default=1, help="(b,h) slices in the CPU-baseline sample")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.file,
+                                         stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, _, flags in rows for i, f in enumerate(flags) if f.lower() == "active"})
+        load = sorted(r[0] for r in rows)
+        return {"sm_mhz": load[len(load) // 2], "sm_max_mhz": rows[0][1], "power_w_max": max(r[2] for r in rows),
+                "samples": len(rows), "reasons": reasons}
+
+
+# ---------------------------------------------------------------------------
+# roofline bookkeeping (algorithmic work per launch)
+# ---------------------------------------------------------------------------
+def algorithmic_work(w, B: int) -> dict:
+    """FLOPs (tensor-bound kernels) or bytes (memory-bound kernels) per launch."""
+    G, T, S, D, M0, C, P = B * w.H, w.T, w.S, w.D, w.M0, w.C, w.P
+    es = 2 if w.dtype in ("bf16", "f16") else 4
+    return {
+        "parent_attn": ("tensor", 4.0 * G * T * M0 * D),          # q.P^T and e @ V
+        "assign": ("tensor", 2.0 * G * S * M0 * D + 2.0 * G * S * C * D),
+        "correct": ("tensor", 2.0 * G * T * P * D * (2 + 2 * C)),  # parent+child logits, value sums
+        "aggregate": ("hbm", G * S * D * es + G * S * 8 + G * M0 * (1 + C) * D * es + G * M0 * (1 + C) * 4),
+        "bucket_sort": ("hbm", G * S * 4 * 4),
+        "route": ("hbm", G * M0 * 8),
+    }
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def load_traffic() -> dict:
+    p = ROOT / "profiles" / "dram_traffic_per_launch.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except json.JSONDecodeError:
+            return {}
+    return {}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle port)
+# ---------------------------------------------------------------------------
+def cpu_baseline(w, slices: int = 1) -> dict:
+    """Time the numpy restatement of the reference on ``slices`` (b,h) slices."""
+    import numpy as np
+    import torch
+
+    from avqa_b200.codebook import codebook_from_keys
+    from avqa_b200.workloads import make_inputs
+    from oracle import avq_oracle as O
+    q, k, v = make_inputs(w, B=1)
+    H, D = w.H, w.D
+    total = 0.0
+    for hh in range(slices):
+        sl = lambda x, n: O.rnd(x.view(1, n, H, D)[:, :, hh].reshape(1, n, D).numpy(), w.dtype)
+        qn, kn, vn = sl(q, w.T), sl(k, w.S), sl(v, w.S)
+        cb = codebook_from_keys(torch.from_numpy(kn), w.M0, w.C, w.seed)
+        pd, cd = O.cast_codebook(cb.parents.numpy(), cb.children.numpy(), w.dtype)
+        cfg = O.ForwardConfig(1, w.M0, w.C, w.P, w.dtype, w.passes, w.pass_decay, w.hvaq)
+        t0 = time.perf_counter()
+        O.forward_heads(qn, kn, vn, pd, cd, cfg)
+        total += time.perf_counter() - t0
+    # one slice serves T queries of one head: 1/H of T query tokens
+    tokens = slices * w.T / H
+    cores = os.cpu_count()
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
+    except Exception:
+        pass
+    return {"value": tokens / total, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{slices} (b,h) slice(s) of the workload (T=S={w.T}, M0={w.M0}, C={w.C}, P={w.P}, "
+                      f"{w.dtype}), oracle/avq_oracle.py numpy restatement; {total:.2f} s"}
+
+
+# ---------------------------------------------------------------------------
+def dist_setup():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def run_reference(args) -> None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from avqa_b200.workloads import WORKLOADS
+    w = WORKLOADS[args.workload]
+    times = []
+    for i in range(args.warmup + args.steps):
+        cb = cpu_baseline(w, slices=args.cpu_slices)
+        if i >= args.warmup:
+            times.append(cb)
+    value = sum(c["value"] for c in times) / len(times)
+    ms_per_step = w.B * w.T / value * 1e3
+    out = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
+           "config": workload_config(w, world),
+           "cpu_baseline": {k: times[-1][k] for k in ("kind", "cores", "sample")} | {"value": value, "unit": UNIT},
+           "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def workload_config(w, world: int) -> dict:
+    return {"workload": f"{w.name}: prefill B={w.B}/GPU Tq=S={w.T} H={w.H} D={w.D} M0={w.M0} C={w.C} P={w.P} "
+                        f"{w.dtype} {w.keys} keys",
+            "global_batch": w.B * world, "seq_len": w.T, "parallelism": f"batch-sharded x{world}, global budget "
+                                                                        f"all-reduce(MIN)",
+            "l2": "inputs (0.8 GB/GPU) exceed L2; no flush"}
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from avqa_b200 import AVQAttention, AVQConfig, _lib
+    from avqa_b200.codebook import codebook_from_keys
+    from avqa_b200.config import AttentionShapeConfig, CodebookConfig, RefinementConfig, RoutingConfig
+    from avqa_b200.workloads import TORCH_DTYPE, WORKLOADS, Workload, make_inputs
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    w: Workload = WORKLOADS[args.workload]
+    dt = TORCH_DTYPE[w.dtype]
+    H, D = w.H, w.D
+    # codebook from batch 0 of the global batch (rank 0's seed), identical on every rank
+    _, k0, _ = make_inputs(w, device=dev, B=1, T=1)
+    cb = codebook_from_keys(k0.to(dt).view(1, w.S, H, D).transpose(1, 2)[0].float(), w.M0, w.C, w.seed)
+    del k0
+    wr = Workload(**{**w.__dict__, "seed": w.seed + 7919 * rank})
+    q, k, v = make_inputs(wr, device=dev)
+    q, k, v = q.to(dt), k.to(dt), v.to(dt)
+    cfg = AVQConfig(attention=AttentionShapeConfig(embed_dim=w.E, num_heads=H),
+                    codebook=CodebookConfig(num_codewords=w.M0, children_per_codeword=w.C),
+                    routing=RoutingConfig(refinement_budget=w.P),
+                    refinement=RefinementConfig(passes=w.passes, pass_decay=w.pass_decay))
+    mod = AVQAttention(cfg, in_proj=False, out_proj=False)
+    mod.codebook.parents, mod.codebook.children = cb.parents.to(dev), cb.children.to(dev)
+    if world > 1:
+        mod.process_group = dist.group.WORLD
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn, steps):
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            mod(q, k, v)
+        with ClockSampler(local) as clk:
+            _lib.profile_begin()
+            total_ms = timed(lambda: mod(q, k, v), args.steps)
+            prof = _lib.profile_end()
+        clocks = clk.summary()
+        ms_step = total_ms / args.steps
+        value = world * w.B * w.T * args.steps / (total_ms / 1e3)
+
+        e2e = None
+        if not args.no_e2e:
+            hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+            hout = torch.empty(w.B, w.T, w.E, dtype=torch.float32).pin_memory()
+
+            def e2e_step():
+                dq = hq.to(dev, non_blocking=True)
+                dk = hk.to(dev, non_blocking=True)
+                dv = hv.to(dev, non_blocking=True)
+                hout.copy_(mod(dq, dk, dv), non_blocking=True)
+
+            for _ in range(2):
+                e2e_step()
+            e2e_ms = timed(e2e_step, max(2, args.steps // 2))
+            nb = max(2, args.steps // 2)
+            e2e = {"value": world * w.B * w.T * nb / (e2e_ms / 1e3), "unit": UNIT,
+                   "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in (hq, hk, hv)),
+                   "d2h_bytes_per_step": hout.numel() * hout.element_size()}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    peaks, peak_src = load_peaks()
+    work = algorithmic_work(w, w.B)
+    traffic = load_traffic()
+    kern = {k: v for k, v in prof.items() if k in work}
+    dom = max(kern, key=lambda k: kern[k][0]) if kern else None
+    roofline = None
+    if dom:
+        bound, amount = work[dom]
+        avg_s = kern[dom][0] / kern[dom][1] / 1e3
+        if bound == "tensor":
+            achieved, peak, unit = amount / avg_s / 1e12, peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]), \
+                "TFLOP/s"
+        else:
+            achieved, peak, unit = amount / avg_s / 1e9, peaks["hbm_gbs"], "GB/s"
+        tr = traffic.get(f"{args.workload}:{dom}")
+        roofline = {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                    "frac": achieved / peak, "traffic": tr, "peak_source": f"{peak_src} (sustained bf16 for kernels "
+                                                                          f"timed inside the step)",
+                    "algorithmic_per_launch": amount, "avg_launch_ms": avg_s * 1e3}
+    kernels = {}
+    for name, (ms, n) in sorted(prof.items(), key=lambda x: -x[1][0]):
+        entry = {"launches": n, "avg_ms": ms / n, "share": ms / sum(v[0] for v in prof.values())}
+        if name in work:
+            bound, amount = work[name]
+            avg_s = ms / n / 1e3
+            if bound == "tensor":
+                a = amount / avg_s / 1e12
+                entry.update(achieved_tflops=a, frac=a / peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+            else:
+                a = amount / avg_s / 1e9
+                entry.update(achieved_gbs=a, frac=a / peaks["hbm_gbs"])
+        kernels[name] = entry
+    per_scope = {"bucket_sort": 3}  # histogram, scan, stable scatter
+    gpu_launches = sum(n * per_scope.get(name, 1) for name, (_, n) in prof.items())
+    try:
+        cpu = cpu_baseline(w, slices=args.cpu_slices)
+    except Exception as exc:  # the baseline must never hide the GPU number
+        cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {exc}"}
+    out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": w.dtype, "data": "synthetic (seeded Gaussian-mixture keys, N(0,1) q/v)",
+           "config": workload_config(w, world), "clocks": clocks, "e2e": e2e, "gpu_launches": gpu_launches,
+           "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu}
+    print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

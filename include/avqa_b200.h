@@ -74,7 +74,8 @@ int avq_quantize(int dtype, const void* keys, const long long* key_strides, cons
  * the sum of the per-pass budget caps for base budget P. */
 int avq_selection_stride(int P, int passes, float pass_decay);
 
-size_t avq_forward_workspace_size(int B, int H, int T, int D, int M0, int P, int passes, float pass_decay);
+size_t avq_forward_workspace_size(int dtype, int B, int H, int T, int D, int M0, int C, int P, int passes,
+                                  float pass_decay, int hvaq);
 
 /* AVQ attention of T queries per (b,h) over a quantized key set.
  * q: dtype with q_strides; out: fp32 with out_strides (module layout
@@ -103,6 +104,14 @@ int avq_append(int dtype, const void* k, const long long* k_strides, const void*
 
 /* *out = min(v[0..n)). */
 int avq_reduce_min(const int* v, int n, int* out, void* stream);
+
+/* Per-kernel device timing (no counterpart in the reference; measurement
+ * support).  avq_profile_begin() starts recording a CUDA event pair around
+ * every kernel the library launches; avq_profile_end() waits for them and
+ * writes, per kernel name (names joined by '\n'), the summed milliseconds and
+ * the launch count; returns the number of kernels (or -1 on error). */
+int avq_profile_begin(void);
+int avq_profile_end(char* names, int names_len, float* total_ms, int* launches, int max_kernels);
 
 #ifdef __cplusplus
 }

@@ -47,11 +47,14 @@ DTYPES = ("f32", "bf16", "f16")
 def _bf16_from_f32(x: np.ndarray) -> np.ndarray:
     """Round float32 values to bf16 (RNE), returned as float32."""
     x = np.ascontiguousarray(x, dtype=np.float32)
-    u = x.view(np.uint32).astype(np.uint64)
-    lsb = (u >> 16) & 1
-    u = (u + 0x7FFF + lsb) & 0xFFFF0000
-    out = u.astype(np.uint32).view(np.float32)
-    return np.where(np.isnan(x), x, out)
+    u = x.view(np.uint32)
+    nan = np.isnan(x)
+    r = ((u >> np.uint32(16)) & np.uint32(1)) + np.uint32(0x7FFF)
+    with np.errstate(over="ignore"):
+        out = ((u + r) & np.uint32(0xFFFF0000)).view(np.float32)  # +inf rounds to +inf; wraps only for NaN
+    if nan.any():
+        out = np.where(nan, x, out)
+    return out
 
 
 def rnd(x, dt: str) -> np.ndarray:
@@ -341,14 +344,16 @@ def correction(m, l, a, probs, pagg, pcnt, cagg, ccnt, sel, u):
         csel = np.take_along_axis(cagg, sel[..., None, None], 1)  # [G,P,C,D] :229-230
         ncsel = np.take_along_axis(ccnt, sel[..., None], 1)  # [G,P,C]
         mm = m[..., None].astype(f32)
-        # fp32 ops: exp is the correctly rounded fp32 value; each product is
-        # an fp32 tensor before the reduction (refinement.py:335-348).
+        # fp32 weights (exp is the correctly rounded fp32 value); the weighted
+        # value sums are evaluated exactly in float64 and rounded once to fp32
+        # (refinement.py:335-348 sums fp32 products in fp32).
         pe = (exp32((x - mm).astype(f32)) * nsel[:, None, :]).astype(f32)  # :335
-        r_l = pe.astype(np.float64).sum(-1)
-        r_a = (pe[..., None] * vsel[:, None]).astype(f32).astype(np.float64).sum(-2)  # :337
+        r_l = pe.sum(-1, dtype=np.float64)
+        r_a = np.einsum("gtp,gpd->gtd", pe.astype(np.float64), vsel.astype(np.float64))  # :337
         ce = (exp32((u - mm[..., None]).astype(f32)) * ncsel[:, None]).astype(f32)  # :341
-        a_l = ce.astype(np.float64).sum((-1, -2))
-        a_a = (ce[..., None] * csel[:, None]).astype(f32).astype(np.float64).sum((-2, -3))  # :346
+        a_l = ce.sum((-1, -2), dtype=np.float64)
+        a_a = np.einsum("gtk,gkd->gtd", ce.reshape(G, T, P * C).astype(np.float64),
+                        csel.reshape(G, P * C, -1).astype(np.float64))  # :346
         l_new = ((l.astype(f32) - r_l.astype(f32)).astype(f32) + a_l.astype(f32)).astype(f32)  # attention.py:149-153
         a_new = ((a.astype(f32) - r_a.astype(f32)).astype(f32) + a_a.astype(f32)).astype(f32)
     return l_new, a_new

@@ -64,6 +64,87 @@ def quant_arrays(state, B: int, H: int) -> dict:
     }
 
 
+def ulp(x: np.ndarray, dt: str) -> np.ndarray:
+    """Spacing of dtype values at |x| (normal range)."""
+    mant = {"f32": 23, "bf16": 7, "f16": 10}[dt]
+    ax = np.maximum(np.abs(np.asarray(x, np.float64)), 1e-30)
+    return np.exp2(np.floor(np.log2(ax)) - mant)
+
+
+def possible_parent_distances(k: np.ndarray, p: np.ndarray, ksq: float, psq: float, dt: str) -> tuple[float, float]:
+    """Range of the reference-rounded distance when the fp32 accumulation of
+    k.p may err by up to 2^-20 |k||p| (any summation order, any tensor-core
+    accumulation), i.e. the cross term may round to a neighbouring value."""
+    x = float(np.dot(k.astype(np.float64), p.astype(np.float64)))
+    delta = 2.0 ** -20 * float(np.linalg.norm(k) * np.linalg.norm(p)) + 1e-30
+    t1 = O.rnd(np.float64(ksq) + np.float64(psq), dt)
+    vals = []
+    for xc in (x - delta, x, x + delta):
+        cross = O.rnd(xc, dt)
+        vals.append(float(O.rnd(np.float64(t1) - O.rnd(2.0 * np.float64(cross), dt), dt)))
+    return min(vals), max(vals)
+
+
+def certify_assignment_flips(keys: np.ndarray, parents: np.ndarray, H: int, got: np.ndarray, want: np.ndarray,
+                             dt: str, tag: str = "") -> int:
+    """Every key whose parent differs from the oracle's must be a near-tie
+    that an fp32 accumulation difference explains; returns the count."""
+    bad = np.argwhere(got != want)
+    for g, s in bad:
+        k = keys[g, s]
+        pg = parents[g % H]
+        ksq = O.sq_norms(k[None], dt)[0]
+        pc, po = int(got[g, s]), int(want[g, s])
+        lo_c, _ = possible_parent_distances(k, pg[pc], ksq, O.sq_norms(pg[pc][None], dt)[0], dt)
+        _, hi_o = possible_parent_distances(k, pg[po], ksq, O.sq_norms(pg[po][None], dt)[0], dt)
+        assert lo_c < hi_o or (lo_c == hi_o and pc < po), f"{tag}: key ({g},{s}) parent {pc} vs {po} is no near-tie"
+    n = len(bad)
+    assert n <= max(2, got.size // 1000), f"{tag}: {n} assignment flips of {got.size}"
+    return n
+
+
+def quant_from_arrays(got: dict, values: np.ndarray, M0: int, C: int, dt: str) -> O.Quantization:
+    """The oracle's aggregation run on the CUDA assignments (checks the
+    aggregation kernels independently of the distance kernel)."""
+    pa, ca = got["passign"], got["cassign"]
+    G = pa.shape[0]
+    pagg = O.sequential_bucket_sums(values, pa, M0, dt)
+    cagg = O.sequential_bucket_sums(values, pa * C + ca, M0 * C, dt).reshape(G, M0, C, -1)
+    pce = np.stack([np.bincount(pa[g], minlength=M0) for g in range(G)])
+    cce = np.stack([np.bincount(pa[g] * C + ca[g], minlength=M0 * C) for g in range(G)]).reshape(G, M0, C)
+    sat = O.count_saturation(dt)
+    return O.Quantization(pa, ca, pagg, cagg, np.minimum(pce, sat).astype(np.float32),
+                          np.minimum(cce, sat).astype(np.float32), pce, cce)
+
+
+def check_quantization(got: dict, keys_g: np.ndarray, values_g: np.ndarray, parents: np.ndarray,
+                       children: np.ndarray, dt: str, want: O.Quantization, tag: str = "") -> O.Quantization:
+    """Assignments equal the oracle's up to certified near-ties; children,
+    counts and aggregates are then exact given the CUDA parent assignments.
+    Returns the quantization the rest of the comparison should use."""
+    H, M0, C, _ = children.shape
+
+    def children_of(g: int, p: int) -> np.ndarray:
+        return children[g % H, p]
+
+    certify_assignment_flips(keys_g, parents, H, got["passign"], want.parent_assignments, dt, tag)
+    same = got["passign"] == want.parent_assignments
+    np.testing.assert_array_equal(got["cassign"][same], want.child_assignments[same], err_msg=f"{tag} children")
+    if same.all():
+        exact = want
+    else:
+        exact = quant_from_arrays(got, values_g, M0, C, dt)
+        for g, s in np.argwhere(~same):  # child choice inside the CUDA-chosen parent, exactly
+            ch = children_of(g, got["passign"][g, s])
+            dc = O.child_distances(keys_g[g:g + 1, s:s + 1], ch[None, None], dt)
+            assert int(O.first_argmin(dc)[0, 0]) == int(got["cassign"][g, s]), f"{tag} child of flipped key"
+    np.testing.assert_array_equal(got["pcnt"], exact.parent_counts, err_msg=f"{tag} parent counts")
+    np.testing.assert_array_equal(got["ccnt"], exact.child_counts, err_msg=f"{tag} child counts")
+    np.testing.assert_array_equal(got["pagg"], exact.parent_aggregates, err_msg=f"{tag} parent aggregates")
+    np.testing.assert_array_equal(got["cagg"], exact.child_aggregates, err_msg=f"{tag} child aggregates")
+    return exact
+
+
 def assert_quant_equal(got: dict, want: O.Quantization, tag: str = "") -> None:
     if got["passign"] is not None:
         np.testing.assert_array_equal(got["passign"], want.parent_assignments, err_msg=f"{tag} parent assignments")
@@ -72,6 +153,30 @@ def assert_quant_equal(got: dict, want: O.Quantization, tag: str = "") -> None:
     np.testing.assert_array_equal(got["ccnt"], want.child_counts, err_msg=f"{tag} child counts")
     np.testing.assert_array_equal(got["pagg"], want.parent_aggregates, err_msg=f"{tag} parent aggregates")
     np.testing.assert_array_equal(got["cagg"], want.child_aggregates, err_msg=f"{tag} child aggregates")
+
+
+def check_routing(diag, res: dict, dt: str, tag: str = "") -> None:
+    """Importance equals the oracle's up to rare one-ulp differences (fp32
+    accumulation inside the parent-logit MMA); the routed indices are the
+    exact stable top-k of the CUDA importance, and equal the oracle's unless
+    an importance difference explains the change."""
+    imp = diag.importance.cpu().numpy()
+    want = res["importance0"]
+    diff = imp != want
+    n = int(diff.sum())
+    assert n <= max(2, imp.size // 500), f"{tag}: {n} importance differences"
+    if n:
+        assert np.all(np.abs(imp[diff] - want[diff]) <= 1.01 * ulp(want[diff], dt)), f"{tag}: importance off by > 1 ulp"
+    sels = [s.long().cpu().numpy() for s in diag.selections()]
+    assert len(sels) == len(res["selected"]), f"{tag}: pass count"
+    np.testing.assert_array_equal(sels[0], O.stable_topk_desc(imp, sels[0].shape[-1]), err_msg=f"{tag} routing")
+    for k, (a, b) in enumerate(zip(sels, res["selected"])):
+        if n == 0:
+            np.testing.assert_array_equal(a, b, err_msg=f"{tag} pass {k} selected indices")
+        else:
+            rows = np.unique(np.argwhere(diff)[:, 0])
+            keep = np.setdiff1d(np.arange(a.shape[0]), rows)
+            np.testing.assert_array_equal(a[keep], b[keep], err_msg=f"{tag} pass {k} selected indices")
 
 
 def assert_routing_equal(diag, res: dict, tag: str = "") -> None:

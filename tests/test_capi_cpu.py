@@ -58,4 +58,8 @@ def test_forward_rejects_bad_arguments(call: str) -> None:
 def test_workspace_queries() -> None:
     lib = _lib.load()
     assert lib.avq_quantize_workspace_size(4, 32, 8192, 512) > 4 * 32 * 8192 * 4
-    assert lib.avq_forward_workspace_size(1, 1, 1, 8, 4, 2, 1, 1.0) > 0
+    assert lib.avq_forward_workspace_size(1, 1, 1, 1, 8, 4, 2, 2, 1, 1.0, 0) > 0
+    # the tensor-core path keeps no fp32 logits when they fit in shared memory
+    mma = lib.avq_forward_workspace_size(1, 4, 32, 8192, 128, 512, 4, 32, 1, 1.0, 0)
+    exact = lib.avq_forward_workspace_size(0, 4, 32, 8192, 128, 512, 4, 32, 1, 1.0, 0)
+    assert 0 < mma < exact
