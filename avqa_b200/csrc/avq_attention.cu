@@ -240,6 +240,11 @@ __device__ void pass_counts(int budget0, int passes, float decay, int M0, int* c
 
 // One CTA per (b,h).  phase 0: pre-HVAQ importance, pass 0 (and, without
 // HVAQ, every later pass).  phase 1: post-HVAQ importance, passes >= 1.
+// descending, NaN first (torch.sort), ties by ascending index
+__device__ __forceinline__ unsigned long long route_key(float w, int p) {
+  return ((unsigned long long)(~float_order_key(w)) << 32) | (unsigned)p;
+}
+
 template <int DT>
 __global__ void __launch_bounds__(1024) route_kernel(const double* __restrict__ imp_part, int nqt,
                                                      const int* __restrict__ pcnt, int M0,
@@ -247,33 +252,78 @@ __global__ void __launch_bounds__(1024) route_kernel(const double* __restrict__ 
                                                      float decay, int phase, int all_passes, PassLayout lay,
                                                      int* __restrict__ sel, int sel_stride,
                                                      int* __restrict__ pass_cnt_out,
-                                                     float* __restrict__ importance_out) {
+                                                     float* __restrict__ importance_out, RouteExact rx) {
   extern __shared__ unsigned long long keys[];  // [npow2]
   __shared__ int cnt[MAX_PASSES];
+  __shared__ int namb;
+  __shared__ double red[32];
   const int g = blockIdx.x;
   int npow2 = 1;
   while (npow2 < M0) npow2 <<= 1;
-  unsigned char* refined = (unsigned char*)(keys + npow2);  // [M0]
+  int* amb = (int*)(keys + npow2);                     // [M0] ambiguous columns
+  unsigned char* refined = (unsigned char*)(amb + M0);  // [M0]
   if (threadIdx.x == 0) {
     const int budget0 = min(P, *min_valid);  // pipeline.py:340-343
     pass_counts(budget0, passes, decay, M0, cnt);
     if (g == 0 && pass_cnt_out)
       for (int k = 0; k < passes; ++k) pass_cnt_out[k] = cnt[k];
+    namb = 0;
   }
+  __syncthreads();
+  // importance = n * dtype(sum_t probs) (routing.py:61-63)
   for (int p = threadIdx.x; p < npow2; p += blockDim.x) {
     if (p < M0) {
-      double s = 0.0;
-      for (int i = 0; i < nqt; ++i) s += imp_part[((long)g * nqt + i) * M0 + p];
-      const float w = rnd<DT>(__fmul_rn(count_dt<DT>(pcnt[(long)g * M0 + p]), rnd64<DT>(s)));
+      const float n = count_dt<DT>(pcnt[(long)g * M0 + p]);
+      float w;
+      if (rx.colpart) {
+        // fp32 tile partials: the sum is within 2^-18 relative of the exact
+        // one; if that window straddles a rounding point, recompute below
+        double s = 0.0;
+        for (int i = 0; i < nqt; ++i) s += (double)rx.colpart[((long)g * nqt + i) * M0 + p];
+        const double eps = fabs(s) * 3.814697265625e-06;
+        w = rnd<DT>(__fmul_rn(n, rnd64<DT>(s)));
+        const float w_lo = rnd<DT>(__fmul_rn(n, rnd64<DT>(s - eps)));
+        const float w_hi = rnd<DT>(__fmul_rn(n, rnd64<DT>(s + eps)));
+        if (w_lo != w_hi) amb[atomicAdd(&namb, 1)] = p;
+      } else {
+        double s = 0.0;
+        for (int i = 0; i < nqt; ++i) s += imp_part[((long)g * nqt + i) * M0 + p];
+        w = rnd<DT>(__fmul_rn(n, rnd64<DT>(s)));
+      }
       if (importance_out) importance_out[(long)g * M0 + p] = w;
-      // descending, NaN first (torch.sort), ties by ascending index
-      keys[p] = ((unsigned long long)(~float_order_key(w)) << 32) | (unsigned)p;
+      keys[p] = route_key(w, p);
       refined[p] = 0;
     } else {
       keys[p] = ~0ull;
     }
   }
   __syncthreads();
+  // exact column sums for the ambiguous entries, from the stored tiles
+  const int LDL = M0 + 8;
+  using T = typename Storage<DT>::T;
+  const T* scr = (const T*)rx.scratch;
+  for (int ia = 0; ia < namb; ++ia) {
+    const int p = amb[ia];
+    double s = 0.0;
+    for (int t = threadIdx.x; t < rx.T; t += blockDim.x) {
+      const long row = (long)g * rx.T + t;
+      const float x = to_f(scr[(((long)g * nqt + (t >> 6)) * 64 + (t & 63)) * LDL + p]);
+      const float e = rx.scr_logits ? fmaxf(exp_dt_fast<DT>(rnd<DT>(x - rx.m[row])), 0.f) : x;
+      const float zc = rx.z[row] < eps_dt<DT>() ? eps_dt<DT>() : rx.z[row];
+      s += (double)div_dt_fast<DT>(e, 1.f / zc, zc);
+    }
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double tot = 0.0;
+      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+      const float w = rnd<DT>(__fmul_rn(count_dt<DT>(pcnt[(long)g * M0 + p]), rnd64<DT>(tot)));
+      if (importance_out) importance_out[(long)g * M0 + p] = w;
+      keys[p] = route_key(w, p);
+    }
+    __syncthreads();
+  }
   for (int k = 2; k <= npow2; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
       for (int i = threadIdx.x; i < npow2; i += blockDim.x) {
@@ -583,7 +633,7 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
   const float sqrtD = (float)std::sqrt((double)a.D);
   int npow2 = 1;
   while (npow2 < a.M0) npow2 <<= 1;
-  const size_t rt_smem = sizeof(unsigned long long) * npow2 + a.M0;
+  const size_t rt_smem = sizeof(unsigned long long) * npow2 + sizeof(int) * a.M0 + a.M0;
   auto rk = route_kernel<DT>;
   cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rt_smem);
   auto route = [&](auto... args) {
@@ -597,21 +647,23 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
     if (mma) {
       const int nqt = (a.T + PM_ROWS_PUBLIC - 1) / PM_ROWS_PUBLIC;
       PAArgs pa{a.q, a.qs, a.B, a.H, a.T, a.D, a.M0, sqrtD, a.parents_dt, a.pagg, a.pcnt, 0, hv ? 1 : 0, w.slog,
-                !hv && parent_attn_mma_smem_mode(a.D, a.M0), w.m, w.l, w.z, w.a, w.part0, sel, sel_stride, pcnt_out,
-                a.hvaq, a.beta0, a.alpha, w.beta};
+                false, w.m, w.l, w.z, w.a, (float*)w.part0, sel, sel_stride, pcnt_out, a.hvaq, a.beta0, a.alpha,
+                w.beta};
       int rc = launch_parent_attn_mma<DT>(pa, st);
       if (rc != AVQ_OK) return rc;
-      route(w.part0, nqt, a.pcnt, a.M0, a.min_valid, a.P, a.passes, a.pass_decay, 0,
-                                   (!hv && a.passes > 1) ? 1 : 0, lay, sel, sel_stride, pcnt_out, imp_out);
+      RouteExact rx0{(const float*)w.part0, w.slog, hv ? 1 : 0, w.m, w.z, a.T};
+      route(w.part0, nqt, a.pcnt, a.M0, a.min_valid, a.P, a.passes, a.pass_decay, 0, (!hv && a.passes > 1) ? 1 : 0,
+            lay, sel, sel_stride, pcnt_out, imp_out, rx0);
       if (hv) {
         pa.mode = 1;
         pa.keep_logits = 0;
-        pa.imp_part = w.part1;
+        pa.colpart = (float*)w.part1;
         rc = launch_parent_attn_mma<DT>(pa, st);
         if (rc != AVQ_OK) return rc;
+        RouteExact rx1{(const float*)w.part1, w.slog, 0, w.m, w.z, a.T};
         if (a.passes > 1)
-          route(w.part1, nqt, a.pcnt, a.M0, a.min_valid, a.P, a.passes, a.pass_decay, 1, 1,
-                                       lay, sel, sel_stride, pcnt_out, w.imp);
+          route(w.part1, nqt, a.pcnt, a.M0, a.min_valid, a.P, a.passes, a.pass_decay, 1, 1, lay, sel, sel_stride,
+                pcnt_out, w.imp, rx1);
       }
       CorrArgs ca{a.q, a.qs, a.B, a.H, a.T, a.D, a.M0, a.C, sqrtD, a.parents_dt, a.children_dt, a.pagg, a.cagg,
                   a.pcnt, a.ccnt, w.m, w.l, w.z, hv ? w.beta : nullptr, w.a, sel, sel_stride, pcnt_out, a.passes,
@@ -641,13 +693,14 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
     else AVQ_PA(256, MODE, PART);                              \
   } while (0)
   AVQ_PA_D(0, w.part0);
+  const RouteExact rxn{nullptr, nullptr, 0, nullptr, nullptr, a.T};
   route(w.part0, nqt, a.pcnt, a.M0, a.min_valid, a.P, a.passes, a.pass_decay, 0,
-                               (!hv && a.passes > 1) ? 1 : 0, lay, sel, sel_stride, pcnt_out, imp_out);
+                               (!hv && a.passes > 1) ? 1 : 0, lay, sel, sel_stride, pcnt_out, imp_out, rxn);
   if (hv) {
     AVQ_PA_D(1, w.part1);
     if (a.passes > 1)
       route(w.part1, nqt, a.pcnt, a.M0, a.min_valid, a.P, a.passes, a.pass_decay, 1, 1, lay,
-                                   sel, sel_stride, pcnt_out, w.imp);
+                                   sel, sel_stride, pcnt_out, w.imp, rxn);
   }
 #undef AVQ_PA_D
 #undef AVQ_PA

@@ -82,6 +82,45 @@ template <int DT> __device__ __forceinline__ float log_rn(float x) {
   return rnd<DT>(__double2float_rn(log((double)x)));
 }
 
+// True when an fp32 value y (within +-3 ulp of the correctly rounded result)
+// is too close to a DT rounding midpoint for the narrowing to be certain
+// (and, for fp16, when the result lies in the fp16 subnormal range).
+template <int DT>
+__device__ __forceinline__ bool near_midpoint(float y) {
+  const uint32_t u = __float_as_uint(y);
+  if (DT == DT_BF16) return ((u & 0xFFFFu) - 0x7FFDu) < 7u;
+  if (DT == DT_F16) return ((u & 0x1FFFu) - 0x0FFDu) < 7u || fabsf(y) < 6.2e-5f;
+  return true;
+}
+
+// DT(correctly rounded fp32 exp(x)): expf is within 2 ulp, so only results
+// near a rounding midpoint need the double-precision recomputation.
+template <int DT>
+__device__ __forceinline__ float exp_dt_fast(float x) {
+  if (DT != DT_F32) {
+    const float y = expf(x);
+    if (!near_midpoint<DT>(y)) return rnd<DT>(y);
+  }
+  return rnd<DT>(__double2float_rn(exp((double)x)));
+}
+
+// DT(a / b) with the correctly rounded fp32 quotient; rb = 1/b (any rounding):
+// a * rb is within 2 ulp of a / b.
+template <int DT>
+__device__ __forceinline__ float div_dt_fast(float a, float rb, float b) {
+  if (DT != DT_F32) {
+    const float y = a * rb;
+    if (isfinite(y) && !near_midpoint<DT>(y)) return rnd<DT>(y);
+  }
+  return rnd<DT>(__fdiv_rn(a, b));
+}
+
+// DT(x / sqrt(D)) with the correctly rounded fp32 quotient (pipeline.py:81).
+template <int DT>
+__device__ __forceinline__ float scale_logit(float x, float sqrtD, float inv_sqrtD) {
+  return div_dt_fast<DT>(x, inv_sqrtD, sqrtD);
+}
+
 // Order-preserving map of a float onto uint32 (ascending); NaN maps above +inf.
 __device__ __forceinline__ uint32_t float_order_key(float f) {
   if (isnan(f)) return 0xFFFFFFFFu;

@@ -101,13 +101,24 @@ struct PAArgs {
   bool s_in_smem;
   float *m, *l, *z;    // [G,T]
   void* a;             // [G,T,D] dtype
-  double* imp_part;    // [G, nqt, M0]
+  float* colpart;      // [G, nqt, M0] fp32 column sums of probs per 64-query tile
   const int* sel0;
   int sel_stride;
   const int* pass_cnt;
   int hvaq;
   float beta0, alpha;
   float* beta;         // [G,T]
+};
+
+// Importance from fp32 per-tile column partials, with the exact fallback
+// reading the parent-attention tiles (see route_kernel).
+struct RouteExact {
+  const float* colpart;  // nullptr: the fp64 partials path
+  const void* scratch;   // dtype tiles [G][nqt][64][M0+8]
+  int scr_logits;        // tiles hold logits (exponentials recomputed from m)
+  const float* m;        // [G,T]
+  const float* z;        // [G,T]
+  int T;
 };
 
 struct PassOffsets {
