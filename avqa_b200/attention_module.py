@@ -89,13 +89,6 @@ class AVQAttention(nn.Module):
         if c.refinement.passes > 8:
             raise BackendError("at most 8 refinement passes are supported", {"passes": c.refinement.passes})
 
-    @property
-    def hvaq_mode(self) -> int:
-        c = self.config
-        if not (c.backend.hopfield and c.hopfield.adaptive != "none"):
-            return 0
-        return {"entropy": 1, "linear": 2}[c.hopfield.adaptive]
-
     # -- helpers -----------------------------------------------------------------
 
     @staticmethod
@@ -148,80 +141,111 @@ class AVQAttention(nn.Module):
         return self.forward_impl(query, key, value, mask, kv_cache)
 
     def forward_impl(self, query, key, value, mask=None, kv_cache=None) -> torch.Tensor:
-        if mask is not None or self.config.causal:
-            raise BackendError("attention masks (user or causal) are not supported by the cuda backend")
-        self.validate_inputs(query, key, value)
-        if not query.is_cuda:
-            raise DeviceError("the cuda backend needs CUDA tensors", expected="cuda", actual=str(query.device))
-        qp, kp, vp = self.maybe_project(query, key, value)
-        H = self.config.attention.num_heads
-        q = self.split_heads(qp, H)
-        k = self.split_heads(kp, H)
-        v = self.split_heads(vp, H)
-        self.sync_codebook_device(q)
-        backend: CUDABackend = self.backend  # type: ignore[assignment]
-        cb = backend.prepared_codebook(self.codebook.parents, self.codebook.children, q.dtype, q.device)
-        state = self.resolve_quantization(k, v, cb, kv_cache)
-        B, _, T, D = q.shape
-        if state.S == 0:
-            # pipeline.py:344-345: budget 0 -> naive attention over zero keys
-            attn = backend.naive_attention(q, k, v)
-            return self.dropout(self.out_proj(self.merge_heads(attn)))
-        min_valid = self.global_min_valid(state)
-        out = torch.empty(B, T, H * D, dtype=torch.float32, device=q.device)
-        out4 = out.view(B, T, H, D).transpose(1, 2)
-        c = self.config
-        beta0 = c.hopfield.beta_init if c.hopfield.beta_init > 0 else 1.0 / math.sqrt(D)
-        backend.forward(q, cb, state, min(c.routing.refinement_budget, cb.dims[1]), c.refinement.passes,
-                        c.refinement.pass_decay, self.hvaq_mode, beta0, c.hopfield.alpha, out=out4,
-                        min_valid=min_valid)
-        return self.dropout(self.out_proj(out))
+        return cuda_run_pipeline(self, query, key, value, mask, kv_cache)
 
-    def global_min_valid(self, state: ops.QuantState) -> torch.Tensor:
-        """The budget floor: min over every (b,h) of the call -- and of every
-        rank when heads are sharded across a process group."""
-        if self.process_group is None:
-            return state.gmin
-        import torch.distributed as dist
-        g = state.gmin.clone()
-        dist.all_reduce(g, op=dist.ReduceOp.MIN, group=self.process_group)
-        return g
 
-    def resolve_quantization(self, k: torch.Tensor, v: torch.Tensor, cb: ops.PreparedCodebook,
-                             kv_cache: KVCache | None) -> ops.QuantState:
-        """Quantize ``k``/``v`` -- or, with a cache, extend the cache's state."""
-        if kv_cache is None:
-            st = ops.quantize(k, v, cb)
-            self.last_keys = k.detach()
-            self.last_parent_assignments = st.passign.view(k.shape[:3]).long()
-            return st
-        skey = (id(self), id(cb), k.dtype)
-        st = kv_cache.quant_states.get(skey)
-        if st is not None and (st.B != k.shape[0] or st.H != k.shape[1]):
-            st = None
-        if st is None:
-            ck, cv = kv_cache.lookup()
-            if ck.shape[-2] > 0:
-                ck = ck.to(device=k.device, dtype=k.dtype)
-                cv = cv.to(device=v.device, dtype=v.dtype)
-                kf, vf = torch.cat([ck, k], dim=-2), torch.cat([cv, v], dim=-2)
-            else:
-                kf, vf = k, v
-            st = ops.quantize(kf, vf, cb, keep_sums=True)
-            kv_cache.append(k, v)
-            kv_cache.quant_states.clear()
-            kv_cache.quant_states[skey] = st
-            return st
-        if isinstance(kv_cache, PagedKVCache) and str(kv_cache.device) == str(k.device) and kv_cache.dtype == k.dtype:
-            cursor = 0
-            for page, slot0, take in kv_cache.reserve(k.shape[0], k.shape[2]):
-                ops.append(st, k[:, :, cursor:cursor + take], v[:, :, cursor:cursor + take], cb,
-                           kv_cache.key_pages[page], kv_cache.value_pages[page], slot0)
-                cursor += take
-        else:
-            ops.append(st, k, v, cb)
-            kv_cache.append(k, v)
+def hvaq_mode(config: AVQConfig) -> int:
+    """0 off, 1 entropy, 2 linear (the gate of pipeline.py:353)."""
+    if not (config.backend.hopfield and config.hopfield.adaptive != "none"):
+        return 0
+    return {"entropy": 1, "linear": 2}[config.hopfield.adaptive]
+
+
+def cuda_run_pipeline(m, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                      mask: torch.Tensor | None = None, kv_cache=None) -> torch.Tensor:
+    """The reference pipeline (pipeline.py:276-399) on the CUDA library.
+
+    ``m`` is any module with the reference ``AVQAttention`` attributes
+    (``config``, ``codebook``, ``q_proj``/``k_proj``/``v_proj``/``out_proj``,
+    ``dropout``, ``validate_inputs``, ``sync_codebook_device``) whose
+    ``backend`` is a :class:`CUDABackend` -- this package's module or the
+    reference's own one.
+    """
+    c = m.config
+    if mask is not None or c.causal:
+        raise BackendError("attention masks (user or causal) are not supported by the cuda backend")
+    m.validate_inputs(query, key, value)
+    if not query.is_cuda:
+        raise DeviceError("the cuda backend needs CUDA tensors", expected="cuda", actual=str(query.device))
+    qp, kp, vp = m.q_proj(query), m.k_proj(key), m.v_proj(value)
+    H = c.attention.num_heads
+    q = AVQAttention.split_heads(qp, H)
+    k = AVQAttention.split_heads(kp, H)
+    v = AVQAttention.split_heads(vp, H)
+    m.sync_codebook_device(q)
+    backend: CUDABackend = m.backend  # type: ignore[assignment]
+    cb = backend.prepared_codebook(m.codebook.parents, m.codebook.children, q.dtype, q.device)
+    state = resolve_quantization(m, k, v, cb, kv_cache)
+    B, _, T, D = q.shape
+    if state.S == 0:
+        # pipeline.py:344-345: budget 0 -> naive attention over zero keys
+        attn = backend.naive_attention(q, k, v)
+        return m.dropout(m.out_proj(AVQAttention.merge_heads(attn)))
+    min_valid = global_min_valid(state, getattr(m, "process_group", None))
+    out = torch.empty(B, T, H * D, dtype=torch.float32, device=q.device)
+    out4 = out.view(B, T, H, D).transpose(1, 2)
+    beta0 = c.hopfield.beta_init if c.hopfield.beta_init > 0 else 1.0 / math.sqrt(D)
+    backend.forward(q, cb, state, min(c.routing.refinement_budget, cb.dims[1]), c.refinement.passes,
+                    c.refinement.pass_decay, hvaq_mode(c), beta0, c.hopfield.alpha, out=out4, min_valid=min_valid)
+    return m.dropout(m.out_proj(out))
+
+
+def global_min_valid(state: ops.QuantState, group=None) -> torch.Tensor:
+    """The budget floor: min over every (b,h) of the call -- and of every
+    rank of ``group`` when batches or heads are sharded."""
+    if group is None:
+        return state.gmin
+    import torch.distributed as dist
+    g = state.gmin.clone()
+    dist.all_reduce(g, op=dist.ReduceOp.MIN, group=group)
+    return g
+
+
+def _cache_states(kv_cache) -> dict:
+    states = getattr(kv_cache, "quant_states", None)
+    if states is None:  # a reference KVCache: attach the device state to it
+        states = {}
+        kv_cache.quant_states = states
+    return states
+
+
+def resolve_quantization(m, k: torch.Tensor, v: torch.Tensor, cb: ops.PreparedCodebook,
+                         kv_cache=None) -> ops.QuantState:
+    """Quantize ``k``/``v`` -- or, with a cache, extend the cache's device state
+    (resolve_kv_cache, attention_module.py:350-367, then the quantizer)."""
+    if kv_cache is None:
+        st = ops.quantize(k, v, cb)
+        m.last_keys = k.detach()
+        m.last_parent_assignments = st.passign.view(k.shape[:3]).long()
         return st
+    states = _cache_states(kv_cache)
+    skey = (id(m), id(cb), k.dtype)
+    st = states.get(skey)
+    if st is not None and (st.B != k.shape[0] or st.H != k.shape[1]):
+        st = None
+    if st is None:
+        ck, cv = kv_cache.lookup()
+        if ck.shape[-2] > 0:
+            ck = ck.to(device=k.device, dtype=k.dtype)
+            cv = cv.to(device=v.device, dtype=v.dtype)
+            kf, vf = torch.cat([ck, k], dim=-2), torch.cat([cv, v], dim=-2)
+        else:
+            kf, vf = k, v
+        st = ops.quantize(kf, vf, cb, keep_sums=True)
+        kv_cache.append(k, v)
+        states.clear()
+        states[skey] = st
+        return st
+    if isinstance(kv_cache, PagedKVCache) and str(kv_cache.device) == str(k.device) and kv_cache.dtype == k.dtype:
+        cursor = 0
+        for page, slot0, take in kv_cache.reserve(k.shape[0], k.shape[2]):
+            ops.append(st, k[:, :, cursor:cursor + take], v[:, :, cursor:cursor + take], cb,
+                       kv_cache.key_pages[page], kv_cache.value_pages[page], slot0)
+            cursor += take
+    else:
+        ops.append(st, k, v, cb)
+        kv_cache.append(k, v)
+    return st
 
 
-__all__ = ["AVQAttention"]
+__all__ = ["AVQAttention", "cuda_run_pipeline", "global_min_valid", "hvaq_mode", "resolve_quantization"]

@@ -232,6 +232,16 @@ __global__ void __launch_bounds__(128, 4) parent_attn_mma_kernel(
   for (int j = 0; j < NT; ++j) oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f;
   load_rows(vb, 0, 0, true);
   cp_async_commit();
+  // logits of the next 16-column step are loaded one step ahead
+  auto load_s = [&](int pk, uint32_t (&s)[4]) {
+#pragma unroll
+    for (int hh = 0; hh < 4; ++hh) {
+      const int p = pk + cq + ((hh >> 1) << 3);
+      s[hh] = p < M0 ? *reinterpret_cast<const uint32_t*>(S_ + (long)((hh & 1) ? r1 : r0) * LDL + p) : 0u;
+    }
+  };
+  uint32_t snext[4];
+  load_s(0, snext);
   for (int ci = 0; ci < nch; ++ci) {
     const int buf = ci & 1, p0 = ci * PM_CH;
     cp_async_wait<0>();
@@ -242,14 +252,17 @@ __global__ void __launch_bounds__(128, 4) parent_attn_mma_kernel(
     const T* svb = sb + buf * PM_CH * LDS;
 #pragma unroll
     for (int k = 0; k < PM_CH / 16; ++k) {
-      uint32_t a[4];
+      uint32_t a[4], scur[4];
+#pragma unroll
+      for (int hh = 0; hh < 4; ++hh) scur[hh] = snext[hh];
+      load_s(p0 + k * 16 + 16, snext);
 #pragma unroll
       for (int hh = 0; hh < 4; ++hh) {  // a[hh]: rows (hh&1 ? r1 : r0), columns +8*(hh>>1)
         const int cl = k * 16 + cq + ((hh >> 1) << 3), p = p0 + cl;
         const int r = (hh & 1) ? r1 : r0;
         uint32_t e2 = 0u;
         if (p < M0) {
-          const uint32_t s2 = *reinterpret_cast<const uint32_t*>(S_ + (long)r * LDL + p);
+          const uint32_t s2 = scur[hh];
           const uint32_t d2 = hsub2_dt<DT>(s2, (hh & 1) ? sf1 : sf0);
           const float e0 = fmaxf(exp_dt_fast<DT>(half_lo<DT>(d2)), 0.f);  // NaN -> 0 (pipeline.py:143-145)
           const float e1 = fmaxf(exp_dt_fast<DT>(half_hi<DT>(d2)), 0.f);
@@ -338,12 +351,15 @@ __global__ void __launch_bounds__(128, 4) parent_attn_mma_kernel(
     const int p = p0 + 2 * lane;
     float c0 = 0.f, c1 = 0.f;
     if (p < M0) {
-#pragma unroll 4
+      uint32_t ws[16];
+#pragma unroll
+      for (int rr = 0; rr < 16; ++rr) ws[rr] = *reinterpret_cast<const uint32_t*>(S_ + (long)(warp * 16 + rr) * LDL + p);
+#pragma unroll
       for (int rr = 0; rr < 16; ++rr) {
         const int r = warp * 16 + rr;
         if (srow[r * 4 + 3] == 0.f) continue;  // query beyond T
         const float zc = srow[r * 4], rz = srow[r * 4 + 1];
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(S_ + (long)r * LDL + p);
+        const uint32_t w = ws[rr];
         float e0 = half_lo<DT>(w), e1 = half_hi<DT>(w);
         if (keep_logits) {  // the slice still holds logits (an HVAQ pass follows)
           const float sf = srow[r * 4 + 2];
