@@ -258,3 +258,80 @@ int avq_reduce_min(const int* v, int n, int* out, void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// avq_quantize_noalloc: the quantizer with its scratch in a fixed device array.
+//
+// It exists for hosts that may not allocate device memory while they run: a
+// serving runtime that carved the whole GPU into its own pool at start-up, or
+// a cgo/JNI host that has no device allocator to call.  Such a host cannot
+// hand avq_quantize a workspace, and a cudaMalloc inside the library would
+// either fail or eat into memory the pool has promised elsewhere (and the
+// matching cudaFree would synchronize the whole device).  So the scratch is a
+// file-scope __device__ array: it comes with the library's device code, one
+// copy per device, and costs AVQ_QUANTIZE_NOALLOC_SCRATCH_BYTES of each
+// device's memory once the code is loaded there.
+//
+// Because every call on a device uses the same array, two calls that run at
+// the same time on one device corrupt each other's bucket order; callers
+// keep them in order on one stream.  No byte of the array needs a known
+// starting value: the histogram kernel writes all M0 bins of every segment
+// (or a memset zeroes them when S == 0), the scan writes every offset and the
+// scatter writes every key position before anything reads them.
+
+namespace {
+
+__device__ __align__(256) unsigned char g_quantize_scratch[AVQ_QUANTIZE_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_scratch[kNoallocMaxDevices] = {};
+
+// Device address of this device's scratch array; looked up once per device.
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(AVQ_ERR_CUDA, "avq_quantize_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  }
+  if (dev < 0 || dev >= kNoallocMaxDevices)
+    return fail(AVQ_ERR_ARG, "avq_quantize_noalloc: device %d beyond the %d supported", dev, kNoallocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_scratch[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_quantize_scratch);
+    if (e != cudaSuccess || !p) {
+      cudaGetLastError();
+      return fail(AVQ_ERR_CUDA, "avq_quantize_noalloc: cudaGetSymbolAddress on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    }
+    g_noalloc_scratch[dev] = p;
+  }
+  *out = g_noalloc_scratch[dev];
+  return AVQ_OK;
+}
+
+}  // namespace
+
+extern "C" int avq_quantize_noalloc(int dtype, const void* keys, const long long* key_strides, const void* values,
+                                    const long long* value_strides, int B, int H, int S, int D, int M0, int C,
+                                    const void* parents_dt, const float* p_sq, const void* children_dt,
+                                    const float* c_sq, int* passign, int* cassign, void* pagg, void* cagg,
+                                    float* pacc, float* cacc, int* pcnt, int* ccnt, int* nvalid, int* gmin_valid,
+                                    void* stream) {
+  // The size check comes first so that an oversized request touches no device.
+  if (B < 0 || H <= 0 || S < 0 || M0 <= 0) return fail(AVQ_ERR_ARG, "avq_quantize_noalloc: bad sizes");
+  const size_t need = avq::quantize_workspace_bytes(B * H, S, M0);
+  if (need > AVQ_QUANTIZE_NOALLOC_SCRATCH_BYTES)
+    return fail(AVQ_ERR_WORKSPACE,
+                "avq_quantize_noalloc: B=%d H=%d S=%d M0=%d needs %zu scratch bytes but the fixed array holds %zu; "
+                "call avq_quantize with a workspace instead",
+                B, H, S, M0, need, (size_t)AVQ_QUANTIZE_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != AVQ_OK) return rc;
+  return avq_quantize(dtype, keys, key_strides, values, value_strides, B, H, S, D, M0, C, parents_dt, p_sq,
+                      children_dt, c_sq, passign, cassign, pagg, cagg, pacc, cacc, pcnt, ccnt, nvalid, gmin_valid,
+                      scratch, AVQ_QUANTIZE_NOALLOC_SCRATCH_BYTES, stream);
+}

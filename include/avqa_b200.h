@@ -25,6 +25,8 @@
  *                         cache.py:246-260, plus the re-quantization of the grown key
  *                         set (quantizer.py:166-278) done incrementally
  *   avq_reduce_min        the budget's min over (b,h) of valid parents, pipeline.py:341-342
+ *   avq_quantize_noalloc  no counterpart: avq_quantize with its scratch in a fixed
+ *                         device array, for hosts that cannot allocate
  */
 #ifndef AVQA_B200_H
 #define AVQA_B200_H
@@ -69,6 +71,45 @@ int avq_quantize(int dtype, const void* keys, const long long* key_strides, cons
                  const float* p_sq, const void* children_dt, const float* c_sq, int* passign, int* cassign,
                  void* pagg, void* cagg, float* pacc, float* cacc, int* pcnt, int* ccnt, int* nvalid,
                  int* gmin_valid, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Size in bytes of the fixed scratch array behind avq_quantize_noalloc: one
+ * array per device, 16 MiB.  A call needs avq_quantize_workspace_size(B, H,
+ * S, M0) bytes of it (12.3 MiB for B=4, H=32, S=8192, M0=512). */
+#define AVQ_QUANTIZE_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+
+/* avq_quantize for callers that cannot supply a device workspace.  No
+ * counterpart in the reference, whose torch quantizer allocates through the
+ * torch caching allocator on every call.
+ *
+ * Arguments, outputs and results are those of avq_quantize (same kernels);
+ * only `workspace`/`workspace_bytes` are gone.  The quantizer's scratch --
+ * bucket histograms, key order, bucket offsets -- lives in a file-scope
+ * device array compiled into the library, so the call allocates nothing.
+ *
+ * Who needs it: a host whose device memory is owned by someone else -- a
+ * serving runtime that reserved the GPU's memory for its own pool up front,
+ * or a foreign-language host (cgo, JNI) with no device allocator of its own
+ * -- where a cudaMalloc would fail, or take memory the pool counts on, and a
+ * cudaFree would synchronize the device in the middle of a prefill.
+ *
+ * Limits and rules:
+ *  - Requests needing more than AVQ_QUANTIZE_NOALLOC_SCRATCH_BYTES fail with
+ *    AVQ_ERR_WORKSPACE before anything is enqueued; use avq_quantize then.
+ *  - The scratch need not start zeroed: every call writes each scratch byte
+ *    before reading it.  gmin_valid, as for avq_quantize, must be initialised
+ *    by the caller.
+ *  - The array is shared by every call on a device: calls that overlap on one
+ *    device (two streams, or two host threads without ordering) race on it.
+ *    Issue them in order on one stream.
+ *  - The first call on each device (the current device) does a one-time setup:
+ *    it looks up the array's device address with cudaGetSymbolAddress, which
+ *    may load the library's device code onto that device.  Make that first
+ *    call before any stream capture begins on the device. */
+int avq_quantize_noalloc(int dtype, const void* keys, const long long* key_strides, const void* values,
+                         const long long* value_strides, int B, int H, int S, int D, int M0, int C,
+                         const void* parents_dt, const float* p_sq, const void* children_dt, const float* c_sq,
+                         int* passign, int* cassign, void* pagg, void* cagg, float* pacc, float* cacc, int* pcnt,
+                         int* ccnt, int* nvalid, int* gmin_valid, void* stream);
 
 /* Number of int32 slots per (b,h) in the `selected` output of avq_forward:
  * the sum of the per-pass budget caps for base budget P. */
