@@ -48,7 +48,10 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c2")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--cpu-slices", type=int, default=1, help="(b,h) slices in the CPU-baseline sample")
+    ap.add_argument("--cpu-slices", type=int, default=1,
+                    help="(b,h) slices in the CPU-baseline sample; 0 skips the baseline (profiling runs)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the per-GPU batch B (smaller cases for profiler captures)")
     return ap.parse_args()
 
 
@@ -56,9 +59,12 @@ def parse_args():
 # clocks
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    """nvidia-smi clocks / throttle reasons, sampled every 50 ms with host
+    timestamps.  ``mark(start, end)`` records the timed window; the summary
+    uses the samples inside it, and widens to the warm-up steps before it
+    (the same work) only when the window held fewer than three samples."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -66,16 +72,25 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.file = None
+        self.t_open = self.t0 = self.t1 = None
 
     def __enter__(self):
         self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.file,
+                                          "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.file,
                                          stderr=subprocess.DEVNULL)
         except (FileNotFoundError, OSError):
             self.proc = None
+            return self
+        deadline = time.time() + 10.0  # wait for the first sample so the window is covered
+        while time.time() < deadline and self.proc.poll() is None and os.path.getsize(self.file.name) == 0:
+            time.sleep(0.02)
+        self.t_open = time.time()
         return self
+
+    def mark(self, t0: float, t1: float) -> None:
+        self.t0, self.t1 = t0, t1
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -86,26 +101,33 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
+        from datetime import datetime
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.file.flush()
         rows = []
         for line in Path(self.file.name).read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+                ts = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(parts[2]), float(parts[3]), float(parts[4]), parts[6:10]))
             except ValueError:
                 continue
         os.unlink(self.file.name)
-        if not rows:
+        window = "timed"
+        sel = [r for r in rows if self.t0 is not None and self.t0 <= r[0] <= self.t1]
+        if len(sel) < 3:
+            window = "warmup+timed"
+            sel = [r for r in rows if self.t_open is not None and self.t_open <= r[0] <= (self.t1 or r[0])]
+        if not sel:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for _, _, _, flags in rows for i, f in enumerate(flags) if f.lower() == "active"})
-        load = sorted(r[0] for r in rows)
-        return {"sm_mhz": load[len(load) // 2], "sm_max_mhz": rows[0][1], "power_w_max": max(r[2] for r in rows),
-                "samples": len(rows), "reasons": reasons}
+        reasons = sorted({names[i] for *_, flags in sel for i, f in enumerate(flags) if f.lower() == "active"})
+        load = sorted(r[1] for r in sel)
+        return {"sm_mhz": load[len(load) // 2], "sm_max_mhz": sel[0][2], "power_w_max": max(r[3] for r in sel),
+                "samples": len(sel), "window": window, "reasons": reasons}
 
 
 # ---------------------------------------------------------------------------
@@ -236,6 +258,8 @@ def run_ours(args) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     w: Workload = WORKLOADS[args.workload]
+    if args.batch:
+        w = Workload(**{**w.__dict__, "B": args.batch})
     dt = TORCH_DTYPE[w.dtype]
     H, D = w.H, w.D
     # codebook from batch 0 of the global batch (rank 0's seed), identical on every rank
@@ -275,11 +299,13 @@ def run_ours(args) -> None:
         return float(ms.item())
 
     with torch.no_grad():
-        for _ in range(args.warmup):
-            mod(q, k, v)
         with ClockSampler(local) as clk:
+            for _ in range(args.warmup):
+                mod(q, k, v)
             _lib.profile_begin()
+            t_start = time.time()
             total_ms = timed(lambda: mod(q, k, v), args.steps)
+            clk.mark(t_start, time.time())
             prof = _lib.profile_end()
         clocks = clk.summary()
         ms_step = total_ms / args.steps
@@ -343,7 +369,7 @@ def run_ours(args) -> None:
     per_scope = {"bucket_sort": 3}  # histogram, scan, stable scatter
     gpu_launches = sum(n * per_scope.get(name, 1) for name, (_, n) in prof.items())
     try:
-        cpu = cpu_baseline(w, slices=args.cpu_slices)
+        cpu = cpu_baseline(w, slices=args.cpu_slices) if args.cpu_slices > 0 else None
     except Exception as exc:  # the baseline must never hide the GPU number
         cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {exc}"}
     out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
