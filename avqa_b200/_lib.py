@@ -35,6 +35,7 @@ _SIGS = {
     "avq_append": ([_I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                     _P, _I, _P], _I),
     "avq_reduce_min": ([_P, _I, _P, _P], _I),
+    "avq_device_fault": ([_P, _P], _I),
     "avq_quantize_noalloc": ([_I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                               _P, _P, _P, _P, _P], _I),
     "avq_profile_begin": ([], _I),

@@ -545,6 +545,7 @@ struct FwdWorkspace {
   double *part0, *part1;
   int *sel, *pass_cnt;
   void* slog;  // tensor-core path: logits scratch when not in shared memory (or kept for HVAQ)
+  void* exptab;  // tcgen05 path: the bf16 exponential table
   size_t bytes;
 };
 
@@ -580,6 +581,7 @@ static FwdWorkspace carve(void* base, int dtype, int G, int T, int D, int M0, in
   w.part1 = hvaq ? (double*)take(sizeof(double) * (long)G * (nqt > 0 ? nqt : 1) * M0) : nullptr;
   w.sel = (int*)take(sizeof(int) * (long)G * sel_stride);
   w.pass_cnt = (int*)take(sizeof(int) * MAX_PASSES);
+  w.exptab = mma ? take(parent_attn_tc_table_bytes()) : nullptr;
   w.bytes = (size_t)(p - (char*)base);
   return w;
 }
@@ -649,7 +651,11 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
       PAArgs pa{a.q, a.qs, a.B, a.H, a.T, a.D, a.M0, sqrtD, a.parents_dt, a.pagg, a.pcnt, 0, hv ? 1 : 0, w.slog,
                 false, w.m, w.l, w.z, w.a, (float*)w.part0, sel, sel_stride, pcnt_out, a.hvaq, a.beta0, a.alpha,
                 w.beta};
-      int rc = launch_parent_attn_mma<DT>(pa, st);
+      // tcgen05 kernel for the plain first pass; the HVAQ variant keeps its
+      // logits for the rescaling pass and runs on the mma.sync kernel
+      int rc = (!hv && parent_attn_tc_ok(DT, a.D, a.M0)) ? launch_parent_attn_tc<DT>(pa, w.exptab, st)
+                                                         : AVQ_ERR_UNSUPPORTED;
+      if (rc == AVQ_ERR_UNSUPPORTED) rc = launch_parent_attn_mma<DT>(pa, st);
       if (rc != AVQ_OK) return rc;
       RouteExact rx0{(const float*)w.part0, w.slog, hv ? 1 : 0, w.m, w.z, a.T};
       route(w.part0, nqt, a.pcnt, a.M0, a.min_valid, a.P, a.passes, a.pass_decay, 0, (!hv && a.passes > 1) ? 1 : 0,

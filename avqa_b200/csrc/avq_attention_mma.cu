@@ -24,20 +24,6 @@ constexpr int PM_ROWS = 64;
 constexpr int PM_CH = 64;
 constexpr int PM_MAX_SMEM_M0 = 1024;
 
-template <int DT>
-__device__ __forceinline__ float half_lo(uint32_t w) {
-  return DT == DT_BF16 ? __uint_as_float(w << 16) : __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
-}
-template <int DT>
-__device__ __forceinline__ float half_hi(uint32_t w) {
-  return DT == DT_BF16 ? __uint_as_float(w & 0xffff0000u) : __half2float(__ushort_as_half((unsigned short)(w >> 16)));
-}
-
-__device__ __forceinline__ float nanmax(float a, float b) {
-  if (isnan(a) || isnan(b)) return NAN;
-  return a > b ? a : b;
-}
-__device__ __forceinline__ float clamp_min_nan(float x, float lo) { return isnan(x) ? x : (x < lo ? lo : x); }
 
 // ---------------------------------------------------------------------------
 // Parent attention kernel.  CTA = 64 queries = 4 warps x 16 rows; a lane quad
@@ -46,27 +32,6 @@ __device__ __forceinline__ float clamp_min_nan(float x, float lo) { return isnan
 // in a per-CTA global slice (64 x (M0+8) dtype values, L2-resident while the
 // CTA runs) that the routing kernel can re-read for its exactness fallback.
 // ---------------------------------------------------------------------------
-template <int DT>
-__device__ __forceinline__ uint32_t hsub2_dt(uint32_t a, uint32_t b) {
-  uint32_t r;
-  if (DT == DT_BF16) asm("sub.rn.bf16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
-  else asm("sub.rn.f16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-
-template <int DT>
-__device__ __forceinline__ uint32_t hmax2_nan_dt(uint32_t a, uint32_t b) {
-  uint32_t r;
-  if (DT == DT_BF16) asm("max.NaN.bf16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
-  else asm("max.NaN.f16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-
-template <int DT>
-__device__ __forceinline__ uint32_t dup2(float x) {
-  return pack2<DT>(x, x);
-}
-
 template <int DT, int D>
 __global__ void __launch_bounds__(128, 4) parent_attn_mma_kernel(
     const typename Storage<DT>::T* __restrict__ q, Strides3 qs, int H, int Tq, int M0, float sqrtD,

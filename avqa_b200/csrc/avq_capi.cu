@@ -257,6 +257,13 @@ int avq_reduce_min(const int* v, int n, int* out, void* stream) {
   return finish(avq::launch_reduce_min(v, n, out, (cudaStream_t)stream), "avq_reduce_min");
 }
 
+int avq_device_fault(int* code, void* stream) {
+  if (!code) return fail(AVQ_ERR_ARG, "avq_device_fault: null pointer");
+  if (avq::read_device_fault(code, (cudaStream_t)stream) != AVQ_OK)
+    return fail(AVQ_ERR_CUDA, "avq_device_fault: %s", cudaGetErrorString(cudaGetLastError()));
+  return AVQ_OK;
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------

@@ -158,6 +158,15 @@ bool parent_attn_mma_smem_mode(int D, int M0);
 size_t parent_attn_mma_scratch(int G, int T, int M0, int dt_bytes);
 constexpr int PM_ROWS_PUBLIC = 64;
 
+// tcgen05 parent attention (first pass without HVAQ): same outputs, scratch
+// slices and 64-query importance partials as launch_parent_attn_mma.
+bool parent_attn_tc_ok(int dt, int D, int M0);
+size_t parent_attn_tc_table_bytes();
+template <int DT>
+int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st);
+// Reads and clears the device fault record (stream-synchronous).
+int read_device_fault(int* code, cudaStream_t st);
+
 template <int DT>
 int launch_append(const AppendArgs& a, cudaStream_t st);
 int launch_reduce_min(const int* v, int n, int* out, cudaStream_t st);

@@ -62,4 +62,54 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return r;
 }
 
+
+// NaN-propagating max and clamp (torch.max / clamp_min semantics).
+__device__ __forceinline__ float nanmax(float a, float b) {
+  if (isnan(a) || isnan(b)) return NAN;
+  return a > b ? a : b;
+}
+__device__ __forceinline__ float clamp_min_nan(float x, float lo) { return isnan(x) ? x : (x < lo ? lo : x); }
+
+// Halves of a DT x2 register as floats.
+template <int DT>
+__device__ __forceinline__ float half_lo(uint32_t w) {
+  return DT == DT_BF16 ? __uint_as_float(w << 16) : __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
+}
+template <int DT>
+__device__ __forceinline__ float half_hi(uint32_t w) {
+  return DT == DT_BF16 ? __uint_as_float(w & 0xffff0000u) : __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t hsub2_dt(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if (DT == DT_BF16) asm("sub.rn.bf16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
+  else asm("sub.rn.f16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t hmax2_nan_dt(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if (DT == DT_BF16) asm("max.NaN.bf16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
+  else asm("max.NaN.f16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t dup2(float x) {
+  return pack2<DT>(x, x);
+}
+
+// DT(a * b) per half: the exact product rounded once (for DT operands whose
+// product is exact in fp32, the same as narrowing the fp32 product).
+template <int DT>
+__device__ __forceinline__ uint32_t hmul2_dt(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if (DT == DT_BF16) asm("mul.rn.bf16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
+  else asm("mul.rn.f16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+
 }  // namespace avq

@@ -1,0 +1,664 @@
+// Parent attention on the sm_100a tensor cores (tcgen05 + TMEM + TMA) for
+// bf16 / fp16 and D in {64, 128} (reference pipeline.py:46-151, :322-339 and
+// routing.py:61-63): the parent logits, their softmax statistics, the value
+// sums a = e @ V and the per-parent importance partials of the first routing
+// pass.
+//
+// CTA = 128 queries of one (b,h) = one UMMA M tile.  Threads 0-127 (warps
+// 0-3) own one query row each, i.e. TMEM lane = row; warp 4 issues the
+// tcgen05.mma instructions; warp 5 streams Q, parent and parent-sum tiles with
+// TMA into 128-byte-swizzled shared memory.
+//
+// TMEM, 256 columns: the fp32 accumulator O = e @ V in [0, D) and two
+// 64-column logit buffers at [D, D+64) and [D+64, D+128).  A buffer receives
+// one 64-parent chunk of Q P^T; in the second pass the row threads overwrite
+// its first 32 columns with the chunk's dtype exponentials (two per column),
+// which are the A operand of the e @ V MMA.
+//
+//   pass 1  S_c = Q P_c^T for every chunk c; row max of the narrowed,
+//           scaled, masked logits.
+//   pass 2  S_c again (the tensor cores recompute it instead of a round trip
+//           through memory); e = DT(exp(DT(s - m))), l += DT(e * n), z += e;
+//           e -> TMEM -> O += e V_c; e -> the scratch slice that the routing
+//           kernel reads for its exact fallback.
+//   pass 3  probs = DT(e / max(z, eps)) summed over each 64-query tile per
+//           parent (fp32 partials, within 2^-19 relative of the exact sums).
+//
+// Rounding points are those of the reference (see avq_common.cuh); for bf16
+// the exponential comes from a table of DT(correctly rounded fp32 exp(x))
+// over every bf16 x in [-128, -2^-9].
+#include <cuda.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <mutex>
+
+#include "avq_kernels.cuh"
+#include "avq_mma.cuh"
+#include "avq_tc.cuh"
+
+namespace avq {
+
+// Bit 0: a kernel gave up on a bounded wait (read by avq_device_fault).
+__device__ int g_device_fault;
+
+namespace {
+
+constexpr int TR = 128;        // queries per CTA
+constexpr int TCH = 64;        // parents per chunk
+constexpr int TTHREADS = 192;  // 4 row warps + MMA warp + TMA warp
+constexpr int TC_TMEM_COLS = 256;
+constexpr uint32_t EXP_BASE = 0x3AFF;  // bf16 bits of the largest |d| whose exp rounds to 1
+constexpr int EXP_N = 2051;            // entries 0..2049: |d| bits EXP_BASE + i; 2050: |d| > 128, inf, NaN
+constexpr int EXP_WORDS = (EXP_N + 1) / 2;
+constexpr int TC_MAX_M0 = 2048;
+
+// Barrier slots.
+constexpr int B_Q = 0, B_PFULL = 1, B_PEMPTY = 3, B_VFULL = 5, B_VEMPTY = 7, B_SFULL = 9, B_EFULL = 11, B_SFREE = 13,
+              B_OFULL = 14, B_COMB = 15, N_BARS = 16;
+
+struct TcLayout {
+  int q, p[2], v[2], exptab, pm2, n2, srow, scomb, bars, misc, total;
+};
+
+__host__ __device__ inline TcLayout tc_layout(int D, int M0) {
+  TcLayout L;
+  const int nch = (M0 + TCH - 1) / TCH;
+  int o = 0;
+  L.q = o;
+  o += TR * D * 2;
+  for (int i = 0; i < 2; ++i) {
+    L.p[i] = o;
+    o += TCH * D * 2;
+  }
+  for (int i = 0; i < 2; ++i) {
+    L.v[i] = o;
+    o += TCH * D * 2;
+  }
+  L.exptab = o;
+  o += EXP_WORDS * 4;
+  o = (o + 15) & ~15;
+  L.pm2 = o;
+  o += nch * 32 * 4;
+  L.n2 = o;
+  o += nch * 32 * 4;
+  L.srow = o;
+  o += TR * 4 * 4;
+  L.scomb = o;
+  o += 2 * 4 * 128 * 4;
+  L.bars = o;
+  o += N_BARS * 8;
+  L.misc = o;
+  o += 16;
+  L.total = o;
+  return L;
+}
+
+// DT(x / sqrt(D)) of the dtype-narrowed fp32 accumulators a0, a1, with -inf
+// where `keep` (0xFFFF per live half) is clear -- empty parents
+// (pipeline.py:81,107).
+template <int DT>
+__device__ __forceinline__ uint32_t logit2(uint32_t a0, uint32_t a1, float sqrtD, float inv, uint32_t keep) {
+  const uint32_t x2 = pack2<DT>(__uint_as_float(a0), __uint_as_float(a1));
+  const float x0 = half_lo<DT>(x2), x1 = half_hi<DT>(x2);
+  float y0 = x0 * inv, y1 = x1 * inv;  // within 2 ulp of the correctly rounded quotient
+  if (near_midpoint<DT>(y0)) y0 = __fdiv_rn(x0, sqrtD);
+  if (near_midpoint<DT>(y1)) y1 = __fdiv_rn(x1, sqrtD);
+  const uint32_t s2 = pack2<DT>(y0, y1);
+  const uint32_t ninf = DT == DT_BF16 ? 0xFF80FF80u : 0xFC00FC00u;
+  return (s2 & keep) | (ninf & ~keep);
+}
+
+// DT(exp(d)) for both halves of d2 (every d <= 0 or NaN); NaN -> 0
+// (pipeline.py:143-145).
+template <int DT>
+__device__ __forceinline__ uint32_t exp2_dt(uint32_t d2, const uint16_t* tab) {
+  if constexpr (DT == DT_BF16) {
+    uint32_t c;
+    asm("max.u16x2 %0, %1, %2;" : "=r"(c) : "r"(d2 & 0x7FFF7FFFu), "r"(EXP_BASE * 0x10001u));
+    asm("min.u16x2 %0, %1, %2;" : "=r"(c) : "r"(c), "r"((EXP_BASE + EXP_N - 1) * 0x10001u));
+    const uint32_t lo = tab[(c & 0xFFFFu) - EXP_BASE], hi = tab[(c >> 16) - EXP_BASE];
+    return lo | (hi << 16);
+  } else {
+    const float e0 = fmaxf(exp_dt_fast<DT>(half_lo<DT>(d2)), 0.f);
+    const float e1 = fmaxf(exp_dt_fast<DT>(half_hi<DT>(d2)), 0.f);
+    return pack2<DT>(e0, e1);
+  }
+}
+
+__global__ void exp_table_kernel(uint16_t* __restrict__ tab) {
+  for (int i = threadIdx.x; i < 2 * EXP_WORDS; i += blockDim.x) {
+    uint16_t v = 0;
+    if (i < EXP_N - 1) {
+      const float x = __uint_as_float((EXP_BASE + (uint32_t)i) << 16);
+      v = __bfloat16_as_ushort(__float2bfloat16_rn(__double2float_rn(exp(-(double)x))));
+    }
+    tab[i] = v;
+  }
+}
+
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Bounded wait that ignores the abort flag (draining copies in flight).
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!tc::mbar_try(bar, parity) && clock64() - t0 < tc::kWaitCycles / 8) {
+  }
+}
+
+template <int DT, int D>
+__global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_p,
+    const __grid_constant__ CUtensorMap tm_v, int4 qpos, int H, int Tq, int M0, float sqrtD,
+    const int* __restrict__ pcnt, const uint16_t* __restrict__ exptab_g, typename Storage<DT>::T* __restrict__ scratch,
+    float* __restrict__ m_out, float* __restrict__ l_out, float* __restrict__ z_out,
+    typename Storage<DT>::T* __restrict__ a_out, float* __restrict__ colpart) {
+  using T = typename Storage<DT>::T;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = tc::smem_addr(smem_raw);
+  unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  const TcLayout L = tc_layout(D, M0);
+  const int g = blockIdx.y, b = g / H, h = g % H, qt = blockIdx.x, t0 = qt * TR;
+  const int nch = (M0 + TCH - 1) / TCH, nv = 2 * nch;
+  const int ntiles = (Tq + 63) / 64, LDL = M0 + 8;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.bars);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + L.misc);
+  volatile int* abort = reinterpret_cast<volatile int*>(sm + L.misc + 4);
+  const uint16_t* exptab = reinterpret_cast<const uint16_t*>(sm + L.exptab);
+  uint32_t* pm2 = reinterpret_cast<uint32_t*>(sm + L.pm2);
+  uint32_t* n2 = reinterpret_cast<uint32_t*>(sm + L.n2);
+  float* srow = reinterpret_cast<float*>(sm + L.srow);
+  float* scomb = reinterpret_cast<float*>(sm + L.scomb);
+
+  // ---- setup: barriers, TMEM, tables ----
+  if (tid == 0) {
+    for (int i = 0; i < N_BARS; ++i) tc::mbar_init(&bars[i], (i == B_EFULL || i == B_EFULL + 1 || i == B_COMB) ? TR : 1);
+    *abort = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 4) tc::tmem_alloc(tslot, TC_TMEM_COLS);
+  if (tid < TR) {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(exptab_g);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(sm + L.exptab);
+    for (int i = tid; i < EXP_WORDS; i += TR) dst[i] = src[i];
+    for (int j = tid; j < nch * 32; j += TR) {
+      const int p = 2 * j;
+      const int c0 = p < M0 ? pcnt[(long)g * M0 + p] : 0, c1 = p + 1 < M0 ? pcnt[(long)g * M0 + p + 1] : 0;
+      pm2[j] = (c0 > 0 ? 0xFFFFu : 0u) | (c1 > 0 ? 0xFFFF0000u : 0u);
+      n2[j] = pack2<DT>(count_dt<DT>(c0), count_dt<DT>(c1));
+    }
+  }
+  tc::tc_before_sync();
+  __syncthreads();
+  tc::tc_after_sync();
+  const uint32_t tbase = *tslot;
+
+  if (warp == 5) {
+    // ---- TMA producer ----
+    if (lane == 0) {
+      tc::tma_prefetch_desc(&tm_q);
+      tc::tma_prefetch_desc(&tm_p);
+      tc::tma_prefetch_desc(&tm_v);
+      int nq = 0, np[2] = {0, 0}, nvv[2] = {0, 0};
+      tc::mbar_expect_tx(&bars[B_Q], TR * D * 2);
+      for (int kb = 0; kb < D / 64; ++kb) {
+        int c[4];
+        c[0] = kb * 64;
+        c[qpos.x] = t0;
+        c[qpos.y] = h;
+        c[qpos.z] = b;
+        tc::tma_load_4d(sm + L.q + kb * TR * 128, &tm_q, c[0], c[1], c[2], c[3], &bars[B_Q]);
+      }
+      nq = 1;
+      for (int v = 0; v < nv; ++v) {
+        const int c = v % nch, s = v & 1;
+        if (v >= 2 && !tc::mbar_wait(&bars[B_PEMPTY + s], ((v - 2) >> 1) & 1, abort)) break;
+        tc::mbar_expect_tx(&bars[B_PFULL + s], TCH * D * 2);
+        for (int kb = 0; kb < D / 64; ++kb)
+          tc::tma_load_3d(sm + L.p[s] + kb * TCH * 128, &tm_p, kb * 64, c * TCH, h, &bars[B_PFULL + s]);
+        ++np[s];
+        if (v >= nch) {
+          const int u = v - nch, vs = u & 1;
+          if (u >= 2 && !tc::mbar_wait(&bars[B_VEMPTY + vs], ((u - 2) >> 1) & 1, abort)) break;
+          tc::mbar_expect_tx(&bars[B_VFULL + vs], TCH * D * 2);
+          for (int nb = 0; nb < D / 64; ++nb)
+            tc::tma_load_3d(sm + L.v[vs] + nb * TCH * 128, &tm_v, nb * 64, c * TCH, g, &bars[B_VFULL + vs]);
+          ++nvv[vs];
+        }
+      }
+      if (*abort) {  // let the copies in flight land before the CTA exits
+        if (nq) drain_wait(&bars[B_Q], 0);
+        for (int s = 0; s < 2; ++s) {
+          if (np[s]) drain_wait(&bars[B_PFULL + s], (np[s] - 1) & 1);
+          if (nvv[s]) drain_wait(&bars[B_VFULL + s], (nvv[s] - 1) & 1);
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      const int fmt = DT == DT_BF16 ? 1 : 0;
+      const uint32_t idS = tc::idesc_f16(fmt, TR, TCH, false);
+      const uint32_t idO = tc::idesc_f16(fmt, TR, D, true);
+      const uint32_t qa = tc::smem_addr(sm + L.q);
+      const uint32_t pa[2] = {tc::smem_addr(sm + L.p[0]), tc::smem_addr(sm + L.p[1])};
+      const uint32_t va[2] = {tc::smem_addr(sm + L.v[0]), tc::smem_addr(sm + L.v[1])};
+      auto issue_S = [&](int v) {
+        const int s = v & 1;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t ad = tc::sdesc_sw128(qa + (kk >> 2) * TR * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::sdesc_sw128(pa[s] + (kk >> 2) * TCH * 128 + (kk & 3) * 32, 16, 1024);
+          tc::mma_ss(tbase + D + 64 * s, ad, bd, idS, kk > 0);
+        }
+        tc::mma_commit(&bars[B_SFULL + s]);
+        tc::mma_commit(&bars[B_PEMPTY + s]);
+      };
+      bool ok = tc::mbar_wait(&bars[B_Q], 0, abort);
+      for (int v = 0; ok && v < 2 && v < nv; ++v) {
+        ok = tc::mbar_wait(&bars[B_PFULL + v], 0, abort);
+        if (ok) {
+          tc::tc_after_sync();
+          issue_S(v);
+        }
+      }
+      int nfree = 0;
+      for (int v = 0; ok && v < nv; ++v) {
+        const int s = v & 1;
+        if (!(ok = tc::mbar_wait(&bars[B_EFULL + s], (v >> 1) & 1, abort))) break;
+        tc::tc_after_sync();
+        if (v >= nch) {
+          const int u = v - nch, vs = u & 1;
+          if (!(ok = tc::mbar_wait(&bars[B_VFULL + vs], (u >> 1) & 1, abort))) break;
+          tc::tc_after_sync();
+#pragma unroll
+          for (int kk = 0; kk < TCH / 16; ++kk) {
+            const uint64_t bd = tc::sdesc_sw128(va[vs] + kk * 16 * 128, TCH * 128, 1024);
+            tc::mma_ts(tbase, tbase + D + 64 * s + kk * 8, bd, idO, u > 0 || kk > 0);
+          }
+          tc::mma_commit(&bars[B_VEMPTY + vs]);
+        }
+        if (v + 2 < nv) {
+          if (v >= nch) {  // the e @ V MMA still reads this buffer
+            tc::mma_commit(&bars[B_SFREE]);
+            if (!(ok = tc::mbar_wait(&bars[B_SFREE], nfree & 1, abort))) break;
+            ++nfree;
+          }
+          if (!(ok = tc::mbar_wait(&bars[B_PFULL + s], ((v + 2) >> 1) & 1, abort))) break;
+          tc::tc_after_sync();
+          issue_S(v + 2);
+        }
+      }
+      tc::mma_commit(&bars[B_OFULL]);  // arrives once every MMA above has completed
+      if (!ok) drain_wait(&bars[B_OFULL], 0);
+    }
+  } else {
+    // ---- row threads ----
+    const int r = tid, t = t0 + r;
+    const bool live = t < Tq;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const float inv_sqrtD = 1.f / sqrtD;
+    const uint32_t ninf2 = DT == DT_BF16 ? 0xFF80FF80u : 0xFC00FC00u;
+    const long row = (long)g * Tq + t;
+    T* srow_g = scratch + (((long)g * ntiles + (t >> 6)) * 64 + (t & 63)) * LDL;
+    bool ok = true;
+    // pass 1: the row max of the logits (pipeline.py:107,137).  Narrowing and
+    // scaling are monotone, so it is the logit of the largest raw accumulator
+    // over the non-empty parents (NaN-propagating, as torch.max).
+    float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    for (int v = 0; v < nch; ++v) {
+      const int s = v & 1;
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_SFULL + s], (v >> 1) & 1, abort));
+      if (!ok) break;
+      tc::tc_after_sync();
+      uint32_t ra[32], rb[32];
+      const uint32_t col = tbase + lane_off + D + 64 * s;
+      tc::tmem_ld32(col, ra);
+      tc::tmem_ld32(col + 32, rb);
+      tc::tmem_wait_ld();
+      tc::tc_before_sync();
+      tc::mbar_arrive(&bars[B_EFULL + s]);
+      const uint4* pm4 = reinterpret_cast<const uint4*>(pm2 + v * 32);
+      uint32_t all = 0xFFFFFFFFu;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const uint4 u = pm4[q];
+        all &= u.x & u.y & u.z & u.w;
+      }
+      if (all == 0xFFFFFFFFu) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          mxa[i & 3] = fmax_nan(mxa[i & 3], __uint_as_float(ra[i]));
+          mxa[i & 3] = fmax_nan(mxa[i & 3], __uint_as_float(rb[i]));
+        }
+      } else {
+        const uint32_t* pm = pm2 + v * 32;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const uint32_t bits = i < 32 ? ra[i] : rb[i - 32];
+          const bool keep = (pm[i >> 1] >> ((i & 1) * 16)) & 1u;
+          mxa[i & 3] = fmax_nan(mxa[i & 3], keep ? __uint_as_float(bits) : -INFINITY);
+        }
+      }
+    }
+    const float amax = fmax_nan(fmax_nan(mxa[0], mxa[1]), fmax_nan(mxa[2], mxa[3]));
+    const float rm = rnd<DT>(__fdiv_rn(rnd<DT>(amax), sqrtD));
+    const float safe = rm == -INFINITY ? 0.f : rm;  // pipeline.py:137-141
+    const uint32_t m2 = dup2<DT>(safe);
+    // pass 2: exponentials, sums, e @ V
+    float la0 = 0.f, la1 = 0.f, za = 0.f;
+    for (int v = nch; ok && v < nv; ++v) {
+      const int c = v - nch, s = v & 1;
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_SFULL + s], (v >> 1) & 1, abort));
+      if (!ok) break;
+      tc::tc_after_sync();
+      const uint32_t col = tbase + lane_off + D + 64 * s;
+      float zh[2];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {  // 32 parents at a time
+        uint32_t ra[32];
+        tc::tmem_ld32(col + 32 * hh, ra);
+        tc::tmem_wait_ld();
+        // logits: DT(DT(acc) / sqrt(D)) (pipeline.py:81), branch-free fast
+        // quotients; a half with a quotient near a rounding point is redone
+        uint32_t s2[16];
+        bool near = false;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const uint32_t x2 = pack2<DT>(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1]));
+          const float y0 = half_lo<DT>(x2) * inv_sqrtD, y1 = half_hi<DT>(x2) * inv_sqrtD;
+          near |= near_midpoint<DT>(y0) | near_midpoint<DT>(y1);
+          s2[j] = pack2<DT>(y0, y1);
+        }
+        if (near) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) s2[j] = logit2<DT>(ra[2 * j], ra[2 * j + 1], sqrtD, inv_sqrtD, 0xFFFFFFFFu);
+        }
+        const uint4* pm4 = reinterpret_cast<const uint4*>(pm2 + c * 32 + hh * 16);
+        const uint4* nn4 = reinterpret_cast<const uint4*>(n2 + c * 32 + hh * 16);
+        uint32_t e2[16];
+        float zs[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 pmq = pm4[q], nnq = nn4[q];
+          const uint32_t pmv[4] = {pmq.x, pmq.y, pmq.z, pmq.w}, nnv[4] = {nnq.x, nnq.y, nnq.z, nnq.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int j = 4 * q + k;
+            const uint32_t sm2 = (s2[j] & pmv[k]) | (ninf2 & ~pmv[k]);  // -inf for empty parents (pipeline.py:107)
+            const uint32_t ee = exp2_dt<DT>(hsub2_dt<DT>(sm2, m2), exptab);
+            e2[j] = ee;
+            const uint32_t w2 = hmul2_dt<DT>(ee, nnv[k]);  // DT(e * n), pipeline.py:146
+            la0 += half_lo<DT>(w2);
+            la1 += half_hi<DT>(w2);
+            zs[j] = half_lo<DT>(ee) + half_hi<DT>(ee);
+          }
+        }
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+          for (int j = 0; j < w; ++j) zs[j] += zs[j + w];
+        zh[hh] = zs[0];
+        tc::tmem_st16(col + 16 * hh, e2);
+        if (live) {
+          uint4* dst = reinterpret_cast<uint4*>(srow_g + c * TCH + 32 * hh);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (c * TCH + 32 * hh + 8 * k < M0) dst[k] = make_uint4(e2[4 * k], e2[4 * k + 1], e2[4 * k + 2], e2[4 * k + 3]);
+        }
+      }
+      za += zh[0] + zh[1];
+      tc::tmem_wait_st();
+      tc::tc_before_sync();
+      tc::mbar_arrive(&bars[B_EFULL + s]);
+    }
+    // z feeds the probabilities.  Each chunk is summed as a pairwise tree
+    // (depth 6) and the chunk sums in sequence, so the fp32 sum is within
+    // (6 + nch) * 2^-24 relative of the exact one; when the window straddles a
+    // dtype rounding point the row is summed again exactly.
+    float z = rnd<DT>(za);
+    if (ok && live) {
+      const float eps = za * (float)(nch + 8) * 5.9604645e-8f;
+      if (rnd<DT>(za - eps) != rnd<DT>(za + eps)) {
+        double ex = 0.0;
+        const uint4* src = reinterpret_cast<const uint4*>(srow_g);
+        for (int k = 0; k < M0 / 8; ++k) {
+          const uint4 u = src[k];
+          ex += (double)half_lo<DT>(u.x) + (double)half_hi<DT>(u.x) + (double)half_lo<DT>(u.y) +
+                (double)half_hi<DT>(u.y) + (double)half_lo<DT>(u.z) + (double)half_hi<DT>(u.z) +
+                (double)half_lo<DT>(u.w) + (double)half_hi<DT>(u.w);
+        }
+        z = rnd64<DT>(ex);
+      }
+    }
+    if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_OFULL], 0, abort));
+    if (ok) {
+      tc::tc_after_sync();
+#pragma unroll
+      for (int d0 = 0; d0 < D; d0 += 64) {
+        uint32_t oa[32], ob[32];
+        tc::tmem_ld32(tbase + lane_off + d0, oa);
+        tc::tmem_ld32(tbase + lane_off + d0 + 32, ob);
+        tc::tmem_wait_ld();
+        if (live) {
+          uint4* dst = reinterpret_cast<uint4*>(a_out + row * D + d0);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t* src = k < 4 ? oa + 8 * k : ob + 8 * (k - 4);
+            dst[k] = make_uint4(pack2<DT>(__uint_as_float(src[0]), __uint_as_float(src[1])),
+                                pack2<DT>(__uint_as_float(src[2]), __uint_as_float(src[3])),
+                                pack2<DT>(__uint_as_float(src[4]), __uint_as_float(src[5])),
+                                pack2<DT>(__uint_as_float(src[6]), __uint_as_float(src[7])));
+          }
+        }
+      }
+      if (live) {
+        m_out[row] = safe;
+        l_out[row] = rnd<DT>(la0 + la1);
+        z_out[row] = z;
+      }
+    }
+    const float zc = clamp_min_nan(z, eps_dt<DT>());
+    srow[r * 4] = zc;
+    srow[r * 4 + 1] = 1.f / zc;
+    srow[r * 4 + 2] = live ? 1.f : 0.f;
+    __syncwarp();
+    // pass 3: importance partials (routing.py:61-63).  Lane = 4 columns; the
+    // warp's 32 rows are summed in order, 8 rows per batch of loads; warps 0+1
+    // and 2+3 are combined into the partials of the two 64-query tiles.
+    for (int p0 = 0, nb = 0; ok && p0 < M0; p0 += 128, ++nb) {
+      const int p = p0 + 4 * lane;
+      float cs[4] = {0.f, 0.f, 0.f, 0.f};
+      if (p < M0) {
+#pragma unroll 1
+        for (int g4 = 0; g4 < 8; ++g4) {
+          const int rw0 = warp * 32 + g4 * 4;
+          if (t0 + rw0 + 3 < Tq) {
+            uint2 w[4];
+            float2 zr[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int tw = t0 + rw0 + i;
+              w[i] = *reinterpret_cast<const uint2*>(scratch + (((long)g * ntiles + (tw >> 6)) * 64 + (tw & 63)) * LDL + p);
+              zr[i] = *reinterpret_cast<const float2*>(srow + (rw0 + i) * 4);
+            }
+            float y[4][4];
+            bool near = false;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float e[4] = {half_lo<DT>(w[i].x), half_hi<DT>(w[i].x), half_lo<DT>(w[i].y), half_hi<DT>(w[i].y)};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                y[i][k] = e[k] * zr[i].y;  // within 2 ulp of e / z
+                near |= near_midpoint<DT>(y[i][k]);
+              }
+            }
+            if (near) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float e[4] = {half_lo<DT>(w[i].x), half_hi<DT>(w[i].x), half_lo<DT>(w[i].y),
+                                    half_hi<DT>(w[i].y)};
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                  if (near_midpoint<DT>(y[i][k])) y[i][k] = __fdiv_rn(e[k], zr[i].x);
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t q01 = pack2<DT>(y[i][0], y[i][1]), q23 = pack2<DT>(y[i][2], y[i][3]);  // DT(e / z)
+              cs[0] += half_lo<DT>(q01);
+              cs[1] += half_hi<DT>(q01);
+              cs[2] += half_lo<DT>(q23);
+              cs[3] += half_hi<DT>(q23);
+            }
+          } else {
+            for (int i = 0; i < 4; ++i) {
+              const int tw = t0 + rw0 + i;
+              if (tw >= Tq) break;  // query beyond T
+              const uint2 wv =
+                  *reinterpret_cast<const uint2*>(scratch + (((long)g * ntiles + (tw >> 6)) * 64 + (tw & 63)) * LDL + p);
+              const float zc_r = srow[(rw0 + i) * 4], rz = srow[(rw0 + i) * 4 + 1];
+              cs[0] += div_dt_fast<DT>(half_lo<DT>(wv.x), rz, zc_r);
+              cs[1] += div_dt_fast<DT>(half_hi<DT>(wv.x), rz, zc_r);
+              cs[2] += div_dt_fast<DT>(half_lo<DT>(wv.y), rz, zc_r);
+              cs[3] += div_dt_fast<DT>(half_hi<DT>(wv.y), rz, zc_r);
+            }
+          }
+        }
+      }
+      float* sc = scomb + (nb & 1) * 512;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) sc[warp * 128 + 4 * lane + k] = cs[k];
+      tc::mbar_arrive(&bars[B_COMB]);
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_COMB], nb & 1, abort));
+      if (!ok) break;
+      for (int o = tid; o < 256; o += TR) {
+        const int tp = o >> 7, cl = o & 127, tile = 2 * qt + tp;
+        if (tile < ntiles && p0 + cl < M0)
+          colpart[((long)g * ntiles + tile) * M0 + p0 + cl] = sc[2 * tp * 128 + cl] + sc[(2 * tp + 1) * 128 + cl];
+      }
+    }
+  }
+
+  // ---- teardown ----
+  tc::tc_before_sync();
+  __syncthreads();
+  if (warp == 4) {
+    tc::tc_after_sync();
+    tc::tmem_free(tbase, TC_TMEM_COLS);
+  }
+  if (tid == 0 && *abort) atomicOr(&g_device_fault, 1);
+}
+
+// ---- host side ----------------------------------------------------------------
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+bool encode(CUtensorMap* m, int dt, int rank, const void* base, const cuuint64_t* dims, const cuuint64_t* strides,
+            const cuuint32_t* box) {
+  EncodeTiled fn = encode_fn();
+  if (!fn) return false;
+  const cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  return fn(m, dt == DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank,
+            const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// AVQ_DISABLE_TCGEN05=1 selects the mma.sync parent-attention kernel (read at
+// every launch, so one process can run both).
+bool tc_disabled() {
+  const char* e = std::getenv("AVQ_DISABLE_TCGEN05");
+  return e && *e && *e != '0';
+}
+
+}  // namespace
+
+bool parent_attn_tc_ok(int dt, int D, int M0) {
+  return !tc_disabled() && dt != DT_F32 && (D == 64 || D == 128) && M0 % 8 == 0 && M0 <= TC_MAX_M0;
+}
+
+size_t parent_attn_tc_table_bytes() { return (size_t)EXP_WORDS * 4; }
+
+template <int DT>
+int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st) {
+  using T = typename Storage<DT>::T;
+  const int G = a.B * a.H, D = a.D, M0 = a.M0;
+  // Q as a 4-D tensor (d, and t/h/b ordered by stride), P [H, M0, D], V [G, M0, D]
+  struct Dim {
+    long stride;
+    long extent;
+    int which;  // 1 t, 2 h, 3 b
+  } dd[3] = {{a.qs.s, a.T, 1}, {a.qs.h, a.H, 2}, {a.qs.b, a.B, 3}};
+  std::sort(dd, dd + 3, [](const Dim& x, const Dim& y) { return x.stride < y.stride; });
+  cuuint64_t qdims[4] = {(cuuint64_t)D, 0, 0, 0}, qstr[3];
+  cuuint32_t qbox[4] = {64, 1, 1, 1};
+  int pos[4] = {0, 0, 0, 0};
+  for (int i = 0; i < 3; ++i) {
+    qdims[i + 1] = (cuuint64_t)dd[i].extent;
+    qstr[i] = (cuuint64_t)dd[i].stride * sizeof(T);
+    pos[dd[i].which] = i + 1;
+    if (dd[i].which == 1) qbox[i + 1] = TR;
+  }
+  const cuuint64_t pdims[3] = {(cuuint64_t)D, (cuuint64_t)M0, (cuuint64_t)a.H};
+  const cuuint64_t vdims[3] = {(cuuint64_t)D, (cuuint64_t)M0, (cuuint64_t)G};
+  const cuuint64_t pstr[2] = {(cuuint64_t)D * sizeof(T), (cuuint64_t)M0 * D * sizeof(T)};
+  const cuuint32_t pbox[3] = {64, TCH, 1};
+  CUtensorMap tq, tp, tv;
+  if (!encode(&tq, DT, 4, a.q, qdims, qstr, qbox) || !encode(&tp, DT, 3, a.parents, pdims, pstr, pbox) ||
+      !encode(&tv, DT, 3, a.pagg, vdims, pstr, pbox))
+    return AVQ_ERR_UNSUPPORTED;
+  const TcLayout L = tc_layout(D, M0);
+  // at least 80 KB so that no more than two CTAs (2 x 256 TMEM columns) share an SM
+  const size_t smem = std::max<size_t>((size_t)L.total + 1024, 80 * 1024);
+  if (DT == DT_BF16) exp_table_kernel<<<1, 256, 0, st>>>(static_cast<uint16_t*>(exptab));
+  const int4 qpos = make_int4(pos[1], pos[2], pos[3], 0);
+  auto go = [&](auto kfn) {
+    AVQ_TIMED("parent_attn_tc", st);
+    cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kfn<<<dim3((a.T + TR - 1) / TR, G), TTHREADS, smem, st>>>(
+        tq, tp, tv, qpos, a.H, a.T, M0, a.sqrtD, a.pcnt, static_cast<const uint16_t*>(exptab),
+        static_cast<T*>(a.sglobal), a.m, a.l, a.z, static_cast<T*>(a.a), a.colpart);
+  };
+  if (D == 64) go(parent_attn_tc_kernel<DT, 64>);
+  else go(parent_attn_tc_kernel<DT, 128>);
+  return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
+}
+
+template int launch_parent_attn_tc<DT_BF16>(const PAArgs&, void*, cudaStream_t);
+template int launch_parent_attn_tc<DT_F16>(const PAArgs&, void*, cudaStream_t);
+
+int read_device_fault(int* code, cudaStream_t st) {
+  int v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, g_device_fault, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return AVQ_ERR_CUDA;
+  const int zero = 0;
+  if (cudaMemcpyToSymbolAsync(g_device_fault, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return AVQ_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return AVQ_ERR_CUDA;
+  *code = v;
+  return AVQ_OK;
+}
+
+}  // namespace avq

@@ -138,7 +138,8 @@ def algorithmic_work(w, B: int) -> dict:
     G, T, S, D, M0, C, P = B * w.H, w.T, w.S, w.D, w.M0, w.C, w.P
     es = 2 if w.dtype in ("bf16", "f16") else 4
     return {
-        "parent_attn": ("tensor", 4.0 * G * T * M0 * D),          # q.P^T and e @ V
+        "parent_attn": ("tensor", 4.0 * G * T * M0 * D),          # q.P^T and e @ V (mma.sync kernel)
+        "parent_attn_tc": ("tensor", 4.0 * G * T * M0 * D),       # the same on tcgen05
         "assign": ("tensor", 2.0 * G * S * M0 * D + 2.0 * G * S * C * D),
         "correct": ("tensor", 2.0 * G * T * P * D * (2 + 2 * C)),  # parent+child logits, value sums
         "aggregate": ("hbm", G * S * D * es + G * S * 8 + G * M0 * (1 + C) * D * es + G * M0 * (1 + C) * 4),

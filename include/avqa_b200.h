@@ -25,6 +25,7 @@
  *                         cache.py:246-260, plus the re-quantization of the grown key
  *                         set (quantizer.py:166-278) done incrementally
  *   avq_reduce_min        the budget's min over (b,h) of valid parents, pipeline.py:341-342
+ *   avq_device_fault      no counterpart: device-side fault record of the bounded waits
  *   avq_quantize_noalloc  no counterpart: avq_quantize with its scratch in a fixed
  *                         device array, for hosts that cannot allocate
  */
@@ -145,6 +146,13 @@ int avq_append(int dtype, const void* k, const long long* k_strides, const void*
 
 /* *out = min(v[0..n)). */
 int avq_reduce_min(const int* v, int n, int* out, void* stream);
+
+/* Read and clear the device-side fault record, after synchronizing `stream`.
+ * *code receives 0, or a nonzero bit set by a kernel that abandoned a
+ * bounded wait (about one second) on one of its own barriers; the kernel
+ * then released its resources and returned with undefined outputs.  No
+ * counterpart in the reference (its CPU kernels have no asynchronous waits). */
+int avq_device_fault(int* code, void* stream);
 
 /* Per-kernel device timing (no counterpart in the reference; measurement
  * support).  avq_profile_begin() starts recording a CUDA event pair around
