@@ -1,0 +1,376 @@
+// Key -> parent -> child assignment on the sm_100a tensor cores for bf16 /
+// fp16 and D in {64, 128} (reference quantizer.py:166-226).
+//
+// CTA = 128 keys of one (b,h); thread r of warps 0-3 owns key r (TMEM lane r);
+// warp 4 issues tcgen05.mma, warp 5 streams the key tile and 128-parent
+// chunks of the head's codebook with TMA.  TMEM holds two 128-column buffers
+// of fp32 cross terms K P_c^T.
+//
+// Parent distance (quantizer.py:207-210), each op rounded to the dtype:
+//   d = DT(DT(k_sq + p_sq) - DT(2 * DT(k . p)))
+// computed with packed dtype x2 arithmetic: for dtype operands the exact sum
+// or difference either fits fp32 or is dominated by one operand, so a single
+// dtype rounding equals the reference's fp32-then-dtype rounding.
+// torch.argmin (first minimum, NaN wins) becomes a signed min over 32-bit
+// keys: the order-preserving integer form of the 16-bit distance in the high
+// half and the parent index in the low half.  A row with a NaN
+// distance (only possible with non-finite inputs) takes a scalar path.
+// Child stage (quantizer.py:218-226): the cross term is a sum of
+// dtype-rounded elementwise products, accumulated in fp64 and rounded once.
+#include <cuda.h>
+
+#include <algorithm>
+
+#include "avq_kernels.cuh"
+#include "avq_mma.cuh"
+#include "avq_tc.cuh"
+
+namespace avq {
+
+extern __device__ int g_device_fault;
+
+namespace {
+
+constexpr int AR = 128;        // keys per CTA
+constexpr int ACH = 128;       // parents per chunk
+constexpr int ATHREADS = 192;  // 4 row warps + MMA warp + TMA warp
+constexpr int A_TMEM_COLS = 256;
+constexpr int A_MAX_M0 = 4096;
+
+constexpr int AB_K = 0, AB_PFULL = 1, AB_PEMPTY = 3, AB_SFULL = 5, AB_SCONS = 7, AB_END = 9, AN_BARS = 10;
+
+struct AssignLayout {
+  int k, p[2], ps2, bars, misc, total;
+};
+
+__host__ __device__ inline AssignLayout assign_layout(int D, int M0) {
+  AssignLayout L;
+  const int nch = (M0 + ACH - 1) / ACH;
+  int o = 0;
+  L.k = o;
+  o += AR * D * 2;
+  for (int i = 0; i < 2; ++i) {
+    L.p[i] = o;
+    o += ACH * D * 2;
+  }
+  L.ps2 = o;
+  o += nch * (ACH / 2) * 4;
+  L.bars = o;
+  o += AN_BARS * 8;
+  L.misc = o;
+  o += 16;
+  L.total = o;
+  return L;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t hadd2_dt(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if (DT == DT_BF16) asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Both halves of a dtype x2 word mapped to order-preserving signed 16-bit
+// integers (negative values: magnitude bits flipped).
+__device__ __forceinline__ uint32_t order2(uint32_t d2) {
+  const uint32_t neg = prmt(d2, 0u, 0xBB99u);  // 0xFFFF in each half whose sign bit is set
+  return d2 ^ (neg & 0x7FFF7FFFu);
+}
+
+__device__ __forceinline__ int key_lo(uint32_t k2, uint32_t idx2) { return (int)prmt(k2, idx2, 0x1054u); }
+__device__ __forceinline__ int key_hi(uint32_t k2, uint32_t idx2) { return (int)prmt(k2, idx2, 0x3276u); }
+
+// torch.argmin order for the child stage: the first minimum; a NaN wins.
+__device__ __forceinline__ bool better_c(float v, int i, float bv, int bi) {
+  if (bi < 0) return true;
+  const bool n = isnan(v), bn = isnan(bv);
+  if (n || bn) return n && (!bn || i < bi);
+  return v < bv || (v == bv && i < bi);
+}
+
+__device__ __forceinline__ void drain(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!tc::mbar_try(bar, parity) && clock64() - t0 < tc::kWaitCycles / 8) {
+  }
+}
+
+template <int DT, int D>
+__global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_p, int4 kpos, int H, int S,
+    int M0, int C, const typename Storage<DT>::T* __restrict__ parents, const float* __restrict__ p_sq,
+    const typename Storage<DT>::T* __restrict__ children, const float* __restrict__ c_sq, int* __restrict__ passign,
+    int* __restrict__ cassign) {
+  using T = typename Storage<DT>::T;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = tc::smem_addr(smem_raw);
+  unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  const AssignLayout L = assign_layout(D, M0);
+  const int g = blockIdx.y, b = g / H, h = g % H, s0 = blockIdx.x * AR;
+  const int nch = (M0 + ACH - 1) / ACH;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.bars);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + L.misc);
+  volatile int* abort = reinterpret_cast<volatile int*>(sm + L.misc + 4);
+  uint32_t* ps2 = reinterpret_cast<uint32_t*>(sm + L.ps2);
+
+  if (tid == 0) {
+    for (int i = 0; i < AN_BARS; ++i) tc::mbar_init(&bars[i], (i == AB_SCONS || i == AB_SCONS + 1) ? AR : 1);
+    *abort = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 4) tc::tmem_alloc(tslot, A_TMEM_COLS);
+  if (tid < AR) {
+    // squared parent norms as dtype pairs; +inf beyond M0 (never the minimum)
+    for (int j = tid; j < nch * (ACH / 2); j += AR) {
+      const int p = 2 * j;
+      const float a0 = p < M0 ? p_sq[(long)h * M0 + p] : INFINITY;
+      const float a1 = p + 1 < M0 ? p_sq[(long)h * M0 + p + 1] : INFINITY;
+      ps2[j] = pack2<DT>(a0, a1);
+    }
+  }
+  tc::tc_before_sync();
+  __syncthreads();
+  tc::tc_after_sync();
+  const uint32_t tbase = *tslot;
+
+  if (warp == 5) {
+    if (lane == 0) {  // ---- TMA producer ----
+      tc::tma_prefetch_desc(&tm_k);
+      tc::tma_prefetch_desc(&tm_p);
+      int np[2] = {0, 0};
+      tc::mbar_expect_tx(&bars[AB_K], AR * D * 2);
+      for (int kb = 0; kb < D / 64; ++kb) {
+        int c[4];
+        c[0] = kb * 64;
+        c[kpos.x] = s0;
+        c[kpos.y] = h;
+        c[kpos.z] = b;
+        tc::tma_load_4d(sm + L.k + kb * AR * 128, &tm_k, c[0], c[1], c[2], c[3], &bars[AB_K]);
+      }
+      for (int ci = 0; ci < nch; ++ci) {
+        const int s = ci & 1;
+        if (ci >= 2 && !tc::mbar_wait(&bars[AB_PEMPTY + s], ((ci - 2) >> 1) & 1, abort)) break;
+        tc::mbar_expect_tx(&bars[AB_PFULL + s], ACH * D * 2);
+        for (int kb = 0; kb < D / 64; ++kb)
+          tc::tma_load_3d(sm + L.p[s] + kb * ACH * 128, &tm_p, kb * 64, ci * ACH, h, &bars[AB_PFULL + s]);
+        ++np[s];
+      }
+      if (*abort) {
+        drain(&bars[AB_K], 0);
+        for (int s = 0; s < 2; ++s)
+          if (np[s]) drain(&bars[AB_PFULL + s], (np[s] - 1) & 1);
+      }
+    }
+  } else if (warp == 4) {
+    if (lane == 0) {  // ---- MMA issuer ----
+      const uint32_t idS = tc::idesc_f16(DT == DT_BF16 ? 1 : 0, AR, ACH, false);
+      const uint32_t ka = tc::smem_addr(sm + L.k);
+      const uint32_t pa[2] = {tc::smem_addr(sm + L.p[0]), tc::smem_addr(sm + L.p[1])};
+      auto issue = [&](int ci) {
+        const int s = ci & 1;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t ad = tc::sdesc_sw128(ka + (kk >> 2) * AR * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::sdesc_sw128(pa[s] + (kk >> 2) * ACH * 128 + (kk & 3) * 32, 16, 1024);
+          tc::mma_ss(tbase + ACH * s, ad, bd, idS, kk > 0);
+        }
+        tc::mma_commit(&bars[AB_SFULL + s]);
+        tc::mma_commit(&bars[AB_PEMPTY + s]);
+      };
+      bool ok = tc::mbar_wait(&bars[AB_K], 0, abort);
+      for (int ci = 0; ok && ci < 2 && ci < nch; ++ci) {
+        ok = tc::mbar_wait(&bars[AB_PFULL + ci], 0, abort);
+        if (ok) {
+          tc::tc_after_sync();
+          issue(ci);
+        }
+      }
+      for (int ci = 0; ok && ci + 2 < nch; ++ci) {
+        const int s = ci & 1;
+        if (!(ok = tc::mbar_wait(&bars[AB_SCONS + s], (ci >> 1) & 1, abort))) break;
+        if (!(ok = tc::mbar_wait(&bars[AB_PFULL + s], ((ci + 2) >> 1) & 1, abort))) break;
+        tc::tc_after_sync();
+        issue(ci + 2);
+      }
+      tc::mma_commit(&bars[AB_END]);
+      if (!ok) drain(&bars[AB_END], 0);
+    }
+  } else {
+    // ---- row threads: key r ----
+    const int r = tid, s = s0 + r;
+    const bool live = s < S;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    bool ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[AB_K], 0, abort));
+    // the key row in the swizzled tile: 16-byte chunk j of slab kb at (j ^ (r & 7))
+    auto key_chunk = [&](int v) -> uint4 {
+      const int kb = v >> 3, j = v & 7;
+      return *reinterpret_cast<const uint4*>(sm + L.k + kb * AR * 128 + r * 128 + ((j ^ (r & 7)) << 4));
+    };
+    float ksq = 0.f;
+    if (ok) {  // k_sq = DT(sum DT(k_d^2)) (quantizer.py:208)
+      double acc = 0.0;
+#pragma unroll 4
+      for (int v = 0; v < D / 8; ++v) {
+        const uint4 u = key_chunk(v);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t sq = hmul2_dt<DT>(w[e], w[e]);
+          acc += (double)half_lo<DT>(sq) + (double)half_hi<DT>(sq);
+        }
+      }
+      ksq = rnd64<DT>(acc);
+    }
+    const uint32_t ksq2 = dup2<DT>(ksq);
+    int best = 0x7FFFFFFF;
+    uint32_t nanacc = 0u;
+    for (int ci = 0; ok && ci < nch; ++ci) {
+      const int sb = ci & 1;
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[AB_SFULL + sb], (ci >> 1) & 1, abort));
+      if (!ok) break;
+      tc::tc_after_sync();
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t ra[32], rb[32];
+        const uint32_t col = tbase + lane_off + ACH * sb + 64 * hh;
+        tc::tmem_ld32(col, ra);
+        tc::tmem_ld32(col + 32, rb);
+        tc::tmem_wait_ld();
+        if (hh == 1) {
+          tc::tc_before_sync();
+          tc::mbar_arrive(&bars[AB_SCONS + sb]);
+        }
+        const uint4* pp = reinterpret_cast<const uint4*>(ps2 + ci * (ACH / 2) + 32 * hh);
+        const uint32_t base2 = (uint32_t)(ci * ACH + 64 * hh) * 0x10001u + 0x10000u;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint4 pq = pp[q];
+          const uint32_t pv[4] = {pq.x, pq.y, pq.z, pq.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int j = 4 * q + k;
+            const uint32_t a0 = j < 16 ? ra[2 * j] : rb[2 * j - 32], a1 = j < 16 ? ra[2 * j + 1] : rb[2 * j - 31];
+            const uint32_t x2 = pack2<DT>(__uint_as_float(a0), __uint_as_float(a1));       // DT(k . p)
+            const uint32_t d2 = hsub2_dt<DT>(hadd2_dt<DT>(ksq2, pv[k]), hadd2_dt<DT>(x2, x2));
+            nanacc = hmax2_nan_dt<DT>(nanacc, d2);
+            const uint32_t k2 = order2(d2), idx2 = base2 + 0x20002u * (uint32_t)j;
+            best = min(best, min(key_lo(k2, idx2), key_hi(k2, idx2)));
+          }
+        }
+      }
+    }
+    int pbest = best & 0xFFFF;
+    const bool has_nan = isnan(half_lo<DT>(nanacc)) || isnan(half_hi<DT>(nanacc));
+    if (ok && live && has_nan) {
+      // a NaN distance wins (torch.argmin): the first parent whose distance is
+      // NaN; NaN-ness does not depend on the summation order of k . p
+      const T* pb = parents + (long)h * M0 * D;
+      for (int p = 0; p < M0; ++p) {
+        float cr = 0.f;
+        for (int v = 0; v < D / 8; ++v) {
+          const uint4 u = key_chunk(v);
+          const uint4 w = *reinterpret_cast<const uint4*>(pb + (long)p * D + 8 * v);
+          const uint32_t ku[4] = {u.x, u.y, u.z, u.w}, pw[4] = {w.x, w.y, w.z, w.w};
+          for (int e = 0; e < 4; ++e)
+            cr += half_lo<DT>(ku[e]) * half_lo<DT>(pw[e]) + half_hi<DT>(ku[e]) * half_hi<DT>(pw[e]);
+        }
+        const float dd = rnd<DT>(__fsub_rn(rnd<DT>(__fadd_rn(ksq, p_sq[(long)h * M0 + p])),
+                                           rnd<DT>(__fmul_rn(2.f, rnd<DT>(cr)))));
+        if (isnan(dd)) {
+          pbest = p;
+          break;
+        }
+      }
+    }
+    // child stage: the assigned parent's children (quantizer.py:218-226)
+    if (ok && live) {
+      const long crow0 = ((long)h * M0 + pbest) * C;
+      float bv = 0.f;
+      int bi = -1;
+      for (int c0 = 0; c0 < C; c0 += 4) {
+        double acc[4] = {0.0, 0.0, 0.0, 0.0};
+        const int nc = min(4, C - c0);
+#pragma unroll 2
+        for (int v = 0; v < D / 8; ++v) {
+          const uint4 u = key_chunk(v);
+          const uint32_t ku[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            if (cc < nc) {
+              const uint4 w = __ldg(reinterpret_cast<const uint4*>(children + (crow0 + c0 + cc) * D) + v);
+              const uint32_t cw[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const uint32_t pr = hmul2_dt<DT>(ku[e], cw[e]);  // DT(k_d * c_d), exact product rounded once
+                acc[cc] += (double)half_lo<DT>(pr) + (double)half_hi<DT>(pr);
+              }
+            }
+          }
+        }
+        for (int cc = 0; cc < nc; ++cc) {
+          const int c = c0 + cc;
+          const float cross = rnd64<DT>(acc[cc]);
+          const float dd = rnd<DT>(__fsub_rn(rnd<DT>(__fadd_rn(ksq, c_sq[crow0 + c])), rnd<DT>(__fmul_rn(2.f, cross))));
+          if (better_c(dd, c, bv, bi)) {
+            bv = dd;
+            bi = c;
+          }
+        }
+      }
+      passign[(long)g * S + s] = pbest;
+      cassign[(long)g * S + s] = bi;
+    }
+  }
+
+  tc::tc_before_sync();
+  __syncthreads();
+  if (warp == 4) {
+    tc::tc_after_sync();
+    tc::tmem_free(tbase, A_TMEM_COLS);
+  }
+  if (tid == 0 && *abort) atomicOr(&g_device_fault, 1);
+}
+
+}  // namespace
+
+bool assign_tc_ok(int dt, int D, int M0) {
+  const char* e = std::getenv("AVQ_DISABLE_TCGEN05");
+  const bool off = e && *e && *e != '0';
+  return !off && dt != DT_F32 && (D == 64 || D == 128) && M0 <= A_MAX_M0;
+}
+
+template <int DT>
+int launch_assign_tc(const QuantizeArgs& a, cudaStream_t st) {
+  using T = typename Storage<DT>::T;
+  const int G = a.B * a.H, D = a.D;
+  CUtensorMap tk, tp;
+  int4 kpos;
+  if (!tc::map_rows4(&tk, DT, a.keys, a.ks, a.B, a.H, a.S, D, AR, &kpos) ||
+      !tc::map_rows3(&tp, DT, a.parents_dt, a.H, a.M0, D, ACH))
+    return AVQ_ERR_UNSUPPORTED;
+  const AssignLayout L = assign_layout(D, a.M0);
+  const size_t smem = std::max<size_t>((size_t)L.total + 1024, 80 * 1024);  // <= 2 CTAs (2 x 256 TMEM columns) per SM
+  auto go = [&](auto kfn) {
+    AVQ_TIMED("assign_tc", st);
+    cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kfn<<<dim3((a.S + AR - 1) / AR, G), ATHREADS, smem, st>>>(tk, tp, kpos, a.H, a.S, a.M0, a.C,
+                                                                static_cast<const T*>(a.parents_dt), a.p_sq,
+                                                                static_cast<const T*>(a.children_dt), a.c_sq,
+                                                                a.passign, a.cassign);
+  };
+  if (D == 64) go(assign_tc_kernel<DT, 64>);
+  else go(assign_tc_kernel<DT, 128>);
+  return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
+}
+
+template int launch_assign_tc<DT_BF16>(const QuantizeArgs&, cudaStream_t);
+template int launch_assign_tc<DT_F16>(const QuantizeArgs&, cudaStream_t);
+
+}  // namespace avq

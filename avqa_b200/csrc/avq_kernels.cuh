@@ -164,6 +164,11 @@ bool parent_attn_tc_ok(int dt, int D, int M0);
 size_t parent_attn_tc_table_bytes();
 template <int DT>
 int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st);
+// tcgen05 key assignment (parent argmin + child argmin), same outputs as the
+// assign kernels of avq_quantize.cu.
+bool assign_tc_ok(int dt, int D, int M0);
+template <int DT>
+int launch_assign_tc(const QuantizeArgs& a, cudaStream_t st);
 // Reads and clears the device fault record (stream-synchronous).
 int read_device_fault(int* code, cudaStream_t st);
 

@@ -31,7 +31,6 @@
 
 #include <algorithm>
 #include <cstdlib>
-#include <mutex>
 
 #include "avq_kernels.cuh"
 #include "avq_mma.cuh"
@@ -556,36 +555,6 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
 }
 
 // ---- host side ----------------------------------------------------------------
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiled encode_fn() {
-  static EncodeTiled fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiled>(p);
-    cudaGetLastError();
-  });
-  return fn;
-}
-
-bool encode(CUtensorMap* m, int dt, int rank, const void* base, const cuuint64_t* dims, const cuuint64_t* strides,
-            const cuuint32_t* box) {
-  EncodeTiled fn = encode_fn();
-  if (!fn) return false;
-  const cuuint32_t es[5] = {1, 1, 1, 1, 1};
-  return fn(m, dt == DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank,
-            const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 // AVQ_DISABLE_TCGEN05=1 selects the mma.sync parent-attention kernel (read at
 // every launch, so one process can run both).
 bool tc_disabled() {
@@ -605,35 +574,16 @@ template <int DT>
 int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st) {
   using T = typename Storage<DT>::T;
   const int G = a.B * a.H, D = a.D, M0 = a.M0;
-  // Q as a 4-D tensor (d, and t/h/b ordered by stride), P [H, M0, D], V [G, M0, D]
-  struct Dim {
-    long stride;
-    long extent;
-    int which;  // 1 t, 2 h, 3 b
-  } dd[3] = {{a.qs.s, a.T, 1}, {a.qs.h, a.H, 2}, {a.qs.b, a.B, 3}};
-  std::sort(dd, dd + 3, [](const Dim& x, const Dim& y) { return x.stride < y.stride; });
-  cuuint64_t qdims[4] = {(cuuint64_t)D, 0, 0, 0}, qstr[3];
-  cuuint32_t qbox[4] = {64, 1, 1, 1};
-  int pos[4] = {0, 0, 0, 0};
-  for (int i = 0; i < 3; ++i) {
-    qdims[i + 1] = (cuuint64_t)dd[i].extent;
-    qstr[i] = (cuuint64_t)dd[i].stride * sizeof(T);
-    pos[dd[i].which] = i + 1;
-    if (dd[i].which == 1) qbox[i + 1] = TR;
-  }
-  const cuuint64_t pdims[3] = {(cuuint64_t)D, (cuuint64_t)M0, (cuuint64_t)a.H};
-  const cuuint64_t vdims[3] = {(cuuint64_t)D, (cuuint64_t)M0, (cuuint64_t)G};
-  const cuuint64_t pstr[2] = {(cuuint64_t)D * sizeof(T), (cuuint64_t)M0 * D * sizeof(T)};
-  const cuuint32_t pbox[3] = {64, TCH, 1};
+  // Q [B,H,T,D] strided, P [H, M0, D], V [G, M0, D]; 128-byte swizzled boxes
   CUtensorMap tq, tp, tv;
-  if (!encode(&tq, DT, 4, a.q, qdims, qstr, qbox) || !encode(&tp, DT, 3, a.parents, pdims, pstr, pbox) ||
-      !encode(&tv, DT, 3, a.pagg, vdims, pstr, pbox))
+  int4 qpos;
+  if (!tc::map_rows4(&tq, DT, a.q, a.qs, a.B, a.H, a.T, D, TR, &qpos) ||
+      !tc::map_rows3(&tp, DT, a.parents, a.H, M0, D, TCH) || !tc::map_rows3(&tv, DT, a.pagg, G, M0, D, TCH))
     return AVQ_ERR_UNSUPPORTED;
   const TcLayout L = tc_layout(D, M0);
   // at least 80 KB so that no more than two CTAs (2 x 256 TMEM columns) share an SM
   const size_t smem = std::max<size_t>((size_t)L.total + 1024, 80 * 1024);
   if (DT == DT_BF16) exp_table_kernel<<<1, 256, 0, st>>>(static_cast<uint16_t*>(exptab));
-  const int4 qpos = make_int4(pos[1], pos[2], pos[3], 0);
   auto go = [&](auto kfn) {
     AVQ_TIMED("parent_attn_tc", st);
     cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -634,7 +634,12 @@ int launch_quantize(const QuantizeArgs& a, cudaStream_t st) {
     const bool aligned = ((uintptr_t)a.keys % 16 == 0) && a.ks.s % 8 == 0 && a.ks.h % 8 == 0 && a.ks.b % 8 == 0;
     bool done = false;
     if constexpr (DT != DT_F32) {
-      if (aligned && (a.D == 64 || a.D == 128)) {
+      if (aligned && assign_tc_ok(DT, a.D, a.M0)) {
+        const int rc = launch_assign_tc<DT>(a, st);
+        if (rc != AVQ_OK && rc != AVQ_ERR_UNSUPPORTED) return rc;
+        done = rc == AVQ_OK;
+      }
+      if (!done && aligned && (a.D == 64 || a.D == 128)) {
         done = true;
       auto launch_mma = [&](auto kfn, int D) {
         AVQ_TIMED("assign", st);

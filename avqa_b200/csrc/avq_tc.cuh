@@ -11,7 +11,10 @@
 #include <cuda.h>
 #include <stdint.h>
 
-#include "avq_common.cuh"
+#include <algorithm>
+#include <mutex>
+
+#include "avq_kernels.cuh"
 
 namespace avq {
 namespace tc {
@@ -155,6 +158,71 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
                : "memory");
+}
+
+// ---- host: TMA tensor maps --------------------------------------------------------
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library); nullptr when unavailable.
+inline EncodeTiled encode_fn() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// A 16-bit tensor with 128-byte-swizzled boxes of 64 elements x `rows`.
+inline bool encode16(CUtensorMap* m, int dt, int rank, const void* base, const cuuint64_t* dims,
+                     const cuuint64_t* strides, const cuuint32_t* box) {
+  EncodeTiled fn = encode_fn();
+  if (!fn) return false;
+  const cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  return fn(m, dt == DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank,
+            const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Contiguous [X, N, D] (D innermost): box 64 x rows x 1, coordinates (d, n, x).
+inline bool map_rows3(CUtensorMap* m, int dt, const void* base, int X, int N, int D, int rows) {
+  const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)N, (cuuint64_t)X};
+  const cuuint64_t str[2] = {(cuuint64_t)D * 2, (cuuint64_t)N * D * 2};
+  const cuuint32_t box[3] = {64, (cuuint32_t)rows, 1};
+  return encode16(m, dt, 3, base, dims, str, box);
+}
+
+// Strided [B, H, N, D] operand (unit d-stride): dimensions after d are ordered
+// by stride; box 64 x rows (along n) x 1 x 1.  *pos receives the coordinate
+// slots of (n, h, b) as (x, y, z).
+inline bool map_rows4(CUtensorMap* m, int dt, const void* base, Strides3 st, int B, int H, int N, int D, int rows,
+                      int4* pos) {
+  struct Dim {
+    long stride, extent;
+    int which;  // 1 n, 2 h, 3 b
+  } dd[3] = {{st.s, N, 1}, {st.h, H, 2}, {st.b, B, 3}};
+  std::sort(dd, dd + 3, [](const Dim& x, const Dim& y) { return x.stride < y.stride; });
+  cuuint64_t dims[4] = {(cuuint64_t)D, 0, 0, 0}, str[3];
+  cuuint32_t box[4] = {64, 1, 1, 1};
+  int p[4] = {0, 0, 0, 0};
+  for (int i = 0; i < 3; ++i) {
+    dims[i + 1] = (cuuint64_t)dd[i].extent;
+    str[i] = (cuuint64_t)dd[i].stride * 2;
+    p[dd[i].which] = i + 1;
+    if (dd[i].which == 1) box[i + 1] = (cuuint32_t)rows;
+  }
+  *pos = make_int4(p[1], p[2], p[3], 0);
+  return encode16(m, dt, 4, base, dims, str, box);
 }
 
 }  // namespace tc

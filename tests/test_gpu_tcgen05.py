@@ -13,6 +13,7 @@ from __future__ import annotations
 import ctypes
 import os
 
+import numpy as np
 import pytest
 import torch
 
@@ -83,3 +84,70 @@ def test_device_fault_record_starts_clear() -> None:
     code = ctypes.c_int(-1)
     _lib.check(_lib.load().avq_device_fault(ctypes.byref(code), None), "avq_device_fault")
     assert code.value == 0
+
+
+QCASES = [
+    Workload("q_tail_bf16", B=2, T=8, S=300, H=2, D=128, M0=200, C=3, P=8, dtype="bf16", keys="mixture", seed=51),
+    Workload("q_d64_f16", B=1, T=8, S=1000, H=3, D=64, M0=136, C=8, P=8, dtype="f16", keys="aniso", seed=52),
+    Workload("q_big_bf16", B=1, T=8, S=2048, H=2, D=128, M0=1024, C=4, P=8, dtype="bf16", keys="student_t", seed=53),
+]
+
+
+def _quantize(w: Workload, k, v, cb, tc: bool):
+    os.environ["AVQ_DISABLE_TCGEN05"] = "0" if tc else "1"
+    try:
+        st = ops.quantize(heads_view(k, w.H), heads_view(v, w.H), cb, keep_sums=True)
+        torch.cuda.synchronize()
+    finally:
+        os.environ.pop("AVQ_DISABLE_TCGEN05", None)
+    code = ctypes.c_int(-1)
+    _lib.check(_lib.load().avq_device_fault(ctypes.byref(code), None), "avq_device_fault")
+    assert code.value == 0
+    return st
+
+
+def _assert_same_quant(a, b, tag: str) -> None:
+    for name in ("passign", "cassign", "pcnt", "ccnt", "nvalid", "gmin", "pacc", "cacc"):
+        assert torch.equal(getattr(a, name), getattr(b, name)), f"{tag}: {name}"
+    for name in ("pagg", "cagg"):
+        assert torch.equal(getattr(a, name).view(torch.int16), getattr(b, name).view(torch.int16)), f"{tag}: {name}"
+
+
+@pytest.mark.parametrize("w", QCASES, ids=lambda w: w.name)
+def test_tcgen05_assignment_matches_mma_and_oracle(w: Workload) -> None:
+    dt = w.dtype
+    _, k, v = make_inputs(w)
+    kn, vn = (O.rnd(x.numpy(), dt) for x in (k, v))
+    kh0 = torch.from_numpy(kn).view(w.B, w.S, w.H, w.D).transpose(1, 2)[0]
+    cbk = codebook_from_keys(kh0, w.M0, w.C, w.seed)
+    cb = ops.prepare_codebook(cbk.parents, cbk.children, TORCH_DTYPE[dt], torch.device("cuda"))
+    kd, vd = to_dev(kn, dt), to_dev(vn, dt)
+    a = _quantize(w, kd, vd, cb, True)
+    b = _quantize(w, kd, vd, cb, False)
+    _assert_same_quant(a, b, w.name)
+    pd, cd = O.cast_codebook(cbk.parents.numpy(), cbk.children.numpy(), dt)
+    want = O.quantize(O.split_heads(kn, w.H), O.split_heads(vn, w.H), pd, cd, dt)
+    check_quantization(quant_arrays(a, w.B, w.H), O.split_heads(kn, w.H), O.split_heads(vn, w.H), pd, cd, dt, want,
+                       tag=w.name)
+
+
+def test_tcgen05_assignment_non_finite_inputs() -> None:
+    """A NaN distance wins the parent argmin (torch.argmin): a NaN key and a
+    parent with an infinite element take the kernel's scalar path."""
+    w = Workload("q_nonfinite", B=1, T=8, S=256, H=1, D=128, M0=128, C=4, P=8, dtype="bf16", keys="mixture", seed=54)
+    _, k, v = make_inputs(w)
+    kn, vn = (O.rnd(x.numpy(), "bf16") for x in (k, v))
+    kn[0, 5, 3] = np.nan
+    kh0 = torch.from_numpy(np.nan_to_num(kn)).view(w.B, w.S, w.H, w.D).transpose(1, 2)[0]
+    cbk = codebook_from_keys(kh0, w.M0, w.C, w.seed)
+    parents = cbk.parents.clone()
+    parents[0, 17, 9] = float("inf")
+    cb = ops.prepare_codebook(parents, cbk.children, torch.bfloat16, torch.device("cuda"))
+    kd, vd = to_dev(kn, "bf16"), to_dev(vn, "bf16")
+    a = _quantize(w, kd, vd, cb, True)
+    b = _quantize(w, kd, vd, cb, False)
+    assert torch.equal(a.passign, b.passign) and torch.equal(a.cassign, b.cassign)
+    assert int(a.passign[0, 5]) == 0  # every distance of the NaN key is NaN: the first parent
+    pd, cd = O.cast_codebook(parents.numpy(), cbk.children.numpy(), "bf16")
+    want = O.quantize(O.split_heads(kn, w.H), O.split_heads(vn, w.H), pd, cd, "bf16")
+    np.testing.assert_array_equal(a.passign.cpu().numpy(), want.parent_assignments)
