@@ -500,11 +500,21 @@ __device__ __forceinline__ void load_row_elems(const typename Storage<DT>::T* p,
 }
 
 // Vectorised aggregation for D = 32 * VPL (VPL = 2 or 4 dtype elements per
-// lane, one 4- or 8-byte load per member).  The warp fetches 32 member ids
-// (and their child ids) at once and keeps 8 value rows in flight; the fp32
-// additions stay in key order.
+// lane).  One warp per parent; the member rows stream through a per-warp
+// ring of AG_RING rows in shared memory filled with cp.async, so AG_RING rows
+// per warp are in flight independently of the register budget.  Lane l copies
+// and later reads only its own VPL-element slice of every row, so the ring
+// needs no cross-lane synchronisation.  The fp32 additions stay in key order
+// (index_add_, quantizer.py:241-262).
+constexpr int AG_WARPS = 8;
+
+template <int BYTES>
+__device__ __forceinline__ void cp_async_slice(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(smem_u32(smem)), "l"(gmem), "n"(BYTES));
+}
+
 template <int DT, int CMAX, int VPL>
-__global__ void __launch_bounds__(256, 2) aggregate_vec_kernel(
+__global__ void __launch_bounds__(AG_WARPS * 32) aggregate_vec_kernel(
     const typename Storage<DT>::T* __restrict__ values, Strides3 vs, int H, int S, int M0, int C,
     const int* __restrict__ order, const int* __restrict__ poff, const int* __restrict__ pcnt,
     const int* __restrict__ cassign, typename Storage<DT>::T* __restrict__ pagg,
@@ -514,10 +524,12 @@ __global__ void __launch_bounds__(256, 2) aggregate_vec_kernel(
   struct alignas(VPL * sizeof(T)) V {
     T e[VPL];
   };
-  constexpr int D = 32 * VPL, U = 8;
-  const int lane = threadIdx.x & 31;
-  const long gp = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  constexpr int D = 32 * VPL, AG_RING = sizeof(T) == 4 ? 8 : 16, SB = VPL * (int)sizeof(T);
+  __shared__ __align__(16) T ring_all[AG_WARPS][AG_RING][D];
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const long gp = (long)blockIdx.x * AG_WARPS + wib;
   if (gp >= rows) return;
+  T (*ring)[D] = ring_all[wib];
   const int g = (int)(gp / M0), b = g / H, h = g % H;
   const T* vbase = values + (long)b * vs.b + (long)h * vs.h + lane * VPL;
   float ap[VPL], ac[CMAX][VPL];
@@ -531,40 +543,54 @@ __global__ void __launch_bounds__(256, 2) aggregate_vec_kernel(
   const int beg = poff[gp], n = pcnt[gp];
   const int* ord = order + (long)g * S + beg;
   const int* cas = cassign + (long)g * S;
+  // member ids: batch i0 in (cur_s, cur_c), the next batch in (nxt_s)
+  int cur_s = lane < n ? ord[lane] : 0;
+  int cur_c = lane < n ? cas[cur_s] : -1;
+  int nxt_s = lane + 32 < n ? ord[lane + 32] : 0;
+  // prologue: the first AG_RING rows
+  const int pre = min(n, AG_RING);
+  for (int i = 0; i < AG_RING; ++i) {
+    if (i < pre) {
+      const int s = __shfl_sync(0xffffffffu, cur_s, i);
+      cp_async_slice<SB>(&ring[i][lane * VPL], vbase + (long)s * vs.s);
+    }
+    cp_async_commit();
+  }
   for (int i0 = 0; i0 < n; i0 += 32) {
     const int m = min(32, n - i0);
-    const int my_s = lane < m ? ord[i0 + lane] : 0;
-    const int my_c = lane < m ? cas[my_s] : -1;
 #pragma unroll
     for (int c = 0; c < CMAX; ++c) {
-      const int k = __popc(__ballot_sync(0xffffffffu, my_c == c));
+      const int k = __popc(__ballot_sync(0xffffffffu, cur_c == c));
       if (lane == c) cn += k;
     }
-    for (int j0 = 0; j0 < m; j0 += U) {
-      float buf[U][VPL];
-      int cc[U];
+    for (int j = 0; j < m; ++j) {
+      const int i = i0 + j;
+      cp_async_wait<AG_RING - 1>();  // row i has landed (groups complete in order)
+      float v[VPL];
+      load_row_elems<DT, VPL>(&ring[i % AG_RING][lane * VPL], v);
+      const int cc = __shfl_sync(0xffffffffu, cur_c, j);
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int j = j0 + u;
-        const int s = __shfl_sync(0xffffffffu, my_s, j & 31);
-        cc[u] = __shfl_sync(0xffffffffu, my_c, j & 31);
-        load_row_elems<DT, VPL>(vbase + (long)(j < m ? s : my_s) * vs.s, buf[u]);
+      for (int q = 0; q < VPL; ++q) {
+        ap[q] = __fadd_rn(ap[q], v[q]);
+#pragma unroll
+        for (int c = 0; c < CMAX; ++c)
+          if (c == cc) ac[c][q] = __fadd_rn(ac[c][q], v[q]);
       }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        if (j0 + u < m) {
-#pragma unroll
-          for (int q = 0; q < VPL; ++q) {
-            const float v = buf[u][q];
-            ap[q] = __fadd_rn(ap[q], v);
-#pragma unroll
-            for (int c = 0; c < CMAX; ++c)
-              if (c == cc[u]) ac[c][q] = __fadd_rn(ac[c][q], v);
-          }
-        }
+      // refill the slot with row i + AG_RING (after the slot's value was used)
+      const int ni = i + AG_RING;
+      if (ni < n) {
+        const int nj = ni - i0;  // < 32 + AG_RING: in this batch or the next
+        const int a = __shfl_sync(0xffffffffu, cur_s, nj & 31), bb = __shfl_sync(0xffffffffu, nxt_s, nj & 31);
+        cp_async_slice<SB>(&ring[i % AG_RING][lane * VPL], vbase + (long)(nj < 32 ? a : bb) * vs.s);
       }
+      cp_async_commit();
     }
+    // advance the id batches
+    cur_s = nxt_s;
+    cur_c = (lane + i0 + 32 < n) ? cas[cur_s] : -1;
+    nxt_s = lane + i0 + 64 < n ? ord[i0 + 64 + lane] : 0;
   }
+  cp_async_wait<0>();
   const long o = gp * D + lane * VPL;
   V pv;
 #pragma unroll
