@@ -546,6 +546,7 @@ struct FwdWorkspace {
   int *sel, *pass_cnt;
   void* slog;  // tensor-core path: logits scratch when not in shared memory (or kept for HVAQ)
   void* exptab;  // tcgen05 path: the bf16 exponential table
+  void* cdesc;   // tcgen05 correction: slot descriptors
   size_t bytes;
 };
 
@@ -582,6 +583,7 @@ static FwdWorkspace carve(void* base, int dtype, int G, int T, int D, int M0, in
   w.sel = (int*)take(sizeof(int) * (long)G * sel_stride);
   w.pass_cnt = (int*)take(sizeof(int) * MAX_PASSES);
   w.exptab = mma ? take(parent_attn_tc_table_bytes()) : nullptr;
+  w.cdesc = (mma && (C == 4 || C == 8)) ? take(correct_tc_desc_bytes(G, sel_stride, C)) : nullptr;
   w.bytes = (size_t)(p - (char*)base);
   return w;
 }
@@ -653,8 +655,9 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
                 w.beta};
       // tcgen05 kernel for the plain first pass; the HVAQ variant keeps its
       // logits for the rescaling pass and runs on the mma.sync kernel
-      int rc = (!hv && parent_attn_tc_ok(DT, a.D, a.M0)) ? launch_parent_attn_tc<DT>(pa, w.exptab, st)
-                                                         : AVQ_ERR_UNSUPPORTED;
+      const bool pa_tc = !hv && parent_attn_tc_ok(DT, a.D, a.M0), corr_tc = correct_tc_ok(DT, a.D, a.C);
+      if (DT == DT_BF16 && (pa_tc || corr_tc)) launch_exp_table(w.exptab, st);
+      int rc = pa_tc ? launch_parent_attn_tc<DT>(pa, w.exptab, st) : AVQ_ERR_UNSUPPORTED;
       if (rc == AVQ_ERR_UNSUPPORTED) rc = launch_parent_attn_mma<DT>(pa, st);
       if (rc != AVQ_OK) return rc;
       RouteExact rx0{(const float*)w.part0, w.slog, hv ? 1 : 0, w.m, w.z, a.T};
@@ -675,7 +678,8 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
                   a.pcnt, a.ccnt, w.m, w.l, w.z, hv ? w.beta : nullptr, w.a, sel, sel_stride, pcnt_out, a.passes,
                   {0, 0, 0, 0, 0, 0, 0, 0}, a.passes > 1 ? 1 : 0, a.out, a.os};
       for (int k = 0; k < a.passes; ++k) ca.pass_off[k] = lay.off[k];
-      rc = launch_correct_mma<DT>(ca, st);
+      rc = (corr_tc && w.cdesc) ? launch_correct_tc(ca, w.exptab, w.cdesc, st) : AVQ_ERR_UNSUPPORTED;
+      if (rc == AVQ_ERR_UNSUPPORTED) rc = launch_correct_mma<DT>(ca, st);
       if (rc != AVQ_OK) return rc;
       return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
     }

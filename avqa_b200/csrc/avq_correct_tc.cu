@@ -1,0 +1,529 @@
+// Child correction on the sm_100a tensor cores for bf16 and D in {64, 128}
+// (reference refinement.py:82-304, attention.py:100-163, multipass.py:207-262,
+// attention_module.py:532-535).
+//
+// CTA = 128 queries of one (b,h); thread r of warps 0-3 owns query r (TMEM
+// lane r) and 96 of them also gather one slot row of the group after next with
+// cp.async; warp 4 loads the query tile with TMA and issues tcgen05.mma.  The
+// slot descriptors (rows, counts, masks) of every group come from a small
+// kernel run before, so the gathers need no dependent loads.
+// The selected parents of a pass are taken J = 48 / (1 + C) at a time with
+// their children: 48 slots (J parents, J*C children, zero padding).
+//
+// TMEM (256 columns): O [0, D) -- the fp32 state a, seeded from the parent
+// pass -- then the 48 slot logits Q L^T and the slot weights as three bf16
+// parts (hi, mid, lo: 24 significant bits, two per column) that are the A
+// operand of O += W V.  Per slot and query, with m, z the parent-pass row max
+// and normaliser:
+//   parent  pi = DT(e / max(z, eps)), e = DT(exp(DT(s - m)));  w = -exp(pi - m) n
+//   child   w = exp(u - m) n_c            (u = -inf for an empty child)
+// and l' = l - sum w_parent + sum w_child per pass; out = O / max(l', 1e-12).
+// The weights are fp32 quantities of the reference's fp32 correction; they use
+// the fast exponential (relative error a few 1e-7), far inside the bf16
+// output tolerance, and never feed a routing decision.
+#include <cuda.h>
+
+#include <algorithm>
+#include <cstdlib>
+
+#include "avq_kernels.cuh"
+#include "avq_mma.cuh"
+#include "avq_tc.cuh"
+
+namespace avq {
+
+extern __device__ int g_device_fault;
+
+namespace {
+
+constexpr int CR = 128;        // queries per CTA
+constexpr int NS = 48;         // slots per group
+constexpr int C_TMEM_COLS = 256;
+constexpr uint32_t EXPB = 0x3AFF;  // exponential table (same layout as the parent-attention table)
+constexpr int EXPN = 2051;
+
+constexpr int CB_Q = 0, CB_FULL = 1, CB_EMPTY = 4, CB_SFULL = 7, CB_SFREE = 8, CB_WFULL = 9, CB_WFREE = 10,
+              CB_OFULL = 11, CN_BARS = 12;
+
+constexpr int NBUF = 3;         // gathered slot buffers
+constexpr int CTHREADS2 = 160;  // 4 row warps + the MMA / TMA warp
+
+struct CorrLayout {
+  int q, l[NBUF], v[NBUF], meta[NBUF], exptab, bars, misc, total;
+};
+
+__host__ __device__ inline CorrLayout corr_layout(int D) {
+  CorrLayout L;
+  int o = 0;
+  L.q = o;
+  o += CR * D * 2;
+  for (int i = 0; i < NBUF; ++i) {
+    L.l[i] = o;
+    o += NS * D * 2;
+  }
+  for (int i = 0; i < NBUF; ++i) {
+    L.v[i] = o;
+    o += NS * D * 2;
+  }
+  for (int i = 0; i < NBUF; ++i) {
+    L.meta[i] = o;
+    o += 2 * NS * 4;  // n [48] then logit mask [48]
+  }
+  L.exptab = o;
+  o += ((EXPN + 1) / 2) * 4;
+  o = (o + 15) & ~15;
+  L.bars = o;
+  o += CN_BARS * 8;
+  L.misc = o;
+  o += 16;
+  L.total = o;
+  return L;
+}
+
+__device__ __forceinline__ void drain_c(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!tc::mbar_try(bar, parity) && clock64() - t0 < tc::kWaitCycles / 8) {
+  }
+}
+
+__device__ __forceinline__ float exp_bf16_tab(float d, const uint16_t* tab) {
+  // DT(exp(d)) for a bf16 value d <= 0 or NaN (NaN -> 0), from the table
+  uint32_t a = (__float_as_uint(d) >> 16) & 0x7FFFu;
+  a = a < EXPB ? EXPB : (a > EXPB + EXPN - 1 ? EXPB + EXPN - 1 : a);
+  return __uint_as_float((uint32_t)tab[a - EXPB] << 16);
+}
+
+// Slot descriptor of (slice g, group, slot): the logit row (>= 0 a parent row
+// of the codebook, <= -2 the child row -2 - x, -1 zeros), the value row (same
+// encoding over the parent / child sums), the count in the dtype (-1: empty
+// slot) and the logit mask.
+struct SlotDesc {
+  int lrow, vrow;
+  float n, mk;
+};
+
+template <int C>
+__global__ void corr_desc_kernel(const int* __restrict__ sel, int sel_stride, const int* __restrict__ pass_cnt,
+                                 int npass, PassOffsets po, int multipass, int H, int M0,
+                                 const int* __restrict__ pcnt, const int* __restrict__ ccnt, int maxgroups,
+                                 SlotDesc* __restrict__ desc) {
+  constexpr int J = NS / (1 + C), NREAL = J * (1 + C);
+  const int g = blockIdx.x, h = g % H;
+  const int* sg = sel + (long)g * sel_stride;
+  int kg = 0;
+  for (int ps = 0; ps < npass; ++ps) {
+    const int cnt = pass_cnt[ps];
+    if (cnt <= 0) break;
+    const bool quirk = multipass && cnt == M0;  // refinement.py:256-260
+    for (int j0 = 0; j0 < cnt && kg < maxgroups; j0 += J, ++kg) {
+      for (int r = threadIdx.x; r < NS; r += blockDim.x) {
+        SlotDesc d{-1, -1, -1.f, 0.f};
+        if (r < J) {
+          const int j = j0 + r;
+          if (j < cnt) {
+            const int p = sg[po.off[ps] + j];
+            d.lrow = h * M0 + p;
+            d.vrow = g * M0 + p;
+            d.n = count_dt<DT_BF16>(pcnt[(long)g * M0 + p]);
+            d.mk = d.n > 0.f ? 1.f : 0.f;
+          }
+        } else if (r < NREAL) {
+          const int jj = (r - J) / C, c = (r - J) % C, j = j0 + jj;
+          if (j < cnt) {
+            const int p = sg[po.off[ps] + j];
+            const int pl = quirk ? j : p;
+            d.lrow = -2 - ((h * M0 + pl) * C + c);
+            d.vrow = -2 - ((g * M0 + p) * C + c);
+            d.n = count_dt<DT_BF16>(ccnt[((long)g * M0 + p) * C + c]);
+            d.mk = ccnt[((long)g * M0 + pl) * C + c] > 0 ? 1.f : 0.f;
+          }
+        }
+        desc[((long)g * maxgroups + kg) * NS + r] = d;
+      }
+    }
+  }
+}
+
+template <int D, int C>
+__global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_q, int4 qpos, int H, int Tq, float sqrtD,
+    const __nv_bfloat16* __restrict__ parents, const __nv_bfloat16* __restrict__ children,
+    const __nv_bfloat16* __restrict__ pagg, const __nv_bfloat16* __restrict__ cagg, const float* __restrict__ m_in,
+    const float* __restrict__ l_in, const float* __restrict__ z_in, const float* __restrict__ beta_in,
+    const __nv_bfloat16* __restrict__ a_in, const int* __restrict__ pass_cnt, int npass, int maxgroups,
+    const SlotDesc* __restrict__ desc, const uint16_t* __restrict__ exptab_g, float* __restrict__ out, Strides3 os) {
+  constexpr int DT = DT_BF16;
+  constexpr int J = NS / (1 + C), NREAL = J * (1 + C), CPR = D / 8;
+  constexpr int OCOL = 0, SCOL = D, WCOL = D + NS;  // TMEM columns
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = tc::smem_addr(smem_raw);
+  unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  const CorrLayout L = corr_layout(D);
+  const int g = blockIdx.y, b = g / H, h = g % H, t0 = blockIdx.x * CR;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.bars);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + L.misc);
+  volatile int* abort = reinterpret_cast<volatile int*>(sm + L.misc + 4);
+  const uint16_t* exptab = reinterpret_cast<const uint16_t*>(sm + L.exptab);
+
+  // groups per pass (the same sequence on every thread)
+  int ngroups = 0;
+  for (int ps = 0; ps < npass; ++ps) {
+    const int cnt = pass_cnt[ps];
+    if (cnt <= 0) break;
+    ngroups += (cnt + J - 1) / J;
+  }
+  ngroups = min(ngroups, maxgroups);
+
+  if (tid == 0) {
+    for (int i = 0; i < CN_BARS; ++i) {
+      const int cnt = ((i >= CB_FULL && i < CB_FULL + NBUF) || i == CB_SFREE || i == CB_WFULL) ? CR : 1;
+      tc::mbar_init(&bars[i], cnt);
+    }
+    *abort = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 4) tc::tmem_alloc(tslot, C_TMEM_COLS);
+  if (tid < CR) {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(exptab_g);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(sm + L.exptab);
+    for (int i = tid; i < (EXPN + 1) / 2; i += CR) dst[i] = src[i];
+  }
+  tc::tc_before_sync();
+  __syncthreads();
+  tc::tc_after_sync();
+  const uint32_t tbase = *tslot;
+
+  if (warp == 4) {
+    // ---- Q tile (TMA) and MMA issue ----
+    if (lane == 0) {
+      tc::tma_prefetch_desc(&tm_q);
+      tc::mbar_expect_tx(&bars[CB_Q], CR * D * 2);
+      for (int kb = 0; kb < D / 64; ++kb) {
+        int c[4];
+        c[0] = kb * 64;
+        c[qpos.x] = t0;
+        c[qpos.y] = h;
+        c[qpos.z] = b;
+        tc::tma_load_4d(sm + L.q + kb * CR * 128, &tm_q, c[0], c[1], c[2], c[3], &bars[CB_Q]);
+      }
+      const uint32_t idS = tc::idesc_f16(1, CR, NS, false);
+      const uint32_t idO = tc::idesc_f16(1, CR, D, true);
+      const uint32_t qa = tc::smem_addr(sm + L.q);
+      uint32_t la[NBUF], va[NBUF];
+      for (int i = 0; i < NBUF; ++i) {
+        la[i] = tc::smem_addr(sm + L.l[i]);
+        va[i] = tc::smem_addr(sm + L.v[i]);
+      }
+      auto issue_S = [&](int kg) -> bool {
+        const int bf = kg % NBUF;
+        if (!tc::mbar_wait(&bars[CB_FULL + bf], (kg / NBUF) & 1, abort)) return false;
+        tc::tc_after_sync();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t ad = tc::sdesc_sw128(qa + (kk >> 2) * CR * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::sdesc_sw128(la[bf] + (kk >> 2) * NS * 128 + (kk & 3) * 32, 16, 1024);
+          tc::mma_ss(tbase + SCOL, ad, bd, idS, kk > 0);
+        }
+        tc::mma_commit(&bars[CB_SFULL]);
+        return true;
+      };
+      bool ok = tc::mbar_wait(&bars[CB_Q], 0, abort);
+      if (ok && ngroups > 0) ok = issue_S(0);
+      for (int kg = 0; ok && kg < ngroups; ++kg) {
+        const int bf = kg % NBUF;
+        if (kg + 1 < ngroups) {
+          if (!(ok = tc::mbar_wait(&bars[CB_SFREE], kg & 1, abort))) break;
+          if (!(ok = issue_S(kg + 1))) break;
+        }
+        if (!(ok = tc::mbar_wait(&bars[CB_WFULL], kg & 1, abort))) break;
+        tc::tc_after_sync();
+#pragma unroll
+        for (int part = 0; part < 3; ++part)
+#pragma unroll
+          for (int kk = 0; kk < NS / 16; ++kk) {
+            const uint64_t bd = tc::sdesc_sw128(va[bf] + kk * 16 * 128, NS * 128, 1024);
+            tc::mma_ts(tbase + OCOL, tbase + WCOL + part * (NS / 2) + kk * 8, bd, idO, true);
+          }
+        tc::mma_commit(&bars[CB_WFREE]);
+        tc::mma_commit(&bars[CB_EMPTY + bf]);
+      }
+      tc::mma_commit(&bars[CB_OFULL]);
+      if (!ok) drain_c(&bars[CB_OFULL], 0);
+    }
+  } else {
+    // ---- row threads: query r; threads 0-95 also gather one slot row each ----
+    const int r = tid, t = t0 + r;
+    const bool live = t < Tq;
+    const long row = (long)g * Tq + (live ? t : 0);
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const float inv_sqrtD = 1.f / sqrtD;
+    const float m = live ? m_in[row] : 0.f;
+    const float zc = clamp_min_nan(live ? z_in[row] : 1.f, eps_dt<DT>()), rz = 1.f / zc;
+    const float bt = beta_in && live ? beta_in[row] : 0.f;
+    float l = live ? l_in[row] : 1.f;
+    // gather role: thread r < 48 copies the logit row of slot r (and writes its
+    // metadata), 48 <= r < 96 the value row of slot r - 48
+    const int gslot = r < NS ? r : r - NS;
+    const bool gathers = r < 2 * NS, isv = r >= NS;
+    const SlotDesc* dg = desc + (long)g * maxgroups * NS + gslot;
+    auto gather = [&](int kg, const SlotDesc& d) {
+      const int bf = kg % NBUF;
+      if (gathers) {
+        const int x = isv ? d.vrow : d.lrow;
+        const __nv_bfloat16* src = x >= 0 ? (isv ? pagg : parents) + (long)x * D
+                                          : (isv ? cagg : children) + (long)(x <= -2 ? -2 - x : 0) * D;
+        unsigned char* dst = sm + (isv ? L.v[bf] : L.l[bf]) + gslot * 128;
+#pragma unroll
+        for (int ch = 0; ch < CPR; ++ch)
+          cp_async16(dst + (ch >> 3) * NS * 128 + (((ch & 7) ^ (gslot & 7)) << 4), src + ch * 8, x != -1);
+        if (!isv) {
+          float* meta = reinterpret_cast<float*>(sm + L.meta[bf]);
+          meta[gslot] = d.n;
+          meta[NS + gslot] = d.mk;
+        }
+      }
+      cp_async_commit();
+    };
+    auto publish = [&](int kg) {  // copies of group kg have landed (this thread's part)
+      tc::fence_async_smem();
+      tc::mbar_arrive(&bars[CB_FULL + kg % NBUF]);
+    };
+    SlotDesc dn1{-1, -1, -1.f, 0.f}, dn2{-1, -1, -1.f, 0.f};  // descriptors of the next groups
+    if (gathers) {
+      if (ngroups > 0) {
+        const SlotDesc d0 = dg[0];
+        gather(0, d0);
+      } else {
+        cp_async_commit();
+      }
+      if (ngroups > 1) dn1 = dg[NS];
+      if (ngroups > 2) dn2 = dg[2 * NS];
+    } else {
+      cp_async_commit();
+    }
+    if (ngroups > 1) gather(1, dn1);
+    else cp_async_commit();
+    cp_async_wait<1>();
+    if (ngroups > 0) publish(0);
+    // O = a (attention.py:154-158)
+#pragma unroll
+    for (int d0 = 0; d0 < D; d0 += 32) {
+      uint32_t o[32];
+      const uint4* src = reinterpret_cast<const uint4*>(a_in + row * D + d0);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint4 u = live ? src[k] : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          o[8 * k + 2 * e] = __float_as_uint(half_lo<DT>(w[e]));
+          o[8 * k + 2 * e + 1] = __float_as_uint(half_hi<DT>(w[e]));
+        }
+      }
+      tc::tmem_st32(tbase + lane_off + OCOL + d0, o);
+    }
+    tc::tmem_wait_st();
+    bool ok = true;
+    int kg = 0;
+    for (int ps = 0; ok && ps < npass; ++ps) {
+      const int cnt = pass_cnt[ps];
+      if (cnt <= 0) break;
+      double rl = 0.0, al = 0.0;
+      for (int j0 = 0; j0 < cnt && kg < ngroups; j0 += J, ++kg) {
+        const int bf = kg % NBUF;
+        ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[CB_SFULL], kg & 1, abort) &&
+                                         tc::mbar_wait(&bars[CB_FULL + bf], (kg / NBUF) & 1, abort));
+        if (!ok) break;
+        tc::tc_after_sync();
+        uint32_t sv[2][24];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t sa[16], sb[8];
+          tc::tmem_ld16(tbase + lane_off + SCOL + 24 * half, sa);
+          tc::tmem_ld8(tbase + lane_off + SCOL + 24 * half + 16, sb);
+#pragma unroll
+          for (int i = 0; i < 24; ++i) sv[half][i] = i < 16 ? sa[i] : sb[i - 16];
+        }
+        tc::tmem_wait_ld();
+        tc::tc_before_sync();
+        tc::mbar_arrive(&bars[CB_SFREE]);
+        // gather group kg + 2 into the buffer of group kg - 1, publish group kg + 1
+        if (kg + 2 < ngroups) {
+          const int nb = (kg + 2) % NBUF;
+          if (kg + 2 >= NBUF) {
+            ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[CB_EMPTY + nb], ((kg + 2) / NBUF - 1) & 1, abort));
+            if (!ok) break;
+          }
+          gather(kg + 2, dn2);
+          cp_async_wait<1>();
+        } else {
+          cp_async_wait<0>();
+        }
+        if (kg + 1 < ngroups) publish(kg + 1);
+        if (gathers && kg + 3 < ngroups) dn2 = dg[(long)(kg + 3) * NS];
+        const float* meta = reinterpret_cast<const float*>(sm + L.meta[bf]);
+        if (kg > 0) {  // the previous group's value MMAs have read the weight columns
+          ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[CB_WFREE], (kg - 1) & 1, abort));
+          if (!ok) break;
+          tc::tc_after_sync();
+        }
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {  // 24 slots at a time
+          // logits DT(DT(acc) / sqrt(D)), branch-free fast quotients with an
+          // exact redo when one is near a rounding point
+          float sl[24];
+          bool near = false;
+#pragma unroll
+          for (int i2 = 0; i2 < 12; ++i2) {
+            const int i = 2 * i2;
+            const uint32_t x2 = pack2<DT>(__uint_as_float(sv[half][i]), __uint_as_float(sv[half][i + 1]));
+            const float y0 = half_lo<DT>(x2) * inv_sqrtD, y1 = half_hi<DT>(x2) * inv_sqrtD;
+            near |= near_midpoint<DT>(y0) | near_midpoint<DT>(y1);
+            const uint32_t s2 = pack2<DT>(y0, y1);
+            sl[i] = half_lo<DT>(s2);
+            sl[i + 1] = half_hi<DT>(s2);
+          }
+          if (near) {
+#pragma unroll
+            for (int i = 0; i < 24; ++i)
+              sl[i] = scale_logit<DT>(rnd<DT>(__uint_as_float(sv[half][i])), sqrtD, inv_sqrtD);
+          }
+          // weights (fp32; refinement.py:335,341-343): -exp(pi - m) n for a parent,
+          // exp(u - m) n_c for a child, 0 for an empty slot
+          const float4* mn4 = reinterpret_cast<const float4*>(meta + 24 * half);
+          const float4* mk4 = reinterpret_cast<const float4*>(meta + NS + 24 * half);
+          float wv[24];
+          float rlg = 0.f, alg = 0.f;
+#pragma unroll
+          for (int q = 0; q < 6; ++q) {
+            const float4 n4 = mn4[q], k4 = mk4[q];
+            const float nv[4] = {n4.x, n4.y, n4.z, n4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = 4 * q + e, k = 24 * half + i;
+              float w = 0.f;
+              if (k < NREAL) {
+                float s = kv[e] > 0.f ? sl[i] : -INFINITY;
+                if (k < J) {
+                  if (beta_in) s = rnd<DT>(__fmul_rn(bt, rnd<DT>(__fmul_rn(s, sqrtD))));
+                  const float ex = exp_bf16_tab(rnd<DT>(s - m), exptab);
+                  const float pi = div_dt_fast<DT>(ex, rz, zc);
+                  w = nv[e] >= 0.f ? __expf(pi - m) * nv[e] : 0.f;
+                  rlg += w;
+                  w = -w;
+                } else {
+                  w = nv[e] >= 0.f ? __expf(s - m) * nv[e] : 0.f;
+                  alg += w;
+                }
+              }
+              wv[i] = w;
+            }
+          }
+          rl += (double)rlg;
+          al += (double)alg;
+          // three bf16 parts per weight (w = hi + mid + lo to 24 bits), packed in pairs
+          uint32_t wp[3][12];
+#pragma unroll
+          for (int i2 = 0; i2 < 12; ++i2) {
+            const float w0 = wv[2 * i2], w1 = wv[2 * i2 + 1];
+            const uint32_t h2 = pack2<DT_BF16>(w0, w1);
+            const float r0 = w0 - half_lo<DT_BF16>(h2), r1 = w1 - half_hi<DT_BF16>(h2);
+            const uint32_t m2 = pack2<DT_BF16>(r0, r1);
+            wp[0][i2] = h2;
+            wp[1][i2] = m2;
+            wp[2][i2] = pack2<DT_BF16>(r0 - half_lo<DT_BF16>(m2), r1 - half_hi<DT_BF16>(m2));
+          }
+#pragma unroll
+          for (int part = 0; part < 3; ++part) {
+            tc::tmem_st8(tbase + lane_off + WCOL + part * (NS / 2) + 12 * half, wp[part]);
+            tc::tmem_st4(tbase + lane_off + WCOL + part * (NS / 2) + 12 * half + 8, wp[part] + 8);
+          }
+        }
+        tc::tmem_wait_st();
+        tc::tc_before_sync();
+        tc::mbar_arrive(&bars[CB_WFULL]);
+      }
+      // OnlineSoftmaxState.replace with unit scales (attention.py:149-153)
+      l = __fadd_rn(__fsub_rn(l, __double2float_rn(rl)), __double2float_rn(al));
+    }
+    cp_async_wait<0>();
+    if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[CB_OFULL], 0, abort));
+    if (ok) {
+      tc::tc_after_sync();
+      const float rden = __fdiv_rn(1.f, clamp_min_nan(l, 1e-12f));
+      float* orow = out + (long)b * os.b + (long)(live ? t : 0) * os.s + (long)h * os.h;
+#pragma unroll
+      for (int d0 = 0; d0 < D; d0 += 32) {
+        uint32_t o[32];
+        tc::tmem_ld32(tbase + lane_off + OCOL + d0, o);
+        tc::tmem_wait_ld();
+        if (live) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            *reinterpret_cast<float4*>(orow + d0 + 4 * k) =
+                make_float4(__uint_as_float(o[4 * k]) * rden, __uint_as_float(o[4 * k + 1]) * rden,
+                            __uint_as_float(o[4 * k + 2]) * rden, __uint_as_float(o[4 * k + 3]) * rden);
+        }
+      }
+    }
+  }
+
+  tc::tc_before_sync();
+  __syncthreads();
+  if (warp == 4) {
+    tc::tc_after_sync();
+    tc::tmem_free(tbase, C_TMEM_COLS);
+  }
+  if (tid == 0 && *abort) atomicOr(&g_device_fault, 1);
+}
+
+}  // namespace
+
+bool correct_tc_ok(int dt, int D, int C) {
+  const char* e = std::getenv("AVQ_DISABLE_TCGEN05");
+  const bool off = e && *e && *e != '0';
+  return !off && dt == DT_BF16 && (D == 64 || D == 128) && (C == 4 || C == 8);
+}
+
+int correct_tc_groups(int sel_stride, int C) {
+  const int J = NS / (1 + C);
+  return (sel_stride + 8 * (J - 1)) / J;  // every pass (at most 8) may end in a partial group
+}
+
+size_t correct_tc_desc_bytes(int G, int sel_stride, int C) {
+  return (size_t)G * correct_tc_groups(sel_stride, C) * NS * sizeof(SlotDesc);
+}
+
+int launch_correct_tc(const CorrArgs& a, const void* exptab, void* desc, cudaStream_t st) {
+  const int G = a.B * a.H, D = a.D;
+  CUtensorMap tq;
+  int4 qpos;
+  if (!tc::map_rows4(&tq, DT_BF16, a.q, a.qs, a.B, a.H, a.T, D, CR, &qpos)) return AVQ_ERR_UNSUPPORTED;
+  if (((uintptr_t)a.out % 16) || a.os.s % 4 || a.os.h % 4 || a.os.b % 4) return AVQ_ERR_UNSUPPORTED;
+  PassOffsets po;
+  for (int k = 0; k < 8; ++k) po.off[k] = a.pass_off[k];
+  const int maxgroups = correct_tc_groups(a.sel_stride, a.C);
+  SlotDesc* sd = static_cast<SlotDesc*>(desc);
+  const CorrLayout L = corr_layout(D);
+  const size_t smem = std::max<size_t>((size_t)L.total + 1024, 80 * 1024);  // <= 2 CTAs (2 x 256 TMEM columns) per SM
+  auto go = [&](auto dfn, auto kfn) {
+    AVQ_TIMED("correct_tc", st);
+    dfn<<<G, 64, 0, st>>>(a.sel, a.sel_stride, a.pass_cnt, a.npass, po, a.multipass, a.H, a.M0, a.pcnt, a.ccnt,
+                          maxgroups, sd);
+    cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kfn<<<dim3((a.T + CR - 1) / CR, G), CTHREADS2, smem, st>>>(
+        tq, qpos, a.H, a.T, a.sqrtD, static_cast<const __nv_bfloat16*>(a.parents),
+        static_cast<const __nv_bfloat16*>(a.children), static_cast<const __nv_bfloat16*>(a.pagg),
+        static_cast<const __nv_bfloat16*>(a.cagg), a.m, a.l, a.z, a.beta, static_cast<const __nv_bfloat16*>(a.a),
+        a.pass_cnt, a.npass, maxgroups, sd, static_cast<const uint16_t*>(exptab), a.out, a.os);
+  };
+  if (a.C == 4) {
+    if (D == 64) go(corr_desc_kernel<4>, correct_tc_kernel<64, 4>); else go(corr_desc_kernel<4>, correct_tc_kernel<128, 4>);
+  } else {
+    if (D == 64) go(corr_desc_kernel<8>, correct_tc_kernel<64, 8>); else go(corr_desc_kernel<8>, correct_tc_kernel<128, 8>);
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
+}
+
+}  // namespace avq

@@ -570,6 +570,8 @@ bool parent_attn_tc_ok(int dt, int D, int M0) {
 
 size_t parent_attn_tc_table_bytes() { return (size_t)EXP_WORDS * 4; }
 
+void launch_exp_table(void* tab, cudaStream_t st) { exp_table_kernel<<<1, 256, 0, st>>>(static_cast<uint16_t*>(tab)); }
+
 template <int DT>
 int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st) {
   using T = typename Storage<DT>::T;
@@ -583,7 +585,6 @@ int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st) {
   const TcLayout L = tc_layout(D, M0);
   // at least 80 KB so that no more than two CTAs (2 x 256 TMEM columns) share an SM
   const size_t smem = std::max<size_t>((size_t)L.total + 1024, 80 * 1024);
-  if (DT == DT_BF16) exp_table_kernel<<<1, 256, 0, st>>>(static_cast<uint16_t*>(exptab));
   auto go = [&](auto kfn) {
     AVQ_TIMED("parent_attn_tc", st);
     cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
