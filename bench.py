@@ -314,22 +314,60 @@ def run_ours(args) -> None:
 
         e2e = None
         if not args.no_e2e:
+            # Through the public API with the copies inside the timed region:
+            # every step copies its q/k/v from pinned host memory and reads the
+            # fp32 output back.  Copies run on their own streams with two device
+            # buffer sets, so step i+1's H2D and step i-1's D2H overlap step i.
             hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
-            hout = torch.empty(w.B, w.T, w.E, dtype=torch.float32).pin_memory()
+            hout = [torch.empty(w.B, w.T, w.E, dtype=torch.float32).pin_memory() for _ in range(2)]
+            dbuf = [[torch.empty(x.shape, dtype=x.dtype, device=dev) for x in (hq, hk, hv)] for _ in range(2)]
+            s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+            ev_in, ev_comp, ev_out = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
 
-            def e2e_step():
-                dq = hq.to(dev, non_blocking=True)
-                dk = hk.to(dev, non_blocking=True)
-                dv = hv.to(dev, non_blocking=True)
-                hout.copy_(mod(dq, dk, dv), non_blocking=True)
+            def e2e_step(i):
+                j = i % 2
+                with torch.cuda.stream(s_in):
+                    if i >= 2:
+                        s_in.wait_event(ev_comp[j])  # step i-2 no longer reads slot j
+                    for d, hx in zip(dbuf[j], (hq, hk, hv)):
+                        d.copy_(hx, non_blocking=True)
+                    ev_in[j].record(s_in)
+                stream.wait_event(ev_in[j])
+                o = mod(*dbuf[j])
+                ev_comp[j].record(stream)
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(ev_comp[j])
+                    if i >= 2:
+                        s_out.wait_event(ev_out[j])
+                    hout[j].copy_(o, non_blocking=True)
+                    ev_out[j].record(s_out)
+                o.record_stream(s_out)
 
-            for _ in range(2):
-                e2e_step()
-            e2e_ms = timed(e2e_step, max(2, args.steps // 2))
-            nb = max(2, args.steps // 2)
+            def e2e_timed(n):
+                barrier()
+                torch.cuda.synchronize(dev)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                s_in.wait_event(e0)
+                for i in range(n):
+                    e2e_step(i)
+                stream.wait_stream(s_out)
+                stream.wait_stream(s_in)
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
+                barrier()
+                ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+                if world > 1:
+                    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+                return float(ms.item())
+
+            e2e_timed(2)
+            nb = max(4, args.steps // 2)
+            e2e_ms = e2e_timed(nb)
             e2e = {"value": world * w.B * w.T * nb / (e2e_ms / 1e3), "unit": UNIT,
                    "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in (hq, hk, hv)),
-                   "d2h_bytes_per_step": hout.numel() * hout.element_size()}
+                   "d2h_bytes_per_step": hout[0].numel() * hout[0].element_size(),
+                   "overlap": "H2D, compute and D2H on separate streams, two device buffer sets"}
 
     if rank != 0:
         if world > 1:
