@@ -214,8 +214,8 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
       return *reinterpret_cast<const uint4*>(sm + L.k + kb * AR * 128 + r * 128 + ((j ^ (r & 7)) << 4));
     };
     float ksq = 0.f;
-    if (ok) {  // k_sq = DT(sum DT(k_d^2)) (quantizer.py:208)
-      double acc = 0.0;
+    if (ok) {  // k_sq = DT(sum DT(k_d^2)) (quantizer.py:208), fp64 partial sums
+      double acc[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll 4
       for (int v = 0; v < D / 8; ++v) {
         const uint4 u = key_chunk(v);
@@ -223,10 +223,10 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const uint32_t sq = hmul2_dt<DT>(w[e], w[e]);
-          acc += (double)half_lo<DT>(sq) + (double)half_hi<DT>(sq);
+          acc[e] += (double)half_lo<DT>(sq) + (double)half_hi<DT>(sq);
         }
       }
-      ksq = rnd64<DT>(acc);
+      ksq = rnd64<DT>((acc[0] + acc[1]) + (acc[2] + acc[3]));
     }
     const uint32_t ksq2 = dup2<DT>(ksq);
     int best = 0x7FFFFFFF;
@@ -236,35 +236,42 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[AB_SFULL + sb], (ci >> 1) & 1, abort));
       if (!ok) break;
       tc::tc_after_sync();
+      // four 32-column quarters; the next quarter's TMEM load is in flight
+      // while the current one is scanned
+      const uint32_t col = tbase + lane_off + ACH * sb;
+      uint32_t qa[32], qb[32];
+      auto scan = [&](const uint32_t (&r)[32], int quarter) {
+        const uint4* pp = reinterpret_cast<const uint4*>(ps2 + ci * (ACH / 2) + 16 * quarter);
+        const uint32_t base2 = (uint32_t)(ci * ACH + 32 * quarter) * 0x10001u + 0x10000u;
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t ra[32], rb[32];
-        const uint32_t col = tbase + lane_off + ACH * sb + 64 * hh;
-        tc::tmem_ld32(col, ra);
-        tc::tmem_ld32(col + 32, rb);
-        tc::tmem_wait_ld();
-        if (hh == 1) {
-          tc::tc_before_sync();
-          tc::mbar_arrive(&bars[AB_SCONS + sb]);
-        }
-        const uint4* pp = reinterpret_cast<const uint4*>(ps2 + ci * (ACH / 2) + 32 * hh);
-        const uint32_t base2 = (uint32_t)(ci * ACH + 64 * hh) * 0x10001u + 0x10000u;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < 4; ++q) {
           const uint4 pq = pp[q];
           const uint32_t pv[4] = {pq.x, pq.y, pq.z, pq.w};
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const int j = 4 * q + k;
-            const uint32_t a0 = j < 16 ? ra[2 * j] : rb[2 * j - 32], a1 = j < 16 ? ra[2 * j + 1] : rb[2 * j - 31];
-            const uint32_t x2 = pack2<DT>(__uint_as_float(a0), __uint_as_float(a1));       // DT(k . p)
+            const uint32_t x2 = pack2<DT>(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));  // DT(k . p)
             const uint32_t d2 = hsub2_dt<DT>(hadd2_dt<DT>(ksq2, pv[k]), hadd2_dt<DT>(x2, x2));
             nanacc = hmax2_nan_dt<DT>(nanacc, d2);
             const uint32_t k2 = order2(d2), idx2 = base2 + 0x20002u * (uint32_t)j;
             best = min(best, min(key_lo(k2, idx2), key_hi(k2, idx2)));
           }
         }
-      }
+      };
+      tc::tmem_ld32(col, qa);
+      tc::tmem_wait_ld();
+      tc::tmem_ld32(col + 32, qb);
+      scan(qa, 0);
+      tc::tmem_wait_ld();
+      tc::tmem_ld32(col + 64, qa);
+      scan(qb, 1);
+      tc::tmem_wait_ld();
+      tc::tmem_ld32(col + 96, qb);
+      scan(qa, 2);
+      tc::tmem_wait_ld();
+      tc::tc_before_sync();
+      tc::mbar_arrive(&bars[AB_SCONS + sb]);
+      scan(qb, 3);
     }
     int pbest = best & 0xFFFF;
     const bool has_nan = isnan(half_lo<DT>(nanacc)) || isnan(half_hi<DT>(nanacc));
@@ -297,7 +304,7 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
       for (int c0 = 0; c0 < C; c0 += 4) {
         double acc[4] = {0.0, 0.0, 0.0, 0.0};
         const int nc = min(4, C - c0);
-#pragma unroll 2
+#pragma unroll 4
         for (int v = 0; v < D / 8; ++v) {
           const uint4 u = key_chunk(v);
           const uint32_t ku[4] = {u.x, u.y, u.z, u.w};

@@ -358,11 +358,17 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       tc::tc_after_sync();
       const uint32_t col = tbase + lane_off + D + 64 * s;
       float zh[2];
+      // 32 parents at a time; the second half's TMEM load is in flight while
+      // the first half is computed (its exponentials go to columns 0-15, the
+      // load reads 32-63)
+      uint32_t rh[2][32];
+      tc::tmem_ld32(col, rh[0]);
+      tc::tmem_wait_ld();
+      tc::tmem_ld32(col + 32, rh[1]);
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {  // 32 parents at a time
-        uint32_t ra[32];
-        tc::tmem_ld32(col + 32 * hh, ra);
-        tc::tmem_wait_ld();
+      for (int hh = 0; hh < 2; ++hh) {
+        if (hh == 1) tc::tmem_wait_ld();
+        const uint32_t (&ra)[32] = rh[hh];
         // logits: DT(DT(acc) / sqrt(D)) (pipeline.py:81), branch-free fast
         // quotients; a half with a quotient near a rounding point is redone
         uint32_t s2[16];
@@ -473,7 +479,67 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     for (int p0 = 0, nb = 0; ok && p0 < M0; p0 += 128, ++nb) {
       const int p = p0 + 4 * lane;
       float cs[4] = {0.f, 0.f, 0.f, 0.f};
-      if (p < M0) {
+      auto srow_at = [&](int tw) {
+        return scratch + (((long)g * ntiles + (tw >> 6)) * 64 + (tw & 63)) * LDL + p;
+      };
+      // DT(e / z) of 4 rows x 4 columns added to cs in row order (branch-free
+      // fast quotients; a batch with one near a rounding point is redone)
+      auto add_batch = [&](const uint2 (&w)[4], const float2 (&zr)[4]) {
+        float y[4][4];
+        bool near = false;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float e[4] = {half_lo<DT>(w[i].x), half_hi<DT>(w[i].x), half_lo<DT>(w[i].y), half_hi<DT>(w[i].y)};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            y[i][k] = e[k] * zr[i].y;
+            near |= near_midpoint<DT>(y[i][k]);
+          }
+        }
+        if (near) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float e[4] = {half_lo<DT>(w[i].x), half_hi<DT>(w[i].x), half_lo<DT>(w[i].y), half_hi<DT>(w[i].y)};
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (near_midpoint<DT>(y[i][k])) y[i][k] = __fdiv_rn(e[k], zr[i].x);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t q01 = pack2<DT>(y[i][0], y[i][1]), q23 = pack2<DT>(y[i][2], y[i][3]);
+          cs[0] += half_lo<DT>(q01);
+          cs[1] += half_hi<DT>(q01);
+          cs[2] += half_lo<DT>(q23);
+          cs[3] += half_hi<DT>(q23);
+        }
+      };
+      if (p < M0 && t0 + TR <= Tq) {
+        // full tile: the next 4-row batch is loading while the current one is summed
+        uint2 wn[4];
+        float2 zn[4];
+        auto load = [&](int g4) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int rw = warp * 32 + g4 * 4 + i;
+            wn[i] = *reinterpret_cast<const uint2*>(srow_at(t0 + rw));
+            zn[i] = *reinterpret_cast<const float2*>(srow + rw * 4);
+          }
+        };
+        load(0);
+#pragma unroll 1
+        for (int g4 = 0; g4 < 8; ++g4) {
+          uint2 w[4];
+          float2 z[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            w[i] = wn[i];
+            z[i] = zn[i];
+          }
+          if (g4 + 1 < 8) load(g4 + 1);
+          add_batch(w, z);
+        }
+      } else if (p < M0) {
 #pragma unroll 1
         for (int g4 = 0; g4 < 8; ++g4) {
           const int rw0 = warp * 32 + g4 * 4;

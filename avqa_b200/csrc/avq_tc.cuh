@@ -48,13 +48,25 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or about `ns` nanoseconds pass (no issue slots spent spinning).
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 // Wait for the phase of `bar` with the given parity to complete.  Gives up
-// when *abort is set by another thread or after kWaitCycles, raising *abort.
+// when *abort is set by another thread (checked at least every millisecond)
+// or after kWaitCycles, raising *abort.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try(bar, parity)) return true;
+    if (mbar_try_sleep(bar, parity, 1000000u)) return true;
     if (*abort) return false;
     if (clock64() - t0 > kWaitCycles) {
       *abort = 1;
