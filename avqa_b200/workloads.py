@@ -87,9 +87,12 @@ def rope_rotate(x: torch.Tensor, positions: torch.Tensor, base: float = 10000.0)
     return torch.cat([x1 * cos - x2 * sin, x1 * sin + x2 * cos], dim=-1)
 
 
-def make_keys(w: Workload, B: int, S: int, gen: torch.Generator, device="cpu", pos0: int = 0) -> torch.Tensor:
-    """Keys ``[B, S, E]`` in fp32 following ``w.keys``."""
+def make_keys(w: Workload, B: int, S: int, gen: torch.Generator, device="cpu", pos0: int = 0,
+              sample_gen: torch.Generator | None = None) -> torch.Tensor:
+    """Keys ``[B, S, E]`` in fp32 following ``w.keys``.  The mixture's centres
+    come from ``gen``; the samples from ``sample_gen`` (default ``gen``)."""
     H, D = w.H, w.D
+    sgen = gen if sample_gen is None else sample_gen
     if w.keys == "readme":
         raise ValueError("readme keys are generated together with q/v")
     if w.keys in ("mixture", "aniso", "mixture_rope"):
@@ -98,9 +101,9 @@ def make_keys(w: Workload, B: int, S: int, gen: torch.Generator, device="cpu", p
         scale = None
         if w.keys == "aniso":
             scale = torch.rand(H, nc, D, generator=gen, device=device) * 0.9 + 0.1
-        idx = torch.randint(0, nc, (B, H, S), generator=gen, device=device)
+        idx = torch.randint(0, nc, (B, H, S), generator=sgen, device=device)
         hix = torch.arange(H, device=device)[None, :, None].expand(B, H, S)
-        noise = torch.randn(B, H, S, D, generator=gen, device=device)
+        noise = torch.randn(B, H, S, D, generator=sgen, device=device)
         if scale is None:
             k = centres[hix, idx] + w.sigma * noise
         else:
@@ -109,17 +112,20 @@ def make_keys(w: Workload, B: int, S: int, gen: torch.Generator, device="cpu", p
             k = rope_rotate(k, torch.arange(pos0, pos0 + S, device=device))
         return k.transpose(1, 2).reshape(B, S, H * D).contiguous()
     if w.keys == "student_t":
-        z = torch.randn(B, S, H * D, generator=gen, device=device)
-        chi = (torch.randn(3, B, S, H * D, generator=gen, device=device) ** 2).sum(0)
+        z = torch.randn(B, S, H * D, generator=sgen, device=device)
+        chi = (torch.randn(3, B, S, H * D, generator=sgen, device=device) ** 2).sum(0)
         return 0.5 * z / torch.sqrt(chi / 3.0)
     raise ValueError(f"unknown key recipe {w.keys!r}")
 
 
-def make_inputs(w: Workload, device="cpu", B: int | None = None, T: int | None = None, S: int | None = None):
+def make_inputs(w: Workload, device="cpu", B: int | None = None, T: int | None = None, S: int | None = None,
+                part: int = 0):
     """Return fp32 ``(q [B,T,E], k [B,S,E], v [B,S,E])`` for workload ``w``.
 
     ``B``/``T``/``S`` override the sizes (parity tests use reduced sizes with
-    the same distributions).
+    the same distributions).  ``part`` > 0 draws another batch of the same
+    distribution: the same mixture centres, independent samples (the batch
+    shards of one global batch across ranks).
     """
     B = w.B if B is None else B
     T = w.T if T is None else T
@@ -132,9 +138,11 @@ def make_inputs(w: Workload, device="cpu", B: int | None = None, T: int | None =
         v = torch.randn(B, S, E)
         return q.to(device), k.to(device), v.to(device)
     gen = torch.Generator(device=device).manual_seed(w.seed)
-    k = make_keys(w, B, S, gen, device)
-    q = torch.randn(B, T, E, generator=gen, device=device)
-    v = torch.randn(B, S, E, generator=gen, device=device)
+    sgen = None if part == 0 else torch.Generator(device=device).manual_seed(w.seed + 7919 * part)
+    k = make_keys(w, B, S, gen, device, sample_gen=sgen)
+    g2 = gen if sgen is None else sgen
+    q = torch.randn(B, T, E, generator=g2, device=device)
+    v = torch.randn(B, S, E, generator=g2, device=device)
     return q, k, v
 
 

@@ -12,7 +12,8 @@ child correction, fp32 output.  The inputs (0.8 GB) exceed the 126 MB L2,
 so no flush is needed between steps.
 
 Multi-GPU (torchrun, one rank per GPU): weak scaling -- every rank processes
-its own batch of 4 (different seeds); the ranks form one global batch, so the
+its own batch of 4 (its shard of one global batch: the same key mixture,
+independent samples); the ranks form one global batch, so the
 routing budget min(P, min over all (b,h) of non-empty parents) is an
 all-reduce(MIN) over NCCL each step, exactly as one reference call over the
 concatenated batch would compute it.
@@ -220,6 +221,11 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    try:  # all host threads for the CPU implementation (torchrun sets OMP_NUM_THREADS=1)
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(os.cpu_count())
+    except Exception:
+        pass
     from avqa_b200.workloads import WORKLOADS
     w = WORKLOADS[args.workload]
     times = []
@@ -267,8 +273,8 @@ def run_ours(args) -> None:
     _, k0, _ = make_inputs(w, device=dev, B=1, T=1)
     cb = codebook_from_keys(k0.to(dt).view(1, w.S, H, D).transpose(1, 2)[0].float(), w.M0, w.C, w.seed)
     del k0
-    wr = Workload(**{**w.__dict__, "seed": w.seed + 7919 * rank})
-    q, k, v = make_inputs(wr, device=dev)
+    # rank r holds batch shard r of one global batch: the same key mixture, its own samples
+    q, k, v = make_inputs(w, device=dev, part=rank)
     q, k, v = q.to(dt), k.to(dt), v.to(dt)
     cfg = AVQConfig(attention=AttentionShapeConfig(embed_dim=w.E, num_heads=H),
                     codebook=CodebookConfig(num_codewords=w.M0, children_per_codeword=w.C),
