@@ -284,7 +284,8 @@ int avq_device_fault(int* code, void* stream) {
 // keep them in order on one stream.  No byte of the array needs a known
 // starting value: the histogram kernel writes all M0 bins of every segment
 // (or a memset zeroes them when S == 0), the scan writes every offset and the
-// scatter writes every key position before anything reads them.
+// scatter writes every key position, and the aggregation's work counter is
+// zeroed by a memset, before anything reads them.
 
 namespace {
 

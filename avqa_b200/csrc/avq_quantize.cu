@@ -12,6 +12,8 @@
 //
 // Index work is exact.  Dot products here accumulate in double, so every
 // distance equals the exactly rounded reference value.
+#include <algorithm>
+
 #include "avq_kernels.cuh"
 #include "avq_mma.cuh"
 
@@ -519,7 +521,7 @@ __global__ void __launch_bounds__(AG_WARPS * 32) aggregate_vec_kernel(
     const int* __restrict__ order, const int* __restrict__ poff, const int* __restrict__ pcnt,
     const int* __restrict__ cassign, typename Storage<DT>::T* __restrict__ pagg,
     typename Storage<DT>::T* __restrict__ cagg, float* __restrict__ pacc, float* __restrict__ cacc,
-    int* __restrict__ ccnt, long rows) {
+    int* __restrict__ ccnt, long rows, int* __restrict__ next_row) {
   using T = typename Storage<DT>::T;
   struct alignas(VPL * sizeof(T)) V {
     T e[VPL];
@@ -527,9 +529,14 @@ __global__ void __launch_bounds__(AG_WARPS * 32) aggregate_vec_kernel(
   constexpr int D = 32 * VPL, AG_RING = sizeof(T) == 4 ? 8 : 16, SB = VPL * (int)sizeof(T);
   __shared__ __align__(16) T ring_all[AG_WARPS][AG_RING][D];
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-  const long gp = (long)blockIdx.x * AG_WARPS + wib;
-  if (gp >= rows) return;
   T (*ring)[D] = ring_all[wib];
+  // persistent warps: each takes the next parent from a counter, so a long
+  // member list never holds up the other warps of its block
+  for (;;) {
+  int gnext = 0;
+  if (lane == 0) gnext = atomicAdd(next_row, 1);
+  const long gp = __shfl_sync(0xffffffffu, gnext, 0);
+  if (gp >= rows) break;
   const int g = (int)(gp / M0), b = g / H, h = g % H;
   const T* vbase = values + (long)b * vs.b + (long)h * vs.h + lane * VPL;
   float ap[VPL], ac[CMAX][VPL];
@@ -612,6 +619,7 @@ __global__ void __launch_bounds__(AG_WARPS * 32) aggregate_vec_kernel(
     }
   }
   if (lane < C) ccnt[gp * C + lane] = cn;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -640,7 +648,7 @@ size_t quantize_workspace_bytes(int G, int S, int M0) {
   int seg_len;
   const int nseg = bucket_segments(S, M0, &seg_len);
   return align_up((size_t)G * nseg * M0 * sizeof(int)) + align_up((size_t)G * (S > 0 ? S : 1) * sizeof(int)) +
-         align_up((size_t)G * M0 * sizeof(int));
+         align_up((size_t)G * M0 * sizeof(int)) + align_up(sizeof(int));
 }
 
 template <int DT>
@@ -656,6 +664,8 @@ int launch_quantize(const QuantizeArgs& a, cudaStream_t st) {
   int* order = (int*)ws;
   ws += align_up((size_t)G * (a.S > 0 ? a.S : 1) * sizeof(int));
   int* poff = (int*)ws;
+  ws += align_up((size_t)G * a.M0 * sizeof(int));
+  int* agg_next = (int*)ws;  // work counter of the persistent aggregation warps
   if (a.S > 0) {
     const bool aligned = ((uintptr_t)a.keys % 16 == 0) && a.ks.s % 8 == 0 && a.ks.h % 8 == 0 && a.ks.b % 8 == 0;
     bool done = false;
@@ -706,10 +716,14 @@ int launch_quantize(const QuantizeArgs& a, cudaStream_t st) {
   const unsigned blocks = (unsigned)((rows + 7) / 8);
   const bool valigned = ((uintptr_t)a.values % 16 == 0) && a.vs.s % 8 == 0 && a.vs.h % 8 == 0 && a.vs.b % 8 == 0;
   if (valigned && (a.D == 64 || a.D == 128)) {
-#define AVQ_AGGV(CM, VP)                                                                                              \
-  aggregate_vec_kernel<DT, CM, VP><<<blocks, 256, 0, st>>>((const T*)a.values, a.vs, a.H, a.S, a.M0, a.C, order, poff, \
-                                                           a.pcnt, a.cassign, (T*)a.pagg, (T*)a.cagg, a.pacc, a.cacc,  \
-                                                           a.ccnt, rows)
+    int dev = 0, nsm = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const unsigned pblocks = (unsigned)std::min<long>((long)blocks, (long)nsm * 8);
+    cudaMemsetAsync(agg_next, 0, sizeof(int), st);
+#define AVQ_AGGV(CM, VP)                                                                                         \
+  aggregate_vec_kernel<DT, CM, VP><<<pblocks, 256, 0, st>>>((const T*)a.values, a.vs, a.H, a.S, a.M0, a.C, order, \
+                                                            poff, a.pcnt, a.cassign, (T*)a.pagg, (T*)a.cagg,     \
+                                                            a.pacc, a.cacc, a.ccnt, rows, agg_next)
     if (a.C <= 4) {
       if (a.D == 64) AVQ_AGGV(4, 2); else AVQ_AGGV(4, 4);
     } else {

@@ -84,7 +84,7 @@ int avq_quantize(int dtype, const void* keys, const long long* key_strides, cons
  *
  * Arguments, outputs and results are those of avq_quantize (same kernels);
  * only `workspace`/`workspace_bytes` are gone.  The quantizer's scratch --
- * bucket histograms, key order, bucket offsets -- lives in a file-scope
+ * bucket histograms, key order, bucket offsets, a work counter -- lives in a file-scope
  * device array compiled into the library, so the call allocates nothing.
  *
  * Who needs it: a host whose device memory is owned by someone else -- a
