@@ -27,7 +27,10 @@
 
 namespace avq {
 
-extern __device__ int g_device_fault;
+namespace {
+// Bit 0: a CTA of this file gave up on a bounded wait.
+__device__ int g_fault;
+}  // namespace
 
 namespace {
 
@@ -342,7 +345,7 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
     tc::tc_after_sync();
     tc::tmem_free(tbase, A_TMEM_COLS);
   }
-  if (tid == 0 && *abort) atomicOr(&g_device_fault, 1);
+  if (tid == 0 && *abort) atomicOr(&g_fault, 1);
 }
 
 }  // namespace
@@ -379,5 +382,20 @@ int launch_assign_tc(const QuantizeArgs& a, cudaStream_t st) {
 
 template int launch_assign_tc<DT_BF16>(const QuantizeArgs&, cudaStream_t);
 template int launch_assign_tc<DT_F16>(const QuantizeArgs&, cudaStream_t);
+
+
+// Reads and clears this file's fault word (device code without relocatable
+// linking keeps one copy per file, so every kernel file has its own).
+int read_fault_assign(int* code, cudaStream_t st) {
+  int v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, g_fault, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return AVQ_ERR_CUDA;
+  const int zero = 0;
+  if (cudaMemcpyToSymbolAsync(g_fault, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return AVQ_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return AVQ_ERR_CUDA;
+  *code = v;
+  return AVQ_OK;
+}
 
 }  // namespace avq

@@ -32,7 +32,10 @@
 
 namespace avq {
 
-extern __device__ int g_device_fault;
+namespace {
+// Bit 0: a CTA of this file gave up on a bounded wait.
+__device__ int g_fault;
+}  // namespace
 
 namespace {
 
@@ -43,10 +46,11 @@ constexpr uint32_t EXPB = 0x3AFF;  // exponential table (same layout as the pare
 constexpr int EXPN = 2051;
 
 constexpr int CB_Q = 0, CB_FULL = 1, CB_EMPTY = 4, CB_SFULL = 7, CB_SFREE = 8, CB_WFULL = 9, CB_WFREE = 10,
-              CB_OFULL = 11, CN_BARS = 12;
+              CB_OFULL = 11, CB_XCH = 12, CB_XFREE = 13, CN_BARS = 14;
 
 constexpr int NBUF = 3;         // gathered slot buffers
-constexpr int CTHREADS2 = 160;  // 4 row warps + the MMA / TMA warp
+constexpr int CTHREADS2 = 288;  // 8 row warps (two threads per query) + the MMA / TMA warp
+constexpr int MW = 8;           // the MMA / TMA warp
 
 struct CorrLayout {
   int q, l[NBUF], v[NBUF], meta[NBUF], exptab, bars, misc, total;
@@ -177,24 +181,27 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
 
   if (tid == 0) {
     for (int i = 0; i < CN_BARS; ++i) {
-      const int cnt = ((i >= CB_FULL && i < CB_FULL + NBUF) || i == CB_SFREE || i == CB_WFULL) ? CR : 1;
+      const int cnt = ((i >= CB_FULL && i < CB_FULL + NBUF) || i == CB_SFREE || i == CB_WFULL || i == CB_XCH ||
+                       i == CB_XFREE)
+                          ? 2 * CR
+                          : 1;
       tc::mbar_init(&bars[i], cnt);
     }
     *abort = 0;
     tc::fence_mbar_init();
   }
-  if (warp == 4) tc::tmem_alloc(tslot, C_TMEM_COLS);
-  if (tid < CR) {
+  if (warp == MW) tc::tmem_alloc(tslot, C_TMEM_COLS);
+  if (tid < 2 * CR) {
     const uint32_t* src = reinterpret_cast<const uint32_t*>(exptab_g);
     uint32_t* dst = reinterpret_cast<uint32_t*>(sm + L.exptab);
-    for (int i = tid; i < (EXPN + 1) / 2; i += CR) dst[i] = src[i];
+    for (int i = tid; i < (EXPN + 1) / 2; i += 2 * CR) dst[i] = src[i];
   }
   tc::tc_before_sync();
   __syncthreads();
   tc::tc_after_sync();
   const uint32_t tbase = *tslot;
 
-  if (warp == 4) {
+  if (warp == MW) {
     // ---- Q tile (TMA) and MMA issue ----
     if (lane == 0) {
       tc::tma_prefetch_desc(&tm_q);
@@ -252,20 +259,23 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
       if (!ok) drain_c(&bars[CB_OFULL], 0);
     }
   } else {
-    // ---- row threads: query r; threads 0-95 also gather one slot row each ----
-    const int r = tid, t = t0 + r;
+    // ---- row threads: two per query.  Warps 0-3 (half 0) and 4-7 (half 1)
+    // both reach TMEM lane r; half h takes slots 24h..24h+23 of every group
+    // and the output columns [h D/2, (h+1) D/2).  Threads r < 48 of half 0
+    // gather the logit row of slot r, those of half 1 its value row.
+    const int hf = tid >> 7, r = tid & (CR - 1), t = t0 + r;
     const bool live = t < Tq;
     const long row = (long)g * Tq + (live ? t : 0);
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    constexpr int XCOL = WCOL + 3 * (NS / 2);  // 8 free columns: the halves' weight sums
+    static_assert(XCOL + 8 <= C_TMEM_COLS, "TMEM columns");
     const float inv_sqrtD = 1.f / sqrtD;
     const float m = live ? m_in[row] : 0.f;
     const float zc = clamp_min_nan(live ? z_in[row] : 1.f, eps_dt<DT>()), rz = 1.f / zc;
     const float bt = beta_in && live ? beta_in[row] : 0.f;
     float l = live ? l_in[row] : 1.f;
-    // gather role: thread r < 48 copies the logit row of slot r (and writes its
-    // metadata), 48 <= r < 96 the value row of slot r - 48
-    const int gslot = r < NS ? r : r - NS;
-    const bool gathers = r < 2 * NS, isv = r >= NS;
+    const int gslot = r;
+    const bool gathers = r < NS, isv = hf == 1;
     const SlotDesc* dg = desc + (long)g * maxgroups * NS + gslot;
     auto gather = [&](int kg, const SlotDesc& d) {
       const int bf = kg % NBUF;
@@ -306,14 +316,14 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
     else cp_async_commit();
     cp_async_wait<1>();
     if (ngroups > 0) publish(0);
-    // O = a (attention.py:154-158)
+    // O = a (attention.py:154-158), this half's columns
 #pragma unroll
-    for (int d0 = 0; d0 < D; d0 += 32) {
+    for (int d0 = 0; d0 < D / 2; d0 += 32) {
+      const int dc = hf * (D / 2) + d0;
       uint32_t o[32];
-      const uint4* src = reinterpret_cast<const uint4*>(a_in + row * D + d0);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const uint4 u = live ? src[k] : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 u = live ? reinterpret_cast<const uint4*>(a_in + row * D + dc)[k] : make_uint4(0u, 0u, 0u, 0u);
         const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -321,11 +331,11 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
           o[8 * k + 2 * e + 1] = __float_as_uint(half_hi<DT>(w[e]));
         }
       }
-      tc::tmem_st32(tbase + lane_off + OCOL + d0, o);
+      tc::tmem_st32(tbase + lane_off + OCOL + dc, o);
     }
     tc::tmem_wait_st();
     bool ok = true;
-    int kg = 0;
+    int kg = 0, npass_done = 0;
     for (int ps = 0; ok && ps < npass; ++ps) {
       const int cnt = pass_cnt[ps];
       if (cnt <= 0) break;
@@ -336,16 +346,15 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
                                          tc::mbar_wait(&bars[CB_FULL + bf], (kg / NBUF) & 1, abort));
         if (!ok) break;
         tc::tc_after_sync();
-        uint32_t sv[2][24];
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
+        uint32_t sv[24];
+        {
           uint32_t sa[16], sb[8];
-          tc::tmem_ld16(tbase + lane_off + SCOL + 24 * half, sa);
-          tc::tmem_ld8(tbase + lane_off + SCOL + 24 * half + 16, sb);
+          tc::tmem_ld16(tbase + lane_off + SCOL + 24 * hf, sa);
+          tc::tmem_ld8(tbase + lane_off + SCOL + 24 * hf + 16, sb);
+          tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 24; ++i) sv[half][i] = i < 16 ? sa[i] : sb[i - 16];
+          for (int i = 0; i < 24; ++i) sv[i] = i < 16 ? sa[i] : sb[i - 16];
         }
-        tc::tmem_wait_ld();
         tc::tc_before_sync();
         tc::mbar_arrive(&bars[CB_SFREE]);
         // gather group kg + 2 into the buffer of group kg - 1, publish group kg + 1
@@ -363,89 +372,112 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
         if (kg + 1 < ngroups) publish(kg + 1);
         if (gathers && kg + 3 < ngroups) dn2 = dg[(long)(kg + 3) * NS];
         const float* meta = reinterpret_cast<const float*>(sm + L.meta[bf]);
+        // logits DT(DT(acc) / sqrt(D)), branch-free fast quotients with an
+        // exact redo when one is near a rounding point
+        float sl[24];
+        bool near = false;
+#pragma unroll
+        for (int i2 = 0; i2 < 12; ++i2) {
+          const int i = 2 * i2;
+          const uint32_t x2 = pack2<DT>(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1]));
+          const float y0 = half_lo<DT>(x2) * inv_sqrtD, y1 = half_hi<DT>(x2) * inv_sqrtD;
+          near |= near_midpoint<DT>(y0) | near_midpoint<DT>(y1);
+          const uint32_t s2 = pack2<DT>(y0, y1);
+          sl[i] = half_lo<DT>(s2);
+          sl[i + 1] = half_hi<DT>(s2);
+        }
+        if (near) {
+#pragma unroll
+          for (int i = 0; i < 24; ++i) sl[i] = scale_logit<DT>(rnd<DT>(__uint_as_float(sv[i])), sqrtD, inv_sqrtD);
+        }
+        // weights (fp32; refinement.py:335,341-343): -exp(pi - m) n for a parent,
+        // exp(u - m) n_c for a child, 0 for an empty slot
+        const float4* mn4 = reinterpret_cast<const float4*>(meta + 24 * hf);
+        const float4* mk4 = reinterpret_cast<const float4*>(meta + NS + 24 * hf);
+        float wv[24];
+        float rlg = 0.f, alg = 0.f;
+#pragma unroll
+        for (int q = 0; q < 6; ++q) {
+          const float4 n4 = mn4[q], k4 = mk4[q];
+          const float nv[4] = {n4.x, n4.y, n4.z, n4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = 4 * q + e, k = 24 * hf + i;
+            float w = 0.f;
+            if (k < NREAL) {
+              float s = kv[e] > 0.f ? sl[i] : -INFINITY;
+              if (k < J) {
+                if (beta_in) s = rnd<DT>(__fmul_rn(bt, rnd<DT>(__fmul_rn(s, sqrtD))));
+                const float ex = exp_bf16_tab(rnd<DT>(s - m), exptab);
+                const float pi = div_dt_fast<DT>(ex, rz, zc);
+                w = nv[e] >= 0.f ? __expf(pi - m) * nv[e] : 0.f;
+                rlg += w;
+                w = -w;
+              } else {
+                w = nv[e] >= 0.f ? __expf(s - m) * nv[e] : 0.f;
+                alg += w;
+              }
+            }
+            wv[i] = w;
+          }
+        }
+        rl += (double)rlg;
+        al += (double)alg;
+        // three bf16 parts per weight (w = hi + mid + lo to 24 bits), packed in pairs
+        uint32_t wp[3][12];
+#pragma unroll
+        for (int i2 = 0; i2 < 12; ++i2) {
+          const float w0 = wv[2 * i2], w1 = wv[2 * i2 + 1];
+          const uint32_t h2 = pack2<DT_BF16>(w0, w1);
+          const float r0 = w0 - half_lo<DT_BF16>(h2), r1 = w1 - half_hi<DT_BF16>(h2);
+          const uint32_t m2 = pack2<DT_BF16>(r0, r1);
+          wp[0][i2] = h2;
+          wp[1][i2] = m2;
+          wp[2][i2] = pack2<DT_BF16>(r0 - half_lo<DT_BF16>(m2), r1 - half_hi<DT_BF16>(m2));
+        }
         if (kg > 0) {  // the previous group's value MMAs have read the weight columns
           ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[CB_WFREE], (kg - 1) & 1, abort));
           if (!ok) break;
           tc::tc_after_sync();
         }
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {  // 24 slots at a time
-          // logits DT(DT(acc) / sqrt(D)), branch-free fast quotients with an
-          // exact redo when one is near a rounding point
-          float sl[24];
-          bool near = false;
-#pragma unroll
-          for (int i2 = 0; i2 < 12; ++i2) {
-            const int i = 2 * i2;
-            const uint32_t x2 = pack2<DT>(__uint_as_float(sv[half][i]), __uint_as_float(sv[half][i + 1]));
-            const float y0 = half_lo<DT>(x2) * inv_sqrtD, y1 = half_hi<DT>(x2) * inv_sqrtD;
-            near |= near_midpoint<DT>(y0) | near_midpoint<DT>(y1);
-            const uint32_t s2 = pack2<DT>(y0, y1);
-            sl[i] = half_lo<DT>(s2);
-            sl[i + 1] = half_hi<DT>(s2);
-          }
-          if (near) {
-#pragma unroll
-            for (int i = 0; i < 24; ++i)
-              sl[i] = scale_logit<DT>(rnd<DT>(__uint_as_float(sv[half][i])), sqrtD, inv_sqrtD);
-          }
-          // weights (fp32; refinement.py:335,341-343): -exp(pi - m) n for a parent,
-          // exp(u - m) n_c for a child, 0 for an empty slot
-          const float4* mn4 = reinterpret_cast<const float4*>(meta + 24 * half);
-          const float4* mk4 = reinterpret_cast<const float4*>(meta + NS + 24 * half);
-          float wv[24];
-          float rlg = 0.f, alg = 0.f;
-#pragma unroll
-          for (int q = 0; q < 6; ++q) {
-            const float4 n4 = mn4[q], k4 = mk4[q];
-            const float nv[4] = {n4.x, n4.y, n4.z, n4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i = 4 * q + e, k = 24 * half + i;
-              float w = 0.f;
-              if (k < NREAL) {
-                float s = kv[e] > 0.f ? sl[i] : -INFINITY;
-                if (k < J) {
-                  if (beta_in) s = rnd<DT>(__fmul_rn(bt, rnd<DT>(__fmul_rn(s, sqrtD))));
-                  const float ex = exp_bf16_tab(rnd<DT>(s - m), exptab);
-                  const float pi = div_dt_fast<DT>(ex, rz, zc);
-                  w = nv[e] >= 0.f ? __expf(pi - m) * nv[e] : 0.f;
-                  rlg += w;
-                  w = -w;
-                } else {
-                  w = nv[e] >= 0.f ? __expf(s - m) * nv[e] : 0.f;
-                  alg += w;
-                }
-              }
-              wv[i] = w;
-            }
-          }
-          rl += (double)rlg;
-          al += (double)alg;
-          // three bf16 parts per weight (w = hi + mid + lo to 24 bits), packed in pairs
-          uint32_t wp[3][12];
-#pragma unroll
-          for (int i2 = 0; i2 < 12; ++i2) {
-            const float w0 = wv[2 * i2], w1 = wv[2 * i2 + 1];
-            const uint32_t h2 = pack2<DT_BF16>(w0, w1);
-            const float r0 = w0 - half_lo<DT_BF16>(h2), r1 = w1 - half_hi<DT_BF16>(h2);
-            const uint32_t m2 = pack2<DT_BF16>(r0, r1);
-            wp[0][i2] = h2;
-            wp[1][i2] = m2;
-            wp[2][i2] = pack2<DT_BF16>(r0 - half_lo<DT_BF16>(m2), r1 - half_hi<DT_BF16>(m2));
-          }
-#pragma unroll
-          for (int part = 0; part < 3; ++part) {
-            tc::tmem_st8(tbase + lane_off + WCOL + part * (NS / 2) + 12 * half, wp[part]);
-            tc::tmem_st4(tbase + lane_off + WCOL + part * (NS / 2) + 12 * half + 8, wp[part] + 8);
-          }
+        for (int part = 0; part < 3; ++part) {
+          tc::tmem_st8(tbase + lane_off + WCOL + part * (NS / 2) + 12 * hf, wp[part]);
+          tc::tmem_st4(tbase + lane_off + WCOL + part * (NS / 2) + 12 * hf + 8, wp[part] + 8);
         }
         tc::tmem_wait_st();
         tc::tc_before_sync();
         tc::mbar_arrive(&bars[CB_WFULL]);
       }
-      // OnlineSoftmaxState.replace with unit scales (attention.py:149-153)
-      l = __fadd_rn(__fsub_rn(l, __double2float_rn(rl)), __double2float_rn(al));
+      if (!ok) break;
+      // the two halves' weight sums meet in TMEM; OnlineSoftmaxState.replace
+      // with unit scales (attention.py:149-153)
+      if (npass_done > 0) {
+        ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[CB_XFREE], (npass_done - 1) & 1, abort));
+        if (!ok) break;
+        tc::tc_after_sync();
+      }
+      {
+        const unsigned long long rb = __double_as_longlong(rl), ab = __double_as_longlong(al);
+        const uint32_t xv[4] = {(uint32_t)rb, (uint32_t)(rb >> 32), (uint32_t)ab, (uint32_t)(ab >> 32)};
+        tc::tmem_st4(tbase + lane_off + XCOL + 4 * hf, xv);
+        tc::tmem_wait_st();
+      }
+      tc::tc_before_sync();
+      tc::mbar_arrive(&bars[CB_XCH]);
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[CB_XCH], npass_done & 1, abort));
+      if (!ok) break;
+      tc::tc_after_sync();
+      uint32_t xo[4];
+      tc::tmem_ld4(tbase + lane_off + XCOL + 4 * (1 - hf), xo);
+      tc::tmem_wait_ld();
+      tc::tc_before_sync();
+      tc::mbar_arrive(&bars[CB_XFREE]);
+      const double rlo = __longlong_as_double((long long)(((unsigned long long)xo[1] << 32) | xo[0]));
+      const double alo = __longlong_as_double((long long)(((unsigned long long)xo[3] << 32) | xo[2]));
+      const double rlt = hf == 0 ? rl + rlo : rlo + rl, alt = hf == 0 ? al + alo : alo + al;
+      l = __fadd_rn(__fsub_rn(l, __double2float_rn(rlt)), __double2float_rn(alt));
+      ++npass_done;
     }
     cp_async_wait<0>();
     if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[CB_OFULL], 0, abort));
@@ -454,14 +486,15 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
       const float rden = __fdiv_rn(1.f, clamp_min_nan(l, 1e-12f));
       float* orow = out + (long)b * os.b + (long)(live ? t : 0) * os.s + (long)h * os.h;
 #pragma unroll
-      for (int d0 = 0; d0 < D; d0 += 32) {
+      for (int d0 = 0; d0 < D / 2; d0 += 32) {
+        const int dc = hf * (D / 2) + d0;
         uint32_t o[32];
-        tc::tmem_ld32(tbase + lane_off + OCOL + d0, o);
+        tc::tmem_ld32(tbase + lane_off + OCOL + dc, o);
         tc::tmem_wait_ld();
         if (live) {
 #pragma unroll
           for (int k = 0; k < 8; ++k)
-            *reinterpret_cast<float4*>(orow + d0 + 4 * k) =
+            *reinterpret_cast<float4*>(orow + dc + 4 * k) =
                 make_float4(__uint_as_float(o[4 * k]) * rden, __uint_as_float(o[4 * k + 1]) * rden,
                             __uint_as_float(o[4 * k + 2]) * rden, __uint_as_float(o[4 * k + 3]) * rden);
         }
@@ -471,11 +504,11 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
 
   tc::tc_before_sync();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == MW) {
     tc::tc_after_sync();
     tc::tmem_free(tbase, C_TMEM_COLS);
   }
-  if (tid == 0 && *abort) atomicOr(&g_device_fault, 1);
+  if (tid == 0 && *abort) atomicOr(&g_fault, 1);
 }
 
 }  // namespace
@@ -524,6 +557,21 @@ int launch_correct_tc(const CorrArgs& a, const void* exptab, void* desc, cudaStr
     if (D == 64) go(corr_desc_kernel<8>, correct_tc_kernel<64, 8>); else go(corr_desc_kernel<8>, correct_tc_kernel<128, 8>);
   }
   return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
+}
+
+
+// Reads and clears this file's fault word (device code without relocatable
+// linking keeps one copy per file, so every kernel file has its own).
+int read_fault_correct(int* code, cudaStream_t st) {
+  int v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, g_fault, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return AVQ_ERR_CUDA;
+  const int zero = 0;
+  if (cudaMemcpyToSymbolAsync(g_fault, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return AVQ_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return AVQ_ERR_CUDA;
+  *code = v;
+  return AVQ_OK;
 }
 
 }  // namespace avq

@@ -176,8 +176,11 @@ int launch_correct_tc(const CorrArgs& a, const void* exptab, void* desc, cudaStr
 bool assign_tc_ok(int dt, int D, int M0);
 template <int DT>
 int launch_assign_tc(const QuantizeArgs& a, cudaStream_t st);
-// Reads and clears the device fault record (stream-synchronous).
+// Reads and clears the device fault record (stream-synchronous): the OR of
+// the fault words of the tcgen05 kernel files.
 int read_device_fault(int* code, cudaStream_t st);
+int read_fault_assign(int* code, cudaStream_t st);
+int read_fault_correct(int* code, cudaStream_t st);
 
 template <int DT>
 int launch_append(const AppendArgs& a, cudaStream_t st);

@@ -38,8 +38,10 @@
 
 namespace avq {
 
-// Bit 0: a kernel gave up on a bounded wait (read by avq_device_fault).
-__device__ int g_device_fault;
+namespace {
+// Bit 0: a CTA of this file gave up on a bounded wait (read by avq_device_fault).
+__device__ int g_fault;
+}  // namespace
 
 namespace {
 
@@ -617,7 +619,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     tc::tc_after_sync();
     tc::tmem_free(tbase, TC_TMEM_COLS);
   }
-  if (tid == 0 && *abort) atomicOr(&g_device_fault, 1);
+  if (tid == 0 && *abort) atomicOr(&g_fault, 1);
 }
 
 // ---- host side ----------------------------------------------------------------
@@ -667,14 +669,15 @@ template int launch_parent_attn_tc<DT_BF16>(const PAArgs&, void*, cudaStream_t);
 template int launch_parent_attn_tc<DT_F16>(const PAArgs&, void*, cudaStream_t);
 
 int read_device_fault(int* code, cudaStream_t st) {
-  int v = 0;
-  if (cudaMemcpyFromSymbolAsync(&v, g_device_fault, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+  int v = 0, va = 0, vc = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, g_fault, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
     return AVQ_ERR_CUDA;
   const int zero = 0;
-  if (cudaMemcpyToSymbolAsync(g_device_fault, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
+  if (cudaMemcpyToSymbolAsync(g_fault, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
     return AVQ_ERR_CUDA;
   if (cudaStreamSynchronize(st) != cudaSuccess) return AVQ_ERR_CUDA;
-  *code = v;
+  if (read_fault_assign(&va, st) != AVQ_OK || read_fault_correct(&vc, st) != AVQ_OK) return AVQ_ERR_CUDA;
+  *code = v | va | vc;
   return AVQ_OK;
 }
 
