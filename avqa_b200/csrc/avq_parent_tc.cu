@@ -56,7 +56,7 @@ constexpr int TC_MAX_M0 = 2048;
 
 // Barrier slots.
 constexpr int B_Q = 0, B_PFULL = 1, B_PEMPTY = 3, B_VFULL = 5, B_VEMPTY = 7, B_SFULL = 9, B_EFULL = 11, B_SFREE = 13,
-              B_OFULL = 14, B_COMB = 15, N_BARS = 16;
+              B_OFULL = 14, B_COMB = 15, B_STG = 16, N_BARS = 18;
 
 struct TcLayout {
   int q, p[2], v[2], exptab, pm2, n2, srow, scomb, bars, misc, total;
@@ -178,7 +178,8 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
 
   // ---- setup: barriers, TMEM, tables ----
   if (tid == 0) {
-    for (int i = 0; i < N_BARS; ++i) tc::mbar_init(&bars[i], (i == B_EFULL || i == B_EFULL + 1 || i == B_COMB) ? TR : 1);
+    for (int i = 0; i < N_BARS; ++i)
+      tc::mbar_init(&bars[i], (i == B_EFULL || i == B_EFULL + 1 || i == B_COMB || i == B_STG || i == B_STG + 1) ? TR : 1);
     *abort = 0;
     tc::fence_mbar_init();
   }
@@ -475,141 +476,83 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     srow[r * 4 + 1] = 1.f / zc;
     srow[r * 4 + 2] = live ? 1.f : 0.f;
     __syncwarp();
-    // pass 3: importance partials (routing.py:61-63).  Lane = 4 columns; the
-    // warp's 32 rows are summed in order, 8 rows per batch of loads; warps 0+1
-    // and 2+3 are combined into the partials of the two 64-query tiles.
-    for (int p0 = 0, nb = 0; ok && p0 < M0; p0 += 128, ++nb) {
-      const int p = p0 + 4 * lane;
-      float cs[4] = {0.f, 0.f, 0.f, 0.f};
-      auto srow_at = [&](int tw) {
-        return scratch + (((long)g * ntiles + (tw >> 6)) * 64 + (tw & 63)) * LDL + p;
-      };
-      // DT(e / z) of 4 rows x 4 columns added to cs in row order (branch-free
-      // fast quotients; a batch with one near a rounding point is redone)
-      auto add_batch = [&](const uint2 (&w)[4], const float2 (&zr)[4]) {
-        float y[4][4];
+    // pass 3: importance partials (routing.py:61-63).  The CTA's exponential
+    // rows stream through the idle tile buffers in 64-column blocks (cp.async,
+    // double-buffered, one wait per block); lane = 2 columns, the warp's 32
+    // rows summed in order; warps 0+1 and 2+3 are combined into the two
+    // 64-query tiles' partials.  Rows beyond T stage as zeros and add 0.
+    constexpr int PB = 64, BLK = TR * PB * 2;
+    unsigned char* stg = sm + L.p[0];  // 2 x 16 KB: the P and V tile buffers are idle now
+    const int nblk = (M0 + PB - 1) / PB;
+    auto stage = [&](int blk) {
+      unsigned char* buf = stg + (blk & 1) * BLK;
+      const int pc = blk * PB, ch = tid & 7;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int rr = (tid >> 3) + 16 * k, tw = t0 + rr;
+        const bool in = tw < Tq && pc + ch * 8 < M0;
+        const int ts = in ? tw : t0;
+        cp_async16(buf + rr * (PB * 2) + ch * 16,
+                   scratch + (((long)g * ntiles + (ts >> 6)) * 64 + (ts & 63)) * LDL + (in ? pc + ch * 8 : 0), in);
+      }
+      cp_async_commit();
+    };
+    if (ok) stage(0);
+    for (int blk = 0; ok && blk < nblk; ++blk) {
+      if (blk + 1 < nblk) {
+        stage(blk + 1);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      tc::mbar_arrive(&bars[B_STG + (blk & 1)]);
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_STG + (blk & 1)], (blk >> 1) & 1, abort));
+      if (!ok) break;
+      const unsigned char* buf = stg + (blk & 1) * BLK;
+      float c0 = 0.f, c1 = 0.f;
+#pragma unroll 1
+      for (int g8 = 0; g8 < 4; ++g8) {
+        uint32_t w[8];
+        float2 zr[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rw = warp * 32 + g8 * 8 + i;
+          w[i] = *reinterpret_cast<const uint32_t*>(buf + rw * (PB * 2) + lane * 4);
+          zr[i] = *reinterpret_cast<const float2*>(srow + rw * 4);
+        }
+        float y[8][2];
         bool near = false;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float e[4] = {half_lo<DT>(w[i].x), half_hi<DT>(w[i].x), half_lo<DT>(w[i].y), half_hi<DT>(w[i].y)};
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            y[i][k] = e[k] * zr[i].y;
-            near |= near_midpoint<DT>(y[i][k]);
-          }
+        for (int i = 0; i < 8; ++i) {
+          y[i][0] = half_lo<DT>(w[i]) * zr[i].y;  // within 2 ulp of e / z
+          y[i][1] = half_hi<DT>(w[i]) * zr[i].y;
+          near |= near_midpoint<DT>(y[i][0]) | near_midpoint<DT>(y[i][1]);
         }
         if (near) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float e[4] = {half_lo<DT>(w[i].x), half_hi<DT>(w[i].x), half_lo<DT>(w[i].y), half_hi<DT>(w[i].y)};
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              if (near_midpoint<DT>(y[i][k])) y[i][k] = __fdiv_rn(e[k], zr[i].x);
+          for (int i = 0; i < 8; ++i) {
+            if (near_midpoint<DT>(y[i][0])) y[i][0] = __fdiv_rn(half_lo<DT>(w[i]), zr[i].x);
+            if (near_midpoint<DT>(y[i][1])) y[i][1] = __fdiv_rn(half_hi<DT>(w[i]), zr[i].x);
           }
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t q01 = pack2<DT>(y[i][0], y[i][1]), q23 = pack2<DT>(y[i][2], y[i][3]);
-          cs[0] += half_lo<DT>(q01);
-          cs[1] += half_hi<DT>(q01);
-          cs[2] += half_lo<DT>(q23);
-          cs[3] += half_hi<DT>(q23);
-        }
-      };
-      if (p < M0 && t0 + TR <= Tq) {
-        // full tile: the next 4-row batch is loading while the current one is summed
-        uint2 wn[4];
-        float2 zn[4];
-        auto load = [&](int g4) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int rw = warp * 32 + g4 * 4 + i;
-            wn[i] = *reinterpret_cast<const uint2*>(srow_at(t0 + rw));
-            zn[i] = *reinterpret_cast<const float2*>(srow + rw * 4);
-          }
-        };
-        load(0);
-#pragma unroll 1
-        for (int g4 = 0; g4 < 8; ++g4) {
-          uint2 w[4];
-          float2 z[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            w[i] = wn[i];
-            z[i] = zn[i];
-          }
-          if (g4 + 1 < 8) load(g4 + 1);
-          add_batch(w, z);
-        }
-      } else if (p < M0) {
-#pragma unroll 1
-        for (int g4 = 0; g4 < 8; ++g4) {
-          const int rw0 = warp * 32 + g4 * 4;
-          if (t0 + rw0 + 3 < Tq) {
-            uint2 w[4];
-            float2 zr[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int tw = t0 + rw0 + i;
-              w[i] = *reinterpret_cast<const uint2*>(scratch + (((long)g * ntiles + (tw >> 6)) * 64 + (tw & 63)) * LDL + p);
-              zr[i] = *reinterpret_cast<const float2*>(srow + (rw0 + i) * 4);
-            }
-            float y[4][4];
-            bool near = false;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float e[4] = {half_lo<DT>(w[i].x), half_hi<DT>(w[i].x), half_lo<DT>(w[i].y), half_hi<DT>(w[i].y)};
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                y[i][k] = e[k] * zr[i].y;  // within 2 ulp of e / z
-                near |= near_midpoint<DT>(y[i][k]);
-              }
-            }
-            if (near) {
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float e[4] = {half_lo<DT>(w[i].x), half_hi<DT>(w[i].x), half_lo<DT>(w[i].y),
-                                    half_hi<DT>(w[i].y)};
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                  if (near_midpoint<DT>(y[i][k])) y[i][k] = __fdiv_rn(e[k], zr[i].x);
-              }
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const uint32_t q01 = pack2<DT>(y[i][0], y[i][1]), q23 = pack2<DT>(y[i][2], y[i][3]);  // DT(e / z)
-              cs[0] += half_lo<DT>(q01);
-              cs[1] += half_hi<DT>(q01);
-              cs[2] += half_lo<DT>(q23);
-              cs[3] += half_hi<DT>(q23);
-            }
-          } else {
-            for (int i = 0; i < 4; ++i) {
-              const int tw = t0 + rw0 + i;
-              if (tw >= Tq) break;  // query beyond T
-              const uint2 wv =
-                  *reinterpret_cast<const uint2*>(scratch + (((long)g * ntiles + (tw >> 6)) * 64 + (tw & 63)) * LDL + p);
-              const float zc_r = srow[(rw0 + i) * 4], rz = srow[(rw0 + i) * 4 + 1];
-              cs[0] += div_dt_fast<DT>(half_lo<DT>(wv.x), rz, zc_r);
-              cs[1] += div_dt_fast<DT>(half_hi<DT>(wv.x), rz, zc_r);
-              cs[2] += div_dt_fast<DT>(half_lo<DT>(wv.y), rz, zc_r);
-              cs[3] += div_dt_fast<DT>(half_hi<DT>(wv.y), rz, zc_r);
-            }
-          }
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t q2 = pack2<DT>(y[i][0], y[i][1]);  // DT(e / z)
+          c0 += half_lo<DT>(q2);
+          c1 += half_hi<DT>(q2);
         }
       }
-      float* sc = scomb + (nb & 1) * 512;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) sc[warp * 128 + 4 * lane + k] = cs[k];
+      float* sc = scomb + (blk & 1) * 256;
+      sc[warp * 64 + 2 * lane] = c0;
+      sc[warp * 64 + 2 * lane + 1] = c1;
       tc::mbar_arrive(&bars[B_COMB]);
-      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_COMB], nb & 1, abort));
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_COMB], blk & 1, abort));
       if (!ok) break;
-      for (int o = tid; o < 256; o += TR) {
-        const int tp = o >> 7, cl = o & 127, tile = 2 * qt + tp;
-        if (tile < ntiles && p0 + cl < M0)
-          colpart[((long)g * ntiles + tile) * M0 + p0 + cl] = sc[2 * tp * 128 + cl] + sc[(2 * tp + 1) * 128 + cl];
-      }
+      const int tile = 2 * qt + (tid >> 6), cl = tid & 63, pcol = blk * PB + cl;
+      if (tile < ntiles && pcol < M0)
+        colpart[((long)g * ntiles + tile) * M0 + pcol] = sc[(tid >> 6) * 128 + cl] + sc[(tid >> 6) * 128 + 64 + cl];
     }
+    cp_async_wait<0>();
   }
 
   // ---- teardown ----
