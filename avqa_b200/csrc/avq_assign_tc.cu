@@ -16,7 +16,8 @@
 // half and the parent index in the low half.  A row with a NaN
 // distance (only possible with non-finite inputs) takes a scalar path.
 // Child stage (quantizer.py:218-226): the cross term is a sum of
-// dtype-rounded elementwise products, accumulated in fp64 and rounded once.
+// dtype-rounded elementwise products, rounded once as its exact value would
+// be (fp32 with an error bound, fp64 where the bound cannot decide).
 #include <cuda.h>
 
 #include <algorithm>
@@ -39,11 +40,14 @@ constexpr int ACH = 128;       // parents per chunk
 constexpr int ATHREADS = 192;  // 4 row warps + MMA warp + TMA warp
 constexpr int A_TMEM_COLS = 256;
 constexpr int A_MAX_M0 = 4096;
+constexpr int A_MAX_C = 8;           // children per parent on this path
+constexpr int A_KP = 4;              // keys per cp.async group of the child stage
+constexpr int A_CSQ_PER_WARP = 64;   // staged child norms per warp: ring slots x C <= 64
 
 constexpr int AB_K = 0, AB_PFULL = 1, AB_PEMPTY = 3, AB_SFULL = 5, AB_SCONS = 7, AB_END = 9, AN_BARS = 10;
 
 struct AssignLayout {
-  int k, p[2], ps2, bars, misc, total;
+  int k, p[2], ps2, csq, bars, misc, total;
 };
 
 __host__ __device__ inline AssignLayout assign_layout(int D, int M0) {
@@ -58,6 +62,8 @@ __host__ __device__ inline AssignLayout assign_layout(int D, int M0) {
   }
   L.ps2 = o;
   o += nch * (ACH / 2) * 4;
+  L.csq = o;
+  o += 4 * A_CSQ_PER_WARP * 4;
   L.bars = o;
   o += AN_BARS * 8;
   L.misc = o;
@@ -90,12 +96,177 @@ __device__ __forceinline__ uint32_t order2(uint32_t d2) {
 __device__ __forceinline__ int key_lo(uint32_t k2, uint32_t idx2) { return (int)prmt(k2, idx2, 0x1054u); }
 __device__ __forceinline__ int key_hi(uint32_t k2, uint32_t idx2) { return (int)prmt(k2, idx2, 0x3276u); }
 
-// torch.argmin order for the child stage: the first minimum; a NaN wins.
-__device__ __forceinline__ bool better_c(float v, int i, float bv, int bi) {
-  if (bi < 0) return true;
-  const bool n = isnan(v), bn = isnan(bv);
-  if (n || bn) return n && (!bn || i < bi);
-  return v < bv || (v == bv && i < bi);
+// cp.async with memory clobbers: shared-memory reads of a ring slot stay
+// between the wait that fills it and the copy that refills it.
+__device__ __forceinline__ void ring_cp16(void* smem, const void* gmem, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem), "r"(pred ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void ring_cp4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void ring_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void ring_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Child stage of one warp's 32 keys (quantizer.py:218-227).  A key's C child
+// rows form one contiguous block; its rows are spread over the warp, G lanes
+// to a row, lane (rsub, vg) holding the 16-byte chunks vg + G*t (t < NV) of
+// row rsub, so one key costs the warp NV coalesced 16-byte copies a lane.
+// The blocks stream through a per-warp ring of NG groups of A_KP keys in
+// shared memory (cp.async), NG - 1 groups ahead of the one being reduced.
+//
+// cross = DT(fp32(sum_d DT(k_d c_d))) with the sum exact (what the fp64 sum
+// of the dtype products gives) is evaluated in fp32: each lane sums its 8*NV
+// products pairwise and the row's G lanes combine by butterfly, a tree of
+// depth 3 + log2(NV*G) <= 7, so the fp32 result S' lies within
+// gamma_7 * sum|t| <= 2^-21 * A' of the exact sum, A' being the same tree's
+// sum of |t|.  fp32 and dtype rounding are monotone, so when both ends of
+// [S' - 2^-21 A', S' + 2^-21 A'] (rounded outwards) round to the same dtype
+// value that value is the exact sum's rounding; otherwise (close to a dtype
+// rounding boundary, or non-finite) the row is summed again in fp64.
+// torch.argmin over the children (first minimum, a NaN wins) is a signed
+// min over 32-bit keys: the order-preserving integer form of the distance,
+// whose low 13 bits are zero for dtype values, or'ed with the child index.
+template <int DT, int D, int NV, int NG>
+__device__ __forceinline__ int child_stage(unsigned char* ring, float* csr, const unsigned char* ktile, int warp,
+                                           int lane, uint32_t livemask, int pbest, float ksq,
+                                           const unsigned char* __restrict__ chh, const float* __restrict__ csqh,
+                                           int C) {
+  constexpr int CPR = D / 8, G = CPR / NV, KP = A_KP, NGRP = 32 / KP;
+  static_assert(G >= 1 && 32 % G == 0, "lanes per row");
+  const unsigned full = 0xffffffffu;
+  const int vg = lane % G, rsub = lane / G;
+  const bool rowon = rsub < C;
+  const int blk = C * D * 2;
+  auto issue = [&](int grp) {  // keys KP*grp .. KP*grp+KP-1 into ring group grp % NG
+    const int sg = grp % NG;
+#pragma unroll
+    for (int kk = 0; kk < KP; ++kk) {
+      const int k = grp * KP + kk;
+      const int pb = __shfl_sync(full, pbest, k);
+      const bool on = ((livemask >> k) & 1u) != 0u;
+      if (rowon) {
+        const long crow = (long)pb * C + rsub;
+        unsigned char* dst = ring + (sg * KP + kk) * blk + rsub * (D * 2);
+        const unsigned char* src = on ? chh + crow * (D * 2) : chh;
+#pragma unroll
+        for (int t = 0; t < NV; ++t) ring_cp16(dst + (vg + G * t) * 16, src + (on ? (vg + G * t) * 16 : 0), on);
+        if (vg == 0 && on) ring_cp4(csr + (sg * KP + kk) * C + rsub, csqh + crow);
+      }
+    }
+    ring_commit();
+  };
+  auto key_chunk = [&](int rk, int v) -> uint4 {  // swizzled key tile: chunk j of slab v/8 at j ^ (rk & 7)
+    return *reinterpret_cast<const uint4*>(ktile + (v >> 3) * AR * 128 + rk * 128 + (((v & 7) ^ (rk & 7)) << 4));
+  };
+  auto blk_chunk = [&](int slot, int t) -> uint4 {
+    return rowon ? *reinterpret_cast<const uint4*>(ring + slot * blk + rsub * (D * 2) + (vg + G * t) * 16)
+                 : make_uint4(0u, 0u, 0u, 0u);
+  };
+
+  int mine = -1;
+#pragma unroll 1
+  for (int gq = 0; gq < NG; ++gq) issue(gq);
+#pragma unroll 1
+  for (int gq = 0; gq < NGRP; ++gq) {
+    ring_wait<NG - 1>();
+    __syncwarp();  // the child norms come from other lanes' copies
+    const int sg = gq % NG;
+    float sx[KP], ax[KP];
+#pragma unroll
+    for (int kk = 0; kk < KP; ++kk) {
+      const int rk = warp * 32 + gq * KP + kk;
+      float ps[NV], pa[NV];
+#pragma unroll
+      for (int t = 0; t < NV; ++t) {
+        const uint4 u = key_chunk(rk, vg + G * t), w = blk_chunk(sg * KP + kk, t);
+        const uint32_t ku[4] = {u.x, u.y, u.z, u.w}, cw[4] = {w.x, w.y, w.z, w.w};
+        float x[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t pr = hmul2_dt<DT>(ku[e], cw[e]);  // DT(k_d * c_d)
+          x[2 * e] = half_lo<DT>(pr);
+          x[2 * e + 1] = half_hi<DT>(pr);
+        }
+        ps[t] = ((x[0] + x[1]) + (x[2] + x[3])) + ((x[4] + x[5]) + (x[6] + x[7]));
+        pa[t] = ((fabsf(x[0]) + fabsf(x[1])) + (fabsf(x[2]) + fabsf(x[3]))) +
+                ((fabsf(x[4]) + fabsf(x[5])) + (fabsf(x[6]) + fabsf(x[7])));
+      }
+#pragma unroll
+      for (int st = 1; st < NV; st <<= 1)
+#pragma unroll
+        for (int t = 0; t + st < NV; t += 2 * st) {
+          ps[t] += ps[t + st];
+          pa[t] += pa[t + st];
+        }
+      sx[kk] = ps[0];
+      ax[kk] = pa[0];
+    }
+#pragma unroll
+    for (int o = 1; o < G; o <<= 1)
+#pragma unroll
+      for (int kk = 0; kk < KP; ++kk) {
+        sx[kk] += __shfl_xor_sync(full, sx[kk], o);
+        ax[kk] += __shfl_xor_sync(full, ax[kk], o);
+      }
+    float cross[KP];
+    bool anybad = false;
+    uint32_t badm = 0u;
+#pragma unroll
+    for (int kk = 0; kk < KP; ++kk) {
+      const float bnd = __fmul_ru(ax[kk], 0x1p-21f);
+      cross[kk] = rnd<DT>(__fsub_rd(sx[kk], bnd));
+      const bool bad = !(cross[kk] == rnd<DT>(__fadd_ru(sx[kk], bnd)));
+      badm |= bad ? 1u << kk : 0u;
+      anybad |= bad && rowon;
+    }
+    if (__any_sync(full, anybad)) {
+#pragma unroll
+      for (int kk = 0; kk < KP; ++kk) {
+        if (!__any_sync(full, ((badm >> kk) & 1u) && rowon)) continue;
+        const int rk = warp * 32 + gq * KP + kk;
+        double e64 = 0.0;
+#pragma unroll
+        for (int t = 0; t < NV; ++t) {
+          const uint4 u = key_chunk(rk, vg + G * t), w = blk_chunk(sg * KP + kk, t);
+          const uint32_t ku[4] = {u.x, u.y, u.z, u.w}, cw[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t pr = hmul2_dt<DT>(ku[e], cw[e]);
+            e64 += (double)half_lo<DT>(pr) + (double)half_hi<DT>(pr);
+          }
+        }
+#pragma unroll
+        for (int o = 1; o < G; o <<= 1) e64 += __shfl_xor_sync(full, e64, o);
+        if ((badm >> kk) & 1u) cross[kk] = rnd64<DT>(e64);
+      }
+    }
+    int key[KP];
+#pragma unroll
+    for (int kk = 0; kk < KP; ++kk) {
+      const float ksk = __shfl_sync(full, ksq, gq * KP + kk);
+      const float cs = rowon ? csr[(sg * KP + kk) * C + rsub] : 0.f;
+      // d = DT(DT(k_sq + c_sq) - DT(2 * cross)); + 0 turns a -0 into +0 (torch compares them equal)
+      const float dd = __fadd_rn(rnd<DT>(__fsub_rn(rnd<DT>(__fadd_rn(ksk, cs)), rnd<DT>(__fmul_rn(2.f, cross[kk])))), 0.f);
+      const int bits = __float_as_int(dd);
+      const int ord = bits >= 0 ? bits : (bits ^ 0x7FFFE000);
+      key[kk] = !rowon ? 0x7FFFFFFF : isnan(dd) ? (int)(0x80000000u | (uint32_t)rsub) : (ord & ~0x1FFF) | rsub;
+    }
+#pragma unroll
+    for (int o = G; o < 32; o <<= 1)
+#pragma unroll
+      for (int kk = 0; kk < KP; ++kk) key[kk] = min(key[kk], __shfl_xor_sync(full, key[kk], o));
+#pragma unroll
+    for (int kk = 0; kk < KP; ++kk)
+      if (lane == gq * KP + kk) mine = key[kk] & 0x1FFF;
+    // every value read from this ring group fed the reductions above: refill it
+    if (gq + NG < NGRP) issue(gq + NG);
+    else ring_commit();
+  }
+  return mine;
 }
 
 __device__ __forceinline__ void drain(uint64_t* bar, uint32_t parity) {
@@ -299,43 +470,27 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
         }
       }
     }
-    // child stage: the assigned parent's children (quantizer.py:218-226)
-    if (ok && live) {
-      const long crow0 = ((long)h * M0 + pbest) * C;
-      float bv = 0.f;
-      int bi = -1;
-      for (int c0 = 0; c0 < C; c0 += 4) {
-        double acc[4] = {0.0, 0.0, 0.0, 0.0};
-        const int nc = min(4, C - c0);
-#pragma unroll 4
-        for (int v = 0; v < D / 8; ++v) {
-          const uint4 u = key_chunk(v);
-          const uint32_t ku[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            if (cc < nc) {
-              const uint4 w = __ldg(reinterpret_cast<const uint4*>(children + (crow0 + c0 + cc) * D) + v);
-              const uint32_t cw[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const uint32_t pr = hmul2_dt<DT>(ku[e], cw[e]);  // DT(k_d * c_d), exact product rounded once
-                acc[cc] += (double)half_lo<DT>(pr) + (double)half_hi<DT>(pr);
-              }
-            }
-          }
-        }
-        for (int cc = 0; cc < nc; ++cc) {
-          const int c = c0 + cc;
-          const float cross = rnd64<DT>(acc[cc]);
-          const float dd = rnd<DT>(__fsub_rn(rnd<DT>(__fadd_rn(ksq, c_sq[crow0 + c])), rnd<DT>(__fmul_rn(2.f, cross))));
-          if (better_c(dd, c, bv, bi)) {
-            bv = dd;
-            bi = c;
-          }
-        }
+    // child stage: the assigned parent's children (quantizer.py:218-226), a
+    // warp's 32 keys through a cp.async ring in the now idle parent buffers
+    if (ok) {
+      const uint32_t livemask = __ballot_sync(0xffffffffu, live);
+      unsigned char* ring = sm + L.p[0] + warp * (ACH * D);
+      float* csr = reinterpret_cast<float*>(sm + L.csq) + warp * A_CSQ_PER_WARP;
+      const unsigned char* chh = reinterpret_cast<const unsigned char*>(children + (long)h * M0 * C * D);
+      const float* csqh = c_sq + (long)h * M0 * C;
+      const unsigned char* kt = sm + L.k;
+      int bi;
+      if (D == 128)
+        bi = C <= 2 ? child_stage<DT, D, 1, 4>(ring, csr, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
+             : C <= 4 ? child_stage<DT, D, 2, 4>(ring, csr, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
+                      : child_stage<DT, D, 4, 2>(ring, csr, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C);
+      else
+        bi = C <= 4 ? child_stage<DT, D, 1, 4>(ring, csr, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
+                    : child_stage<DT, D, 2, 2>(ring, csr, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C);
+      if (live) {
+        passign[(long)g * S + s] = pbest;
+        cassign[(long)g * S + s] = bi;
       }
-      passign[(long)g * S + s] = pbest;
-      cassign[(long)g * S + s] = bi;
     }
   }
 
@@ -365,6 +520,7 @@ int launch_assign_tc(const QuantizeArgs& a, cudaStream_t st) {
   if (!tc::map_rows4(&tk, DT, a.keys, a.ks, a.B, a.H, a.S, D, AR, &kpos) ||
       !tc::map_rows3(&tp, DT, a.parents_dt, a.H, a.M0, D, ACH))
     return AVQ_ERR_UNSUPPORTED;
+  if (a.C < 1 || a.C > A_MAX_C) return AVQ_ERR_UNSUPPORTED;
   const AssignLayout L = assign_layout(D, a.M0);
   const size_t smem = std::max<size_t>((size_t)L.total + 1024, 80 * 1024);  // <= 2 CTAs (2 x 256 TMEM columns) per SM
   auto go = [&](auto kfn) {

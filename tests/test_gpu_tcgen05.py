@@ -156,3 +156,29 @@ def test_tcgen05_assignment_non_finite_inputs() -> None:
     pd, cd = O.cast_codebook(parents.numpy(), cbk.children.numpy(), "bf16")
     want = O.quantize(O.split_heads(kn, w.H), O.split_heads(vn, w.H), pd, cd, "bf16")
     np.testing.assert_array_equal(a.passign.cpu().numpy(), want.parent_assignments)
+
+
+@pytest.mark.parametrize("dt,D,C", [("bf16", 128, 4), ("f16", 64, 8), ("bf16", 128, 2)])
+def test_tcgen05_assignment_integer_ties(dt: str, D: int, C: int) -> None:
+    """Small-integer keys and codebooks: the child cross terms are integers
+    whose dtype rounding often sits exactly on a tie, where the fp32 error
+    bound cannot decide and the row is summed again in fp64; distance ties
+    exercise the first-minimum rule."""
+    B, S, H, M0 = 1, 1536, 2, 64
+    g = torch.Generator().manual_seed(55 + D + C)
+    kn = torch.randint(-6, 7, (B, S, H * D), generator=g).float().numpy()
+    vn = O.rnd(torch.randn(B, S, H * D, generator=g).numpy(), dt)
+    parents = torch.randint(-6, 7, (H, M0, D), generator=g).float()
+    children = parents[:, :, None, :] + torch.randint(-2, 3, (H, M0, C, D), generator=g).float()
+    cb = ops.prepare_codebook(parents, children, TORCH_DTYPE[dt], torch.device("cuda"))
+    w = Workload("q_int", B=B, T=8, S=S, H=H, D=D, M0=M0, C=C, P=8, dtype=dt, keys="mixture", seed=55)
+    kd, vd = to_dev(kn, dt), to_dev(vn, dt)
+    a = _quantize(w, kd, vd, cb, True)
+    b = _quantize(w, kd, vd, cb, False)
+    _assert_same_quant(a, b, f"int_{dt}_{D}_{C}")
+    pd, cd = O.cast_codebook(parents.numpy(), children.numpy(), dt)
+    want = O.quantize(O.split_heads(kn, H), O.split_heads(vn, H), pd, cd, dt)
+    np.testing.assert_array_equal(a.passign.cpu().numpy().reshape(want.parent_assignments.shape),
+                                  want.parent_assignments)
+    np.testing.assert_array_equal(a.cassign.cpu().numpy().reshape(want.child_assignments.shape),
+                                  want.child_assignments)
