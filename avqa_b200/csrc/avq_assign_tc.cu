@@ -111,6 +111,28 @@ __device__ __forceinline__ void ring_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
+// Packed fp32 pair addition (one instruction for both lanes, IEEE
+// round-to-nearest per element).
+__device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// Bound on sum_d |DT(k_d c_d)| from the dtype norms: |k_d c_d| <= (k_d^2 +
+// c_d^2) / 2, and k_sq, c_sq are the once-rounded exact sums of the dtype
+// squares, so sum_d k_d^2 <= k_sq (1 + 2.1 u) + D eta (u the dtype's unit
+// roundoff, eta half its smallest subnormal).  Scaled by 2^-21 >= gamma_7:
+//   err <= 2^-21 * (0.52 (k_sq + c_sq) + 4 D eta).
+template <int DT>
+struct ChildBound {
+  static constexpr float scale = 0.52f * 0x1p-21f;
+  static constexpr float slack = DT == DT_F16 ? 0x1p-36f : 0x1p-140f;  // >= 2^-21 * 4 * 128 * eta
+};
+
 // Child stage of one warp's 32 keys (quantizer.py:218-227).  A key's C child
 // rows form one contiguous block; its rows are spread over the warp, G lanes
 // to a row, lane (rsub, vg) holding the 16-byte chunks vg + G*t (t < NV) of
@@ -122,48 +144,59 @@ __device__ __forceinline__ void ring_wait() {
 // of the dtype products gives) is evaluated in fp32: each lane sums its 8*NV
 // products pairwise and the row's G lanes combine by butterfly, a tree of
 // depth 3 + log2(NV*G) <= 7, so the fp32 result S' lies within
-// gamma_7 * sum|t| <= 2^-21 * A' of the exact sum, A' being the same tree's
-// sum of |t|.  fp32 and dtype rounding are monotone, so when both ends of
-// [S' - 2^-21 A', S' + 2^-21 A'] (rounded outwards) round to the same dtype
-// value that value is the exact sum's rounding; otherwise (close to a dtype
-// rounding boundary, or non-finite) the row is summed again in fp64.
-// torch.argmin over the children (first minimum, a NaN wins) is a signed
-// min over 32-bit keys: the order-preserving integer form of the distance,
-// whose low 13 bits are zero for dtype values, or'ed with the child index.
+// gamma_7 * sum|t| of the exact sum, bounded by ChildBound.  fp32 and dtype
+// rounding are monotone, so when both ends of [S' - b, S' + b] (rounded
+// outwards) round to the same dtype value that value is the exact sum's
+// rounding; otherwise (close to a dtype rounding boundary, or non-finite)
+// the row is summed again in fp64.  After the butterfly every lane of a row
+// holds the row's sums of all A_KP keys, so lane vg finishes key vg % A_KP:
+// the rounding test, the distance and the argmin run once per lane, not once
+// per key.  torch.argmin over the children (first minimum, a NaN wins) is a
+// signed min over 32-bit keys: the order-preserving integer form of the
+// distance, whose low 13 bits are zero for dtype values, or'ed with the
+// child index.
 template <int DT, int D, int NV, int NG>
 __device__ __forceinline__ int child_stage(unsigned char* ring, float* csr, const unsigned char* ktile, int warp,
                                            int lane, uint32_t livemask, int pbest, float ksq,
                                            const unsigned char* __restrict__ chh, const float* __restrict__ csqh,
                                            int C) {
   constexpr int CPR = D / 8, G = CPR / NV, KP = A_KP, NGRP = 32 / KP;
-  static_assert(G >= 1 && 32 % G == 0, "lanes per row");
+  static_assert(G >= KP && G % KP == 0 && 32 % G == 0, "lanes per row");
+  constexpr int RB = D * 2;  // bytes per child row
   const unsigned full = 0xffffffffu;
-  const int vg = lane % G, rsub = lane / G;
+  const int vg = lane % G, rsub = lane / G, kq = lane % KP;
   const bool rowon = rsub < C;
-  const int blk = C * D * 2;
+  const int blk = C * RB;
+  const int boff_mine = pbest * blk;  // byte offset of this lane's key's child block in the head
+  const int lane_off = rsub * RB + vg * 16;
   auto issue = [&](int grp) {  // keys KP*grp .. KP*grp+KP-1 into ring group grp % NG
     const int sg = grp % NG;
 #pragma unroll
     for (int kk = 0; kk < KP; ++kk) {
       const int k = grp * KP + kk;
-      const int pb = __shfl_sync(full, pbest, k);
+      const int boff = __shfl_sync(full, boff_mine, k);
       const bool on = ((livemask >> k) & 1u) != 0u;
       if (rowon) {
-        const long crow = (long)pb * C + rsub;
-        unsigned char* dst = ring + (sg * KP + kk) * blk + rsub * (D * 2);
-        const unsigned char* src = on ? chh + crow * (D * 2) : chh;
+        unsigned char* dst = ring + (sg * KP + kk) * blk + lane_off;
+        const unsigned char* src = on ? chh + boff + lane_off : chh;
 #pragma unroll
-        for (int t = 0; t < NV; ++t) ring_cp16(dst + (vg + G * t) * 16, src + (on ? (vg + G * t) * 16 : 0), on);
-        if (vg == 0 && on) ring_cp4(csr + (sg * KP + kk) * C + rsub, csqh + crow);
+        for (int t = 0; t < NV; ++t) ring_cp16(dst + G * 16 * t, src + (on ? G * 16 * t : 0), on);
+        if (vg == 0 && on) ring_cp4(csr + (sg * KP + kk) * C + rsub, csqh + boff / RB + rsub);
       }
     }
     ring_commit();
   };
-  auto key_chunk = [&](int rk, int v) -> uint4 {  // swizzled key tile: chunk j of slab v/8 at j ^ (rk & 7)
-    return *reinterpret_cast<const uint4*>(ktile + (v >> 3) * AR * 128 + rk * 128 + (((v & 7) ^ (rk & 7)) << 4));
+  uint32_t koff[NV];  // this lane's key chunks in the swizzled key tile, before the row swizzle
+#pragma unroll
+  for (int t = 0; t < NV; ++t) {
+    const int v = vg + G * t;
+    koff[t] = (uint32_t)((v >> 3) * AR * 128 + ((v & 7) << 4));
+  }
+  auto key_chunk = [&](int rk, int t) -> uint4 {  // chunk j of slab v/8 sits at j ^ (rk & 7)
+    return *reinterpret_cast<const uint4*>(ktile + rk * 128 + (koff[t] ^ ((rk & 7) << 4)));
   };
   auto blk_chunk = [&](int slot, int t) -> uint4 {
-    return rowon ? *reinterpret_cast<const uint4*>(ring + slot * blk + rsub * (D * 2) + (vg + G * t) * 16)
+    return rowon ? *reinterpret_cast<const uint4*>(ring + slot * blk + lane_off + G * 16 * t)
                  : make_uint4(0u, 0u, 0u, 0u);
   };
 
@@ -175,63 +208,50 @@ __device__ __forceinline__ int child_stage(unsigned char* ring, float* csr, cons
     ring_wait<NG - 1>();
     __syncwarp();  // the child norms come from other lanes' copies
     const int sg = gq % NG;
-    float sx[KP], ax[KP];
+    float sx[KP];
 #pragma unroll
     for (int kk = 0; kk < KP; ++kk) {
       const int rk = warp * 32 + gq * KP + kk;
-      float ps[NV], pa[NV];
+      float2 acc[NV * 4];
 #pragma unroll
       for (int t = 0; t < NV; ++t) {
-        const uint4 u = key_chunk(rk, vg + G * t), w = blk_chunk(sg * KP + kk, t);
+        const uint4 u = key_chunk(rk, t), w = blk_chunk(sg * KP + kk, t);
         const uint32_t ku[4] = {u.x, u.y, u.z, u.w}, cw[4] = {w.x, w.y, w.z, w.w};
-        float x[8];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const uint32_t pr = hmul2_dt<DT>(ku[e], cw[e]);  // DT(k_d * c_d)
-          x[2 * e] = half_lo<DT>(pr);
-          x[2 * e + 1] = half_hi<DT>(pr);
+          acc[4 * t + e] = make_float2(half_lo<DT>(pr), half_hi<DT>(pr));
         }
-        ps[t] = ((x[0] + x[1]) + (x[2] + x[3])) + ((x[4] + x[5]) + (x[6] + x[7]));
-        pa[t] = ((fabsf(x[0]) + fabsf(x[1])) + (fabsf(x[2]) + fabsf(x[3]))) +
-                ((fabsf(x[4]) + fabsf(x[5])) + (fabsf(x[6]) + fabsf(x[7])));
       }
 #pragma unroll
-      for (int st = 1; st < NV; st <<= 1)
+      for (int st = 1; st < NV * 4; st <<= 1)
 #pragma unroll
-        for (int t = 0; t + st < NV; t += 2 * st) {
-          ps[t] += ps[t + st];
-          pa[t] += pa[t + st];
-        }
-      sx[kk] = ps[0];
-      ax[kk] = pa[0];
+        for (int i = 0; i + st < NV * 4; i += 2 * st) acc[i] = add_f32x2(acc[i], acc[i + st]);
+      sx[kk] = acc[0].x + acc[0].y;
     }
 #pragma unroll
     for (int o = 1; o < G; o <<= 1)
 #pragma unroll
-      for (int kk = 0; kk < KP; ++kk) {
-        sx[kk] += __shfl_xor_sync(full, sx[kk], o);
-        ax[kk] += __shfl_xor_sync(full, ax[kk], o);
-      }
-    float cross[KP];
-    bool anybad = false;
-    uint32_t badm = 0u;
+      for (int kk = 0; kk < KP; ++kk) sx[kk] += __shfl_xor_sync(full, sx[kk], o);
+    // this lane's key: kq = vg % KP
+    float sv = sx[0];
 #pragma unroll
-    for (int kk = 0; kk < KP; ++kk) {
-      const float bnd = __fmul_ru(ax[kk], 0x1p-21f);
-      cross[kk] = rnd<DT>(__fsub_rd(sx[kk], bnd));
-      const bool bad = !(cross[kk] == rnd<DT>(__fadd_ru(sx[kk], bnd)));
-      badm |= bad ? 1u << kk : 0u;
-      anybad |= bad && rowon;
-    }
-    if (__any_sync(full, anybad)) {
+    for (int kk = 1; kk < KP; ++kk) sv = kq == kk ? sx[kk] : sv;
+    const float ksk = __shfl_sync(full, ksq, gq * KP + kq);
+    const float cs = rowon ? csr[(sg * KP + kq) * C + rsub] : 0.f;
+    const float bnd = __fmaf_ru(__fadd_ru(ksk, cs), ChildBound<DT>::scale, ChildBound<DT>::slack);
+    float cross = rnd<DT>(__fsub_rd(sv, bnd));
+    const bool bad = rowon && !(cross == rnd<DT>(__fadd_ru(sv, bnd)));
+    const uint32_t badb = __ballot_sync(full, bad);
+    if (badb) {
 #pragma unroll
       for (int kk = 0; kk < KP; ++kk) {
-        if (!__any_sync(full, ((badm >> kk) & 1u) && rowon)) continue;
+        if (!(badb & (0x11111111u << kk))) continue;  // lanes finishing key kk: lane % KP == kk
         const int rk = warp * 32 + gq * KP + kk;
         double e64 = 0.0;
 #pragma unroll
         for (int t = 0; t < NV; ++t) {
-          const uint4 u = key_chunk(rk, vg + G * t), w = blk_chunk(sg * KP + kk, t);
+          const uint4 u = key_chunk(rk, t), w = blk_chunk(sg * KP + kk, t);
           const uint32_t ku[4] = {u.x, u.y, u.z, u.w}, cw[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -241,27 +261,19 @@ __device__ __forceinline__ int child_stage(unsigned char* ring, float* csr, cons
         }
 #pragma unroll
         for (int o = 1; o < G; o <<= 1) e64 += __shfl_xor_sync(full, e64, o);
-        if ((badm >> kk) & 1u) cross[kk] = rnd64<DT>(e64);
+        if (bad && kq == kk) cross = rnd64<DT>(e64);
       }
     }
-    int key[KP];
+    // d = DT(DT(k_sq + c_sq) - DT(2 * cross)); + 0 turns a -0 into +0 (torch compares them equal)
+    const float dd = __fadd_rn(rnd<DT>(__fsub_rn(rnd<DT>(__fadd_rn(ksk, cs)), rnd<DT>(__fmul_rn(2.f, cross)))), 0.f);
+    const int bits = __float_as_int(dd);
+    const int ord = bits >= 0 ? bits : (bits ^ 0x7FFFE000);
+    int key = !rowon ? 0x7FFFFFFF : isnan(dd) ? (int)(0x80000000u | (uint32_t)rsub) : (ord & ~0x1FFF) | rsub;
 #pragma unroll
-    for (int kk = 0; kk < KP; ++kk) {
-      const float ksk = __shfl_sync(full, ksq, gq * KP + kk);
-      const float cs = rowon ? csr[(sg * KP + kk) * C + rsub] : 0.f;
-      // d = DT(DT(k_sq + c_sq) - DT(2 * cross)); + 0 turns a -0 into +0 (torch compares them equal)
-      const float dd = __fadd_rn(rnd<DT>(__fsub_rn(rnd<DT>(__fadd_rn(ksk, cs)), rnd<DT>(__fmul_rn(2.f, cross[kk])))), 0.f);
-      const int bits = __float_as_int(dd);
-      const int ord = bits >= 0 ? bits : (bits ^ 0x7FFFE000);
-      key[kk] = !rowon ? 0x7FFFFFFF : isnan(dd) ? (int)(0x80000000u | (uint32_t)rsub) : (ord & ~0x1FFF) | rsub;
-    }
-#pragma unroll
-    for (int o = G; o < 32; o <<= 1)
-#pragma unroll
-      for (int kk = 0; kk < KP; ++kk) key[kk] = min(key[kk], __shfl_xor_sync(full, key[kk], o));
-#pragma unroll
-    for (int kk = 0; kk < KP; ++kk)
-      if (lane == gq * KP + kk) mine = key[kk] & 0x1FFF;
+    for (int o = G; o < 32; o <<= 1) key = min(key, __shfl_xor_sync(full, key, o));
+    // lanes 0 .. KP-1 (row 0, vg = kk) now hold keys 0 .. KP-1 of the group
+    const int res = __shfl_sync(full, key, kq);
+    if (lane / KP == gq) mine = res & 0x1FFF;
     // every value read from this ring group fed the reductions above: refill it
     if (gq + NG < NGRP) issue(gq + NG);
     else ring_commit();
@@ -480,7 +492,7 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
       const float* csqh = c_sq + (long)h * M0 * C;
       const unsigned char* kt = sm + L.k;
       int bi;
-      if (D == 128)
+      if constexpr (D == 128)
         bi = C <= 2 ? child_stage<DT, D, 1, 4>(ring, csr, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
              : C <= 4 ? child_stage<DT, D, 2, 4>(ring, csr, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
                       : child_stage<DT, D, 4, 2>(ring, csr, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C);

@@ -1,0 +1,132 @@
+"""The child-distance rounding test of the tcgen05 assignment kernel, on CPU.
+
+The kernel evaluates the child cross term DT(fp32(sum_d DT(k_d c_d))) (the sum
+exact, quantizer.py:224-226) in fp32 along a fixed tree, then accepts the
+result only when both ends of [S' - b, S' + b] round to the same dtype value,
+with b = RU(RU(k_sq + c_sq) * 0.52 * 2^-21 + slack).  This emulates that
+tree and test with exact directed rounding and checks, over distributions
+chosen to stress it (near ties, integers, mismatched norms, f16 underflow,
+overflow), that every accepted value equals the oracle's exact rounding.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+from oracle import avq_oracle as O
+
+SCALE = 0.52 * 2.0 ** -21
+SLACK = {"bf16": 2.0 ** -140, "f16": 2.0 ** -36}
+
+
+def _round_dir(exact_hi: np.ndarray, exact_lo: np.ndarray, up: bool) -> np.ndarray:
+    """float32 rounding of hi + lo (an f64 pair, |lo| tiny) towards +inf or -inf."""
+    with np.errstate(over="ignore", invalid="ignore"):
+        f = exact_hi.astype(np.float32)
+    fd = f.astype(np.float64)
+    if up:
+        step = (fd < exact_hi) | ((fd == exact_hi) & (exact_lo > 0))
+        return np.where(step, np.nextafter(f, np.float32(np.inf)), f)
+    step = (fd > exact_hi) | ((fd == exact_hi) & (exact_lo < 0))
+    return np.where(step, np.nextafter(f, np.float32(-np.inf)), f)
+
+
+def _two_sum(a: np.ndarray, b: np.ndarray):
+    s = a + b
+    bb = s - a
+    return s, (a - (s - bb)) + (b - bb)
+
+
+def _add_dir(a, b, up: bool) -> np.ndarray:
+    with np.errstate(invalid="ignore", over="ignore"):
+        s, e = _two_sum(np.asarray(a, np.float64), np.asarray(b, np.float64))
+    return _round_dir(s, np.nan_to_num(e), up)
+
+
+def _pairwise(x: np.ndarray) -> np.ndarray:
+    """Pairwise fp32 sum over the last axis (adjacent pairs, then pairs of pairs)."""
+    while x.shape[-1] > 1:
+        x = (x[..., 0::2] + x[..., 1::2]).astype(np.float32)
+    return x[..., 0]
+
+
+def kernel_cross(k: np.ndarray, c: np.ndarray, dt: str, nv: int, scale: float = SCALE):
+    """(accepted, value) as the kernel computes them for rows k, c [N, D]."""
+    N, D = k.shape
+    cpr = D // 8
+    g = cpr // nv
+    with np.errstate(over="ignore", invalid="ignore"):
+        p = O.rnd(k.astype(np.float64) * c, dt)  # DT(k_d c_d)
+        ksq = O.rnd(np.array([math.fsum(r) for r in O.rnd(k.astype(np.float64) ** 2, dt).astype(np.float64)]), dt)
+        csq = O.rnd(np.array([math.fsum(r) for r in O.rnd(c.astype(np.float64) ** 2, dt).astype(np.float64)]), dt)
+        # lane vg holds chunks vg + g*t; acc[4t+e] = the pair (2e, 2e+1) of that chunk
+        ch = p.reshape(N, nv, g, 4, 2).transpose(0, 2, 1, 3, 4).reshape(N, g, nv * 4, 2)
+        acc = _pairwise(ch.transpose(0, 1, 3, 2))  # [N, g, 2]
+        lane = (acc[..., 0] + acc[..., 1]).astype(np.float32)
+        s = _pairwise(lane)
+        t = _add_dir(ksq, csq, True).astype(np.float64)
+        b = _add_dir(t * scale, np.full(N, SLACK[dt]), True)
+        lo = _add_dir(s, -b.astype(np.float64), False)
+        hi = _add_dir(s, b, True)
+        rl, rh = O.rnd(lo, dt), O.rnd(hi, dt)
+        p64 = p.astype(np.float64)
+        fin = np.isfinite(p64).all(axis=1)
+        exact = O.rnd(np.array([math.fsum(r) if f else r.sum() for r, f in zip(p64, fin)]), dt)
+    return rl == rh, rl, exact
+
+
+def absorbed_rows(dt: str, D: int, rng: np.random.Generator, n: int = 512):
+    """Rows (k, c = 1) whose fp32 tree sum lands below a dtype midpoint while
+    the exact sum lies above it: +2^-19 meets +B in the tree's first level
+    (elements 0 and 2 share a packed lane) and vanishes, -B cancels B one level
+    up, and 1 + h - 2^-20 (h half a dtype ulp at 1) is summed elsewhere."""
+    h, big, top = (2.0 ** -8, 256.0, 4) if dt == "bf16" else (2.0 ** -11, 64.0, 2)  # f16: k_sq stays finite
+    k = np.zeros((n, D))
+    k[:, 0], k[:, 2], k[:, 4] = big, 2.0 ** -19, -big
+    k[:, 8], k[:, 16], k[:, 24] = 1.0, h, -2.0 ** -20
+    k *= (2.0 ** rng.integers(-3, top, n) * rng.choice([-1.0, 1.0], n))[:, None]
+    return k, np.ones((n, D))
+
+
+def _cases(dt: str, D: int, rng: np.random.Generator):
+    n = 4000
+    z = lambda *s: rng.standard_normal(s)
+    k = z(n, D)
+    yield "near", k, k + 0.05 * z(n, D)
+    yield "unrelated", z(n, D), z(n, D)
+    yield "scaled_small", 1e-3 * z(n, D), 1e-3 * z(n, D)
+    yield "scaled_large", 30.0 * z(n, D), 30.0 * z(n, D)
+    yield "mismatched", 10.0 * z(n, D), 0.1 * z(n, D)
+    yield "integers", rng.integers(-6, 7, (n, D)).astype(np.float64), rng.integers(-8, 9, (n, D)).astype(np.float64)
+    yield "heavy_tail", rng.standard_t(2.0, (n, D)), rng.standard_t(2.0, (n, D))
+    yield "tiny", 3e-4 * z(n, D), 3e-4 * z(n, D)
+    yield "overflow", 300.0 * z(n, D), 300.0 * z(n, D)
+    yield ("absorbed",) + absorbed_rows(dt, D, rng)
+
+
+@pytest.mark.parametrize("dt,D,nv", [("bf16", 128, 2), ("bf16", 128, 4), ("bf16", 128, 1), ("f16", 64, 1),
+                                     ("f16", 64, 2), ("f16", 128, 2)])
+def test_accepted_cross_terms_are_exactly_rounded(dt: str, D: int, nv: int) -> None:
+    rng = np.random.default_rng(1000 + D + nv + (dt == "f16"))
+    for name, k, c in _cases(dt, D, rng):
+        k, c = O.rnd(k, dt), O.rnd(c, dt)
+        ok, got, exact = kernel_cross(k, c, dt, nv)
+        wrong = ok & ~((got == exact) | (np.isnan(got) & np.isnan(exact)))
+        assert not wrong.any(), f"{dt} D={D} nv={nv} {name}: {int(wrong.sum())} accepted values differ"
+        floor = {"near": 0.99, "unrelated": 0.9}.get(name)
+        if floor is not None:  # children near their keys, as VQ assigns them, almost never take the fp64 path
+            assert ok.mean() > floor, f"{name}: acceptance {ok.mean():.3f}"
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_absorbed_rows_need_the_bound(dt: str) -> None:
+    """The absorbed rows defeat a bound 2^19 times too small: the test above
+    can see a wrong bound."""
+    k, c = absorbed_rows(dt, 128, np.random.default_rng(7))
+    k, c = O.rnd(k, dt), O.rnd(c, dt)
+    ok, got, exact = kernel_cross(k, c, dt, 2)
+    assert not ok.any()
+    ok, got, exact = kernel_cross(k, c, dt, 2, scale=SCALE * 2.0 ** -19)
+    assert (ok & (got != exact)).all()
