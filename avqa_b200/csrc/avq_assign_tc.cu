@@ -43,11 +43,12 @@ constexpr int A_MAX_M0 = 4096;
 constexpr int A_MAX_C = 8;           // children per parent on this path
 constexpr int A_KP = 4;              // keys per cp.async group of the child stage
 constexpr int A_CSQ_PER_WARP = 64;   // staged child norms per warp: ring slots x C <= 64
+constexpr int A_RING_GROUPS = 4;     // most ring groups of a row warp's child stage
 
 constexpr int AB_K = 0, AB_PFULL = 1, AB_PEMPTY = 3, AB_SFULL = 5, AB_SCONS = 7, AB_END = 9, AN_BARS = 10;
 
 struct AssignLayout {
-  int k, p[2], ps2, csq, bars, misc, total;
+  int k, p[2], ps2, csq, rbar, bars, misc, total;
 };
 
 __host__ __device__ inline AssignLayout assign_layout(int D, int M0) {
@@ -64,10 +65,12 @@ __host__ __device__ inline AssignLayout assign_layout(int D, int M0) {
   o += nch * (ACH / 2) * 4;
   L.csq = o;
   o += 4 * A_CSQ_PER_WARP * 4;
+  L.rbar = o;  // child-stage ring barriers, A_RING_GROUPS per row warp
+  o += 4 * A_RING_GROUPS * 8;
   L.bars = o;
   o += AN_BARS * 8;
   L.misc = o;
-  o += 16;
+  o += 32;  // TMEM slot, abort flag, per-warp maxima of the parent norms
   L.total = o;
   return L;
 }
@@ -77,6 +80,20 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
   return r;
 }
+
+template <int DT>
+__device__ __forceinline__ uint32_t hfma2_dt(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  if (DT == DT_BF16) asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  else asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+
+// A quarter of the dtype's largest finite value.
+template <int DT>
+struct DtQuarterMax {
+  static constexpr float v = DT == DT_F16 ? 16376.f : 0x1.FEp125f;
+};
 
 template <int DT>
 __device__ __forceinline__ uint32_t hadd2_dt(uint32_t a, uint32_t b) {
@@ -96,12 +113,22 @@ __device__ __forceinline__ uint32_t order2(uint32_t d2) {
 __device__ __forceinline__ int key_lo(uint32_t k2, uint32_t idx2) { return (int)prmt(k2, idx2, 0x1054u); }
 __device__ __forceinline__ int key_hi(uint32_t k2, uint32_t idx2) { return (int)prmt(k2, idx2, 0x3276u); }
 
-// cp.async with memory clobbers: shared-memory reads of a ring slot stay
-// between the wait that fills it and the copy that refills it.
-__device__ __forceinline__ void ring_cp16(void* smem, const void* gmem, bool pred) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem), "r"(pred ? 16 : 0)
+__device__ __forceinline__ void drain(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!tc::mbar_try(bar, parity) && clock64() - t0 < tc::kWaitCycles / 8) {
+  }
+}
+
+// Global -> shared bulk copy (TMA engine, no tensor map), completing on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   tc::smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(tc::smem_addr(bar))
                : "memory");
 }
+
+// cp.async with memory clobbers: shared-memory reads of a ring slot stay
+// between the wait that fills it and the copy that refills it.
 __device__ __forceinline__ void ring_cp4(void* smem, const void* gmem) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
 }
@@ -148,41 +175,51 @@ struct ChildBound {
 // rounding are monotone, so when both ends of [S' - b, S' + b] (rounded
 // outwards) round to the same dtype value that value is the exact sum's
 // rounding; otherwise (close to a dtype rounding boundary, or non-finite)
-// the row is summed again in fp64.  After the butterfly every lane of a row
-// holds the row's sums of all A_KP keys, so lane vg finishes key vg % A_KP:
-// the rounding test, the distance and the argmin run once per lane, not once
-// per key.  torch.argmin over the children (first minimum, a NaN wins) is a
+// the row is summed again in fp64.  The row's lanes reduce-scatter the A_KP
+// keys' sums, so each lane finishes one key: the rounding test, the distance
+// and the argmin run once per lane, not once per key.  torch.argmin over the children (first minimum, a NaN wins) is a
 // signed min over 32-bit keys: the order-preserving integer form of the
 // distance, whose low 13 bits are zero for dtype values, or'ed with the
 // child index.
 template <int DT, int D, int NV, int NG>
-__device__ __forceinline__ int child_stage(unsigned char* ring, float* csr, const unsigned char* ktile, int warp,
-                                           int lane, uint32_t livemask, int pbest, float ksq,
-                                           const unsigned char* __restrict__ chh, const float* __restrict__ csqh,
-                                           int C) {
+__device__ __forceinline__ int child_stage(unsigned char* ring, float* csr, uint64_t* rbar, volatile int* abort,
+                                           const unsigned char* ktile, int warp, int lane, uint32_t livemask, int pbest,
+                                           float ksq, const unsigned char* __restrict__ chh,
+                                           const float* __restrict__ csqh, int C) {
+  static_assert(NG <= A_RING_GROUPS, "ring barriers");
   constexpr int CPR = D / 8, G = CPR / NV, KP = A_KP, NGRP = 32 / KP;
   static_assert(G >= KP && G % KP == 0 && 32 % G == 0, "lanes per row");
   constexpr int RB = D * 2;  // bytes per child row
   const unsigned full = 0xffffffffu;
-  const int vg = lane % G, rsub = lane / G, kq = lane % KP;
+  static_assert(KP == 4, "two halving levels");
+  const int vg = lane % G, rsub = lane / G;
+  const bool hb1 = (vg & (G / 2)) != 0, hb2 = (vg & (G / 4)) != 0;
+  const int kq = (hb1 ? 2 : 0) + (hb2 ? 1 : 0);  // the key of the group this lane finishes
   const bool rowon = rsub < C;
   const int blk = C * RB;
   const int boff_mine = pbest * blk;  // byte offset of this lane's key's child block in the head
   const int lane_off = rsub * RB + vg * 16;
-  auto issue = [&](int grp) {  // keys KP*grp .. KP*grp+KP-1 into ring group grp % NG
-    const int sg = grp % NG;
-#pragma unroll
-    for (int kk = 0; kk < KP; ++kk) {
-      const int k = grp * KP + kk;
-      const int boff = __shfl_sync(full, boff_mine, k);
-      const bool on = ((livemask >> k) & 1u) != 0u;
-      if (rowon) {
-        unsigned char* dst = ring + (sg * KP + kk) * blk + lane_off;
-        const unsigned char* src = on ? chh + boff + lane_off : chh;
-#pragma unroll
-        for (int t = 0; t < NV; ++t) ring_cp16(dst + G * 16 * t, src + (on ? G * 16 * t : 0), on);
-        if (vg == 0 && on) ring_cp4(csr + (sg * KP + kk) * C + rsub, csqh + boff / RB + rsub);
-      }
+  (void)warp;
+  // keys KP*grp .. KP*grp+KP-1 into ring group grp % NG: each live key's
+  // owner lane copies its block with one bulk copy, and its C norms with a
+  // second one when they are whole 16-byte units (else 4-byte cp.async); the
+  // group's first owner arms the barrier.  Every lane's reads of the slot fed
+  // the shuffles of the reductions before, so they are complete when the
+  // owner's copy is issued.
+  auto issue = [&](int grp) {
+    const bool csq_bulk = (C & 3) == 0 && ((uintptr_t)csqh & 15u) == 0;
+    const uint32_t key_bytes = (uint32_t)blk + (csq_bulk ? 4u * C : 0u);
+    const int sg = grp % NG, kk = lane % KP;
+    const uint32_t gl = (livemask >> (grp * KP)) & ((1u << KP) - 1u);
+    if (lane == grp * KP) tc::mbar_expect_tx(&rbar[sg], (uint32_t)__popc(gl) * key_bytes);
+    __syncwarp();
+    if (lane / KP == grp && ((gl >> kk) & 1u)) {
+      bulk_g2s(ring + (sg * KP + kk) * blk, chh + boff_mine, (uint32_t)blk, &rbar[sg]);
+      float* cdst = csr + (sg * KP + kk) * C;
+      const float* csrc = csqh + pbest * C;
+      if (csq_bulk) bulk_g2s(cdst, csrc, 4u * C, &rbar[sg]);
+      else
+        for (int c = 0; c < C; ++c) ring_cp4(cdst + c, csrc + c);
     }
     ring_commit();
   };
@@ -203,11 +240,13 @@ __device__ __forceinline__ int child_stage(unsigned char* ring, float* csr, cons
   int mine = -1;
 #pragma unroll 1
   for (int gq = 0; gq < NG; ++gq) issue(gq);
+  int gq = 0;
 #pragma unroll 1
-  for (int gq = 0; gq < NGRP; ++gq) {
+  for (; gq < NGRP; ++gq) {
+    const int sg = gq % NG;
+    if (!__all_sync(full, tc::mbar_wait(&rbar[sg], (gq / NG) & 1, abort))) break;
     ring_wait<NG - 1>();
     __syncwarp();  // the child norms come from other lanes' copies
-    const int sg = gq % NG;
     float sx[KP];
 #pragma unroll
     for (int kk = 0; kk < KP; ++kk) {
@@ -229,24 +268,29 @@ __device__ __forceinline__ int child_stage(unsigned char* ring, float* csr, cons
         for (int i = 0; i + st < NV * 4; i += 2 * st) acc[i] = add_f32x2(acc[i], acc[i + st]);
       sx[kk] = acc[0].x + acc[0].y;
     }
+    // reduce-scatter of the four keys' row sums over the row's G lanes: the
+    // lanes G/2 apart swap a pair of keys and keep the other, the lanes G/4
+    // apart one key of the pair, and a butterfly over the rest completes the
+    // lane's key kq (every lane of it then holds the same sum)
+    float sv;
+    {
+      const float s0 = hb1 ? sx[0] : sx[2], s1 = hb1 ? sx[1] : sx[3];
+      const float r0 = __shfl_xor_sync(full, s0, G / 2), r1 = __shfl_xor_sync(full, s1, G / 2);
+      const float w0 = (hb1 ? sx[2] : sx[0]) + r0, w1 = (hb1 ? sx[3] : sx[1]) + r1;
+      const float r = __shfl_xor_sync(full, hb2 ? w0 : w1, G / 4);
+      sv = (hb2 ? w1 : w0) + r;
+    }
 #pragma unroll
-    for (int o = 1; o < G; o <<= 1)
-#pragma unroll
-      for (int kk = 0; kk < KP; ++kk) sx[kk] += __shfl_xor_sync(full, sx[kk], o);
-    // this lane's key: kq = vg % KP
-    float sv = sx[0];
-#pragma unroll
-    for (int kk = 1; kk < KP; ++kk) sv = kq == kk ? sx[kk] : sv;
+    for (int o = 1; o < G / 4; o <<= 1) sv += __shfl_xor_sync(full, sv, o);
     const float ksk = __shfl_sync(full, ksq, gq * KP + kq);
     const float cs = rowon ? csr[(sg * KP + kq) * C + rsub] : 0.f;
     const float bnd = __fmaf_ru(__fadd_ru(ksk, cs), ChildBound<DT>::scale, ChildBound<DT>::slack);
     float cross = rnd<DT>(__fsub_rd(sv, bnd));
     const bool bad = rowon && !(cross == rnd<DT>(__fadd_ru(sv, bnd)));
-    const uint32_t badb = __ballot_sync(full, bad);
-    if (badb) {
+    if (__any_sync(full, bad)) {
 #pragma unroll
       for (int kk = 0; kk < KP; ++kk) {
-        if (!(badb & (0x11111111u << kk))) continue;  // lanes finishing key kk: lane % KP == kk
+        if (!__any_sync(full, bad && kq == kk)) continue;
         const int rk = warp * 32 + gq * KP + kk;
         double e64 = 0.0;
 #pragma unroll
@@ -271,20 +315,20 @@ __device__ __forceinline__ int child_stage(unsigned char* ring, float* csr, cons
     int key = !rowon ? 0x7FFFFFFF : isnan(dd) ? (int)(0x80000000u | (uint32_t)rsub) : (ord & ~0x1FFF) | rsub;
 #pragma unroll
     for (int o = G; o < 32; o <<= 1) key = min(key, __shfl_xor_sync(full, key, o));
-    // lanes 0 .. KP-1 (row 0, vg = kk) now hold keys 0 .. KP-1 of the group
-    const int res = __shfl_sync(full, key, kq);
+    // row 0's lane vg = (kk >> 1) G/2 + (kk & 1) G/4 now holds key kk of the group
+    const int kk_own = lane % KP;
+    const int res = __shfl_sync(full, key, (kk_own >> 1) * (G / 2) + (kk_own & 1) * (G / 4));
     if (lane / KP == gq) mine = res & 0x1FFF;
     // every value read from this ring group fed the reductions above: refill it
     if (gq + NG < NGRP) issue(gq + NG);
     else ring_commit();
   }
-  return mine;
-}
-
-__device__ __forceinline__ void drain(uint64_t* bar, uint32_t parity) {
-  const long long t0 = clock64();
-  while (!tc::mbar_try(bar, parity) && clock64() - t0 < tc::kWaitCycles / 8) {
+  if (gq < NGRP) {  // a wait gave up: let the copies in flight land before the CTA exits
+    for (int g2 = gq; g2 < NGRP && g2 < gq + NG; ++g2) drain(&rbar[g2 % NG], (g2 / NG) & 1);
+    ring_wait<0>();
+    return -1;
   }
+  return mine;
 }
 
 template <int DT, int D>
@@ -304,22 +348,54 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.bars);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + L.misc);
   volatile int* abort = reinterpret_cast<volatile int*>(sm + L.misc + 4);
+  float* psq_wmax = reinterpret_cast<float*>(sm + L.misc + 16);
   uint32_t* ps2 = reinterpret_cast<uint32_t*>(sm + L.ps2);
+  int np[2] = {0, 0};  // parent chunks issued per buffer (TMA producer)
 
-  if (tid == 0) {
+  if (warp == 5 && lane == 0) {
+    // the producer initialises the barriers and starts the key tile and the
+    // first two parent chunks while the other warps set up
     for (int i = 0; i < AN_BARS; ++i) tc::mbar_init(&bars[i], (i == AB_SCONS || i == AB_SCONS + 1) ? AR : 1);
+    for (int i = 0; i < 4 * A_RING_GROUPS; ++i) tc::mbar_init(reinterpret_cast<uint64_t*>(sm + L.rbar) + i, 1);
     *abort = 0;
     tc::fence_mbar_init();
+    tc::tma_prefetch_desc(&tm_k);
+    tc::tma_prefetch_desc(&tm_p);
+    tc::mbar_expect_tx(&bars[AB_K], AR * D * 2);
+    for (int kb = 0; kb < D / 64; ++kb) {
+      int c[4];
+      c[0] = kb * 64;
+      c[kpos.x] = s0;
+      c[kpos.y] = h;
+      c[kpos.z] = b;
+      tc::tma_load_4d(sm + L.k + kb * AR * 128, &tm_k, c[0], c[1], c[2], c[3], &bars[AB_K]);
+    }
+    for (int ci = 0; ci < 2 && ci < nch; ++ci) {
+      tc::mbar_expect_tx(&bars[AB_PFULL + ci], ACH * D * 2);
+      for (int kb = 0; kb < D / 64; ++kb)
+        tc::tma_load_3d(sm + L.p[ci] + kb * ACH * 128, &tm_p, kb * 64, ci * ACH, h, &bars[AB_PFULL + ci]);
+      ++np[ci];
+    }
   }
   if (warp == 4) tc::tmem_alloc(tslot, A_TMEM_COLS);
   if (tid < AR) {
     // squared parent norms as dtype pairs; +inf beyond M0 (never the minimum)
+    float mx = 0.f;
     for (int j = tid; j < nch * (ACH / 2); j += AR) {
       const int p = 2 * j;
       const float a0 = p < M0 ? p_sq[(long)h * M0 + p] : INFINITY;
       const float a1 = p + 1 < M0 ? p_sq[(long)h * M0 + p + 1] : INFINITY;
       ps2[j] = pack2<DT>(a0, a1);
+      // largest real norm; a NaN sticks (fmaxf would drop it)
+      if (p < M0) mx = (a0 > mx || isnan(a0)) ? a0 : mx;
+      if (p + 1 < M0) mx = (a1 > mx || isnan(a1)) ? a1 : mx;
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float y = __shfl_xor_sync(0xffffffffu, mx, o);
+      mx = (y > mx || isnan(y)) ? y : mx;
+    }
+    if (lane == 0) psq_wmax[warp] = mx;
   }
   tc::tc_before_sync();
   __syncthreads();
@@ -327,22 +403,10 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
   const uint32_t tbase = *tslot;
 
   if (warp == 5) {
-    if (lane == 0) {  // ---- TMA producer ----
-      tc::tma_prefetch_desc(&tm_k);
-      tc::tma_prefetch_desc(&tm_p);
-      int np[2] = {0, 0};
-      tc::mbar_expect_tx(&bars[AB_K], AR * D * 2);
-      for (int kb = 0; kb < D / 64; ++kb) {
-        int c[4];
-        c[0] = kb * 64;
-        c[kpos.x] = s0;
-        c[kpos.y] = h;
-        c[kpos.z] = b;
-        tc::tma_load_4d(sm + L.k + kb * AR * 128, &tm_k, c[0], c[1], c[2], c[3], &bars[AB_K]);
-      }
-      for (int ci = 0; ci < nch; ++ci) {
+    if (lane == 0) {  // ---- TMA producer: parent chunks from the third on ----
+      for (int ci = 2; ci < nch; ++ci) {
         const int s = ci & 1;
-        if (ci >= 2 && !tc::mbar_wait(&bars[AB_PEMPTY + s], ((ci - 2) >> 1) & 1, abort)) break;
+        if (!tc::mbar_wait(&bars[AB_PEMPTY + s], ((ci - 2) >> 1) & 1, abort)) break;
         tc::mbar_expect_tx(&bars[AB_PFULL + s], ACH * D * 2);
         for (int kb = 0; kb < D / 64; ++kb)
           tc::tma_load_3d(sm + L.p[s] + kb * ACH * 128, &tm_p, kb * 64, ci * ACH, h, &bars[AB_PFULL + s]);
@@ -400,8 +464,12 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
       return *reinterpret_cast<const uint4*>(sm + L.k + kb * AR * 128 + r * 128 + ((j ^ (r & 7)) << 4));
     };
     float ksq = 0.f;
-    if (ok) {  // k_sq = DT(sum DT(k_d^2)) (quantizer.py:208), fp64 partial sums
-      double acc[4] = {0.0, 0.0, 0.0, 0.0};
+    if (ok) {
+      // k_sq = DT(sum DT(k_d^2)) with the sum exact (quantizer.py:208): fp32
+      // pairs accumulate D/8 terms each, then three more additions, so the
+      // rounding error of the nonnegative sum is at most gamma_18 S <= 2^-19 S';
+      // where that interval straddles a dtype rounding boundary, fp64
+      float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll 4
       for (int v = 0; v < D / 8; ++v) {
         const uint4 u = key_chunk(v);
@@ -409,12 +477,35 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const uint32_t sq = hmul2_dt<DT>(w[e], w[e]);
-          acc[e] += (double)half_lo<DT>(sq) + (double)half_hi<DT>(sq);
+          acc[e] = add_f32x2(acc[e], make_float2(half_lo<DT>(sq), half_hi<DT>(sq)));
         }
       }
-      ksq = rnd64<DT>((acc[0] + acc[1]) + (acc[2] + acc[3]));
+      const float2 t2 = add_f32x2(add_f32x2(acc[0], acc[1]), add_f32x2(acc[2], acc[3]));
+      const float s32 = t2.x + t2.y;
+      const float bnd = __fmul_ru(s32, 0x1p-19f);
+      ksq = rnd<DT>(__fsub_rd(s32, bnd));
+      if (!(ksq == rnd<DT>(__fadd_ru(s32, bnd)))) {
+        double a64 = 0.0;
+        for (int v = 0; v < D / 8; ++v) {
+          const uint4 u = key_chunk(v);
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t sq = hmul2_dt<DT>(w[e], w[e]);
+            a64 += (double)half_lo<DT>(sq) + (double)half_hi<DT>(sq);
+          }
+        }
+        ksq = rnd64<DT>(a64);
+      }
     }
     const uint32_t ksq2 = dup2<DT>(ksq);
+    // every distance of the warp's keys is finite when k_sq + max p_sq stays
+    // below a quarter of the dtype's range (|2 k.p| <= k_sq + p_sq up to
+    // rounding): then no NaN can win, and DT(s - DT(2x)) = fma(-2, x, s) as
+    // doubling is exact
+    const float psqmax = fmaxf(fmaxf(psq_wmax[0], psq_wmax[1]), fmaxf(psq_wmax[2], psq_wmax[3]));
+    const bool finite_w =
+        __all_sync(0xffffffffu, !isnan(psq_wmax[0] + psq_wmax[1] + psq_wmax[2] + psq_wmax[3]) &&
+                                    ksq + psqmax <= DtQuarterMax<DT>::v);
     int best = 0x7FFFFFFF;
     uint32_t nanacc = 0u;
     for (int ci = 0; ok && ci < nch; ++ci) {
@@ -428,6 +519,24 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
       uint32_t qa[32], qb[32];
       auto scan = [&](const uint32_t (&r)[32], int quarter) {
         const uint4* pp = reinterpret_cast<const uint4*>(ps2 + ci * (ACH / 2) + 16 * quarter);
+        if (finite_w) {
+          int qbest = 0x7FFFFFFF;  // keys with the index within the quarter
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 pq = pp[q];
+            const uint32_t pv[4] = {pq.x, pq.y, pq.z, pq.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int j = 4 * q + k;
+              const uint32_t x2 = pack2<DT>(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));  // DT(k . p)
+              const uint32_t d2 = hfma2_dt<DT>(x2, 0xC000C000u, hadd2_dt<DT>(ksq2, pv[k]));
+              const uint32_t k2 = order2(d2), il = (uint32_t)(2 * j) | ((uint32_t)(2 * j + 1) << 16);
+              qbest = min(qbest, min(key_lo(k2, il), key_hi(k2, il)));
+            }
+          }
+          best = min(best, qbest + (ci * ACH + 32 * quarter));  // the index half has room: M0 <= 4096
+          return;
+        }
         const uint32_t base2 = (uint32_t)(ci * ACH + 32 * quarter) * 0x10001u + 0x10000u;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -484,25 +593,27 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
     }
     // child stage: the assigned parent's children (quantizer.py:218-226), a
     // warp's 32 keys through a cp.async ring in the now idle parent buffers
+    int bi = -1;
     if (ok) {
       const uint32_t livemask = __ballot_sync(0xffffffffu, live);
       unsigned char* ring = sm + L.p[0] + warp * (ACH * D);
       float* csr = reinterpret_cast<float*>(sm + L.csq) + warp * A_CSQ_PER_WARP;
+      uint64_t* rbar = reinterpret_cast<uint64_t*>(sm + L.rbar) + warp * A_RING_GROUPS;
       const unsigned char* chh = reinterpret_cast<const unsigned char*>(children + (long)h * M0 * C * D);
       const float* csqh = c_sq + (long)h * M0 * C;
       const unsigned char* kt = sm + L.k;
-      int bi;
       if constexpr (D == 128)
-        bi = C <= 2 ? child_stage<DT, D, 1, 4>(ring, csr, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
-             : C <= 4 ? child_stage<DT, D, 2, 4>(ring, csr, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
-                      : child_stage<DT, D, 4, 2>(ring, csr, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C);
+        bi = C <= 2 ? child_stage<DT, D, 1, 4>(ring, csr, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
+             : C <= 4 ? child_stage<DT, D, 2, 4>(ring, csr, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
+                      : child_stage<DT, D, 4, 2>(ring, csr, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C);
       else
-        bi = C <= 4 ? child_stage<DT, D, 1, 4>(ring, csr, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
-                    : child_stage<DT, D, 2, 2>(ring, csr, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C);
-      if (live) {
-        passign[(long)g * S + s] = pbest;
-        cassign[(long)g * S + s] = bi;
-      }
+        bi = C <= 4 ? child_stage<DT, D, 1, 4>(ring, csr, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
+                    : child_stage<DT, D, 2, 2>(ring, csr, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C);
+    }
+    if (live) {  // a CTA that gave up on a wait still leaves indices in range for the later kernels
+      const bool good = ok && bi >= 0;
+      passign[(long)g * S + s] = good ? pbest : 0;
+      cassign[(long)g * S + s] = good ? bi : 0;
     }
   }
 
@@ -532,7 +643,9 @@ int launch_assign_tc(const QuantizeArgs& a, cudaStream_t st) {
   if (!tc::map_rows4(&tk, DT, a.keys, a.ks, a.B, a.H, a.S, D, AR, &kpos) ||
       !tc::map_rows3(&tp, DT, a.parents_dt, a.H, a.M0, D, ACH))
     return AVQ_ERR_UNSUPPORTED;
-  if (a.C < 1 || a.C > A_MAX_C) return AVQ_ERR_UNSUPPORTED;
+  // the child blocks move with bulk copies: 16-byte aligned rows
+  if (a.C < 1 || a.C > A_MAX_C || (uintptr_t)a.children_dt % 16 != 0 || (uintptr_t)a.c_sq % 4 != 0)
+    return AVQ_ERR_UNSUPPORTED;
   const AssignLayout L = assign_layout(D, a.M0);
   const size_t smem = std::max<size_t>((size_t)L.total + 1024, 80 * 1024);  // <= 2 CTAs (2 x 256 TMEM columns) per SM
   auto go = [&](auto kfn) {

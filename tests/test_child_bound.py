@@ -52,6 +52,16 @@ def _pairwise(x: np.ndarray) -> np.ndarray:
     return x[..., 0]
 
 
+def _lane_tree(lane: np.ndarray) -> np.ndarray:
+    """The kernel's combination of a row's G lane sums: lanes G/2 apart, then
+    G/4 apart (the reduce-scatter of the keys), then 1, 2, ... (butterfly)."""
+    g = lane.shape[-1]
+    idx = np.arange(g)
+    for o in [g // 2, g // 4] + [1 << i for i in range(int(math.log2(g // 4)))]:
+        lane = (lane + lane[..., idx ^ o]).astype(np.float32)
+    return lane[..., 0]
+
+
 def kernel_cross(k: np.ndarray, c: np.ndarray, dt: str, nv: int, scale: float = SCALE):
     """(accepted, value) as the kernel computes them for rows k, c [N, D]."""
     N, D = k.shape
@@ -65,7 +75,7 @@ def kernel_cross(k: np.ndarray, c: np.ndarray, dt: str, nv: int, scale: float = 
         ch = p.reshape(N, nv, g, 4, 2).transpose(0, 2, 1, 3, 4).reshape(N, g, nv * 4, 2)
         acc = _pairwise(ch.transpose(0, 1, 3, 2))  # [N, g, 2]
         lane = (acc[..., 0] + acc[..., 1]).astype(np.float32)
-        s = _pairwise(lane)
+        s = _lane_tree(lane)
         t = _add_dir(ksq, csq, True).astype(np.float64)
         b = _add_dir(t * scale, np.full(N, SLACK[dt]), True)
         lo = _add_dir(s, -b.astype(np.float64), False)

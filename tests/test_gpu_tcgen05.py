@@ -182,3 +182,23 @@ def test_tcgen05_assignment_integer_ties(dt: str, D: int, C: int) -> None:
                                   want.parent_assignments)
     np.testing.assert_array_equal(a.cassign.cpu().numpy().reshape(want.child_assignments.shape),
                                   want.child_assignments)
+
+
+def test_tcgen05_assignment_large_f16_takes_the_guarded_scan() -> None:
+    """f16 keys large enough that k_sq + max p_sq exceeds a quarter of the
+    f16 range: the parent scan keeps its NaN tracking and separate doubling."""
+    w = Workload("q_large_f16", B=1, T=8, S=700, H=2, D=64, M0=96, C=4, P=8, dtype="f16", keys="mixture", seed=56)
+    _, k, v = make_inputs(w)
+    kn, vn = O.rnd(12.0 * k.numpy(), "f16"), O.rnd(v.numpy(), "f16")
+    kh0 = torch.from_numpy(kn).view(w.B, w.S, w.H, w.D).transpose(1, 2)[0]
+    cbk = codebook_from_keys(kh0, w.M0, w.C, w.seed)
+    pd, cd = O.cast_codebook(cbk.parents.numpy(), cbk.children.numpy(), "f16")
+    assert float(O.sq_norms(kn.reshape(-1, w.D), "f16").max() + O.sq_norms(pd.reshape(-1, w.D), "f16").max()) > 16376
+    cb = ops.prepare_codebook(cbk.parents, cbk.children, torch.float16, torch.device("cuda"))
+    kd, vd = to_dev(kn, "f16"), to_dev(vn, "f16")
+    a = _quantize(w, kd, vd, cb, True)
+    b = _quantize(w, kd, vd, cb, False)
+    _assert_same_quant(a, b, w.name)
+    want = O.quantize(O.split_heads(kn, w.H), O.split_heads(vn, w.H), pd, cd, "f16")
+    check_quantization(quant_arrays(a, w.B, w.H), O.split_heads(kn, w.H), O.split_heads(vn, w.H), pd, cd, "f16", want,
+                       tag=w.name)
