@@ -4,16 +4,18 @@
 // sums a = e @ V and the per-parent importance partials of the first routing
 // pass.
 //
-// CTA = 128 queries of one (b,h) = one UMMA M tile.  Threads 0-127 (warps
-// 0-3) own one query row each, i.e. TMEM lane = row; warp 4 issues the
-// tcgen05.mma instructions; warp 5 streams Q, parent and parent-sum tiles with
-// TMA into 128-byte-swizzled shared memory.
+// CTA = 128 queries of one (b,h) = one UMMA M tile.  Each query row has two
+// threads (warps w and w+4 share TMEM lane quarter w): half hf takes parents
+// 32hf..32hf+31 of every 64-parent chunk, and the halves combine their row
+// statistics once per pass.  Warp 8 issues the tcgen05.mma instructions;
+// warp 9 streams Q, parent and parent-sum tiles with TMA into
+// 128-byte-swizzled shared memory.
 //
 // TMEM, 256 columns: the fp32 accumulator O = e @ V in [0, D) and two
 // 64-column logit buffers at [D, D+64) and [D+64, D+128).  A buffer receives
-// one 64-parent chunk of Q P^T; in the second pass the row threads overwrite
-// its first 32 columns with the chunk's dtype exponentials (two per column),
-// which are the A operand of the e @ V MMA.
+// one 64-parent chunk of Q P^T; in the second pass half hf overwrites the
+// first 16 of its 32 columns with its 32 dtype exponentials (two per column),
+// the A operand of the e @ V MMA (K steps at columns 0, 8, 32, 40).
 //
 //   pass 1  S_c = Q P_c^T for every chunk c; row max of the narrowed,
 //           scaled, masked logits.
@@ -47,7 +49,9 @@ namespace {
 
 constexpr int TR = 128;        // queries per CTA
 constexpr int TCH = 64;        // parents per chunk
-constexpr int TTHREADS = 192;  // 4 row warps + MMA warp + TMA warp
+constexpr int TROW = 256;      // two row threads per query
+constexpr int TTHREADS = 320;  // 8 row warps + MMA warp + TMA warp
+constexpr int W_MMA = 8, W_TMA = 9;
 constexpr int TC_TMEM_COLS = 256;
 constexpr uint32_t EXP_BASE = 0x3AFF;  // bf16 bits of the largest |d| whose exp rounds to 1
 constexpr int EXP_N = 2051;            // entries 0..2049: |d| bits EXP_BASE + i; 2050: |d| > 128, inf, NaN
@@ -59,7 +63,7 @@ constexpr int B_Q = 0, B_PFULL = 1, B_PEMPTY = 3, B_VFULL = 5, B_VEMPTY = 7, B_S
               B_OFULL = 14, B_COMB = 15, B_STG = 16, N_BARS = 18;
 
 struct TcLayout {
-  int q, p[2], v[2], exptab, pm2, n2, srow, scomb, bars, misc, total;
+  int q, p[2], v[2], exptab, pm2, n2, srow, scomb, xch, bars, misc, total;
 };
 
 __host__ __device__ inline TcLayout tc_layout(int D, int M0) {
@@ -86,7 +90,11 @@ __host__ __device__ inline TcLayout tc_layout(int D, int M0) {
   L.srow = o;
   o += TR * 4 * 4;
   L.scomb = o;
-  o += 2 * 4 * 128 * 4;
+  o += 2 * 8 * 64 * 4;
+  // the halves' row statistics [3][2][TR] before pass 3: pass 3 writes the
+  // combine buffers only after its first staging barrier, which every row
+  // thread reaches after its last exchange read
+  L.xch = L.scomb;
   L.bars = o;
   o += N_BARS * 8;
   L.misc = o;
@@ -151,6 +159,9 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// Barrier of the 256 row threads (the MMA and TMA warps do not take part).
+__device__ __forceinline__ void rows_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
 template <int DT, int D>
 __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_p,
@@ -175,20 +186,22 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
   uint32_t* n2 = reinterpret_cast<uint32_t*>(sm + L.n2);
   float* srow = reinterpret_cast<float*>(sm + L.srow);
   float* scomb = reinterpret_cast<float*>(sm + L.scomb);
+  float* xch = reinterpret_cast<float*>(sm + L.xch);
 
   // ---- setup: barriers, TMEM, tables ----
   if (tid == 0) {
     for (int i = 0; i < N_BARS; ++i)
-      tc::mbar_init(&bars[i], (i == B_EFULL || i == B_EFULL + 1 || i == B_COMB || i == B_STG || i == B_STG + 1) ? TR : 1);
+      tc::mbar_init(&bars[i],
+                    (i == B_EFULL || i == B_EFULL + 1 || i == B_COMB || i == B_STG || i == B_STG + 1) ? TROW : 1);
     *abort = 0;
     tc::fence_mbar_init();
   }
-  if (warp == 4) tc::tmem_alloc(tslot, TC_TMEM_COLS);
-  if (tid < TR) {
+  if (warp == W_MMA) tc::tmem_alloc(tslot, TC_TMEM_COLS);
+  if (tid < TROW) {
     const uint32_t* src = reinterpret_cast<const uint32_t*>(exptab_g);
     uint32_t* dst = reinterpret_cast<uint32_t*>(sm + L.exptab);
-    for (int i = tid; i < EXP_WORDS; i += TR) dst[i] = src[i];
-    for (int j = tid; j < nch * 32; j += TR) {
+    for (int i = tid; i < EXP_WORDS; i += TROW) dst[i] = src[i];
+    for (int j = tid; j < nch * 32; j += TROW) {
       const int p = 2 * j;
       const int c0 = p < M0 ? pcnt[(long)g * M0 + p] : 0, c1 = p + 1 < M0 ? pcnt[(long)g * M0 + p + 1] : 0;
       pm2[j] = (c0 > 0 ? 0xFFFFu : 0u) | (c1 > 0 ? 0xFFFF0000u : 0u);
@@ -200,7 +213,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
   tc::tc_after_sync();
   const uint32_t tbase = *tslot;
 
-  if (warp == 5) {
+  if (warp == W_TMA) {
     // ---- TMA producer ----
     if (lane == 0) {
       tc::tma_prefetch_desc(&tm_q);
@@ -241,7 +254,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
         }
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == W_MMA) {
     // ---- MMA issuer ----
     if (lane == 0) {
       const int fmt = DT == DT_BF16 ? 1 : 0;
@@ -278,10 +291,11 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
           const int u = v - nch, vs = u & 1;
           if (!(ok = tc::mbar_wait(&bars[B_VFULL + vs], (u >> 1) & 1, abort))) break;
           tc::tc_after_sync();
+          // K steps of 16 parents: columns 0, 8 (half 0) and 32, 40 (half 1)
 #pragma unroll
           for (int kk = 0; kk < TCH / 16; ++kk) {
             const uint64_t bd = tc::sdesc_sw128(va[vs] + kk * 16 * 128, TCH * 128, 1024);
-            tc::mma_ts(tbase, tbase + D + 64 * s + kk * 8, bd, idO, u > 0 || kk > 0);
+            tc::mma_ts(tbase, tbase + D + 64 * s + (kk >> 1) * 32 + (kk & 1) * 8, bd, idO, u > 0 || kk > 0);
           }
           tc::mma_commit(&bars[B_VEMPTY + vs]);
         }
@@ -300,10 +314,10 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       if (!ok) drain_wait(&bars[B_OFULL], 0);
     }
   } else {
-    // ---- row threads ----
-    const int r = tid, t = t0 + r;
+    // ---- row threads: query r, half hf (parents 32hf..32hf+31 of each chunk) ----
+    const int r = tid & (TR - 1), hf = tid >> 7, t = t0 + r;
     const bool live = t < Tq;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const float inv_sqrtD = 1.f / sqrtD;
     const uint32_t ninf2 = DT == DT_BF16 ? 0xFF80FF80u : 0xFC00FC00u;
     const long row = (long)g * Tq + t;
@@ -318,37 +332,33 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_SFULL + s], (v >> 1) & 1, abort));
       if (!ok) break;
       tc::tc_after_sync();
-      uint32_t ra[32], rb[32];
-      const uint32_t col = tbase + lane_off + D + 64 * s;
-      tc::tmem_ld32(col, ra);
-      tc::tmem_ld32(col + 32, rb);
+      uint32_t ra[32];
+      tc::tmem_ld32(tbase + lane_off + D + 64 * s + 32 * hf, ra);
       tc::tmem_wait_ld();
       tc::tc_before_sync();
       tc::mbar_arrive(&bars[B_EFULL + s]);
-      const uint4* pm4 = reinterpret_cast<const uint4*>(pm2 + v * 32);
+      const uint32_t* pm = pm2 + v * 32 + 16 * hf;
+      const uint4* pm4 = reinterpret_cast<const uint4*>(pm);
       uint32_t all = 0xFFFFFFFFu;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < 4; ++q) {
         const uint4 u = pm4[q];
         all &= u.x & u.y & u.z & u.w;
       }
       if (all == 0xFFFFFFFFu) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          mxa[i & 3] = fmax_nan(mxa[i & 3], __uint_as_float(ra[i]));
-          mxa[i & 3] = fmax_nan(mxa[i & 3], __uint_as_float(rb[i]));
-        }
+        for (int i = 0; i < 32; ++i) mxa[i & 3] = fmax_nan(mxa[i & 3], __uint_as_float(ra[i]));
       } else {
-        const uint32_t* pm = pm2 + v * 32;
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const uint32_t bits = i < 32 ? ra[i] : rb[i - 32];
+        for (int i = 0; i < 32; ++i) {
           const bool keep = (pm[i >> 1] >> ((i & 1) * 16)) & 1u;
-          mxa[i & 3] = fmax_nan(mxa[i & 3], keep ? __uint_as_float(bits) : -INFINITY);
+          mxa[i & 3] = fmax_nan(mxa[i & 3], keep ? __uint_as_float(ra[i]) : -INFINITY);
         }
       }
     }
-    const float amax = fmax_nan(fmax_nan(mxa[0], mxa[1]), fmax_nan(mxa[2], mxa[3]));
+    xch[hf * TR + r] = fmax_nan(fmax_nan(mxa[0], mxa[1]), fmax_nan(mxa[2], mxa[3]));
+    rows_sync();
+    const float amax = fmax_nan(xch[r], xch[TR + r]);
     const float rm = rnd<DT>(__fdiv_rn(rnd<DT>(amax), sqrtD));
     const float safe = rm == -INFINITY ? 0.f : rm;  // pipeline.py:137-141
     const uint32_t m2 = dup2<DT>(safe);
@@ -359,25 +369,25 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_SFULL + s], (v >> 1) & 1, abort));
       if (!ok) break;
       tc::tc_after_sync();
-      const uint32_t col = tbase + lane_off + D + 64 * s;
+      const uint32_t col = tbase + lane_off + D + 64 * s + 32 * hf;
       float zh[2];
-      // 32 parents at a time; the second half's TMEM load is in flight while
-      // the first half is computed (its exponentials go to columns 0-15, the
-      // load reads 32-63)
-      uint32_t rh[2][32];
-      tc::tmem_ld32(col, rh[0]);
+      // 16 parents at a time; the second block's TMEM load is in flight while
+      // the first is computed (its exponentials go to columns 0-7, the load
+      // reads 16-31)
+      uint32_t rh[2][16];
+      tc::tmem_ld16(col, rh[0]);
       tc::tmem_wait_ld();
-      tc::tmem_ld32(col + 32, rh[1]);
+      tc::tmem_ld16(col + 16, rh[1]);
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         if (hh == 1) tc::tmem_wait_ld();
-        const uint32_t (&ra)[32] = rh[hh];
+        const uint32_t (&ra)[16] = rh[hh];
         // logits: DT(DT(acc) / sqrt(D)) (pipeline.py:81), branch-free fast
-        // quotients; a half with a quotient near a rounding point is redone
-        uint32_t s2[16];
+        // quotients; a block with a quotient near a rounding point is redone
+        uint32_t s2[8];
         bool near = false;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
+        for (int j = 0; j < 8; ++j) {
           const uint32_t x2 = pack2<DT>(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1]));
           const float y0 = half_lo<DT>(x2) * inv_sqrtD, y1 = half_hi<DT>(x2) * inv_sqrtD;
           near |= near_midpoint<DT>(y0) | near_midpoint<DT>(y1);
@@ -385,14 +395,15 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
         }
         if (near) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) s2[j] = logit2<DT>(ra[2 * j], ra[2 * j + 1], sqrtD, inv_sqrtD, 0xFFFFFFFFu);
+          for (int j = 0; j < 8; ++j) s2[j] = logit2<DT>(ra[2 * j], ra[2 * j + 1], sqrtD, inv_sqrtD, 0xFFFFFFFFu);
         }
-        const uint4* pm4 = reinterpret_cast<const uint4*>(pm2 + c * 32 + hh * 16);
-        const uint4* nn4 = reinterpret_cast<const uint4*>(n2 + c * 32 + hh * 16);
-        uint32_t e2[16];
-        float zs[16];
+        const int pw = c * 32 + hf * 16 + hh * 8;  // first parent pair of the block
+        const uint4* pm4 = reinterpret_cast<const uint4*>(pm2 + pw);
+        const uint4* nn4 = reinterpret_cast<const uint4*>(n2 + pw);
+        uint32_t e2[8];
+        float zs[8];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 2; ++q) {
           const uint4 pmq = pm4[q], nnq = nn4[q];
           const uint32_t pmv[4] = {pmq.x, pmq.y, pmq.z, pmq.w}, nnv[4] = {nnq.x, nnq.y, nnq.z, nnq.w};
 #pragma unroll
@@ -408,16 +419,15 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
           }
         }
 #pragma unroll
-        for (int w = 8; w >= 1; w >>= 1)
+        for (int w = 4; w >= 1; w >>= 1)
 #pragma unroll
           for (int j = 0; j < w; ++j) zs[j] += zs[j + w];
         zh[hh] = zs[0];
-        tc::tmem_st16(col + 16 * hh, e2);
-        if (live) {
-          uint4* dst = reinterpret_cast<uint4*>(srow_g + c * TCH + 32 * hh);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            if (c * TCH + 32 * hh + 8 * k < M0) dst[k] = make_uint4(e2[4 * k], e2[4 * k + 1], e2[4 * k + 2], e2[4 * k + 3]);
+        tc::tmem_st8(col + 8 * hh, e2);
+        if (live && 2 * pw < M0) {  // M0 is a multiple of 8: a block of 16 is all in or all out
+          uint4* dst = reinterpret_cast<uint4*>(srow_g + 2 * pw);
+          dst[0] = make_uint4(e2[0], e2[1], e2[2], e2[3]);
+          dst[1] = make_uint4(e2[4], e2[5], e2[6], e2[7]);
         }
       }
       za += zh[0] + zh[1];
@@ -425,14 +435,22 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       tc::tc_before_sync();
       tc::mbar_arrive(&bars[B_EFULL + s]);
     }
-    // z feeds the probabilities.  Each chunk is summed as a pairwise tree
-    // (depth 6) and the chunk sums in sequence, so the fp32 sum is within
-    // (6 + nch) * 2^-24 relative of the exact one; when the window straddles a
-    // dtype rounding point the row is summed again exactly.
-    float z = rnd<DT>(za);
+    // the halves' sums: z and l are the half-0 part plus the half-1 part in
+    // both threads of the row
+    xch[2 * TR + hf * TR + r] = za;
+    xch[4 * TR + hf * TR + r] = la0 + la1;
+    rows_sync();
+    const float zsum = xch[2 * TR + r] + xch[3 * TR + r];
+    const float lsum = xch[4 * TR + r] + xch[5 * TR + r];
+    // z feeds the probabilities.  Each half sums a chunk's 32 exponentials as
+    // a pairwise tree (depth 5), the halves' chunk sums add in sequence and
+    // the two halves once more, so the fp32 sum is within (6 + nch) * 2^-24
+    // relative of the exact one; when the window straddles a dtype rounding
+    // point the row is summed again exactly (by both threads, alike).
+    float z = rnd<DT>(zsum);
     if (ok && live) {
-      const float eps = za * (float)(nch + 8) * 5.9604645e-8f;
-      if (rnd<DT>(za - eps) != rnd<DT>(za + eps)) {
+      const float eps = zsum * (float)(nch + 8) * 5.9604645e-8f;
+      if (rnd<DT>(zsum - eps) != rnd<DT>(zsum + eps)) {
         double ex = 0.0;
         const uint4* src = reinterpret_cast<const uint4*>(srow_g);
         for (int k = 0; k < M0 / 8; ++k) {
@@ -447,17 +465,18 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_OFULL], 0, abort));
     if (ok) {
       tc::tc_after_sync();
+      // half hf writes output columns [hf D/2, (hf+1) D/2)
 #pragma unroll
-      for (int d0 = 0; d0 < D; d0 += 64) {
-        uint32_t oa[32], ob[32];
-        tc::tmem_ld32(tbase + lane_off + d0, oa);
-        tc::tmem_ld32(tbase + lane_off + d0 + 32, ob);
+      for (int d0 = 0; d0 < D / 2; d0 += 32) {
+        uint32_t oa[32];
+        const int dc = hf * (D / 2) + d0;
+        tc::tmem_ld32(tbase + lane_off + dc, oa);
         tc::tmem_wait_ld();
         if (live) {
-          uint4* dst = reinterpret_cast<uint4*>(a_out + row * D + d0);
+          uint4* dst = reinterpret_cast<uint4*>(a_out + row * D + dc);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t* src = k < 4 ? oa + 8 * k : ob + 8 * (k - 4);
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t* src = oa + 8 * k;
             dst[k] = make_uint4(pack2<DT>(__uint_as_float(src[0]), __uint_as_float(src[1])),
                                 pack2<DT>(__uint_as_float(src[2]), __uint_as_float(src[3])),
                                 pack2<DT>(__uint_as_float(src[4]), __uint_as_float(src[5])),
@@ -465,31 +484,34 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
           }
         }
       }
-      if (live) {
+      if (live && hf == 0) {
         m_out[row] = safe;
-        l_out[row] = rnd<DT>(la0 + la1);
+        l_out[row] = rnd<DT>(lsum);
         z_out[row] = z;
       }
     }
     const float zc = clamp_min_nan(z, eps_dt<DT>());
-    srow[r * 4] = zc;
-    srow[r * 4 + 1] = 1.f / zc;
-    srow[r * 4 + 2] = live ? 1.f : 0.f;
-    __syncwarp();
+    if (hf == 0) {
+      srow[r * 4] = zc;
+      srow[r * 4 + 1] = 1.f / zc;
+      srow[r * 4 + 2] = live ? 1.f : 0.f;
+    }
     // pass 3: importance partials (routing.py:61-63).  The CTA's exponential
     // rows stream through the idle tile buffers in 64-column blocks (cp.async,
-    // double-buffered, one wait per block); lane = 2 columns, the warp's 32
-    // rows summed in order; warps 0+1 and 2+3 are combined into the two
-    // 64-query tiles' partials.  Rows beyond T stage as zeros and add 0.
+    // double-buffered, one wait per block); lane = 2 columns, each thread sums
+    // 16 rows in order (rows 32(w%4) + 16hf + i), and the four 16-row sums of
+    // each 64-query tile are added in row order.  Rows beyond T stage as
+    // zeros and add 0.
     constexpr int PB = 64, BLK = TR * PB * 2;
     unsigned char* stg = sm + L.p[0];  // 2 x 16 KB: the P and V tile buffers are idle now
     const int nblk = (M0 + PB - 1) / PB;
+    const int rbase = 32 * (warp & 3) + 16 * hf;
     auto stage = [&](int blk) {
       unsigned char* buf = stg + (blk & 1) * BLK;
       const int pc = blk * PB, ch = tid & 7;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int rr = (tid >> 3) + 16 * k, tw = t0 + rr;
+      for (int k = 0; k < 4; ++k) {
+        const int rr = (tid >> 3) + 32 * k, tw = t0 + rr;
         const bool in = tw < Tq && pc + ch * 8 < M0;
         const int ts = in ? tw : t0;
         cp_async16(buf + rr * (PB * 2) + ch * 16,
@@ -511,12 +533,12 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       const unsigned char* buf = stg + (blk & 1) * BLK;
       float c0 = 0.f, c1 = 0.f;
 #pragma unroll 1
-      for (int g8 = 0; g8 < 4; ++g8) {
+      for (int g8 = 0; g8 < 2; ++g8) {
         uint32_t w[8];
         float2 zr[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int rw = warp * 32 + g8 * 8 + i;
+          const int rw = rbase + g8 * 8 + i;
           w[i] = *reinterpret_cast<const uint32_t*>(buf + rw * (PB * 2) + lane * 4);
           zr[i] = *reinterpret_cast<const float2*>(srow + rw * 4);
         }
@@ -542,15 +564,19 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
           c1 += half_hi<DT>(q2);
         }
       }
-      float* sc = scomb + (blk & 1) * 256;
+      float* sc = scomb + (blk & 1) * 512;
       sc[warp * 64 + 2 * lane] = c0;
       sc[warp * 64 + 2 * lane + 1] = c1;
       tc::mbar_arrive(&bars[B_COMB]);
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_COMB], blk & 1, abort));
       if (!ok) break;
-      const int tile = 2 * qt + (tid >> 6), cl = tid & 63, pcol = blk * PB + cl;
-      if (tile < ntiles && pcol < M0)
-        colpart[((long)g * ntiles + tile) * M0 + pcol] = sc[(tid >> 6) * 128 + cl] + sc[(tid >> 6) * 128 + 64 + cl];
+      if (tid < TR) {
+        // tile tl: rows 64tl + [0,16) warp 2tl, [16,32) warp 2tl+4, [32,48) warp 2tl+1, [48,64) warp 2tl+5
+        const int tl = tid >> 6, cl = tid & 63, pcol = blk * PB + cl, tile = 2 * qt + tl;
+        if (tile < ntiles && pcol < M0)
+          colpart[((long)g * ntiles + tile) * M0 + pcol] =
+              (sc[(2 * tl) * 64 + cl] + sc[(2 * tl + 4) * 64 + cl]) + (sc[(2 * tl + 1) * 64 + cl] + sc[(2 * tl + 5) * 64 + cl]);
+      }
     }
     cp_async_wait<0>();
   }
@@ -558,7 +584,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
   // ---- teardown ----
   tc::tc_before_sync();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == W_MMA) {
     tc::tc_after_sync();
     tc::tmem_free(tbase, TC_TMEM_COLS);
   }
