@@ -138,16 +138,6 @@ __device__ __forceinline__ void ring_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
-// Packed fp32 pair addition (one instruction for both lanes, IEEE
-// round-to-nearest per element).
-__device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
 
 // Bound on sum_d |DT(k_d c_d)| from the dtype norms: |k_d c_d| <= (k_d^2 +
 // c_d^2) / 2, and k_sq, c_sq are the once-rounded exact sums of the dtype

@@ -70,6 +70,26 @@ __device__ __forceinline__ float nanmax(float a, float b) {
 }
 __device__ __forceinline__ float clamp_min_nan(float x, float lo) { return isnan(x) ? x : (x < lo ? lo : x); }
 
+// Packed fp32 pair arithmetic (sm_100): one instruction for both elements,
+// IEEE rounding per element to nearest (rn), down (rm) or up (rp).
+#define AVQ_F32X2_OP(name, op)                                                                   \
+  __device__ __forceinline__ float2 name(float2 a, float2 b) {                                  \
+    float2 d;                                                                                    \
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t" op \
+        " rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"                                            \
+        : "=f"(d.x), "=f"(d.y)                                                                   \
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));                                               \
+    return d;                                                                                    \
+  }
+AVQ_F32X2_OP(add_f32x2, "add.rn.f32x2")
+AVQ_F32X2_OP(mul_f32x2_rd, "mul.rm.f32x2")
+AVQ_F32X2_OP(mul_f32x2_ru, "mul.rp.f32x2")
+#undef AVQ_F32X2_OP
+
+// The neighbouring fp32 values of a positive finite nonzero x.
+__device__ __forceinline__ float next_down(float x) { return __uint_as_float(__float_as_uint(x) - 1u); }
+__device__ __forceinline__ float next_up(float x) { return __uint_as_float(__float_as_uint(x) + 1u); }
+
 // Halves of a DT x2 register as floats.
 template <int DT>
 __device__ __forceinline__ float half_lo(uint32_t w) {

@@ -319,6 +319,8 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     const bool live = t < Tq;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const float inv_sqrtD = 1.f / sqrtD;
+    const float2 invl2 = make_float2(next_down(inv_sqrtD), next_down(inv_sqrtD));  // <= 1/sqrt(D)
+    const float2 invh2 = make_float2(next_up(inv_sqrtD), next_up(inv_sqrtD));      // >= 1/sqrt(D)
     const uint32_t ninf2 = DT == DT_BF16 ? 0xFF80FF80u : 0xFC00FC00u;
     const long row = (long)g * Tq + t;
     T* srow_g = scratch + (((long)g * ntiles + (t >> 6)) * 64 + (t & 63)) * LDL;
@@ -363,7 +365,8 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     const float safe = rm == -INFINITY ? 0.f : rm;  // pipeline.py:137-141
     const uint32_t m2 = dup2<DT>(safe);
     // pass 2: exponentials, sums, e @ V
-    float la0 = 0.f, la1 = 0.f, za = 0.f;
+    float2 la2 = make_float2(0.f, 0.f);
+    float za = 0.f;
     for (int v = nch; ok && v < nv; ++v) {
       const int c = v - nch, s = v & 1;
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_SFULL + s], (v >> 1) & 1, abort));
@@ -382,16 +385,22 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       for (int hh = 0; hh < 2; ++hh) {
         if (hh == 1) tc::tmem_wait_ld();
         const uint32_t (&ra)[16] = rh[hh];
-        // logits: DT(DT(acc) / sqrt(D)) (pipeline.py:81), branch-free fast
-        // quotients; a block with a quotient near a rounding point is redone
+        // logits: DT(DT(acc) / sqrt(D)) (pipeline.py:81).  |x| / sqrt(D) lies
+        // between RD(|x| invl) and RU(|x| invh); when both round to the same
+        // dtype value, so does the correctly rounded quotient, and rounding to
+        // nearest is symmetric, so the sign is copied back.  A block where
+        // some pair's ends disagree is redone with correctly rounded quotients.
         uint32_t s2[8];
         bool near = false;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint32_t x2 = pack2<DT>(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1]));
-          const float y0 = half_lo<DT>(x2) * inv_sqrtD, y1 = half_hi<DT>(x2) * inv_sqrtD;
-          near |= near_midpoint<DT>(y0) | near_midpoint<DT>(y1);
-          s2[j] = pack2<DT>(y0, y1);
+          const uint32_t a2 = x2 & 0x7FFF7FFFu;
+          const float2 av = make_float2(half_lo<DT>(a2), half_hi<DT>(a2));
+          const float2 ylo = mul_f32x2_rd(av, invl2), yhi = mul_f32x2_ru(av, invh2);
+          const uint32_t qlo = pack2<DT>(ylo.x, ylo.y);
+          near |= qlo != pack2<DT>(yhi.x, yhi.y);
+          s2[j] = qlo | (x2 & 0x80008000u);
         }
         if (near) {
 #pragma unroll
@@ -413,8 +422,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
             const uint32_t ee = exp2_dt<DT>(hsub2_dt<DT>(sm2, m2), exptab);
             e2[j] = ee;
             const uint32_t w2 = hmul2_dt<DT>(ee, nnv[k]);  // DT(e * n), pipeline.py:146
-            la0 += half_lo<DT>(w2);
-            la1 += half_hi<DT>(w2);
+            la2 = add_f32x2(la2, make_float2(half_lo<DT>(w2), half_hi<DT>(w2)));
             zs[j] = half_lo<DT>(ee) + half_hi<DT>(ee);
           }
         }
@@ -438,7 +446,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     // the halves' sums: z and l are the half-0 part plus the half-1 part in
     // both threads of the row
     xch[2 * TR + hf * TR + r] = za;
-    xch[4 * TR + hf * TR + r] = la0 + la1;
+    xch[4 * TR + hf * TR + r] = la2.x + la2.y;
     rows_sync();
     const float zsum = xch[2 * TR + r] + xch[3 * TR + r];
     const float lsum = xch[4 * TR + r] + xch[5 * TR + r];
@@ -491,10 +499,11 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       }
     }
     const float zc = clamp_min_nan(z, eps_dt<DT>());
-    if (hf == 0) {
+    if (hf == 0) {  // z and the fp32 neighbours of RN(1/z), which bracket 1/z
+      const float zi = 1.f / zc;
       srow[r * 4] = zc;
-      srow[r * 4 + 1] = 1.f / zc;
-      srow[r * 4 + 2] = live ? 1.f : 0.f;
+      srow[r * 4 + 1] = next_down(zi);
+      srow[r * 4 + 2] = next_up(zi);
     }
     // pass 3: importance partials (routing.py:61-63).  The CTA's exponential
     // rows stream through the idle tile buffers in 64-column blocks (cp.async,
@@ -531,42 +540,40 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_STG + (blk & 1)], (blk >> 1) & 1, abort));
       if (!ok) break;
       const unsigned char* buf = stg + (blk & 1) * BLK;
-      float c0 = 0.f, c1 = 0.f;
+      float2 c2 = make_float2(0.f, 0.f);
 #pragma unroll 1
       for (int g8 = 0; g8 < 2; ++g8) {
-        uint32_t w[8];
-        float2 zr[8];
+        uint32_t w[8], q[8], bad = 0u;
+        float4 zr[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int rw = rbase + g8 * 8 + i;
           w[i] = *reinterpret_cast<const uint32_t*>(buf + rw * (PB * 2) + lane * 4);
-          zr[i] = *reinterpret_cast<const float2*>(srow + rw * 4);
+          zr[i] = *reinterpret_cast<const float4*>(srow + rw * 4);
         }
-        float y[8][2];
-        bool near = false;
+        // DT(e / z), e >= 0: e / z lies between RD(e zl) and RU(e zh); when
+        // both round to the same dtype value so does the correctly rounded
+        // quotient, else the pair is divided exactly
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          y[i][0] = half_lo<DT>(w[i]) * zr[i].y;  // within 2 ulp of e / z
-          y[i][1] = half_hi<DT>(w[i]) * zr[i].y;
-          near |= near_midpoint<DT>(y[i][0]) | near_midpoint<DT>(y[i][1]);
+          const float2 ev = make_float2(half_lo<DT>(w[i]), half_hi<DT>(w[i]));
+          const float2 ylo = mul_f32x2_rd(ev, make_float2(zr[i].y, zr[i].y));
+          const float2 yhi = mul_f32x2_ru(ev, make_float2(zr[i].z, zr[i].z));
+          q[i] = pack2<DT>(ylo.x, ylo.y);
+          bad |= (q[i] != pack2<DT>(yhi.x, yhi.y) ? 1u : 0u) << i;
         }
-        if (near) {
+        if (bad) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            if (near_midpoint<DT>(y[i][0])) y[i][0] = __fdiv_rn(half_lo<DT>(w[i]), zr[i].x);
-            if (near_midpoint<DT>(y[i][1])) y[i][1] = __fdiv_rn(half_hi<DT>(w[i]), zr[i].x);
-          }
+          for (int i = 0; i < 8; ++i)
+            if ((bad >> i) & 1u)
+              q[i] = pack2<DT>(__fdiv_rn(half_lo<DT>(w[i]), zr[i].x), __fdiv_rn(half_hi<DT>(w[i]), zr[i].x));
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint32_t q2 = pack2<DT>(y[i][0], y[i][1]);  // DT(e / z)
-          c0 += half_lo<DT>(q2);
-          c1 += half_hi<DT>(q2);
-        }
+        for (int i = 0; i < 8; ++i) c2 = add_f32x2(c2, make_float2(half_lo<DT>(q[i]), half_hi<DT>(q[i])));
       }
       float* sc = scomb + (blk & 1) * 512;
-      sc[warp * 64 + 2 * lane] = c0;
-      sc[warp * 64 + 2 * lane + 1] = c1;
+      sc[warp * 64 + 2 * lane] = c2.x;
+      sc[warp * 64 + 2 * lane + 1] = c2.y;
       tc::mbar_arrive(&bars[B_COMB]);
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_COMB], blk & 1, abort));
       if (!ok) break;
