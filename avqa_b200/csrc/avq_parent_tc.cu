@@ -60,7 +60,7 @@ constexpr int TC_MAX_M0 = 2048;
 
 // Barrier slots.
 constexpr int B_Q = 0, B_PFULL = 1, B_PEMPTY = 3, B_VFULL = 5, B_VEMPTY = 7, B_SFULL = 9, B_EFULL = 11, B_SFREE = 13,
-              B_OFULL = 14, B_COMB = 15, B_STG = 16, N_BARS = 18;
+              B_OFULL = 14, N_BARS = 15;
 
 struct TcLayout {
   int q, p[2], v[2], exptab, pm2, n2, srow, scomb, xch, bars, misc, total;
@@ -161,6 +161,16 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
 
 // Barrier of the 256 row threads (the MMA and TMA warps do not take part).
 __device__ __forceinline__ void rows_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// The same barrier, returning whether `p` holds in every row thread.
+__device__ __forceinline__ bool rows_all(bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred a, b;\n\tsetp.ne.u32 a, %1, 0;\n\tbar.red.and.pred b, 1, 256, a;\n\tselp.u32 %0, 1, 0, b;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)p)
+      : "memory");
+  return r != 0;
+}
 
 template <int DT, int D>
 __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
@@ -191,8 +201,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
   // ---- setup: barriers, TMEM, tables ----
   if (tid == 0) {
     for (int i = 0; i < N_BARS; ++i)
-      tc::mbar_init(&bars[i],
-                    (i == B_EFULL || i == B_EFULL + 1 || i == B_COMB || i == B_STG || i == B_STG + 1) ? TROW : 1);
+      tc::mbar_init(&bars[i], (i == B_EFULL || i == B_EFULL + 1) ? TROW : 1);
     *abort = 0;
     tc::fence_mbar_init();
   }
@@ -506,17 +515,20 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       srow[r * 4 + 2] = next_up(zi);
     }
     // pass 3: importance partials (routing.py:61-63).  The CTA's exponential
-    // rows stream through the idle tile buffers in 64-column blocks (cp.async,
-    // double-buffered, one wait per block); lane = 2 columns, each thread sums
-    // 16 rows in order (rows 32(w%4) + 16hf + i), and the four 16-row sums of
-    // each 64-query tile are added in row order.  Rows beyond T stage as
-    // zeros and add 0.
+    // rows stream through the idle Q, P and V tile buffers in 64-column
+    // blocks (cp.async, NSTG blocks in flight, a row-thread barrier per
+    // block); lane = 2 columns, each thread sums 16 rows in order (rows
+    // 32(w%4) + 16hf + i), and the four 16-row sums of each 64-query tile are
+    // added in row order.  Rows beyond T stage as zeros and add 0.  Every row
+    // thread runs the same blocks (one vote first), so the barriers match.
     constexpr int PB = 64, BLK = TR * PB * 2;
-    unsigned char* stg = sm + L.p[0];  // 2 x 16 KB: the P and V tile buffers are idle now
+    constexpr int NSTG = (TR * D * 2 + 4 * TCH * D * 2) / BLK;  // Q, P, V buffers: 6 blocks (D 128), 3 (D 64)
+    static_assert(NSTG >= 2, "staging depth");
+    unsigned char* stg = sm + L.q;
     const int nblk = (M0 + PB - 1) / PB;
     const int rbase = 32 * (warp & 3) + 16 * hf;
     auto stage = [&](int blk) {
-      unsigned char* buf = stg + (blk & 1) * BLK;
+      unsigned char* buf = stg + (blk % NSTG) * BLK;
       const int pc = blk * PB, ch = tid & 7;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -526,20 +538,21 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
         cp_async16(buf + rr * (PB * 2) + ch * 16,
                    scratch + (((long)g * ntiles + (ts >> 6)) * 64 + (ts & 63)) * LDL + (in ? pc + ch * 8 : 0), in);
       }
-      cp_async_commit();
     };
-    if (ok) stage(0);
-    for (int blk = 0; ok && blk < nblk; ++blk) {
-      if (blk + 1 < nblk) {
-        stage(blk + 1);
-        cp_async_wait<1>();
-      } else {
-        cp_async_wait<0>();
+    const bool ok3 = rows_all(ok);
+    if (ok3) {
+      for (int i = 0; i < NSTG - 1; ++i) {  // NSTG - 1 groups, some empty
+        if (i < nblk) stage(i);
+        cp_async_commit();
       }
-      tc::mbar_arrive(&bars[B_STG + (blk & 1)]);
-      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_STG + (blk & 1)], (blk >> 1) & 1, abort));
-      if (!ok) break;
-      const unsigned char* buf = stg + (blk & 1) * BLK;
+    }
+    for (int blk = 0; ok3 && blk < nblk; ++blk) {
+      // buffer (blk + NSTG - 1) % NSTG was read in the previous block, before its barrier
+      if (blk + NSTG - 1 < nblk) stage(blk + NSTG - 1);
+      cp_async_commit();
+      cp_async_wait<NSTG - 1>();
+      rows_sync();  // every thread's copies of block blk have landed
+      const unsigned char* buf = stg + (blk % NSTG) * BLK;
       float2 c2 = make_float2(0.f, 0.f);
 #pragma unroll 1
       for (int g8 = 0; g8 < 2; ++g8) {
@@ -574,9 +587,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       float* sc = scomb + (blk & 1) * 512;
       sc[warp * 64 + 2 * lane] = c2.x;
       sc[warp * 64 + 2 * lane + 1] = c2.y;
-      tc::mbar_arrive(&bars[B_COMB]);
-      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_COMB], blk & 1, abort));
-      if (!ok) break;
+      rows_sync();  // the partials are visible, and block blk's buffer is read
       if (tid < TR) {
         // tile tl: rows 64tl + [0,16) warp 2tl, [16,32) warp 2tl+4, [32,48) warp 2tl+1, [48,64) warp 2tl+5
         const int tl = tid >> 6, cl = tid & 63, pcol = blk * PB + cl, tile = 2 * qt + tl;
