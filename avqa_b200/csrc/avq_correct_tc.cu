@@ -24,6 +24,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <cstdlib>
 
 #include "avq_kernels.cuh"
@@ -270,6 +271,8 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
     constexpr int XCOL = WCOL + 3 * (NS / 2);  // 8 free columns: the halves' weight sums
     static_assert(XCOL + 8 <= C_TMEM_COLS, "TMEM columns");
     const float inv_sqrtD = 1.f / sqrtD;
+    const float2 invl2 = make_float2(next_down(inv_sqrtD), next_down(inv_sqrtD));  // <= 1/sqrt(D)
+    const float2 invh2 = make_float2(next_up(inv_sqrtD), next_up(inv_sqrtD));      // >= 1/sqrt(D)
     const float m = live ? m_in[row] : 0.f;
     const float zc = clamp_min_nan(live ? z_in[row] : 1.f, eps_dt<DT>()), rz = 1.f / zc;
     const float bt = beta_in && live ? beta_in[row] : 0.f;
@@ -299,6 +302,12 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
       tc::fence_async_smem();
       tc::mbar_arrive(&bars[CB_FULL + kg % NBUF]);
     };
+    // this half's columns of the parent pass's a (attention.py:154-158), loaded
+    // first so that their latency overlaps the first gathers
+    uint4 a_seed[D / 16];
+#pragma unroll
+    for (int k = 0; k < D / 16; ++k)
+      a_seed[k] = live ? reinterpret_cast<const uint4*>(a_in + row * D + hf * (D / 2))[k] : make_uint4(0u, 0u, 0u, 0u);
     SlotDesc dn1{-1, -1, -1.f, 0.f}, dn2{-1, -1, -1.f, 0.f};  // descriptors of the next groups
     if (gathers) {
       if (ngroups > 0) {
@@ -316,14 +325,14 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
     else cp_async_commit();
     cp_async_wait<1>();
     if (ngroups > 0) publish(0);
-    // O = a (attention.py:154-158), this half's columns
+    // O = a, this half's columns
 #pragma unroll
     for (int d0 = 0; d0 < D / 2; d0 += 32) {
       const int dc = hf * (D / 2) + d0;
       uint32_t o[32];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const uint4 u = live ? reinterpret_cast<const uint4*>(a_in + row * D + dc)[k] : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 u = a_seed[d0 / 8 + k];
         const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -372,17 +381,21 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
         if (kg + 1 < ngroups) publish(kg + 1);
         if (gathers && kg + 3 < ngroups) dn2 = dg[(long)(kg + 3) * NS];
         const float* meta = reinterpret_cast<const float*>(sm + L.meta[bf]);
-        // logits DT(DT(acc) / sqrt(D)), branch-free fast quotients with an
-        // exact redo when one is near a rounding point
+        // logits DT(DT(acc) / sqrt(D)): |x| / sqrt(D) lies between RD(|x| invl)
+        // and RU(|x| invh); when both round to the same dtype value, so does
+        // the correctly rounded quotient (sign copied back); else exact redo
         float sl[24];
         bool near = false;
 #pragma unroll
         for (int i2 = 0; i2 < 12; ++i2) {
           const int i = 2 * i2;
           const uint32_t x2 = pack2<DT>(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1]));
-          const float y0 = half_lo<DT>(x2) * inv_sqrtD, y1 = half_hi<DT>(x2) * inv_sqrtD;
-          near |= near_midpoint<DT>(y0) | near_midpoint<DT>(y1);
-          const uint32_t s2 = pack2<DT>(y0, y1);
+          const uint32_t a2 = x2 & 0x7FFF7FFFu;
+          const float2 av = make_float2(half_lo<DT>(a2), half_hi<DT>(a2));
+          const float2 ylo = mul_f32x2_rd(av, invl2), yhi = mul_f32x2_ru(av, invh2);
+          const uint32_t qlo = pack2<DT>(ylo.x, ylo.y);
+          near |= qlo != pack2<DT>(yhi.x, yhi.y);
+          const uint32_t s2 = qlo | (x2 & 0x80008000u);
           sl[i] = half_lo<DT>(s2);
           sl[i + 1] = half_hi<DT>(s2);
         }
@@ -392,35 +405,41 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
         }
         // weights (fp32; refinement.py:335,341-343): -exp(pi - m) n for a parent,
         // exp(u - m) n_c for a child, 0 for an empty slot
-        const float4* mn4 = reinterpret_cast<const float4*>(meta + 24 * hf);
-        const float4* mk4 = reinterpret_cast<const float4*>(meta + NS + 24 * hf);
         float wv[24];
         float rlg = 0.f, alg = 0.f;
+        // the slot kinds of a half are fixed: one copy of the loop per half
+        auto weights = [&](auto hfc) {
+          constexpr int HF = decltype(hfc)::value;
+          const float4* mn4 = reinterpret_cast<const float4*>(meta + 24 * HF);
+          const float4* mk4 = reinterpret_cast<const float4*>(meta + NS + 24 * HF);
 #pragma unroll
-        for (int q = 0; q < 6; ++q) {
-          const float4 n4 = mn4[q], k4 = mk4[q];
-          const float nv[4] = {n4.x, n4.y, n4.z, n4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
+          for (int q = 0; q < 6; ++q) {
+            const float4 n4 = mn4[q], k4 = mk4[q];
+            const float nv[4] = {n4.x, n4.y, n4.z, n4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = 4 * q + e, k = 24 * hf + i;
-            float w = 0.f;
-            if (k < NREAL) {
-              float s = kv[e] > 0.f ? sl[i] : -INFINITY;
-              if (k < J) {
-                if (beta_in) s = rnd<DT>(__fmul_rn(bt, rnd<DT>(__fmul_rn(s, sqrtD))));
-                const float ex = exp_bf16_tab(rnd<DT>(s - m), exptab);
-                const float pi = div_dt_fast<DT>(ex, rz, zc);
-                w = nv[e] >= 0.f ? __expf(pi - m) * nv[e] : 0.f;
-                rlg += w;
-                w = -w;
-              } else {
-                w = nv[e] >= 0.f ? __expf(s - m) * nv[e] : 0.f;
-                alg += w;
+            for (int e = 0; e < 4; ++e) {
+              const int i = 4 * q + e, k = 24 * HF + i;
+              float w = 0.f;
+              if (k < NREAL) {
+                float s = kv[e] > 0.f ? sl[i] : -INFINITY;
+                if (k < J) {
+                  if (beta_in) s = rnd<DT>(__fmul_rn(bt, rnd<DT>(__fmul_rn(s, sqrtD))));
+                  const float ex = exp_bf16_tab(rnd<DT>(s - m), exptab);
+                  const float pi = div_dt_fast<DT>(ex, rz, zc);
+                  w = nv[e] >= 0.f ? __expf(pi - m) * nv[e] : 0.f;
+                  rlg += w;
+                  w = -w;
+                } else {
+                  w = nv[e] >= 0.f ? __expf(s - m) * nv[e] : 0.f;
+                  alg += w;
+                }
               }
+              wv[i] = w;
             }
-            wv[i] = w;
           }
-        }
+        };
+        if (hf == 0) weights(std::integral_constant<int, 0>{});
+        else weights(std::integral_constant<int, 1>{});
         rl += (double)rlg;
         al += (double)alg;
         // three bf16 parts per weight (w = hi + mid + lo to 24 bits), packed in pairs
