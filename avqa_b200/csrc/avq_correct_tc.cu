@@ -275,6 +275,7 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
     const float2 invh2 = make_float2(next_up(inv_sqrtD), next_up(inv_sqrtD));      // >= 1/sqrt(D)
     const float m = live ? m_in[row] : 0.f;
     const float zc = clamp_min_nan(live ? z_in[row] : 1.f, eps_dt<DT>()), rz = 1.f / zc;
+    const float zl = next_down(rz), zh = next_up(rz);  // bracket 1 / zc
     const float bt = beta_in && live ? beta_in[row] : 0.f;
     float l = live ? l_in[row] : 1.f;
     const int gslot = r;
@@ -407,6 +408,8 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
         // exp(u - m) n_c for a child, 0 for an empty slot
         float wv[24];
         float rlg = 0.f, alg = 0.f;
+        uint32_t pbad = 0u;  // parent slots whose quotient is redone
+        float pe[J];         // their exponentials
         // the slot kinds of a half are fixed: one copy of the loop per half
         auto weights = [&](auto hfc) {
           constexpr int HF = decltype(hfc)::value;
@@ -425,10 +428,12 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
                 if (k < J) {
                   if (beta_in) s = rnd<DT>(__fmul_rn(bt, rnd<DT>(__fmul_rn(s, sqrtD))));
                   const float ex = exp_bf16_tab(rnd<DT>(s - m), exptab);
-                  const float pi = div_dt_fast<DT>(ex, rz, zc);
-                  w = nv[e] >= 0.f ? __expf(pi - m) * nv[e] : 0.f;
-                  rlg += w;
-                  w = -w;
+                  // pi = DT(e / z): e / z lies between RD(e zl) and RU(e zh)
+                  // (e >= 0); ends that round apart are redone exactly below
+                  const float pi = rnd<DT>(__fmul_rd(ex, zl));
+                  if (pi != rnd<DT>(__fmul_ru(ex, zh))) pbad |= 1u << i;
+                  pe[i] = ex;
+                  w = nv[e] >= 0.f ? -__expf(pi - m) * nv[e] : 0.f;  // summed into rlg below
                 } else {
                   w = nv[e] >= 0.f ? __expf(s - m) * nv[e] : 0.f;
                   alg += w;
@@ -440,6 +445,20 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
         };
         if (hf == 0) weights(std::integral_constant<int, 0>{});
         else weights(std::integral_constant<int, 1>{});
+        if (__any_sync(0xffffffffu, pbad != 0u)) {
+#pragma unroll
+          for (int i = 0; i < J; ++i) {
+            if ((pbad >> i) & 1u) {  // only half 0 holds parent slots
+              const float pi = rnd<DT>(__fdiv_rn(pe[i], zc));
+              const float nvi = meta[i];
+              wv[i] = nvi >= 0.f ? -__expf(pi - m) * nvi : 0.f;
+            }
+          }
+        }
+        if (hf == 0) {
+#pragma unroll
+          for (int i = 0; i < J; ++i) rlg += -wv[i];  // slot order, as the weights were made
+        }
         rl += (double)rlg;
         al += (double)alg;
         // three bf16 parts per weight (w = hi + mid + lo to 24 bits), packed in pairs
