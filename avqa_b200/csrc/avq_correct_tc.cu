@@ -367,20 +367,11 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
         }
         tc::tc_before_sync();
         tc::mbar_arrive(&bars[CB_SFREE]);
-        // gather group kg + 2 into the buffer of group kg - 1, publish group kg + 1
-        if (kg + 2 < ngroups) {
-          const int nb = (kg + 2) % NBUF;
-          if (kg + 2 >= NBUF) {
-            ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[CB_EMPTY + nb], ((kg + 2) / NBUF - 1) & 1, abort));
-            if (!ok) break;
-          }
-          gather(kg + 2, dn2);
-          cp_async_wait<1>();
-        } else {
-          cp_async_wait<0>();
-        }
+        // publish group kg + 1 (gathered a group ago); group kg + 2 is gathered
+        // after the weights, when the value MMAs of group kg - 1 that read its
+        // buffer have had time to finish
+        cp_async_wait<0>();
         if (kg + 1 < ngroups) publish(kg + 1);
-        if (gathers && kg + 3 < ngroups) dn2 = dg[(long)(kg + 3) * NS];
         const float* meta = reinterpret_cast<const float*>(sm + L.meta[bf]);
         // logits DT(DT(acc) / sqrt(D)): |x| / sqrt(D) lies between RD(|x| invl)
         // and RU(|x| invh); when both round to the same dtype value, so does
@@ -461,6 +452,15 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
         }
         rl += (double)rlg;
         al += (double)alg;
+        if (kg + 2 < ngroups) {
+          const int nb = (kg + 2) % NBUF;
+          if (kg + 2 >= NBUF) {
+            ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[CB_EMPTY + nb], ((kg + 2) / NBUF - 1) & 1, abort));
+            if (!ok) break;
+          }
+          gather(kg + 2, dn2);
+          if (gathers && kg + 3 < ngroups) dn2 = dg[(long)(kg + 3) * NS];
+        }
         // three bf16 parts per weight (w = hi + mid + lo to 24 bits), packed in pairs
         uint32_t wp[3][12];
 #pragma unroll
