@@ -326,58 +326,89 @@ __global__ void bucket_hist_kernel(const int* __restrict__ passign, int S, int M
 
 // Per g: bucket totals -> exclusive offsets; hist rewritten in place as each
 // segment's first slot per bucket.  Writes parent offsets/counts, the number
-// of non-empty parents and folds it into the global minimum.
-__global__ void bucket_scan_kernel(int* __restrict__ hist, int M0, int nseg, int* __restrict__ poff,
-                                   int* __restrict__ pcnt, int* __restrict__ nvalid, int* __restrict__ gmin_valid) {
-  extern __shared__ int sh[];  // [M0] totals, then scan scratch
-  const int g = blockIdx.x;
+// of non-empty parents and folds it into the global minimum.  The segment
+// counts of a bucket are read in batches of independent loads, and the
+// totals are scanned with warp shuffles.
+__global__ void __launch_bounds__(1024) bucket_scan_kernel(int* __restrict__ hist, int M0, int nseg,
+                                                           int* __restrict__ poff, int* __restrict__ pcnt,
+                                                           int* __restrict__ nvalid, int* __restrict__ gmin_valid) {
+  extern __shared__ int sh[];  // [M0] bucket totals, then the buckets' first slots
+  __shared__ int wsum[32];
+  constexpr unsigned full = 0xffffffffu;
+  const int g = blockIdx.x, tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
   int* base = hist + (long)g * nseg * M0;
-  for (int p = threadIdx.x; p < M0; p += blockDim.x) {
-    int run = 0;
-    for (int seg = 0; seg < nseg; ++seg) {
-      const int c = base[(long)seg * M0 + p];
-      base[(long)seg * M0 + p] = run;
-      run += c;
+  for (int p = tid; p < M0; p += nt) {
+    int tot = 0;
+    for (int s0 = 0; s0 < nseg; s0 += 8) {
+      int c[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) c[k] = s0 + k < nseg ? base[(long)(s0 + k) * M0 + p] : 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) tot += c[k];
     }
-    sh[p] = run;
+    sh[p] = tot;
   }
   __syncthreads();
-  // exclusive scan of the totals (M0 <= 8192), sequential per thread chunk
-  __shared__ int chunk_sum[1024];
-  const int nt = blockDim.x, per = (M0 + nt - 1) / nt;
-  const int lo = threadIdx.x * per, hi = min(M0, lo + per);
+  // exclusive scan of the totals (M0 <= 8192): a contiguous chunk per thread,
+  // an inclusive shuffle scan over the warp, then over the warp sums
+  const int per = (M0 + nt - 1) / nt, lo = min(M0, tid * per), hi = min(M0, lo + per);
   int acc = 0, nz = 0;
   for (int p = lo; p < hi; ++p) {
     acc += sh[p];
     nz += sh[p] > 0;
   }
-  chunk_sum[threadIdx.x] = acc;
+  int incl = acc;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(full, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) wsum[warp] = incl;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0;
-    for (int t = 0; t < nt; ++t) {
-      const int c = chunk_sum[t];
-      chunk_sum[t] = run;
-      run += c;
+  if (warp == 0) {
+    const int v = lane < nt / 32 ? wsum[lane] : 0;
+    int iv = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(full, iv, o);
+      if (lane >= o) iv += y;
     }
+    if (lane < nt / 32) wsum[lane] = iv - v;
   }
   __syncthreads();
-  int run = chunk_sum[threadIdx.x];
+  int run = wsum[warp] + incl - acc;
   for (int p = lo; p < hi; ++p) {
     const int c = sh[p];
     poff[(long)g * M0 + p] = run;
     pcnt[(long)g * M0 + p] = c;
-    for (int seg = 0; seg < nseg; ++seg) base[(long)seg * M0 + p] += run;
+    sh[p] = run;
     run += c;
   }
+  __syncthreads();
+  // each segment's first slot per bucket: the bucket start plus the counts of
+  // the segments before it
+  for (int p = tid; p < M0; p += nt) {
+    int r = sh[p];
+    for (int s0 = 0; s0 < nseg; s0 += 8) {
+      int c[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) c[k] = s0 + k < nseg ? base[(long)(s0 + k) * M0 + p] : 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (s0 + k < nseg) base[(long)(s0 + k) * M0 + p] = r;
+        r += c[k];
+      }
+    }
+  }
   // number of valid parents
-  for (int o = 16; o > 0; o >>= 1) nz += __shfl_xor_sync(0xffffffffu, nz, o);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) nz += __shfl_xor_sync(full, nz, o);
   __syncthreads();
-  if ((threadIdx.x & 31) == 0) chunk_sum[threadIdx.x >> 5] = nz;
+  if (lane == 0) wsum[warp] = nz;
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     int tot = 0;
-    for (int w = 0; w < (nt + 31) / 32; ++w) tot += chunk_sum[w];
+    for (int w = 0; w < nt / 32; ++w) tot += wsum[w];
     nvalid[g] = tot;
     if (gmin_valid) atomicMin(gmin_valid, tot);
   }
@@ -509,6 +540,7 @@ __device__ __forceinline__ void load_row_elems(const typename Storage<DT>::T* p,
 // needs no cross-lane synchronisation.  The fp32 additions stay in key order
 // (index_add_, quantizer.py:241-262).
 constexpr int AG_WARPS = 8;
+constexpr int AG_BATCH = 4;  // parents per work-counter increment
 
 template <int BYTES>
 __device__ __forceinline__ void cp_async_slice(void* smem, const void* gmem) {
@@ -530,13 +562,18 @@ __global__ void __launch_bounds__(AG_WARPS * 32) aggregate_vec_kernel(
   __shared__ __align__(16) T ring_all[AG_WARPS][AG_RING][D];
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   T (*ring)[D] = ring_all[wib];
-  // persistent warps: each takes the next parent from a counter, so a long
-  // member list never holds up the other warps of its block
+  // persistent warps: each takes the next AG_BATCH parents from a counter, so a
+  // long member list never holds up the other warps of its block; the batch's
+  // member offsets and counts come in one load
   for (;;) {
   int gnext = 0;
-  if (lane == 0) gnext = atomicAdd(next_row, 1);
-  const long gp = __shfl_sync(0xffffffffu, gnext, 0);
-  if (gp >= rows) break;
+  if (lane == 0) gnext = atomicAdd(next_row, AG_BATCH);
+  const long gb = __shfl_sync(0xffffffffu, gnext, 0);
+  if (gb >= rows) break;
+  const int bpoff = lane < AG_BATCH && gb + lane < rows ? poff[gb + lane] : 0;
+  const int bpcnt = lane < AG_BATCH && gb + lane < rows ? pcnt[gb + lane] : 0;
+  for (int kb = 0; kb < AG_BATCH && gb + kb < rows; ++kb) {
+  const long gp = gb + kb;
   const int g = (int)(gp / M0), b = g / H, h = g % H;
   const T* vbase = values + (long)b * vs.b + (long)h * vs.h + lane * VPL;
   float ap[VPL], ac[CMAX][VPL];
@@ -547,7 +584,7 @@ __global__ void __launch_bounds__(AG_WARPS * 32) aggregate_vec_kernel(
 #pragma unroll
     for (int c = 0; c < CMAX; ++c) ac[c][j] = 0.f;
   }
-  const int beg = poff[gp], n = pcnt[gp];
+  const int beg = __shfl_sync(0xffffffffu, bpoff, kb), n = __shfl_sync(0xffffffffu, bpcnt, kb);
   const int* ord = order + (long)g * S + beg;
   const int* cas = cassign + (long)g * S;
   // member ids: batch i0 in (cur_s, cur_c), the next batch in (nxt_s)
@@ -619,6 +656,7 @@ __global__ void __launch_bounds__(AG_WARPS * 32) aggregate_vec_kernel(
     }
   }
   if (lane < C) ccnt[gp * C + lane] = cn;
+  }
   }
 }
 
