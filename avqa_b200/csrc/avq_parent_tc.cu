@@ -516,42 +516,35 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     }
     // pass 3: importance partials (routing.py:61-63).  The CTA's exponential
     // rows stream through the idle Q, P and V tile buffers in 64-column
-    // blocks (cp.async, NSTG blocks in flight, a row-thread barrier per
-    // block); lane = 2 columns, each thread sums 16 rows in order (rows
-    // 32(w%4) + 16hf + i), and the four 16-row sums of each 64-query tile are
-    // added in row order.  Rows beyond T stage as zeros and add 0.  Every row
-    // thread runs the same blocks (one vote first), so the barriers match.
+    // blocks (cp.async, NSTG block buffers); each iteration takes two blocks
+    // between two row-thread barriers.  Lane = 2 columns, each thread sums 16
+    // rows in order (rows 32(w%4) + 16hf + i), and the four 16-row sums of
+    // each 64-query tile are added in row order.  Rows beyond T stage as zeros
+    // and add 0.  Every row thread runs the same iterations (one vote first),
+    // so the barriers match.
     constexpr int PB = 64, BLK = TR * PB * 2;
     constexpr int NSTG = (TR * D * 2 + 4 * TCH * D * 2) / BLK;  // Q, P, V buffers: 6 blocks (D 128), 3 (D 64)
-    static_assert(NSTG >= 2, "staging depth");
+    static_assert(NSTG >= 3, "staging depth");
     unsigned char* stg = sm + L.q;
     const int nblk = (M0 + PB - 1) / PB;
     const int rbase = 32 * (warp & 3) + 16 * hf;
-    auto stage = [&](int blk) {
-      unsigned char* buf = stg + (blk % NSTG) * BLK;
-      const int pc = blk * PB, ch = tid & 7;
+    auto stage = [&](int blk) {  // one cp.async group, empty beyond the last block
+      if (blk < nblk) {
+        unsigned char* buf = stg + (blk % NSTG) * BLK;
+        const int pc = blk * PB, ch = tid & 7;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int rr = (tid >> 3) + 32 * k, tw = t0 + rr;
-        const bool in = tw < Tq && pc + ch * 8 < M0;
-        const int ts = in ? tw : t0;
-        cp_async16(buf + rr * (PB * 2) + ch * 16,
-                   scratch + (((long)g * ntiles + (ts >> 6)) * 64 + (ts & 63)) * LDL + (in ? pc + ch * 8 : 0), in);
+        for (int k = 0; k < 4; ++k) {
+          const int rr = (tid >> 3) + 32 * k, tw = t0 + rr;
+          const bool in = tw < Tq && pc + ch * 8 < M0;
+          const int ts = in ? tw : t0;
+          cp_async16(buf + rr * (PB * 2) + ch * 16,
+                     scratch + (((long)g * ntiles + (ts >> 6)) * 64 + (ts & 63)) * LDL + (in ? pc + ch * 8 : 0), in);
+        }
       }
-    };
-    const bool ok3 = rows_all(ok);
-    if (ok3) {
-      for (int i = 0; i < NSTG - 1; ++i) {  // NSTG - 1 groups, some empty
-        if (i < nblk) stage(i);
-        cp_async_commit();
-      }
-    }
-    for (int blk = 0; ok3 && blk < nblk; ++blk) {
-      // buffer (blk + NSTG - 1) % NSTG was read in the previous block, before its barrier
-      if (blk + NSTG - 1 < nblk) stage(blk + NSTG - 1);
       cp_async_commit();
-      cp_async_wait<NSTG - 1>();
-      rows_sync();  // every thread's copies of block blk have landed
+    };
+    // the column sums of one block over this thread's 16 rows
+    auto block_sums = [&](int blk) -> float2 {
       const unsigned char* buf = stg + (blk % NSTG) * BLK;
       float2 c2 = make_float2(0.f, 0.f);
 #pragma unroll 1
@@ -584,13 +577,30 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
 #pragma unroll
         for (int i = 0; i < 8; ++i) c2 = add_f32x2(c2, make_float2(half_lo<DT>(q[i]), half_hi<DT>(q[i])));
       }
-      float* sc = scomb + (blk & 1) * 512;
-      sc[warp * 64 + 2 * lane] = c2.x;
-      sc[warp * 64 + 2 * lane + 1] = c2.y;
-      rows_sync();  // the partials are visible, and block blk's buffer is read
-      if (tid < TR) {
-        // tile tl: rows 64tl + [0,16) warp 2tl, [16,32) warp 2tl+4, [32,48) warp 2tl+1, [48,64) warp 2tl+5
-        const int tl = tid >> 6, cl = tid & 63, pcol = blk * PB + cl, tile = 2 * qt + tl;
+      return c2;
+    };
+    const bool ok3 = rows_all(ok);
+    if (ok3)
+      for (int i = 0; i < NSTG - 2; ++i) stage(i);
+    for (int blk = 0; ok3 && blk < nblk; blk += 2) {
+      // the buffers of blocks blk - 2 and blk - 1 were read before the last barrier
+      stage(blk + NSTG - 2);
+      stage(blk + NSTG - 1);
+      cp_async_wait<NSTG - 2>();
+      rows_sync();  // every thread's copies of blocks blk and blk + 1 have landed
+      const float2 s0 = block_sums(blk);
+      const float2 s1 = blk + 1 < nblk ? block_sums(blk + 1) : make_float2(0.f, 0.f);
+      scomb[warp * 64 + 2 * lane] = s0.x;
+      scomb[warp * 64 + 2 * lane + 1] = s0.y;
+      scomb[512 + warp * 64 + 2 * lane] = s1.x;
+      scomb[512 + warp * 64 + 2 * lane + 1] = s1.y;
+      rows_sync();  // the partials are visible, and both blocks' buffers are read
+      {
+        // tile tl: rows 64tl + [0,16) warp 2tl, [16,32) warp 2tl+4, [32,48) warp 2tl+1, [48,64) warp 2tl+5;
+        // thread tid handles block blk + (tid >> 7)
+        const int bb = tid >> 7, t2 = tid & 127, tl = t2 >> 6, cl = t2 & 63, pcol = (blk + bb) * PB + cl;
+        const int tile = 2 * qt + tl;
+        const float* sc = scomb + 512 * bb;
         if (tile < ntiles && pcol < M0)
           colpart[((long)g * ntiles + tile) * M0 + pcol] =
               (sc[(2 * tl) * 64 + cl] + sc[(2 * tl + 4) * 64 + cl]) + (sc[(2 * tl + 1) * 64 + cl] + sc[(2 * tl + 5) * 64 + cl]);

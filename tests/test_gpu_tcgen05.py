@@ -38,6 +38,9 @@ CASES = [
              hvaq=True),
     Workload("quirk_bf16", B=1, T=64, S=200, H=2, D=64, M0=8, C=4, P=8, dtype="bf16", keys="mixture", seed=47,
              passes=2, pass_decay=1.0),
+    # the largest parent count of the tcgen05 parent attention (32 chunks, one CTA per SM)
+    Workload("m2048_bf16", B=1, T=160, S=4096, H=1, D=128, M0=2048, C=4, P=64, dtype="bf16", keys="mixture",
+             seed=48),
 ]
 
 
@@ -95,6 +98,9 @@ QCASES = [
     Workload("q_tail_bf16", B=2, T=8, S=300, H=2, D=128, M0=200, C=3, P=8, dtype="bf16", keys="mixture", seed=51),
     Workload("q_d64_f16", B=1, T=8, S=1000, H=3, D=64, M0=136, C=8, P=8, dtype="f16", keys="aniso", seed=52),
     Workload("q_big_bf16", B=1, T=8, S=2048, H=2, D=128, M0=1024, C=4, P=8, dtype="bf16", keys="student_t", seed=53),
+    # the child stage's other lane splits: 16 lanes per child row (C <= 2, D = 128), 8 (C = 1, D = 64)
+    Workload("q_c2_bf16", B=1, T=8, S=900, H=2, D=128, M0=96, C=2, P=8, dtype="bf16", keys="mixture", seed=57),
+    Workload("q_c1_f16", B=2, T=8, S=500, H=1, D=64, M0=64, C=1, P=8, dtype="f16", keys="aniso", seed=58),
 ]
 
 
