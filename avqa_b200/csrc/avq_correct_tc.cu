@@ -85,6 +85,19 @@ __host__ __device__ inline CorrLayout corr_layout(int D) {
   return L;
 }
 
+// Barrier of the 256 row threads (the MMA / TMA warp does not take part), and
+// the same barrier returning whether `p` holds in every row thread.
+__device__ __forceinline__ void corr_rows_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ bool corr_rows_all(bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred a, b;\n\tsetp.ne.u32 a, %1, 0;\n\tbar.red.and.pred b, 1, 256, a;\n\tselp.u32 %0, 1, 0, b;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)p)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ void drain_c(uint64_t* bar, uint32_t parity) {
   const long long t0 = clock64();
   while (!tc::mbar_try(bar, parity) && clock64() - t0 < tc::kWaitCycles / 8) {
@@ -519,23 +532,37 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
     }
     cp_async_wait<0>();
     if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[CB_OFULL], 0, abort));
-    if (ok) {
+    // every row thread takes the same branch below (one vote), so the barrier matches
+    if (corr_rows_all(ok)) {
       tc::tc_after_sync();
+      // the output tile goes through the idle Q, slot-row and value buffers, so
+      // that each warp stores whole rows (512 contiguous bytes) instead of 32
+      // rows' 16-byte pieces
+      constexpr int SLD = D + 4;  // padded row: the 16-byte writes of a warp hit distinct banks
+      static_assert(CR * SLD * 4 <= CR * D * 2 + 2 * NBUF * NS * D * 2, "output staging");
+      float* stg = reinterpret_cast<float*>(sm + L.q);
       const float rden = __fdiv_rn(1.f, clamp_min_nan(l, 1e-12f));
-      float* orow = out + (long)b * os.b + (long)(live ? t : 0) * os.s + (long)h * os.h;
 #pragma unroll
       for (int d0 = 0; d0 < D / 2; d0 += 32) {
         const int dc = hf * (D / 2) + d0;
         uint32_t o[32];
         tc::tmem_ld32(tbase + lane_off + OCOL + dc, o);
         tc::tmem_wait_ld();
-        if (live) {
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
-            *reinterpret_cast<float4*>(orow + dc + 4 * k) =
-                make_float4(__uint_as_float(o[4 * k]) * rden, __uint_as_float(o[4 * k + 1]) * rden,
-                            __uint_as_float(o[4 * k + 2]) * rden, __uint_as_float(o[4 * k + 3]) * rden);
-        }
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<float4*>(stg + r * SLD + dc + 4 * k) =
+              make_float4(__uint_as_float(o[4 * k]) * rden, __uint_as_float(o[4 * k + 1]) * rden,
+                          __uint_as_float(o[4 * k + 2]) * rden, __uint_as_float(o[4 * k + 3]) * rden);
+      }
+      corr_rows_sync();
+      constexpr int F4 = D / 4, RPI = 32 / F4;  // float4 per row, rows per warp instruction
+      const int c4 = lane % F4;
+#pragma unroll 4
+      for (int i = 0; i < CR / 8; i += RPI) {
+        const int rr = warp * (CR / 8) + i + lane / F4, tt = t0 + rr;
+        if (tt < Tq)
+          *reinterpret_cast<float4*>(out + (long)b * os.b + (long)tt * os.s + (long)h * os.h + 4 * c4) =
+              *reinterpret_cast<const float4*>(stg + rr * SLD + 4 * c4);
       }
     }
   }
