@@ -480,26 +480,41 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       }
     }
     if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_OFULL], 0, abort));
-    if (ok) {
+    // every row thread takes the same branch below (one vote), so the barrier matches
+    if (rows_all(ok)) {
       tc::tc_after_sync();
-      // half hf writes output columns [hf D/2, (hf+1) D/2)
+      // the tile of a goes through the idle Q, P and V buffers (pass 3 refills
+      // them only after its own vote), so that each warp stores whole rows
+      // instead of 32 rows' 16-byte pieces; half hf stages columns
+      // [hf D/2, (hf+1) D/2) of its row
+      constexpr int SLDB = D * 2 + 16;  // padded row bytes: a warp's 16-byte writes hit distinct banks
+      static_assert(TR * SLDB <= TR * D * 2 + 4 * TCH * D * 2, "output staging");
+      unsigned char* stga = sm + L.q;
 #pragma unroll
       for (int d0 = 0; d0 < D / 2; d0 += 32) {
         uint32_t oa[32];
         const int dc = hf * (D / 2) + d0;
         tc::tmem_ld32(tbase + lane_off + dc, oa);
         tc::tmem_wait_ld();
-        if (live) {
-          uint4* dst = reinterpret_cast<uint4*>(a_out + row * D + dc);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint32_t* src = oa + 8 * k;
-            dst[k] = make_uint4(pack2<DT>(__uint_as_float(src[0]), __uint_as_float(src[1])),
-                                pack2<DT>(__uint_as_float(src[2]), __uint_as_float(src[3])),
-                                pack2<DT>(__uint_as_float(src[4]), __uint_as_float(src[5])),
-                                pack2<DT>(__uint_as_float(src[6]), __uint_as_float(src[7])));
-          }
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t* src = oa + 8 * k;
+          *reinterpret_cast<uint4*>(stga + r * SLDB + dc * 2 + 16 * k) =
+              make_uint4(pack2<DT>(__uint_as_float(src[0]), __uint_as_float(src[1])),
+                         pack2<DT>(__uint_as_float(src[2]), __uint_as_float(src[3])),
+                         pack2<DT>(__uint_as_float(src[4]), __uint_as_float(src[5])),
+                         pack2<DT>(__uint_as_float(src[6]), __uint_as_float(src[7])));
         }
+      }
+      rows_sync();
+      constexpr int U4 = D / 8, RPI = 32 / U4;  // 16-byte pieces per row, rows per warp instruction
+      const int c16 = lane % U4;
+#pragma unroll 4
+      for (int i = 0; i < TR / 8; i += RPI) {
+        const int rr = (warp & 7) * (TR / 8) + i + lane / U4, tt = t0 + rr;
+        if (tt < Tq)
+          reinterpret_cast<uint4*>(a_out + ((long)g * Tq + tt) * D)[c16] =
+              *reinterpret_cast<const uint4*>(stga + rr * SLDB + 16 * c16);
       }
       if (live && hf == 0) {
         m_out[row] = safe;
