@@ -15,9 +15,11 @@
 // keys: the order-preserving integer form of the 16-bit distance in the high
 // half and the parent index in the low half.  A row with a NaN
 // distance (only possible with non-finite inputs) takes a scalar path.
-// Child stage (quantizer.py:218-226): the cross term is a sum of
-// dtype-rounded elementwise products, rounded once as its exact value would
-// be (fp32 with an error bound, fp64 where the bound cannot decide).
+// Child stage (quantizer.py:218-226): each row warp then takes its 32 keys
+// one group of four at a time, the keys' child blocks arriving by bulk copy
+// in the idle parent buffers; the cross term is a sum of dtype-rounded
+// elementwise products, rounded once as its exact value would be (fp32 with
+// an error bound, fp64 where the bound cannot decide).
 #include <cuda.h>
 
 #include <algorithm>
