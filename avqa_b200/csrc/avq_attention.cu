@@ -271,20 +271,50 @@ __global__ void __launch_bounds__(1024) route_kernel(const double* __restrict__ 
   }
   __syncthreads();
   // importance = n * dtype(sum_t probs) (routing.py:61-63)
+  // fp32 tile partials: their sum is within 2^-18 relative of the exact one;
+  // where that window straddles a rounding point the column is recomputed
+  // exactly below, so the fp64 order of the partials does not matter
+  auto tile_sum = [&](int p, int i0, int i1) -> double {  // 16 independent loads at a time
+    const float* cp = rx.colpart + (long)g * nqt * M0 + p;
+    double acc = 0.0;
+    for (int b0 = i0; b0 < i1; b0 += 16) {
+      float x[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) x[k] = b0 + k < i1 ? cp[(long)(b0 + k) * M0] : 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) acc += (double)x[k];
+    }
+    return acc;
+  };
+  auto from_partials = [&](int p, double s) {
+    const float n = count_dt<DT>(pcnt[(long)g * M0 + p]);
+    const double eps = fabs(s) * 3.814697265625e-06;
+    const float w = rnd<DT>(__fmul_rn(n, rnd64<DT>(s)));
+    const float w_lo = rnd<DT>(__fmul_rn(n, rnd64<DT>(s - eps)));
+    const float w_hi = rnd<DT>(__fmul_rn(n, rnd64<DT>(s + eps)));
+    if (w_lo != w_hi) amb[atomicAdd(&namb, 1)] = p;
+    if (importance_out) importance_out[(long)g * M0 + p] = w;
+    keys[p] = route_key(w, p);
+    refined[p] = 0;
+  };
+  if (rx.colpart && 2 * M0 <= (int)blockDim.x) {
+    // two threads per parent: thread p sums the first half of the tiles,
+    // thread M0 + p the second, which passes through the parent's key slot
+    const int half = threadIdx.x / M0, p = threadIdx.x % M0, hq = (nqt + 1) / 2;
+    double part = 0.0;
+    if (half < 2) part = tile_sum(p, half ? hq : 0, half ? nqt : hq);
+    if (half == 1) keys[p] = (unsigned long long)__double_as_longlong(part);
+    __syncthreads();
+    if (half == 0) from_partials(p, part + __longlong_as_double((long long)keys[p]));
+    for (int q = M0 + threadIdx.x; q < npow2; q += blockDim.x) keys[q] = ~0ull;
+  } else {
   for (int p = threadIdx.x; p < npow2; p += blockDim.x) {
     if (p < M0) {
       const float n = count_dt<DT>(pcnt[(long)g * M0 + p]);
       float w;
       if (rx.colpart) {
-        // fp32 tile partials: the sum is within 2^-18 relative of the exact
-        // one; if that window straddles a rounding point, recompute below
-        double s = 0.0;
-        for (int i = 0; i < nqt; ++i) s += (double)rx.colpart[((long)g * nqt + i) * M0 + p];
-        const double eps = fabs(s) * 3.814697265625e-06;
-        w = rnd<DT>(__fmul_rn(n, rnd64<DT>(s)));
-        const float w_lo = rnd<DT>(__fmul_rn(n, rnd64<DT>(s - eps)));
-        const float w_hi = rnd<DT>(__fmul_rn(n, rnd64<DT>(s + eps)));
-        if (w_lo != w_hi) amb[atomicAdd(&namb, 1)] = p;
+        from_partials(p, tile_sum(p, 0, nqt));
+        continue;
       } else {
         double s = 0.0;
         for (int i = 0; i < nqt; ++i) s += imp_part[((long)g * nqt + i) * M0 + p];
@@ -296,6 +326,7 @@ __global__ void __launch_bounds__(1024) route_kernel(const double* __restrict__ 
     } else {
       keys[p] = ~0ull;
     }
+  }
   }
   __syncthreads();
   // exact column sums for the ambiguous entries, from the stored tiles
