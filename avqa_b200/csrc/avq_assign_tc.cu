@@ -43,14 +43,13 @@ constexpr int ATHREADS = 192;  // 4 row warps + MMA warp + TMA warp
 constexpr int A_TMEM_COLS = 256;
 constexpr int A_MAX_M0 = 4096;
 constexpr int A_MAX_C = 8;           // children per parent on this path
-constexpr int A_KP = 4;              // keys per cp.async group of the child stage
-constexpr int A_CSQ_PER_WARP = 64;   // staged child norms per warp: ring slots x C <= 64
+constexpr int A_KP = 4;              // keys per ring group of the child stage
 constexpr int A_RING_GROUPS = 4;     // most ring groups of a row warp's child stage
 
 constexpr int AB_K = 0, AB_PFULL = 1, AB_PEMPTY = 3, AB_SFULL = 5, AB_SCONS = 7, AB_END = 9, AN_BARS = 10;
 
 struct AssignLayout {
-  int k, p[2], ps2, csq, rbar, bars, misc, total;
+  int k, p[2], ps2, rbar, bars, misc, total;
 };
 
 __host__ __device__ inline AssignLayout assign_layout(int D, int M0) {
@@ -65,8 +64,6 @@ __host__ __device__ inline AssignLayout assign_layout(int D, int M0) {
   }
   L.ps2 = o;
   o += nch * (ACH / 2) * 4;
-  L.csq = o;
-  o += 4 * A_CSQ_PER_WARP * 4;
   L.rbar = o;  // child-stage ring barriers, A_RING_GROUPS per row warp
   o += 4 * A_RING_GROUPS * 8;
   L.bars = o;
@@ -129,18 +126,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                : "memory");
 }
 
-// cp.async with memory clobbers: shared-memory reads of a ring slot stay
-// between the wait that fills it and the copy that refills it.
-__device__ __forceinline__ void ring_cp4(void* smem, const void* gmem) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void ring_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void ring_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
-
-
 // Bound on sum_d |DT(k_d c_d)| from the dtype norms: |k_d c_d| <= (k_d^2 +
 // c_d^2) / 2, and k_sq, c_sq are the once-rounded exact sums of the dtype
 // squares, so sum_d k_d^2 <= k_sq (1 + 2.1 u) + D eta (u the dtype's unit
@@ -155,9 +140,10 @@ struct ChildBound {
 // Child stage of one warp's 32 keys (quantizer.py:218-227).  A key's C child
 // rows form one contiguous block; its rows are spread over the warp, G lanes
 // to a row, lane (rsub, vg) holding the 16-byte chunks vg + G*t (t < NV) of
-// row rsub, so one key costs the warp NV coalesced 16-byte copies a lane.
-// The blocks stream through a per-warp ring of NG groups of A_KP keys in
-// shared memory (cp.async), NG - 1 groups ahead of the one being reduced.
+// row rsub.  The blocks stream through a per-warp ring of NG groups of A_KP
+// keys in shared memory, one bulk copy per key issued by the key's own lane,
+// NG - 1 groups ahead of the one being reduced; each key's C child norms sit
+// in its lane's registers.
 //
 // cross = DT(fp32(sum_d DT(k_d c_d))) with the sum exact (what the fp64 sum
 // of the dtype products gives) is evaluated in fp32: each lane sums its 8*NV
@@ -174,7 +160,7 @@ struct ChildBound {
 // distance, whose low 13 bits are zero for dtype values, or'ed with the
 // child index.
 template <int DT, int D, int NV, int NG>
-__device__ __forceinline__ int child_stage(unsigned char* ring, float* csr, uint64_t* rbar, volatile int* abort,
+__device__ __forceinline__ int child_stage(unsigned char* ring, uint64_t* rbar, volatile int* abort,
                                            const unsigned char* ktile, int warp, int lane, uint32_t livemask, int pbest,
                                            float ksq, const unsigned char* __restrict__ chh,
                                            const float* __restrict__ csqh, int C) {
@@ -193,28 +179,25 @@ __device__ __forceinline__ int child_stage(unsigned char* ring, float* csr, uint
   const int lane_off = rsub * RB + vg * 16;
   (void)warp;
   // keys KP*grp .. KP*grp+KP-1 into ring group grp % NG: each live key's
-  // owner lane copies its block with one bulk copy, and its C norms with a
-  // second one when they are whole 16-byte units (else 4-byte cp.async); the
-  // group's first owner arms the barrier.  Every lane's reads of the slot fed
-  // the shuffles of the reductions before, so they are complete when the
-  // owner's copy is issued.
+  // owner lane copies its block with one bulk copy; the group's first owner
+  // arms the barrier.  Every lane's reads of the slot fed the shuffles of the
+  // reductions before, so they are complete when the owner's copy is issued.
   auto issue = [&](int grp) {
-    const bool csq_bulk = (C & 3) == 0 && ((uintptr_t)csqh & 15u) == 0;
-    const uint32_t key_bytes = (uint32_t)blk + (csq_bulk ? 4u * C : 0u);
     const int sg = grp % NG, kk = lane % KP;
     const uint32_t gl = (livemask >> (grp * KP)) & ((1u << KP) - 1u);
-    if (lane == grp * KP) tc::mbar_expect_tx(&rbar[sg], (uint32_t)__popc(gl) * key_bytes);
+    if (lane == grp * KP) tc::mbar_expect_tx(&rbar[sg], (uint32_t)__popc(gl) * (uint32_t)blk);
     __syncwarp();
-    if (lane / KP == grp && ((gl >> kk) & 1u)) {
+    if (lane / KP == grp && ((gl >> kk) & 1u))
       bulk_g2s(ring + (sg * KP + kk) * blk, chh + boff_mine, (uint32_t)blk, &rbar[sg]);
-      float* cdst = csr + (sg * KP + kk) * C;
-      const float* csrc = csqh + pbest * C;
-      if (csq_bulk) bulk_g2s(cdst, csrc, 4u * C, &rbar[sg]);
-      else
-        for (int c = 0; c < C; ++c) ring_cp4(cdst + c, csrc + c);
-    }
-    ring_commit();
   };
+  // this lane's key's child norms, read once; the epilogue takes them from the
+  // key's owner lane
+  // the largest C that this lane split serves (the dispatch picks NV from C)
+  constexpr int CQ = D == 128 ? (NV >= 4 ? 8 : (NV == 2 ? 4 : 2)) : (NV >= 2 ? 8 : 4);
+  float cq[CQ];
+  const bool live_mine = ((livemask >> lane) & 1u) != 0u;
+#pragma unroll
+  for (int c = 0; c < CQ; ++c) cq[c] = live_mine && c < C ? csqh[pbest * C + c] : 0.f;
   uint32_t koff[NV];  // this lane's key chunks in the swizzled key tile, before the row swizzle
 #pragma unroll
   for (int t = 0; t < NV; ++t) {
@@ -237,8 +220,6 @@ __device__ __forceinline__ int child_stage(unsigned char* ring, float* csr, uint
   for (; gq < NGRP; ++gq) {
     const int sg = gq % NG;
     if (!__all_sync(full, tc::mbar_wait(&rbar[sg], (gq / NG) & 1, abort))) break;
-    ring_wait<NG - 1>();
-    __syncwarp();  // the child norms come from other lanes' copies
     float sx[KP];
 #pragma unroll
     for (int kk = 0; kk < KP; ++kk) {
@@ -275,7 +256,14 @@ __device__ __forceinline__ int child_stage(unsigned char* ring, float* csr, uint
 #pragma unroll
     for (int o = 1; o < G / 4; o <<= 1) sv += __shfl_xor_sync(full, sv, o);
     const float ksk = __shfl_sync(full, ksq, gq * KP + kq);
-    const float cs = rowon ? csr[(sg * KP + kq) * C + rsub] : 0.f;
+    float cs = 0.f;  // c_sq of this lane's (key, child) pair, from the key's owner lane
+#pragma unroll
+    for (int c = 0; c < CQ; ++c) {
+      if (c < C) {
+        const float v = __shfl_sync(full, cq[c], gq * KP + kq);
+        cs = rsub == c ? v : cs;
+      }
+    }
     const float bnd = __fmaf_ru(__fadd_ru(ksk, cs), ChildBound<DT>::scale, ChildBound<DT>::slack);
     float cross = rnd<DT>(__fsub_rd(sv, bnd));
     const bool bad = rowon && !(cross == rnd<DT>(__fadd_ru(sv, bnd)));
@@ -313,11 +301,9 @@ __device__ __forceinline__ int child_stage(unsigned char* ring, float* csr, uint
     if (lane / KP == gq) mine = res & 0x1FFF;
     // every value read from this ring group fed the reductions above: refill it
     if (gq + NG < NGRP) issue(gq + NG);
-    else ring_commit();
   }
   if (gq < NGRP) {  // a wait gave up: let the copies in flight land before the CTA exits
     for (int g2 = gq; g2 < NGRP && g2 < gq + NG; ++g2) drain(&rbar[g2 % NG], (g2 / NG) & 1);
-    ring_wait<0>();
     return -1;
   }
   return mine;
@@ -589,18 +575,17 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
     if (ok) {
       const uint32_t livemask = __ballot_sync(0xffffffffu, live);
       unsigned char* ring = sm + L.p[0] + warp * (ACH * D);
-      float* csr = reinterpret_cast<float*>(sm + L.csq) + warp * A_CSQ_PER_WARP;
       uint64_t* rbar = reinterpret_cast<uint64_t*>(sm + L.rbar) + warp * A_RING_GROUPS;
       const unsigned char* chh = reinterpret_cast<const unsigned char*>(children + (long)h * M0 * C * D);
       const float* csqh = c_sq + (long)h * M0 * C;
       const unsigned char* kt = sm + L.k;
       if constexpr (D == 128)
-        bi = C <= 2 ? child_stage<DT, D, 1, 4>(ring, csr, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
-             : C <= 4 ? child_stage<DT, D, 2, 4>(ring, csr, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
-                      : child_stage<DT, D, 4, 2>(ring, csr, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C);
+        bi = C <= 2 ? child_stage<DT, D, 1, 4>(ring, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
+             : C <= 4 ? child_stage<DT, D, 2, 4>(ring, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
+                      : child_stage<DT, D, 4, 2>(ring, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C);
       else
-        bi = C <= 4 ? child_stage<DT, D, 1, 4>(ring, csr, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
-                    : child_stage<DT, D, 2, 2>(ring, csr, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C);
+        bi = C <= 4 ? child_stage<DT, D, 1, 4>(ring, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
+                    : child_stage<DT, D, 2, 2>(ring, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C);
     }
     if (live) {  // a CTA that gave up on a wait still leaves indices in range for the later kernels
       const bool good = ok && bi >= 0;
