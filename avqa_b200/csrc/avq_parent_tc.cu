@@ -9,13 +9,17 @@
 // 32hf..32hf+31 of every 64-parent chunk, and the halves combine their row
 // statistics once per pass.  Warp 8 issues the tcgen05.mma instructions;
 // warp 9 streams Q, parent and parent-sum tiles with TMA into
-// 128-byte-swizzled shared memory.
+// 128-byte-swizzled shared memory: after Q, one ring of four tile buffers
+// takes the parent tiles of pass 1 and then the parent and parent-sum tiles
+// of pass 2 alternately, in that order.
 //
 // TMEM, 256 columns: the fp32 accumulator O = e @ V in [0, D) and two
-// 64-column logit buffers at [D, D+64) and [D+64, D+128).  A buffer receives
-// one 64-parent chunk of Q P^T; in the second pass half hf overwrites the
-// first 16 of its 32 columns with its 32 dtype exponentials (two per column),
-// the A operand of the e @ V MMA (K steps at columns 0, 8, 32, 40).
+// 64-column logit slots at [D, D+64) and [D+64, D+128).  A slot receives one
+// 64-parent chunk of Q P^T; in the second pass half hf overwrites the first
+// 16 of its 32 columns with its 32 dtype exponentials (two per column), the A
+// operand of the e @ V MMA (K steps at columns 0, 8, 32, 40).  Pass 1, which
+// leaves O unused, has two more logit slots in O's columns (and past D + 128
+// for D = 64), so four chunks are in flight.
 //
 //   pass 1  S_c = Q P_c^T for every chunk c; row max of the narrowed,
 //           scaled, masked logits.
@@ -58,9 +62,16 @@ constexpr int EXP_N = 2051;            // entries 0..2049: |d| bits EXP_BASE + i
 constexpr int EXP_WORDS = (EXP_N + 1) / 2;
 constexpr int TC_MAX_M0 = 2048;
 
-// Barrier slots.
-constexpr int B_Q = 0, B_PFULL = 1, B_PEMPTY = 3, B_VFULL = 5, B_VEMPTY = 7, B_SFULL = 9, B_EFULL = 11, B_SFREE = 13,
-              B_OFULL = 14, N_BARS = 15;
+// Barrier slots: the tile ring's full and empty barriers, the logit slots'
+// full (MMA done) and consumed (row threads done) barriers.
+constexpr int B_Q = 0, B_RFULL = 1, B_REMPTY = 5, B_SFULL = 9, B_EFULL = 13, B_SFREE = 17, B_OFULL = 18, N_BARS = 19;
+constexpr int NRING = 4;  // tile ring buffers (the layout's p[0], p[1], v[0], v[1], contiguous)
+
+// TMEM column of logit slot k; slots 2 and 3 only in pass 1.
+template <int D>
+__device__ __forceinline__ uint32_t s_col(int k) {
+  return k < 2 ? D + 64 * k : (D == 128 ? 64 * (k - 2) : (k == 2 ? 0 : D + 128));
+}
 
 struct TcLayout {
   int q, p[2], v[2], exptab, pm2, n2, srow, scomb, xch, bars, misc, total;
@@ -198,12 +209,41 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
   float* scomb = reinterpret_cast<float*>(sm + L.scomb);
   float* xch = reinterpret_cast<float*>(sm + L.xch);
 
+  const int ntl = nch + nv;  // ring tiles: P_0..P_{nch-1}, then P_0, V_0, P_1, V_1, ...
+  constexpr int RB = TCH * D * 2;
+  // ring tile i into buffer i % NRING (expect_tx, then the 64-column boxes)
+  auto load_tile = [&](int i) {
+    const int k = i & (NRING - 1);
+    unsigned char* buf = sm + L.p[0] + k * RB;
+    tc::mbar_expect_tx(&bars[B_RFULL + k], RB);
+    const bool par = i < nch || ((i - nch) & 1) == 0;
+    const int c = i < nch ? i : (i - nch) >> 1;
+    for (int kb = 0; kb < D / 64; ++kb) {
+      if (par) tc::tma_load_3d(buf + kb * TCH * 128, &tm_p, kb * 64, c * TCH, h, &bars[B_RFULL + k]);
+      else tc::tma_load_3d(buf + kb * TCH * 128, &tm_v, kb * 64, c * TCH, g, &bars[B_RFULL + k]);
+    }
+  };
+
   // ---- setup: barriers, TMEM, tables ----
-  if (tid == 0) {
-    for (int i = 0; i < N_BARS; ++i)
-      tc::mbar_init(&bars[i], (i == B_EFULL || i == B_EFULL + 1) ? TROW : 1);
+  // The producer thread initialises the barriers and issues Q and the first
+  // ring tiles at once, so the copies overlap the table fill.
+  if (warp == W_TMA && lane == 0) {
+    for (int i = 0; i < N_BARS; ++i) tc::mbar_init(&bars[i], (i >= B_EFULL && i < B_EFULL + 4) ? TROW : 1);
     *abort = 0;
     tc::fence_mbar_init();
+    tc::tma_prefetch_desc(&tm_q);
+    tc::tma_prefetch_desc(&tm_p);
+    tc::tma_prefetch_desc(&tm_v);
+    tc::mbar_expect_tx(&bars[B_Q], TR * D * 2);
+    for (int kb = 0; kb < D / 64; ++kb) {
+      int c[4];
+      c[0] = kb * 64;
+      c[qpos.x] = t0;
+      c[qpos.y] = h;
+      c[qpos.z] = b;
+      tc::tma_load_4d(sm + L.q + kb * TR * 128, &tm_q, c[0], c[1], c[2], c[3], &bars[B_Q]);
+    }
+    for (int i = 0; i < NRING && i < ntl; ++i) load_tile(i);
   }
   if (warp == W_MMA) tc::tmem_alloc(tslot, TC_TMEM_COLS);
   if (tid < TROW) {
@@ -223,44 +263,17 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
   const uint32_t tbase = *tslot;
 
   if (warp == W_TMA) {
-    // ---- TMA producer ----
+    // ---- TMA producer: the rest of the ring, each buffer once its last tile is consumed ----
     if (lane == 0) {
-      tc::tma_prefetch_desc(&tm_q);
-      tc::tma_prefetch_desc(&tm_p);
-      tc::tma_prefetch_desc(&tm_v);
-      int nq = 0, np[2] = {0, 0}, nvv[2] = {0, 0};
-      tc::mbar_expect_tx(&bars[B_Q], TR * D * 2);
-      for (int kb = 0; kb < D / 64; ++kb) {
-        int c[4];
-        c[0] = kb * 64;
-        c[qpos.x] = t0;
-        c[qpos.y] = h;
-        c[qpos.z] = b;
-        tc::tma_load_4d(sm + L.q + kb * TR * 128, &tm_q, c[0], c[1], c[2], c[3], &bars[B_Q]);
-      }
-      nq = 1;
-      for (int v = 0; v < nv; ++v) {
-        const int c = v % nch, s = v & 1;
-        if (v >= 2 && !tc::mbar_wait(&bars[B_PEMPTY + s], ((v - 2) >> 1) & 1, abort)) break;
-        tc::mbar_expect_tx(&bars[B_PFULL + s], TCH * D * 2);
-        for (int kb = 0; kb < D / 64; ++kb)
-          tc::tma_load_3d(sm + L.p[s] + kb * TCH * 128, &tm_p, kb * 64, c * TCH, h, &bars[B_PFULL + s]);
-        ++np[s];
-        if (v >= nch) {
-          const int u = v - nch, vs = u & 1;
-          if (u >= 2 && !tc::mbar_wait(&bars[B_VEMPTY + vs], ((u - 2) >> 1) & 1, abort)) break;
-          tc::mbar_expect_tx(&bars[B_VFULL + vs], TCH * D * 2);
-          for (int nb = 0; nb < D / 64; ++nb)
-            tc::tma_load_3d(sm + L.v[vs] + nb * TCH * 128, &tm_v, nb * 64, c * TCH, g, &bars[B_VFULL + vs]);
-          ++nvv[vs];
-        }
+      int issued = ntl < NRING ? ntl : NRING;
+      for (int i = NRING; i < ntl; ++i) {
+        if (!tc::mbar_wait(&bars[B_REMPTY + (i & (NRING - 1))], ((i >> 2) - 1) & 1, abort)) break;
+        load_tile(i);
+        issued = i + 1;
       }
       if (*abort) {  // let the copies in flight land before the CTA exits
-        if (nq) drain_wait(&bars[B_Q], 0);
-        for (int s = 0; s < 2; ++s) {
-          if (np[s]) drain_wait(&bars[B_PFULL + s], (np[s] - 1) & 1);
-          if (nvv[s]) drain_wait(&bars[B_VFULL + s], (nvv[s] - 1) & 1);
-        }
+        drain_wait(&bars[B_Q], 0);
+        for (int k = 0; k < NRING && k < issued; ++k) drain_wait(&bars[B_RFULL + k], ((issued - 1 - k) >> 2) & 1);
       }
     }
   } else if (warp == W_MMA) {
@@ -269,54 +282,73 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       const int fmt = DT == DT_BF16 ? 1 : 0;
       const uint32_t idS = tc::idesc_f16(fmt, TR, TCH, false);
       const uint32_t idO = tc::idesc_f16(fmt, TR, D, true);
-      const uint32_t qa = tc::smem_addr(sm + L.q);
-      const uint32_t pa[2] = {tc::smem_addr(sm + L.p[0]), tc::smem_addr(sm + L.p[1])};
-      const uint32_t va[2] = {tc::smem_addr(sm + L.v[0]), tc::smem_addr(sm + L.v[1])};
-      auto issue_S = [&](int v) {
-        const int s = v & 1;
+      const uint32_t qa = tc::smem_addr(sm + L.q), ra0 = tc::smem_addr(sm + L.p[0]);
+      // chunk w's logits in logit slot slot(w), from ring tile s_tile(w); the
+      // e @ V MMA of second-pass chunk u reads ring tile nch + 2u + 1
+      auto slot = [&](int w) { return w < nch ? (w & 3) : (w & 1); };
+      auto s_tile = [&](int w) { return w < nch ? w : nch + 2 * (w - nch); };
+      auto issue_S = [&](int w) {
+        const int i = s_tile(w), k = i & (NRING - 1), sl = slot(w);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t ad = tc::sdesc_sw128(qa + (kk >> 2) * TR * 128 + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = tc::sdesc_sw128(pa[s] + (kk >> 2) * TCH * 128 + (kk & 3) * 32, 16, 1024);
-          tc::mma_ss(tbase + D + 64 * s, ad, bd, idS, kk > 0);
+          const uint64_t bd = tc::sdesc_sw128(ra0 + k * RB + (kk >> 2) * TCH * 128 + (kk & 3) * 32, 16, 1024);
+          tc::mma_ss(tbase + s_col<D>(sl), ad, bd, idS, kk > 0);
         }
-        tc::mma_commit(&bars[B_SFULL + s]);
-        tc::mma_commit(&bars[B_PEMPTY + s]);
+        tc::mma_commit(&bars[B_SFULL + sl]);
+        tc::mma_commit(&bars[B_REMPTY + k]);
+      };
+      auto tile_ready = [&](int i) { return tc::mbar_wait(&bars[B_RFULL + (i & (NRING - 1))], (i >> 2) & 1, abort); };
+      // the next chunk to use chunk v's logit slot, or -1.  The second pass
+      // takes slots 0 and 1 after the first pass's last chunks there.
+      auto next_user = [&](int v) {
+        if (v >= nch) return v + 2 < nv ? v + 2 : -1;
+        if (v + 4 < nch) return v + 4;
+        const int k = v & 3, w = nch + ((k - nch) & 1);
+        return k < 2 && w < nv ? w : -1;
       };
       bool ok = tc::mbar_wait(&bars[B_Q], 0, abort);
-      for (int v = 0; ok && v < 2 && v < nv; ++v) {
-        ok = tc::mbar_wait(&bars[B_PFULL + v], 0, abort);
-        if (ok) {
+      // the chunks whose slot has no earlier user: the first four, and the
+      // second pass's chunk 1 when there is one parent chunk
+      for (int w = 0; ok && w < 4 && w < nch; ++w) {
+        if ((ok = tile_ready(s_tile(w)))) {
           tc::tc_after_sync();
-          issue_S(v);
+          issue_S(w);
         }
       }
+      if (ok && nch == 1 && (ok = tile_ready(s_tile(1)))) {
+        tc::tc_after_sync();
+        issue_S(1);
+      }
       int nfree = 0;
+      uint32_t eph = 0u;  // phase bit per logit slot's consumed barrier
       for (int v = 0; ok && v < nv; ++v) {
-        const int s = v & 1;
-        if (!(ok = tc::mbar_wait(&bars[B_EFULL + s], (v >> 1) & 1, abort))) break;
+        const int sl = slot(v);
+        if (!(ok = tc::mbar_wait(&bars[B_EFULL + sl], (eph >> sl) & 1u, abort))) break;
+        eph ^= 1u << sl;
         tc::tc_after_sync();
         if (v >= nch) {
-          const int u = v - nch, vs = u & 1;
-          if (!(ok = tc::mbar_wait(&bars[B_VFULL + vs], (u >> 1) & 1, abort))) break;
+          const int u = v - nch, i = nch + 2 * u + 1, k = i & (NRING - 1);
+          if (!(ok = tile_ready(i))) break;
           tc::tc_after_sync();
           // K steps of 16 parents: columns 0, 8 (half 0) and 32, 40 (half 1)
 #pragma unroll
           for (int kk = 0; kk < TCH / 16; ++kk) {
-            const uint64_t bd = tc::sdesc_sw128(va[vs] + kk * 16 * 128, TCH * 128, 1024);
-            tc::mma_ts(tbase, tbase + D + 64 * s + (kk >> 1) * 32 + (kk & 1) * 8, bd, idO, u > 0 || kk > 0);
+            const uint64_t bd = tc::sdesc_sw128(ra0 + k * RB + kk * 16 * 128, TCH * 128, 1024);
+            tc::mma_ts(tbase, tbase + D + 64 * sl + (kk >> 1) * 32 + (kk & 1) * 8, bd, idO, u > 0 || kk > 0);
           }
-          tc::mma_commit(&bars[B_VEMPTY + vs]);
+          tc::mma_commit(&bars[B_REMPTY + k]);
         }
-        if (v + 2 < nv) {
-          if (v >= nch) {  // the e @ V MMA still reads this buffer
+        const int w = next_user(v);
+        if (w >= 0) {
+          if (v >= nch) {  // the e @ V MMA still reads this slot
             tc::mma_commit(&bars[B_SFREE]);
             if (!(ok = tc::mbar_wait(&bars[B_SFREE], nfree & 1, abort))) break;
             ++nfree;
           }
-          if (!(ok = tc::mbar_wait(&bars[B_PFULL + s], ((v + 2) >> 1) & 1, abort))) break;
+          if (!(ok = tile_ready(s_tile(w)))) break;
           tc::tc_after_sync();
-          issue_S(v + 2);
+          issue_S(w);
         }
       }
       tc::mma_commit(&bars[B_OFULL]);  // arrives once every MMA above has completed
@@ -338,16 +370,18 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     // scaling are monotone, so it is the logit of the largest raw accumulator
     // over the non-empty parents (NaN-propagating, as torch.max).
     float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    uint32_t sph = 0u;  // phase bit per logit slot's full barrier
     for (int v = 0; v < nch; ++v) {
-      const int s = v & 1;
-      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_SFULL + s], (v >> 1) & 1, abort));
+      const int sl = v & 3;
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_SFULL + sl], (sph >> sl) & 1u, abort));
+      sph ^= 1u << sl;
       if (!ok) break;
       tc::tc_after_sync();
       uint32_t ra[32];
-      tc::tmem_ld32(tbase + lane_off + D + 64 * s + 32 * hf, ra);
+      tc::tmem_ld32(tbase + lane_off + s_col<D>(sl) + 32 * hf, ra);
       tc::tmem_wait_ld();
       tc::tc_before_sync();
-      tc::mbar_arrive(&bars[B_EFULL + s]);
+      tc::mbar_arrive(&bars[B_EFULL + sl]);
       const uint32_t* pm = pm2 + v * 32 + 16 * hf;
       const uint4* pm4 = reinterpret_cast<const uint4*>(pm);
       uint32_t all = 0xFFFFFFFFu;
@@ -378,7 +412,8 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     float za = 0.f;
     for (int v = nch; ok && v < nv; ++v) {
       const int c = v - nch, s = v & 1;
-      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_SFULL + s], (v >> 1) & 1, abort));
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_SFULL + s], (sph >> s) & 1u, abort));
+      sph ^= 1u << s;
       if (!ok) break;
       tc::tc_after_sync();
       const uint32_t col = tbase + lane_off + D + 64 * s + 32 * hf;
