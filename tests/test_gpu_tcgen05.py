@@ -38,6 +38,12 @@ CASES = [
              hvaq=True),
     Workload("quirk_bf16", B=1, T=64, S=200, H=2, D=64, M0=8, C=4, P=8, dtype="bf16", keys="mixture", seed=47,
              passes=2, pass_decay=1.0),
+    # 5 and 7 parent chunks (the last one partial): the first pass's four logit slots run
+    # out at different chunks and the second pass starts on an odd chunk
+    Workload("m320_bf16", B=1, T=200, S=2048, H=2, D=128, M0=320, C=4, P=16, dtype="bf16", keys="mixture",
+             seed=49),
+    Workload("m440_d64_bf16", B=1, T=130, S=2048, H=2, D=64, M0=440, C=4, P=16, dtype="bf16", keys="aniso",
+             seed=50),
     # the largest parent count of the tcgen05 parent attention (32 chunks, one CTA per SM)
     Workload("m2048_bf16", B=1, T=160, S=4096, H=1, D=128, M0=2048, C=4, P=64, dtype="bf16", keys="mixture",
              seed=48),
