@@ -330,7 +330,7 @@ __global__ void __launch_bounds__(1024) route_kernel(const double* __restrict__ 
   }
   __syncthreads();
   // exact column sums for the ambiguous entries, from the stored tiles
-  const int LDL = M0 + 8;
+  const int LDL = exp_slice_pitch(M0);
   using T = typename Storage<DT>::T;
   const T* scr = (const T*)rx.scratch;
   for (int ia = 0; ia < namb; ++ia) {

@@ -29,7 +29,7 @@ constexpr int PM_MAX_SMEM_M0 = 1024;
 // Parent attention kernel.  CTA = 64 queries = 4 warps x 16 rows; a lane quad
 // owns two rows (r0, r0+8) and a quarter of their columns, so row statistics
 // combine with two shuffles.  The logits / exponentials of the CTA's rows live
-// in a per-CTA global slice (64 x (M0+8) dtype values, L2-resident while the
+// in a per-CTA global slice (64 x exp_slice_pitch(M0) dtype values, L2-resident while the
 // CTA runs) that the routing kernel can re-read for its exactness fallback.
 // ---------------------------------------------------------------------------
 template <int DT, int D>
@@ -51,7 +51,7 @@ __global__ void __launch_bounds__(128, 4) parent_attn_mma_kernel(
   float* scomb = srow + 4 * PM_ROWS;           // [4][64] column partials of the 4 warps
   const int g = blockIdx.y, b = g / H, h = g % H, qt = blockIdx.x, t0 = qt * PM_ROWS, nqt = gridDim.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int LDL = M0 + 8;
+  const int LDL = exp_slice_pitch(M0);
   const float inv_sqrtD = 1.f / sqrtD;
   T* S_ = scratch + ((long)g * nqt + qt) * PM_ROWS * LDL;
   const int r0 = warp * 16 + (lane >> 2), r1 = r0 + 8, cq = (lane & 3) * 2;
@@ -669,14 +669,14 @@ size_t parent_attn_mma_smem(int D, int M0, bool s_in_smem, int dt_bytes) {
 
 bool parent_attn_mma_ok(int dt, int D, int M0) { return dt != DT_F32 && (D == 64 || D == 128) && M0 % 8 == 0; }
 
-// The logits always live in the per-CTA global slice (64 x (M0+8) dtype
+// The logits always live in the per-CTA global slice (64 x exp_slice_pitch(M0) dtype
 // values): shared-memory logits would cost occupancy, and the routing
 // kernel's exactness fallback re-reads the slices.
 bool parent_attn_mma_smem_mode(int D, int M0) { return false; }
 
 size_t parent_attn_mma_scratch(int G, int T, int M0, int dt_bytes) {
   const int nqt = (T + PM_ROWS - 1) / PM_ROWS;
-  return (size_t)G * nqt * PM_ROWS * (M0 + 8) * dt_bytes;
+  return (size_t)G * nqt * PM_ROWS * exp_slice_pitch(M0) * dt_bytes;
 }
 
 template <int DT>

@@ -13,6 +13,12 @@ struct Strides3 {
 
 inline size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
 
+// Row pitch, in elements, of the per-64-query exponential slices that the
+// parent-attention kernels write and the routing kernel re-reads: M0 rounded up
+// to 16, plus 16, so that every row of a 16-bit slice starts on a 32-byte
+// boundary.
+__host__ __device__ inline int exp_slice_pitch(int M0) { return ((M0 + 15) & ~15) + 16; }
+
 struct QuantizeArgs {
   const void* keys;
   Strides3 ks;
@@ -114,7 +120,7 @@ struct PAArgs {
 // reading the parent-attention tiles (see route_kernel).
 struct RouteExact {
   const float* colpart;  // nullptr: the fp64 partials path
-  const void* scratch;   // dtype tiles [G][nqt][64][M0+8]
+  const void* scratch;   // dtype tiles [G][nqt][64][exp_slice_pitch(M0)]
   int scr_logits;        // tiles hold logits (exponentials recomputed from m)
   const float* m;        // [G,T]
   const float* z;        // [G,T]

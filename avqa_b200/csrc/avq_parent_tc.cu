@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
   const TcLayout L = tc_layout(D, M0);
   const int g = blockIdx.y, b = g / H, h = g % H, qt = blockIdx.x, t0 = qt * TR;
   const int nch = (M0 + TCH - 1) / TCH, nv = 2 * nch;
-  const int ntiles = (Tq + 63) / 64, LDL = M0 + 8;
+  const int ntiles = (Tq + 63) / 64, LDL = exp_slice_pitch(M0);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.bars);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + L.misc);
@@ -365,6 +365,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     const uint32_t ninf2 = DT == DT_BF16 ? 0xFF80FF80u : 0xFC00FC00u;
     const long row = (long)g * Tq + t;
     T* srow_g = scratch + (((long)g * ntiles + (t >> 6)) * 64 + (t & 63)) * LDL;
+    const bool sector_stores = (reinterpret_cast<uintptr_t>(scratch) & 31u) == 0u;
     bool ok = true;
     // pass 1: the row max of the logits (pipeline.py:107,137).  Narrowing and
     // scaling are monotone, so it is the logit of the largest raw accumulator
@@ -477,9 +478,18 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
         zh[hh] = zs[0];
         tc::tmem_st8(col + 8 * hh, e2);
         if (live && 2 * pw < M0) {  // M0 is a multiple of 8: a block of 16 is all in or all out
-          uint4* dst = reinterpret_cast<uint4*>(srow_g + 2 * pw);
-          dst[0] = make_uint4(e2[0], e2[1], e2[2], e2[3]);
-          dst[1] = make_uint4(e2[4], e2[5], e2[6], e2[7]);
+          // one whole 32-byte sector per store when the slices are 32-byte
+          // aligned (the pitch keeps every row so), else two 16-byte halves
+          T* dst = srow_g + 2 * pw;
+          if (sector_stores) {
+            asm volatile("st.global.L1::no_allocate.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst),
+                         "r"(e2[0]), "r"(e2[1]), "r"(e2[2]), "r"(e2[3]), "r"(e2[4]), "r"(e2[5]), "r"(e2[6]), "r"(e2[7])
+                         : "memory");
+          } else {
+            uint4* d4 = reinterpret_cast<uint4*>(dst);
+            d4[0] = make_uint4(e2[0], e2[1], e2[2], e2[3]);
+            d4[1] = make_uint4(e2[4], e2[5], e2[6], e2[7]);
+          }
         }
       }
       za += zh[0] + zh[1];
