@@ -59,11 +59,53 @@ def parse_args():
 # ---------------------------------------------------------------------------
 # clocks
 # ---------------------------------------------------------------------------
+class _NvmlPoller(threading.Thread):
+    """Read-only NVML reads of the SM clock, its maximum, power and the clock
+    event reasons every 5 ms, so that a timed region shorter than the
+    nvidia-smi interval still holds samples.  Rows have the nvidia-smi
+    sampler's shape; without NVML (no driver) it records nothing."""
+
+    REASONS = ("nvmlClocksEventReasonHwSlowdown", "nvmlClocksEventReasonHwThermalSlowdown",
+               "nvmlClocksEventReasonSwThermalSlowdown", "nvmlClocksEventReasonSwPowerCap")
+
+    def __init__(self, gpu_index: int, period: float = 0.005):
+        super().__init__(daemon=True)
+        self.gpu, self.period, self.rows = gpu_index, period, []
+        self.stop_evt = threading.Event()
+
+    def run(self) -> None:
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            sm_max = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            masks = [getattr(pynvml, n) for n in self.REASONS]
+        except Exception:
+            return
+        try:
+            while not self.stop_evt.is_set():
+                try:
+                    sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    flags = ["Active" if rs & m else "Not Active" for m in masks]
+                    self.rows.append((time.time(), sm, sm_max, pw, flags))
+                except Exception:
+                    return
+                self.stop_evt.wait(self.period)
+        finally:
+            try:
+                pynvml.nvmlShutdown()
+            except Exception:
+                pass
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons, sampled every 50 ms with host
-    timestamps.  ``mark(start, end)`` records the timed window; the summary
-    uses the samples inside it, and widens to the warm-up steps before it
-    (the same work) only when the window held fewer than three samples."""
+    timestamps, joined by NVML reads every 5 ms.  ``mark(start, end)`` records
+    the timed window; the summary uses the samples inside it, and widens to
+    the warm-up steps before it (the same work) only when the window held
+    fewer than three samples."""
 
     FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -74,8 +116,10 @@ class ClockSampler:
         self.proc = None
         self.file = None
         self.t_open = self.t0 = self.t1 = None
+        self.nvml = _NvmlPoller(gpu_index)
 
     def __enter__(self):
+        self.nvml.start()
         self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
@@ -94,6 +138,8 @@ class ClockSampler:
         self.t0, self.t1 = t0, t1
 
     def __exit__(self, *exc):
+        self.nvml.stop_evt.set()
+        self.nvml.join(timeout=2)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -103,10 +149,10 @@ class ClockSampler:
 
     def summary(self) -> dict:
         from datetime import datetime
-        if self.proc is None:
+        rows = list(self.nvml.rows)
+        if self.proc is None and not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.file.flush()
-        rows = []
         for line in Path(self.file.name).read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 10:
