@@ -30,8 +30,8 @@ _SIGS = {
                       _P, _P, _P, _Z, _P], _I),
     "avq_selection_stride": ([_I, _I, _F], _I),
     "avq_forward_workspace_size": ([_I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I], _Z),
-    "avq_forward": ([_I, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _I, _F, _F, _P, _P,
-                     _P, _P, _P, _P, _Z, _P], _I),
+    "avq_forward": ([_I, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I, _I, _F, _I, _F, _F,
+                     _P, _P, _P, _P, _P, _P, _Z, _P], _I),
     "avq_append": ([_I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                     _P, _I, _P], _I),
     "avq_reduce_min": ([_P, _I, _P, _P], _I),

@@ -143,6 +143,23 @@ class AVQAttention(nn.Module):
     def forward_impl(self, query, key, value, mask=None, kv_cache=None) -> torch.Tensor:
         return cuda_run_pipeline(self, query, key, value, mask, kv_cache)
 
+    def forward_chunked(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                        chunk_size: int) -> torch.Tensor:
+        """``forward`` of ``query`` in sequential chunks of ``chunk_size``
+        queries over the same ``key``/``value``.
+
+        The result equals one ``forward(query[:, chunk], key, value)`` call per
+        chunk, concatenated: each chunk gets its own routing (importance summed
+        over its own queries), and every chunk sees the same budget because the
+        keys are the same.  The reference re-quantizes the keys on every such
+        call (``attention_module.py:392-440``); quantization is deterministic,
+        so here it runs once and every chunk attends to the cached state.  With
+        batch 1 all chunks run in one launch sequence.
+        """
+        if chunk_size <= 0:
+            raise ShapeError("chunk_size must be positive", expected="> 0", actual=chunk_size)
+        return cuda_run_pipeline(self, query, key, value, None, None, chunk_size=chunk_size)
+
 
 def hvaq_mode(config: AVQConfig) -> int:
     """0 off, 1 entropy, 2 linear (the gate of pipeline.py:353)."""
@@ -152,14 +169,14 @@ def hvaq_mode(config: AVQConfig) -> int:
 
 
 def cuda_run_pipeline(m, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
-                      mask: torch.Tensor | None = None, kv_cache=None) -> torch.Tensor:
+                      mask: torch.Tensor | None = None, kv_cache=None, chunk_size: int = 0) -> torch.Tensor:
     """The reference pipeline (pipeline.py:276-399) on the CUDA library.
 
     ``m`` is any module with the reference ``AVQAttention`` attributes
     (``config``, ``codebook``, ``q_proj``/``k_proj``/``v_proj``/``out_proj``,
     ``dropout``, ``validate_inputs``, ``sync_codebook_device``) whose
     ``backend`` is a :class:`CUDABackend` -- this package's module or the
-    reference's own one.
+    reference's own one, once its ``run_pipeline`` is routed here.
     """
     c = m.config
     if mask is not None or c.causal:
@@ -181,24 +198,68 @@ def cuda_run_pipeline(m, query: torch.Tensor, key: torch.Tensor, value: torch.Te
         # pipeline.py:344-345: budget 0 -> naive attention over zero keys
         attn = backend.naive_attention(q, k, v)
         return m.dropout(m.out_proj(AVQAttention.merge_heads(attn)))
-    min_valid = global_min_valid(state, getattr(m, "process_group", None))
+    min_valid, ready = global_min_valid(state, getattr(m, "process_group", None))
     out = torch.empty(B, T, H * D, dtype=torch.float32, device=q.device)
-    out4 = out.view(B, T, H, D).transpose(1, 2)
     beta0 = c.hopfield.beta_init if c.hopfield.beta_init > 0 else 1.0 / math.sqrt(D)
-    backend.forward(q, cb, state, min(c.routing.refinement_budget, cb.dims[1]), c.refinement.passes,
-                    c.refinement.pass_decay, hvaq_mode(c), beta0, c.hopfield.alpha, out=out4, min_valid=min_valid)
+    args = (min(c.routing.refinement_budget, cb.dims[1]), c.refinement.passes, c.refinement.pass_decay, hvaq_mode(c),
+            beta0, c.hopfield.alpha)
+    for q_part, out_part in query_chunks(q, out, H, chunk_size):
+        backend.forward(q_part, cb, state, *args, out=out_part, min_valid=min_valid, min_valid_ready=ready)
+        ready = None  # later chunks are ordered after the first one's wait
     return m.dropout(m.out_proj(out))
 
 
-def global_min_valid(state: ops.QuantState, group=None) -> torch.Tensor:
+def query_chunks(q: torch.Tensor, out: torch.Tensor, H: int, chunk: int):
+    """``(queries [b, H, t, D], output [b, H, t, D] view)`` pairs covering
+    ``q [B, H, T, D]`` in chunks of ``chunk`` queries (all of T when 0).
+
+    With batch 1 the whole chunks form one query batch (chunk c = batch entry
+    c, a strided view) that attends to the batch-1 key state in one call; the
+    ragged tail and batches > 1 go chunk by chunk."""
+    B, _, T, D = q.shape
+    out4 = out.view(B, T, H, D)
+    if chunk <= 0 or chunk >= T:
+        yield q, out4.transpose(1, 2)
+        return
+    full = T // chunk
+    if B == 1 and full > 1:
+        qs = q.as_strided((full, H, chunk, D), (q.stride(2) * chunk, q.stride(1), q.stride(2), q.stride(3)))
+        os_ = out4.as_strided((full, H, chunk, D), (out4.stride(1) * chunk, out4.stride(2), out4.stride(1), 1))
+        yield qs, os_
+        start = full * chunk
+    else:
+        start = 0
+    for t0 in range(start, T, chunk):
+        t1 = min(t0 + chunk, T)
+        yield q[:, :, t0:t1], out4[:, t0:t1].transpose(1, 2)
+
+
+_SIDE_STREAMS: dict = {}
+
+
+def global_min_valid(state: ops.QuantState, group=None) -> tuple[torch.Tensor, torch.cuda.Event | None]:
     """The budget floor: min over every (b,h) of the call -- and of every
-    rank of ``group`` when batches or heads are sharded."""
+    rank of ``group`` when batches or heads are sharded.
+
+    With a group the all-reduce(MIN) runs on a side stream after the
+    quantization; the returned event marks its completion, and the forward
+    waits on it only before routing, so parent attention overlaps it."""
     if group is None:
-        return state.gmin
+        return state.gmin, None
     import torch.distributed as dist
+    dev = state.gmin.device
+    main = torch.cuda.current_stream(dev)
+    side = _SIDE_STREAMS.get(dev)
+    if side is None:
+        side = _SIDE_STREAMS[dev] = torch.cuda.Stream(dev)
     g = state.gmin.clone()
-    dist.all_reduce(g, op=dist.ReduceOp.MIN, group=group)
-    return g
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        dist.all_reduce(g, op=dist.ReduceOp.MIN, group=group)
+        ready = torch.cuda.Event()
+        ready.record(side)
+    g.record_stream(side)
+    return g, ready
 
 
 def _cache_states(kv_cache) -> dict:
@@ -248,4 +309,5 @@ def resolve_quantization(m, k: torch.Tensor, v: torch.Tensor, cb: ops.PreparedCo
     return st
 
 
-__all__ = ["AVQAttention", "cuda_run_pipeline", "global_min_valid", "hvaq_mode", "resolve_quantization"]
+__all__ = ["AVQAttention", "cuda_run_pipeline", "global_min_valid", "hvaq_mode", "query_chunks",
+           "resolve_quantization"]

@@ -98,8 +98,16 @@ def _lloyd_children(keys: torch.Tensor, parents: torch.Tensor, children: torch.T
     """One fp32 hierarchical assignment of ``keys [H,S,D]``; returns child means.
 
     Same arithmetic as the reference quantizer in fp32 (``quantizer.py:196-269``).
+    Heads are independent, so they run in groups that keep the ``[h, S, M0]``
+    distance tensor near 2^28 elements (the long-context codebook would
+    otherwise need 137 GB); every bucket sums its keys in the same order.
     """
     H, S, D = keys.shape
+    M0 = children.shape[1]
+    step = max(1, (1 << 28) // max(1, S * M0))
+    if step < H:
+        return torch.cat([_lloyd_children(keys[h:h + step], parents[h:h + step], children[h:h + step])
+                          for h in range(0, H, step)])
     M0, C = children.shape[1], children.shape[2]
     k_sq = (keys * keys).sum(-1, keepdim=True)
     p_sq = (parents * parents).sum(-1).unsqueeze(1)

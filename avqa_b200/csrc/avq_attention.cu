@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(256) parent_attn_kernel(
     const int* __restrict__ pcnt, int mode, float* __restrict__ sbuf, float* __restrict__ m_io,
     float* __restrict__ l_out, float* __restrict__ z_io, float* __restrict__ a_out, double* __restrict__ imp_part,
     const int* __restrict__ sel0, int sel_stride, const int* __restrict__ pass_cnt, int hvaq, float beta0,
-    float alpha, float* __restrict__ beta_out) {
+    float alpha, float* __restrict__ beta_out, int sG) {
   constexpr int NK = DMAX / 8;
   extern __shared__ float smem[];
   const int ld = D + 1;
@@ -51,7 +51,7 @@ __global__ void __launch_bounds__(256) parent_attn_kernel(
   float* pp = qq + PA_ROWS * ld;         // [PA_COLS][ld]
   float* ee = pp + PA_COLS * ld;         // [PA_ROWS][PA_COLS + 1]
   float* nn = ee + PA_ROWS * (PA_COLS + 1);  // [PA_COLS]
-  const int g = blockIdx.y, b = g / H, h = g % H, qt = blockIdx.x;
+  const int g = blockIdx.y, b = g / H, h = g % H, qt = blockIdx.x, gs = g % sG;
   const int tid = threadIdx.x, r = tid >> 3, l8 = tid & 7;
   const int t = qt * PA_ROWS + r;
   const bool live = t < T;
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(256) parent_attn_kernel(
         const int p = p0 + l8 + 8 * i;
         if (p < M0) {
           // pipeline.py:81 (matmul, / sqrt(D)) and :107 (invalid -> -inf)
-          float s = pcnt[(long)g * M0 + p] > 0 ? rnd<DT>(__fdiv_rn(rnd64<DT>(acc[i]), sqrtD)) : -INFINITY;
+          float s = pcnt[(long)gs * M0 + p] > 0 ? rnd<DT>(__fdiv_rn(rnd64<DT>(acc[i]), sqrtD)) : -INFINITY;
           if (live) sbuf[srow + p] = s;
           rowmax = nanmax(rowmax, s);
         }
@@ -144,9 +144,9 @@ __global__ void __launch_bounds__(256) parent_attn_kernel(
   for (int p0 = 0; p0 < M0; p0 += PA_COLS) {
     for (int e = tid; e < PA_COLS * D; e += blockDim.x) {
       const int j = e / D, d = e % D;
-      pp[j * ld + d] = p0 + j < M0 ? to_f(pagg[((long)g * M0 + p0 + j) * D + d]) : 0.f;
+      pp[j * ld + d] = p0 + j < M0 ? to_f(pagg[((long)gs * M0 + p0 + j) * D + d]) : 0.f;
     }
-    if (tid < PA_COLS) nn[tid] = p0 + tid < M0 ? count_dt<DT>(pcnt[(long)g * M0 + p0 + tid]) : 0.f;
+    if (tid < PA_COLS) nn[tid] = p0 + tid < M0 ? count_dt<DT>(pcnt[(long)gs * M0 + p0 + tid]) : 0.f;
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < PA_COLS / 8; ++i) {
@@ -252,12 +252,13 @@ __global__ void __launch_bounds__(1024) route_kernel(const double* __restrict__ 
                                                      float decay, int phase, int all_passes, PassLayout lay,
                                                      int* __restrict__ sel, int sel_stride,
                                                      int* __restrict__ pass_cnt_out,
-                                                     float* __restrict__ importance_out, RouteExact rx) {
+                                                     float* __restrict__ importance_out, RouteExact rx,
+                                                     int sG) {
   extern __shared__ unsigned long long keys[];  // [npow2]
   __shared__ int cnt[MAX_PASSES];
   __shared__ int namb;
   __shared__ double red[32];
-  const int g = blockIdx.x;
+  const int g = blockIdx.x, gs = g % sG;
   int npow2 = 1;
   while (npow2 < M0) npow2 <<= 1;
   int* amb = (int*)(keys + npow2);                     // [M0] ambiguous columns
@@ -287,7 +288,7 @@ __global__ void __launch_bounds__(1024) route_kernel(const double* __restrict__ 
     return acc;
   };
   auto from_partials = [&](int p, double s) {
-    const float n = count_dt<DT>(pcnt[(long)g * M0 + p]);
+    const float n = count_dt<DT>(pcnt[(long)gs * M0 + p]);
     const double eps = fabs(s) * 3.814697265625e-06;
     const float w = rnd<DT>(__fmul_rn(n, rnd64<DT>(s)));
     const float w_lo = rnd<DT>(__fmul_rn(n, rnd64<DT>(s - eps)));
@@ -310,7 +311,7 @@ __global__ void __launch_bounds__(1024) route_kernel(const double* __restrict__ 
   } else {
   for (int p = threadIdx.x; p < npow2; p += blockDim.x) {
     if (p < M0) {
-      const float n = count_dt<DT>(pcnt[(long)g * M0 + p]);
+      const float n = count_dt<DT>(pcnt[(long)gs * M0 + p]);
       float w;
       if (rx.colpart) {
         from_partials(p, tile_sum(p, 0, nqt));
@@ -349,7 +350,7 @@ __global__ void __launch_bounds__(1024) route_kernel(const double* __restrict__ 
     if (threadIdx.x == 0) {
       double tot = 0.0;
       for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
-      const float w = rnd<DT>(__fmul_rn(count_dt<DT>(pcnt[(long)g * M0 + p]), rnd64<DT>(tot)));
+      const float w = rnd<DT>(__fmul_rn(count_dt<DT>(pcnt[(long)gs * M0 + p]), rnd64<DT>(tot)));
       if (importance_out) importance_out[(long)g * M0 + p] = w;
       keys[p] = route_key(w, p);
     }
@@ -406,7 +407,7 @@ __global__ void __launch_bounds__(256) correct_kernel(
     const typename Storage<DT>::T* __restrict__ cagg, const int* __restrict__ pcnt, const int* __restrict__ ccnt,
     const float* __restrict__ sbuf, const float* __restrict__ m_in, const float* __restrict__ z_in,
     const float* __restrict__ l_in, const float* __restrict__ a_in, const int* __restrict__ sel, int sel_stride,
-    const int* __restrict__ pass_cnt, PassLayout lay, int multipass, float* __restrict__ out, Strides3 os) {
+    const int* __restrict__ pass_cnt, PassLayout lay, int multipass, float* __restrict__ out, Strides3 os, int sG) {
   constexpr int NK = DMAX / 8;
   constexpr int NCH = CJ * CMAX;
   extern __shared__ float smem[];
@@ -421,7 +422,7 @@ __global__ void __launch_bounds__(256) correct_kernel(
   float* cmask = ncc + NCH;               // [NCH] 1 if the logit's child is non-empty
   float* nsel = cmask + NCH;              // [CJ]
   int* psel = (int*)(nsel + CJ);          // [CJ]
-  const int g = blockIdx.y, b = g / H, h = g % H, qt = blockIdx.x;
+  const int g = blockIdx.y, b = g / H, h = g % H, qt = blockIdx.x, gs = g % sG;
   const int tid = threadIdx.x, r = tid >> 3, l8 = tid & 7;
   const int t = qt * PA_ROWS + r;
   const bool live = t < T;
@@ -458,14 +459,14 @@ __global__ void __launch_bounds__(256) correct_kernel(
           const int p = sg[lay.off[pass] + j];
           const int pl = quirk ? j : p;
           cv = to_f(children[(((long)h * M0 + pl) * C + c) * D + d]);
-          ca = to_f(cagg[(((long)g * M0 + p) * C + c) * D + d]);
+          ca = to_f(cagg[(((long)gs * M0 + p) * C + c) * D + d]);
         }
         chv[(jj * CMAX + c) * ld + d] = cv;
         cav[(jj * CMAX + c) * D + d] = ca;
       }
       for (int e = tid; e < CJ * D; e += blockDim.x) {
         const int jj = e / D, d = e % D, j = j0 + jj;
-        pav[jj * D + d] = j < cnt ? to_f(pagg[((long)g * M0 + sg[lay.off[pass] + j]) * D + d]) : 0.f;
+        pav[jj * D + d] = j < cnt ? to_f(pagg[((long)gs * M0 + sg[lay.off[pass] + j]) * D + d]) : 0.f;
       }
       if (tid < CJ * CMAX) {
         const int jj = tid / CMAX, c = tid % CMAX, j = j0 + jj;
@@ -473,8 +474,8 @@ __global__ void __launch_bounds__(256) correct_kernel(
         if (j < cnt && c < C) {
           const int p = sg[lay.off[pass] + j];
           const int pl = quirk ? j : p;
-          n = count_dt<DT>(ccnt[((long)g * M0 + p) * C + c]);
-          mk = ccnt[((long)g * M0 + pl) * C + c] > 0 ? 1.f : 0.f;
+          n = count_dt<DT>(ccnt[((long)gs * M0 + p) * C + c]);
+          mk = ccnt[((long)gs * M0 + pl) * C + c] > 0 ? 1.f : 0.f;
         }
         ncc[tid] = n;
         cmask[tid] = mk;
@@ -483,7 +484,7 @@ __global__ void __launch_bounds__(256) correct_kernel(
         const int j = j0 + tid;
         const int p = j < cnt ? sg[lay.off[pass] + j] : -1;
         psel[tid] = p;
-        nsel[tid] = p >= 0 ? count_dt<DT>(pcnt[(long)g * M0 + p]) : 0.f;
+        nsel[tid] = p >= 0 ? count_dt<DT>(pcnt[(long)gs * M0 + p]) : 0.f;
       }
       __syncthreads();
       // weights: parent terms exp(pi - m) * n (refinement.py:335), child
@@ -624,6 +625,9 @@ size_t forward_workspace_bytes(int dtype, int G, int T, int D, int M0, int C, in
   return carve(nullptr, dtype, G, T, D, M0, C, selection_stride(P, passes, decay), hvaq).bytes;
 }
 
+// Groups of the quantized state (see ForwardArgs::state_groups).
+static int state_groups(const ForwardArgs& a) { return a.state_groups > 0 ? a.state_groups : a.B * a.H; }
+
 template <int DT, int DMAX, int CMAX>
 static void launch_correct(const ForwardArgs& a, const FwdWorkspace& w, float sqrtD, int sel_stride,
                            const PassLayout& lay, cudaStream_t st) {
@@ -641,7 +645,7 @@ static void launch_correct(const ForwardArgs& a, const FwdWorkspace& w, float sq
                                      (const T*)a.pagg, (const T*)a.cagg, a.pcnt, a.ccnt, w.sbuf, w.m, w.z, w.l, w.a,
                                      a.selected_out ? a.selected_out : w.sel, sel_stride,
                                      a.pass_counts_out ? a.pass_counts_out : w.pass_cnt, lay, a.passes > 1 ? 1 : 0,
-                                     a.out, a.os);
+                                     a.out, a.os, state_groups(a));
 }
 
 template <int DT>
@@ -671,9 +675,15 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
   const size_t rt_smem = sizeof(unsigned long long) * npow2 + sizeof(int) * a.M0 + a.M0;
   auto rk = route_kernel<DT>;
   cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rt_smem);
+  const int sG = state_groups(a);
+  bool waited = false;
   auto route = [&](auto... args) {
+    if (!waited && a.min_valid_ready) {  // *min_valid comes from another stream (a cross-rank reduction)
+      cudaStreamWaitEvent(st, static_cast<cudaEvent_t>(a.min_valid_ready), 0);
+      waited = true;
+    }
     AVQ_TIMED("route", st);
-    rk<<<G, 1024, rt_smem, st>>>(args...);
+    rk<<<G, 1024, rt_smem, st>>>(args..., sG);
   };
   const bool hv = a.hvaq != 0;
   float* imp_out = a.importance_out ? a.importance_out : w.imp;
@@ -683,7 +693,7 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
       const int nqt = (a.T + PM_ROWS_PUBLIC - 1) / PM_ROWS_PUBLIC;
       PAArgs pa{a.q, a.qs, a.B, a.H, a.T, a.D, a.M0, sqrtD, a.parents_dt, a.pagg, a.pcnt, 0, hv ? 1 : 0, w.slog,
                 false, w.m, w.l, w.z, w.a, (float*)w.part0, sel, sel_stride, pcnt_out, a.hvaq, a.beta0, a.alpha,
-                w.beta};
+                w.beta, sG};
       // tcgen05 kernel for the plain first pass; the HVAQ variant keeps its
       // logits for the rescaling pass and runs on the mma.sync kernel
       const bool pa_tc = !hv && parent_attn_tc_ok(DT, a.D, a.M0), corr_tc = correct_tc_ok(DT, a.D, a.C);
@@ -707,7 +717,7 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
       }
       CorrArgs ca{a.q, a.qs, a.B, a.H, a.T, a.D, a.M0, a.C, sqrtD, a.parents_dt, a.children_dt, a.pagg, a.cagg,
                   a.pcnt, a.ccnt, w.m, w.l, w.z, hv ? w.beta : nullptr, w.a, sel, sel_stride, pcnt_out, a.passes,
-                  {0, 0, 0, 0, 0, 0, 0, 0}, a.passes > 1 ? 1 : 0, a.out, a.os};
+                  {0, 0, 0, 0, 0, 0, 0, 0}, a.passes > 1 ? 1 : 0, a.out, a.os, sG};
       for (int k = 0; k < a.passes; ++k) ca.pass_off[k] = lay.off[k];
       rc = (corr_tc && w.cdesc) ? launch_correct_tc(ca, w.exptab, w.cdesc, st) : AVQ_ERR_UNSUPPORTED;
       if (rc == AVQ_ERR_UNSUPPORTED) rc = launch_correct_mma<DT>(ca, st);
@@ -725,7 +735,7 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pa_smem);                              \
     k<<<dim3(nqt, G), 256, pa_smem, st>>>((const T*)a.q, a.qs, a.H, a.T, a.D, a.M0, sqrtD, (const T*)a.parents_dt,   \
                                           (const T*)a.pagg, a.pcnt, MODE, w.sbuf, w.m, w.l, w.z, w.a, PART, sel,     \
-                                          sel_stride, pcnt_out, a.hvaq, a.beta0, a.alpha, w.beta);                   \
+                                          sel_stride, pcnt_out, a.hvaq, a.beta0, a.alpha, w.beta, sG);               \
   } while (0)
 #define AVQ_PA_D(MODE, PART)                                   \
   do {                                                         \

@@ -40,7 +40,7 @@ __global__ void __launch_bounds__(128, 4) parent_attn_mma_kernel(
     float* __restrict__ m_io, float* __restrict__ l_out, float* __restrict__ z_io,
     typename Storage<DT>::T* __restrict__ a_out, float* __restrict__ colpart, const int* __restrict__ sel0,
     int sel_stride, const int* __restrict__ pass_cnt, int hvaq, float beta0, float alpha,
-    float* __restrict__ beta_out) {
+    float* __restrict__ beta_out, int sG) {
   using T = typename Storage<DT>::T;
   constexpr int LDS = D + 8, KS = D / 16, CPR = D / 8, NT = D / 8;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -49,7 +49,7 @@ __global__ void __launch_bounds__(128, 4) parent_attn_mma_kernel(
   float* sn = (float*)(sb + 2 * PM_CH * LDS);  // [2][PM_CH] counts
   float* srow = sn + 2 * PM_CH;                // [64][4] per-row zc, 1/zc, max, live
   float* scomb = srow + 4 * PM_ROWS;           // [4][64] column partials of the 4 warps
-  const int g = blockIdx.y, b = g / H, h = g % H, qt = blockIdx.x, t0 = qt * PM_ROWS, nqt = gridDim.x;
+  const int g = blockIdx.y, b = g / H, h = g % H, qt = blockIdx.x, t0 = qt * PM_ROWS, nqt = gridDim.x, gs = g % sG;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int LDL = exp_slice_pitch(M0);
   const float inv_sqrtD = 1.f / sqrtD;
@@ -64,7 +64,7 @@ __global__ void __launch_bounds__(128, 4) parent_attn_mma_kernel(
   }
   cp_async_commit();
   const T* pb = parents + (long)h * M0 * D;
-  const T* vb = pagg + (long)g * M0 * D;
+  const T* vb = pagg + (long)gs * M0 * D;
   auto load_rows = [&](const T* src, int buf, int p0, bool dtype_counts) {
     for (int i = tid; i < PM_CH * CPR; i += blockDim.x) {
       const int r = i / CPR, c = i % CPR, p = p0 + r;
@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(128, 4) parent_attn_mma_kernel(
     }
     if (tid < PM_CH) {
       const int p = p0 + tid;
-      const int n = p < M0 ? pcnt[(long)g * M0 + p] : 0;
+      const int n = p < M0 ? pcnt[(long)gs * M0 + p] : 0;
       sn[buf * PM_CH + tid] = dtype_counts ? count_dt<DT>(n) : (float)n;
     }
   };
@@ -399,7 +399,7 @@ __global__ void __launch_bounds__(128) correct_mma_kernel(
     const float* __restrict__ l_in, const float* __restrict__ z_in, const float* __restrict__ beta_in,
     const typename Storage<DT>::T* __restrict__ a_in, const int* __restrict__ sel, int sel_stride,
     const int* __restrict__ pass_cnt, int npass, PassOffsets po, int multipass, float* __restrict__ out,
-    Strides3 os) {
+    Strides3 os, int sG) {
   using T = typename Storage<DT>::T;
   constexpr bool TC = DT == DT_BF16;  // tensor-core value sums
   constexpr int LDS = D + 8, KS = D / 16, CPR = D / 8, NT = D / 8, NCH = CM_J * C;
@@ -413,7 +413,7 @@ __global__ void __launch_bounds__(128) correct_mma_kernel(
   float* snc = snp + CM_J;                 // [NCH] child counts (dtype)
   float* smk = snc + NCH;                  // [NCH] 1: logit child non-empty
   float* sw = smk + NCH;                   // fp16 path: [64][16] weights of one group
-  const int g = blockIdx.y, b = g / H, h = g % H, t0 = blockIdx.x * CM_ROWS;
+  const int g = blockIdx.y, b = g / H, h = g % H, t0 = blockIdx.x * CM_ROWS, gs = g % sG;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r0 = warp * 16 + (lane >> 2), r1 = r0 + 8, cq = (lane & 3) * 2;
   const bool live0 = t0 + r0 < Tq, live1 = t0 + r1 < Tq;
@@ -450,8 +450,8 @@ __global__ void __launch_bounds__(128) correct_mma_kernel(
   const int* sg = sel + (long)g * sel_stride;
   const T* pbase = parents + (long)h * M0 * D;
   const T* cbase = children + (long)h * M0 * C * D;
-  const T* pvb = pagg + (long)g * M0 * D;
-  const T* cvb = cagg + (long)g * M0 * C * D;
+  const T* pvb = pagg + (long)gs * M0 * D;
+  const T* cvb = cagg + (long)gs * M0 * C * D;
 
   // 16 rows x 16 slots of logits -> weights w (two m16n8 tiles), then
   // oa += sign * w @ V[16 slots] (V rows staged in sv)
@@ -524,7 +524,7 @@ __global__ void __launch_bounds__(128) correct_mma_kernel(
       cp_async_commit();
       if (tid < CM_J) {
         const int j = j0 + tid;
-        snp[tid] = j < cnt ? count_dt<DT>(pcnt[(long)g * M0 + sg[po.off[pass] + j]]) : -1.f;
+        snp[tid] = j < cnt ? count_dt<DT>(pcnt[(long)gs * M0 + sg[po.off[pass] + j]]) : -1.f;
       }
       for (int jc = tid; jc < NCH; jc += blockDim.x) {
         const int jj = jc / C, ch = jc % C, j = j0 + jj;
@@ -532,8 +532,8 @@ __global__ void __launch_bounds__(128) correct_mma_kernel(
         if (j < cnt) {
           const int p = sg[po.off[pass] + j];
           const int pl = quirk ? j : p;
-          n = count_dt<DT>(ccnt[((long)g * M0 + p) * C + ch]);
-          mk = ccnt[((long)g * M0 + pl) * C + ch] > 0 ? 1.f : 0.f;
+          n = count_dt<DT>(ccnt[((long)gs * M0 + p) * C + ch]);
+          mk = ccnt[((long)gs * M0 + pl) * C + ch] > 0 ? 1.f : 0.f;
         }
         snc[jc] = n;
         smk[jc] = mk;
@@ -645,7 +645,7 @@ int launch_correct_mma(const CorrArgs& a, cudaStream_t st) {
     kfn<<<dim3(nqt, G), 128, smem, st>>>((const T*)a.q, a.qs, a.H, a.T, a.M0, a.sqrtD, (const T*)a.parents,
                                           (const T*)a.children, (const T*)a.pagg, (const T*)a.cagg, a.pcnt, a.ccnt,
                                           a.m, a.l, a.z, a.beta, (const T*)a.a, a.sel, a.sel_stride, a.pass_cnt,
-                                          a.npass, po, a.multipass, a.out, a.os);
+                                          a.npass, po, a.multipass, a.out, a.os, a.sG > 0 ? a.sG : G);
   };
   if (a.C == 4) {
     if (a.D == 64) go(correct_mma_kernel<DT, 64, 4>); else go(correct_mma_kernel<DT, 128, 4>);
@@ -690,7 +690,7 @@ int launch_parent_attn_mma(const PAArgs& a, cudaStream_t st) {
     kfn<<<dim3(nqt, G), 128, smem, st>>>((const T*)a.q, a.qs, a.H, a.T, a.M0, a.sqrtD, (const T*)a.parents,
                                           (const T*)a.pagg, a.pcnt, a.mode, a.keep_logits, (T*)a.sglobal, a.m, a.l,
                                           a.z, (T*)a.a, a.colpart, a.sel0, a.sel_stride, a.pass_cnt, a.hvaq, a.beta0,
-                                          a.alpha, a.beta);
+                                          a.alpha, a.beta, a.sG > 0 ? a.sG : G);
   };
   if (a.D == 64) go(parent_attn_mma_kernel<DT, 64>);
   else go(parent_attn_mma_kernel<DT, 128>);

@@ -1,5 +1,6 @@
 // extern "C" entry points (include/avqa_b200.h): argument checks, dtype
 // dispatch and error reporting around the kernel launchers.
+#include <climits>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -7,6 +8,8 @@
 #include <mutex>
 #include <string>
 #include <vector>
+
+#include <cuda.h>
 
 #include "../../include/avqa_b200.h"
 #include "avq_kernels.cuh"
@@ -74,6 +77,10 @@ namespace {
 
 bool bad_dtype(int dt) { return dt < 0 || dt > 2; }
 
+// B * H (the number of (b,h) groups) must stay an int: every kernel indexes
+// groups with int arithmetic.  Checked in 64 bits before any size is derived.
+bool too_many_groups(int B, int H) { return (long long)B * (long long)H > (long long)INT_MAX; }
+
 }  // namespace
 
 extern "C" {
@@ -105,6 +112,7 @@ int avq_prepare_codebook(int dtype, const float* parents32, const float* childre
 }
 
 size_t avq_quantize_workspace_size(int B, int H, int S, int M0) {
+  if (B < 0 || H <= 0 || S < 0 || M0 <= 0 || too_many_groups(B, H)) return 0;
   return avq::quantize_workspace_bytes(B * H, S, M0);
 }
 
@@ -120,6 +128,7 @@ int avq_quantize(int dtype, const void* keys, const long long* key_strides, cons
     return fail(AVQ_ERR_ARG, "avq_quantize: null pointer");
   if (S > 0 && (!keys || !values || !passign || !cassign)) return fail(AVQ_ERR_ARG, "avq_quantize: null key pointer");
   if ((pacc == nullptr) != (cacc == nullptr)) return fail(AVQ_ERR_ARG, "avq_quantize: pacc and cacc go together");
+  if (too_many_groups(B, H)) return fail(AVQ_ERR_ARG, "avq_quantize: B*H = %lld exceeds INT_MAX", (long long)B * H);
   const size_t need = avq::quantize_workspace_bytes(B * H, S, M0);
   if (workspace_bytes < need || (need && !workspace))
     return fail(AVQ_ERR_WORKSPACE, "avq_quantize: workspace %zu < %zu bytes", workspace_bytes, need);
@@ -144,17 +153,20 @@ int avq_selection_stride(int P, int passes, float pass_decay) {
 
 size_t avq_forward_workspace_size(int dtype, int B, int H, int T, int D, int M0, int C, int P, int passes,
                                   float pass_decay, int hvaq) {
-  if (bad_dtype(dtype) || P <= 0 || passes <= 0 || passes > 8) return 0;
+  if (bad_dtype(dtype) || P <= 0 || passes <= 0 || passes > 8 || B < 0 || H <= 0 || too_many_groups(B, H)) return 0;
   return avq::forward_workspace_bytes(dtype, B * H, T, D, M0, C, P, passes, pass_decay, hvaq);
 }
 
 int avq_forward(int dtype, const void* q, const long long* q_strides, int B, int H, int T, int D, int M0, int C,
                 const void* parents_dt, const void* children_dt, const void* pagg, const void* cagg, const int* pcnt,
-                const int* ccnt, const int* min_valid, int P, int passes, float pass_decay, int hvaq, float beta0,
+                const int* ccnt, int state_batch, const int* min_valid, void* min_valid_ready, int P, int passes,
+                float pass_decay, int hvaq, float beta0,
                 float alpha, float* out, const long long* out_strides, float* importance_out, int* selected_out,
                 int* pass_counts_out, void* workspace, size_t workspace_bytes, void* stream) {
   if (bad_dtype(dtype)) return fail(AVQ_ERR_ARG, "avq_forward: bad dtype %d", dtype);
   if (B < 0 || H <= 0 || T < 0 || D <= 0 || M0 <= 0 || C <= 0) return fail(AVQ_ERR_ARG, "avq_forward: bad sizes");
+  if (state_batch != B && state_batch != 1)
+    return fail(AVQ_ERR_ARG, "avq_forward: state_batch must be B (%d) or 1, got %d", B, state_batch);
   if (P <= 0) return fail(AVQ_ERR_ARG, "avq_forward: budget must be > 0, got %d", P);
   if (P > M0) return fail(AVQ_ERR_ARG, "avq_forward: budget (%d) exceeds number of parents (%d)", P, M0);
   if (passes <= 0 || passes > 8) return fail(AVQ_ERR_ARG, "avq_forward: passes must be in [1, 8], got %d", passes);
@@ -164,13 +176,14 @@ int avq_forward(int dtype, const void* q, const long long* q_strides, int B, int
   if (hvaq && !(beta0 > 0.f)) return fail(AVQ_ERR_ARG, "avq_forward: beta_init must be > 0");
   if (!q_strides || !out_strides || !parents_dt || !children_dt || !pagg || !cagg || !pcnt || !ccnt || !min_valid)
     return fail(AVQ_ERR_ARG, "avq_forward: null pointer");
-  if (B * T > 0 && (!q || !out)) return fail(AVQ_ERR_ARG, "avq_forward: null q/out");
+  if (too_many_groups(B, H)) return fail(AVQ_ERR_ARG, "avq_forward: B*H = %lld exceeds INT_MAX", (long long)B * H);
+  if ((long long)B * T > 0 && (!q || !out)) return fail(AVQ_ERR_ARG, "avq_forward: null q/out");
   const size_t need = avq::forward_workspace_bytes(dtype, B * H, T, D, M0, C, P, passes, pass_decay, hvaq);
   if (workspace_bytes < need || !workspace)
     return fail(AVQ_ERR_WORKSPACE, "avq_forward: workspace %zu < %zu bytes", workspace_bytes, need);
   avq::ForwardArgs a{q, st3(q_strides), B, H, T, D, M0, C, parents_dt, children_dt, pagg, cagg, pcnt, ccnt, min_valid,
                      P, passes, pass_decay, hvaq, beta0, alpha, out, st3(out_strides), importance_out, selected_out,
-                     pass_counts_out, workspace, workspace_bytes};
+                     pass_counts_out, workspace, workspace_bytes, state_batch * H, min_valid_ready};
   cudaStream_t st = (cudaStream_t)stream;
   int rc;
   switch (dtype) {
@@ -193,6 +206,7 @@ int avq_append(int dtype, const void* k, const long long* k_strides, const void*
     return fail(AVQ_ERR_ARG, "avq_append: null pointer");
   if ((kpage == nullptr) != (vpage == nullptr) || (kpage && !page_strides))
     return fail(AVQ_ERR_ARG, "avq_append: kpage, vpage and page_strides go together");
+  if (too_many_groups(B, H)) return fail(AVQ_ERR_ARG, "avq_append: B*H = %lld exceeds INT_MAX", (long long)B * H);
   avq::AppendArgs a{k, st3(k_strides), v, st3(v_strides), B, H, Tn, D, M0, C, parents_dt, p_sq, children_dt, c_sq,
                     pacc, cacc, pagg, cagg, pcnt, ccnt, nvalid, kpage, vpage,
                     kpage ? st3(page_strides) : avq::Strides3{0, 0, 0}, slot0};
@@ -291,32 +305,71 @@ namespace {
 
 __device__ __align__(256) unsigned char g_quantize_scratch[AVQ_QUANTIZE_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kNoallocMaxDevices = 64;
+// The array's device address belongs to the CUDA context that loaded the
+// library's device code: one address per context, so the cache is keyed by the
+// context current at the call (the device's primary context for runtime-API
+// hosts; the host's own context for a driver-API host).
+struct NoallocEntry {
+  void* ctx;
+  void* scratch;
+};
+constexpr int kNoallocMaxContexts = 64;
 std::mutex g_noalloc_mu;
-void* g_noalloc_scratch[kNoallocMaxDevices] = {};
+NoallocEntry g_noalloc[kNoallocMaxContexts] = {};
+int g_noalloc_n = 0;
 
-// Device address of this device's scratch array; looked up once per device.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// The current context, through the runtime's driver entry point (the library
+// links only the runtime); *ctx is null when none is current yet.
+int current_context(void** ctx) {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  if (!fn) return fail(AVQ_ERR_CUDA, "avq_quantize_noalloc: cuCtxGetCurrent is unavailable");
+  CUcontext c = nullptr;
+  if (fn(&c) != CUDA_SUCCESS) return fail(AVQ_ERR_CUDA, "avq_quantize_noalloc: cuCtxGetCurrent failed");
+  *ctx = c;
+  return AVQ_OK;
+}
+
+// Device address of the scratch array in the current context; looked up once
+// per context, with that context current.
 int noalloc_scratch(void** out) {
   int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
+  cudaError_t e = cudaGetDevice(&dev);  // also makes the device's primary context current if none is
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(AVQ_ERR_CUDA, "avq_quantize_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
   }
-  if (dev < 0 || dev >= kNoallocMaxDevices)
-    return fail(AVQ_ERR_ARG, "avq_quantize_noalloc: device %d beyond the %d supported", dev, kNoallocMaxDevices);
+  void* ctx = nullptr;
+  int rc = current_context(&ctx);
+  if (rc != AVQ_OK) return rc;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_scratch[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_quantize_scratch);
-    if (e != cudaSuccess || !p) {
-      cudaGetLastError();
-      return fail(AVQ_ERR_CUDA, "avq_quantize_noalloc: cudaGetSymbolAddress on device %d: %s", dev,
-                  cudaGetErrorString(e));
-    }
-    g_noalloc_scratch[dev] = p;
+  if (ctx) {
+    for (int i = 0; i < g_noalloc_n; ++i)
+      if (g_noalloc[i].ctx == ctx) {
+        *out = g_noalloc[i].scratch;
+        return AVQ_OK;
+      }
   }
-  *out = g_noalloc_scratch[dev];
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_quantize_scratch);
+  if (e != cudaSuccess || !p) {
+    cudaGetLastError();
+    return fail(AVQ_ERR_CUDA, "avq_quantize_noalloc: cudaGetSymbolAddress on device %d: %s", dev,
+                cudaGetErrorString(e));
+  }
+  if (!ctx) {  // the lookup above created the primary context: key by it from now on
+    if ((rc = current_context(&ctx)) != AVQ_OK) return rc;
+  }
+  if (ctx && g_noalloc_n < kNoallocMaxContexts) g_noalloc[g_noalloc_n++] = {ctx, p};
+  *out = p;
   return AVQ_OK;
 }
 
@@ -330,6 +383,8 @@ extern "C" int avq_quantize_noalloc(int dtype, const void* keys, const long long
                                     void* stream) {
   // The size check comes first so that an oversized request touches no device.
   if (B < 0 || H <= 0 || S < 0 || M0 <= 0) return fail(AVQ_ERR_ARG, "avq_quantize_noalloc: bad sizes");
+  if (too_many_groups(B, H))
+    return fail(AVQ_ERR_ARG, "avq_quantize_noalloc: B*H = %lld exceeds INT_MAX", (long long)B * H);
   const size_t need = avq::quantize_workspace_bytes(B * H, S, M0);
   if (need > AVQ_QUANTIZE_NOALLOC_SCRATCH_BYTES)
     return fail(AVQ_ERR_WORKSPACE,

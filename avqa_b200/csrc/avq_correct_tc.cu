@@ -124,9 +124,9 @@ template <int C>
 __global__ void corr_desc_kernel(const int* __restrict__ sel, int sel_stride, const int* __restrict__ pass_cnt,
                                  int npass, PassOffsets po, int multipass, int H, int M0,
                                  const int* __restrict__ pcnt, const int* __restrict__ ccnt, int maxgroups,
-                                 SlotDesc* __restrict__ desc) {
+                                 SlotDesc* __restrict__ desc, int sG) {
   constexpr int J = NS / (1 + C), NREAL = J * (1 + C);
-  const int g = blockIdx.x, h = g % H;
+  const int g = blockIdx.x, h = g % H, gs = g % sG;
   const int* sg = sel + (long)g * sel_stride;
   int kg = 0;
   for (int ps = 0; ps < npass; ++ps) {
@@ -141,8 +141,8 @@ __global__ void corr_desc_kernel(const int* __restrict__ sel, int sel_stride, co
           if (j < cnt) {
             const int p = sg[po.off[ps] + j];
             d.lrow = h * M0 + p;
-            d.vrow = g * M0 + p;
-            d.n = count_dt<DT_BF16>(pcnt[(long)g * M0 + p]);
+            d.vrow = gs * M0 + p;
+            d.n = count_dt<DT_BF16>(pcnt[(long)gs * M0 + p]);
             d.mk = d.n > 0.f ? 1.f : 0.f;
           }
         } else if (r < NREAL) {
@@ -151,9 +151,9 @@ __global__ void corr_desc_kernel(const int* __restrict__ sel, int sel_stride, co
             const int p = sg[po.off[ps] + j];
             const int pl = quirk ? j : p;
             d.lrow = -2 - ((h * M0 + pl) * C + c);
-            d.vrow = -2 - ((g * M0 + p) * C + c);
-            d.n = count_dt<DT_BF16>(ccnt[((long)g * M0 + p) * C + c]);
-            d.mk = ccnt[((long)g * M0 + pl) * C + c] > 0 ? 1.f : 0.f;
+            d.vrow = -2 - ((gs * M0 + p) * C + c);
+            d.n = count_dt<DT_BF16>(ccnt[((long)gs * M0 + p) * C + c]);
+            d.mk = ccnt[((long)gs * M0 + pl) * C + c] > 0 ? 1.f : 0.f;
           }
         }
         desc[((long)g * maxgroups + kg) * NS + r] = d;
@@ -608,7 +608,7 @@ int launch_correct_tc(const CorrArgs& a, const void* exptab, void* desc, cudaStr
   auto go = [&](auto dfn, auto kfn) {
     AVQ_TIMED("correct_tc", st);
     dfn<<<G, 64, 0, st>>>(a.sel, a.sel_stride, a.pass_cnt, a.npass, po, a.multipass, a.H, a.M0, a.pcnt, a.ccnt,
-                          maxgroups, sd);
+                          maxgroups, sd, a.sG > 0 ? a.sG : G);
     cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     kfn<<<dim3((a.T + CR - 1) / CR, G), CTHREADS2, smem, st>>>(
         tq, qpos, a.H, a.T, a.sqrtD, static_cast<const __nv_bfloat16*>(a.parents),

@@ -67,6 +67,11 @@ struct ForwardArgs {
   int* pass_counts_out;   // optional [passes]
   void* workspace;
   size_t workspace_bytes;
+  // Groups (b,h) of the quantized state: B*H, or H when one state (batch 1)
+  // serves every query batch -- query chunks over one cached key set.  The
+  // state of query group g is g % state_groups.  0 means B*H.
+  int state_groups = 0;
+  void* min_valid_ready = nullptr;  // optional cudaEvent_t awaited before routing
 };
 
 struct AppendArgs {
@@ -114,6 +119,7 @@ struct PAArgs {
   int hvaq;
   float beta0, alpha;
   float* beta;         // [G,T]
+  int sG = 0;          // state groups: the state of query group g is g % sG
 };
 
 // Importance from fp32 per-tile column partials, with the exact fallback
@@ -152,6 +158,7 @@ struct CorrArgs {
   int multipass;
   float* out;
   Strides3 os;
+  int sG = 0;  // state groups: the state of query group g is g % sG
 };
 
 template <int DT>

@@ -60,7 +60,7 @@ constexpr int TC_TMEM_COLS = 256;
 constexpr uint32_t EXP_BASE = 0x3AFF;  // bf16 bits of the largest |d| whose exp rounds to 1
 constexpr int EXP_N = 2051;            // entries 0..2049: |d| bits EXP_BASE + i; 2050: |d| > 128, inf, NaN
 constexpr int EXP_WORDS = (EXP_N + 1) / 2;
-constexpr int TC_MAX_M0 = 2048;
+constexpr int TC_MAX_M0 = 8192;  // above 2048 the shared memory allows one CTA per SM
 
 // Barrier slots: the tile ring's full and empty barriers, the logit slots'
 // full (MMA done) and consumed (row threads done) barriers.
@@ -189,13 +189,13 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     const __grid_constant__ CUtensorMap tm_v, int4 qpos, int H, int Tq, int M0, float sqrtD,
     const int* __restrict__ pcnt, const uint16_t* __restrict__ exptab_g, typename Storage<DT>::T* __restrict__ scratch,
     float* __restrict__ m_out, float* __restrict__ l_out, float* __restrict__ z_out,
-    typename Storage<DT>::T* __restrict__ a_out, float* __restrict__ colpart) {
+    typename Storage<DT>::T* __restrict__ a_out, float* __restrict__ colpart, int sG) {
   using T = typename Storage<DT>::T;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_addr(smem_raw);
   unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   const TcLayout L = tc_layout(D, M0);
-  const int g = blockIdx.y, b = g / H, h = g % H, qt = blockIdx.x, t0 = qt * TR;
+  const int g = blockIdx.y, b = g / H, h = g % H, qt = blockIdx.x, t0 = qt * TR, gs = g % sG;
   const int nch = (M0 + TCH - 1) / TCH, nv = 2 * nch;
   const int ntiles = (Tq + 63) / 64, LDL = exp_slice_pitch(M0);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     const int c = i < nch ? i : (i - nch) >> 1;
     for (int kb = 0; kb < D / 64; ++kb) {
       if (par) tc::tma_load_3d(buf + kb * TCH * 128, &tm_p, kb * 64, c * TCH, h, &bars[B_RFULL + k]);
-      else tc::tma_load_3d(buf + kb * TCH * 128, &tm_v, kb * 64, c * TCH, g, &bars[B_RFULL + k]);
+      else tc::tma_load_3d(buf + kb * TCH * 128, &tm_v, kb * 64, c * TCH, gs, &bars[B_RFULL + k]);
     }
   };
 
@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     for (int i = tid; i < EXP_WORDS; i += TROW) dst[i] = src[i];
     for (int j = tid; j < nch * 32; j += TROW) {
       const int p = 2 * j;
-      const int c0 = p < M0 ? pcnt[(long)g * M0 + p] : 0, c1 = p + 1 < M0 ? pcnt[(long)g * M0 + p + 1] : 0;
+      const int c0 = p < M0 ? pcnt[(long)gs * M0 + p] : 0, c1 = p + 1 < M0 ? pcnt[(long)gs * M0 + p + 1] : 0;
       pm2[j] = (c0 > 0 ? 0xFFFFu : 0u) | (c1 > 0 ? 0xFFFF0000u : 0u);
       n2[j] = pack2<DT>(count_dt<DT>(c0), count_dt<DT>(c1));
     }
@@ -477,7 +477,10 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
           for (int j = 0; j < w; ++j) zs[j] += zs[j + w];
         zh[hh] = zs[0];
         tc::tmem_st8(col + 8 * hh, e2);
-        if (live && 2 * pw < M0) {  // M0 is a multiple of 8: a block of 16 is all in or all out
+        // a block of 16 starting below M0 is stored whole: when M0 % 16 == 8 the
+        // last block spills 8 columns past M0, into the row pitch's padding
+        // (exp_slice_pitch(M0) >= round_up(M0, 16), asserted on the host)
+        if (live && 2 * pw < M0) {
           // one whole 32-byte sector per store when the slices are 32-byte
           // aligned (the pitch keeps every row so), else two 16-byte halves
           T* dst = srow_g + 2 * pw;
@@ -700,13 +703,14 @@ void launch_exp_table(void* tab, cudaStream_t st) { exp_table_kernel<<<1, 256, 0
 template <int DT>
 int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st) {
   using T = typename Storage<DT>::T;
-  const int G = a.B * a.H, D = a.D, M0 = a.M0;
-  // Q [B,H,T,D] strided, P [H, M0, D], V [G, M0, D]; 128-byte swizzled boxes
+  const int G = a.B * a.H, D = a.D, M0 = a.M0, sG = a.sG > 0 ? a.sG : G;
+  // Q [B,H,T,D] strided, P [H, M0, D], V [sG, M0, D]; 128-byte swizzled boxes
   CUtensorMap tq, tp, tv;
   int4 qpos;
   if (!tc::map_rows4(&tq, DT, a.q, a.qs, a.B, a.H, a.T, D, TR, &qpos) ||
-      !tc::map_rows3(&tp, DT, a.parents, a.H, M0, D, TCH) || !tc::map_rows3(&tv, DT, a.pagg, G, M0, D, TCH))
+      !tc::map_rows3(&tp, DT, a.parents, a.H, M0, D, TCH) || !tc::map_rows3(&tv, DT, a.pagg, sG, M0, D, TCH))
     return AVQ_ERR_UNSUPPORTED;
+  if (exp_slice_pitch(M0) < ((M0 + 15) & ~15)) return AVQ_ERR_UNSUPPORTED;  // whole 16-column stores
   const TcLayout L = tc_layout(D, M0);
   // at least 80 KB so that no more than two CTAs (2 x 256 TMEM columns) share an SM
   const size_t smem = std::max<size_t>((size_t)L.total + 1024, 80 * 1024);
@@ -715,7 +719,7 @@ int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st) {
     cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     kfn<<<dim3((a.T + TR - 1) / TR, G), TTHREADS, smem, st>>>(
         tq, tp, tv, qpos, a.H, a.T, M0, a.sqrtD, a.pcnt, static_cast<const uint16_t*>(exptab),
-        static_cast<T*>(a.sglobal), a.m, a.l, a.z, static_cast<T*>(a.a), a.colpart);
+        static_cast<T*>(a.sglobal), a.m, a.l, a.z, static_cast<T*>(a.a), a.colpart, sG);
   };
   if (D == 64) go(parent_attn_tc_kernel<DT, 64>);
   else go(parent_attn_tc_kernel<DT, 128>);

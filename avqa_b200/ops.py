@@ -169,8 +169,16 @@ def pass_caps(P: int, passes: int, decay: float) -> list[int]:
 
 def forward(q: torch.Tensor, cb: PreparedCodebook, st: QuantState, P: int, passes: int = 1, pass_decay: float = 1.0,
             hvaq: int = 0, beta0: float = 0.0, alpha: float = 1.0, out: torch.Tensor | None = None,
-            min_valid: torch.Tensor | None = None, diagnostics: bool = False):
+            min_valid: torch.Tensor | None = None, diagnostics: bool = False,
+            min_valid_ready: torch.cuda.Event | None = None):
     """AVQ attention of ``q`` ``[B, H, T, D]`` over ``st``.
+
+    ``st`` holds either B batches of keys, or one batch that every query
+    batch attends to (query chunks of one sequence over keys quantized once;
+    each batch entry is routed on its own, exactly as separate calls over the
+    same keys).  ``min_valid_ready``: an event recorded after ``min_valid``
+    was produced on another stream; the library waits on it only right
+    before routing.
 
     Returns ``out`` as a ``[B, H, T, D]`` fp32 view (module layout when
     ``out`` is given as a ``[B, T, H, D]``-strided tensor) and optional
@@ -181,6 +189,9 @@ def forward(q: torch.Tensor, cb: PreparedCodebook, st: QuantState, P: int, passe
     B, H, T, D = q.shape
     _, M0, C, _ = cb.dims
     dev = q.device
+    if st.B != B and st.B != 1:
+        raise BackendError("quantized state batch must equal the query batch or be 1",
+                           {"state_batch": st.B, "query_batch": B})
     if out is None:
         out = torch.empty(B, T, H, D, dtype=torch.float32, device=dev).permute(0, 2, 1, 3)
     ws_bytes = lib.avq_forward_workspace_size(_lib.dtype_code(q.dtype), B, H, T, D, M0, C, P, passes, pass_decay, hvaq)
@@ -196,9 +207,10 @@ def forward(q: torch.Tensor, cb: PreparedCodebook, st: QuantState, P: int, passe
     mv = st.gmin if min_valid is None else min_valid
     rc = lib.avq_forward(_lib.dtype_code(q.dtype), q.data_ptr(), _lib.strides3(q), B, H, T, D, M0, C,
                          cb.parents.data_ptr(), cb.children.data_ptr(), st.pagg.data_ptr(), st.cagg.data_ptr(),
-                         st.pcnt.data_ptr(), st.ccnt.data_ptr(), mv.data_ptr(), P, passes, pass_decay, hvaq, beta0,
-                         alpha, out.data_ptr(), _lib.strides3(out), _lib.ptr(imp), _lib.ptr(sel), _lib.ptr(pc),
-                         ws.data_ptr(), ws_bytes, _lib.stream_of(dev))
+                         st.pcnt.data_ptr(), st.ccnt.data_ptr(), st.B, mv.data_ptr(),
+                         None if min_valid_ready is None else min_valid_ready.cuda_event, P, passes, pass_decay,
+                         hvaq, beta0, alpha, out.data_ptr(), _lib.strides3(out), _lib.ptr(imp), _lib.ptr(sel),
+                         _lib.ptr(pc), ws.data_ptr(), ws_bytes, _lib.stream_of(dev))
     _lib.check(rc, "avq_forward")
     return out, diag
 

@@ -35,8 +35,11 @@ class ShardCompute(Protocol):
     def quantize(self, k: torch.Tensor, v: torch.Tensor):
         """Quantize ``[B,h,S,D]`` keys/values; returns (state, local min-valid int32 tensor [1])."""
 
-    def forward(self, q: torch.Tensor, state, min_valid: torch.Tensor) -> torch.Tensor:
-        """AVQ forward of ``[B,h,T,D]`` queries; returns ``[B,h,T,D]`` fp32."""
+    def forward(self, q: torch.Tensor, state, min_valid: torch.Tensor, chunk_size: int = 0,
+                ready: torch.cuda.Event | None = None) -> torch.Tensor:
+        """AVQ forward of ``[B,h,T,D]`` queries (in chunks of ``chunk_size``
+        queries when > 0, each routed on its own); returns ``[B,h,T,D]`` fp32.
+        ``ready``: event after which ``min_valid`` holds the global floor."""
 
 
 class CudaShardCompute:
@@ -49,28 +52,64 @@ class CudaShardCompute:
         self.config = config
         self.cb = ops.prepare_codebook(parents, children, dtype, device)
 
-    def quantize(self, k, v):
-        st = self.ops.quantize(k, v, self.cb)
+    def quantize(self, k, v, kv_cache=None):
+        """Quantize the keys -- or, with a KV cache of this rank's heads,
+        extend the cache's quantized state by the new tokens (decode)."""
+        if kv_cache is None:
+            st = self.ops.quantize(k, v, self.cb)
+        else:
+            from avqa_b200.attention_module import resolve_quantization
+            st = resolve_quantization(self, k, v, self.cb, kv_cache)
         return st, st.gmin
 
-    def forward(self, q, state, min_valid):
+    def forward(self, q, state, min_valid, chunk_size=0, ready=None):
         import math
-        from avqa_b200.attention_module import hvaq_mode
+        from avqa_b200.attention_module import hvaq_mode, query_chunks
         c = self.config
-        D = q.shape[-1]
+        B, h, T, D = q.shape
         hv = hvaq_mode(c)
         beta0 = c.hopfield.beta_init if c.hopfield.beta_init > 0 else 1.0 / math.sqrt(D)
-        out, _ = self.ops.forward(q, self.cb, state, min(c.routing.refinement_budget, self.cb.dims[1]),
-                                  c.refinement.passes, c.refinement.pass_decay, hv, beta0, c.hopfield.alpha,
-                                  min_valid=min_valid)
-        return out
+        out = torch.empty(B, T, h * D, dtype=torch.float32, device=q.device)
+        args = (min(c.routing.refinement_budget, self.cb.dims[1]), c.refinement.passes, c.refinement.pass_decay, hv,
+                beta0, c.hopfield.alpha)
+        for q_part, o_part in query_chunks(q, out, h, chunk_size):
+            self.ops.forward(q_part, self.cb, state, *args, out=o_part, min_valid=min_valid, min_valid_ready=ready)
+            ready = None
+        return out.view(B, T, h, D).transpose(1, 2)
+
+
+_SIDE: dict = {}
+
+
+def reduce_min(mv: torch.Tensor, group=None) -> tuple[torch.Tensor, torch.cuda.Event | None]:
+    """All-reduce(MIN) of the budget floor over ``group``.  For a CUDA tensor
+    it runs on a side stream and returns an event marking its completion (the
+    forward waits on it only before routing); on the CPU it is synchronous."""
+    g = mv.clone()
+    if not g.is_cuda:
+        dist.all_reduce(g, op=dist.ReduceOp.MIN, group=group)
+        return g, None
+    main = torch.cuda.current_stream(g.device)
+    side = _SIDE.get(g.device)
+    if side is None:
+        side = _SIDE[g.device] = torch.cuda.Stream(g.device)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        dist.all_reduce(g, op=dist.ReduceOp.MIN, group=group)
+        ready = torch.cuda.Event()
+        ready.record(side)
+    g.record_stream(side)
+    return g, ready
 
 
 class ShardedAVQAttention:
     """AVQ attention over the heads of a process group (no projections).
 
-    ``forward(query, key, value)`` takes the full ``[B, T, E]`` tensors on
-    every rank and returns the full ``[B, T, E]`` fp32 output on every rank.
+    ``forward(query, key, value, chunk_size=0)`` takes the full ``[B, T, E]``
+    tensors on every rank and returns the full ``[B, T, E]`` fp32 output on
+    every rank.  Rank r quantizes the keys of its heads once, attends to them
+    (chunk by chunk when ``chunk_size`` > 0) and the output head-slices meet
+    in one all-gather.
     """
 
     def __init__(self, config: AVQConfig, parents32: torch.Tensor, children32: torch.Tensor,
@@ -94,12 +133,19 @@ class ShardedAVQAttention:
         B, T, _ = x.shape
         return x[:, :, self.h0 * self.D:self.h1 * self.D].reshape(B, T, self.h1 - self.h0, self.D).transpose(1, 2)
 
-    def forward(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor) -> torch.Tensor:
-        st, mv = self.compute.quantize(self._local(key), self._local(value))
-        mv = mv.clone()
+    def forward(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                chunk_size: int = 0, kv_cache=None) -> torch.Tensor:
+        """``kv_cache``: a cache of this rank's heads (``num_heads`` = its
+        head count); the new tokens are appended and attention covers the
+        cached ones too, as in ``AVQAttention.forward``."""
+        if kv_cache is None:
+            st, mv = self.compute.quantize(self._local(key), self._local(value))
+        else:
+            st, mv = self.compute.quantize(self._local(key), self._local(value), kv_cache)
+        ready = None
         if self.world > 1:
-            dist.all_reduce(mv, op=dist.ReduceOp.MIN, group=self.group)
-        out = self.compute.forward(self._local(query), st, mv)  # [B, h, T, D]
+            mv, ready = reduce_min(mv, self.group)
+        out = self.compute.forward(self._local(query), st, mv, chunk_size, ready)  # [B, h, T, D]
         B, h, T, D = out.shape
         local = out.transpose(1, 2).reshape(B, T, h * D).contiguous()
         if self.world == 1:
@@ -107,6 +153,10 @@ class ShardedAVQAttention:
         H = self.config.attention.num_heads
         sizes = [head_range(H, self.world, r) for r in range(self.world)]
         hmax = max(b - a for a, b in sizes)
+        if all(b - a == hmax for a, b in sizes):
+            parts = [torch.empty_like(local) for _ in sizes]
+            dist.all_gather(parts, local, group=self.group)
+            return torch.cat(parts, dim=-1)
         padded = torch.zeros(B, T, hmax * D, dtype=local.dtype, device=local.device)
         padded[:, :, :h * D] = local
         parts = [torch.empty_like(padded) for _ in sizes]
@@ -116,4 +166,4 @@ class ShardedAVQAttention:
     __call__ = forward
 
 
-__all__ = ["CudaShardCompute", "ShardCompute", "ShardedAVQAttention", "head_range"]
+__all__ = ["CudaShardCompute", "ShardCompute", "ShardedAVQAttention", "head_range", "reduce_min"]

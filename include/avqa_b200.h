@@ -102,10 +102,15 @@ int avq_quantize(int dtype, const void* keys, const long long* key_strides, cons
  *  - The array is shared by every call on a device: calls that overlap on one
  *    device (two streams, or two host threads without ordering) race on it.
  *    Issue them in order on one stream.
- *  - The first call on each device (the current device) does a one-time setup:
- *    it looks up the array's device address with cudaGetSymbolAddress, which
- *    may load the library's device code onto that device.  Make that first
- *    call before any stream capture begins on the device. */
+ *  - The first call in each CUDA context (the context current at the call:
+ *    the device's primary context for a runtime-API host, the host's own
+ *    context for a driver-API host) does a one-time setup: it looks up the
+ *    array's device address with cudaGetSymbolAddress, which may load the
+ *    library's device code into that context.  Make that first call before
+ *    any stream capture begins on the device.  The address is cached per
+ *    context handle; a host that destroys a context and creates another one
+ *    under the same handle (cudaDeviceReset) must not call this entry point
+ *    afterwards. */
 int avq_quantize_noalloc(int dtype, const void* keys, const long long* key_strides, const void* values,
                          const long long* value_strides, int B, int H, int S, int D, int M0, int C,
                          const void* parents_dt, const float* p_sq, const void* children_dt, const float* c_sq,
@@ -121,16 +126,24 @@ size_t avq_forward_workspace_size(int dtype, int B, int H, int T, int D, int M0,
 
 /* AVQ attention of T queries per (b,h) over a quantized key set.
  * q: dtype with q_strides; out: fp32 with out_strides (module layout
- * [B,T,H*D] -> {T*H*D, D, H*D}).  min_valid: device int, the minimum over
- * every (b,h) of the call (or of all ranks) of non-empty parents; the
- * routing budget is min(P, *min_valid).  hvaq: 0 off, 1 entropy schedule,
+ * [B,T,H*D] -> {T*H*D, D, H*D}).  state_batch: the batch of the quantized
+ * state (pagg, cagg, pcnt, ccnt): B, or 1 when one key set serves all B query
+ * batches (query chunks of one sequence over keys quantized once; each chunk
+ * is routed on its own, as a separate reference call over the same keys would
+ * be).  min_valid: device int, the minimum over every (b,h) of the call (or
+ * of all ranks) of non-empty parents; the routing budget is
+ * min(P, *min_valid).  min_valid_ready: NULL, or a cudaEvent_t recorded by
+ * whatever produces *min_valid (e.g. a cross-rank all-reduce on another
+ * stream): `stream` waits on it only before the routing kernel, so the
+ * parent-attention kernel overlaps the reduction.  hvaq: 0 off, 1 entropy schedule,
  * 2 linear schedule; beta0 the base temperature (1/sqrt(D) when the config
  * says 0), alpha the linear slope.  importance_out [G,M0] fp32, selected_out
  * [G, avq_selection_stride()] int32 and pass_counts_out [passes] int32 are
  * optional diagnostics (NULL to skip). */
 int avq_forward(int dtype, const void* q, const long long* q_strides, int B, int H, int T, int D, int M0, int C,
                 const void* parents_dt, const void* children_dt, const void* pagg, const void* cagg, const int* pcnt,
-                const int* ccnt, const int* min_valid, int P, int passes, float pass_decay, int hvaq, float beta0,
+                const int* ccnt, int state_batch, const int* min_valid, void* min_valid_ready, int P, int passes,
+                float pass_decay, int hvaq, float beta0,
                 float alpha, float* out, const long long* out_strides, float* importance_out, int* selected_out,
                 int* pass_counts_out, void* workspace, size_t workspace_bytes, void* stream);
 

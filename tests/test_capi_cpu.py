@@ -37,7 +37,7 @@ def test_selection_stride_matches_pass_caps() -> None:
     assert lib.avq_selection_stride(5, 3, 0.3) == sum(pass_caps(5, 3, 0.3))
 
 
-@pytest.mark.parametrize("call", ["bad_dtype", "bad_budget", "null"])
+@pytest.mark.parametrize("call", ["bad_dtype", "bad_budget", "null", "state_batch"])
 def test_forward_rejects_bad_arguments(call: str) -> None:
     lib = _lib.load()
     s = (ctypes.c_longlong * 3)(1, 1, 1)
@@ -46,13 +46,26 @@ def test_forward_rejects_bad_arguments(call: str) -> None:
         args["dtype"] = 7
     if call == "bad_budget":
         args["P"] = 9
+    sb = 3 if call == "state_batch" else 1
     rc = lib.avq_forward(args["dtype"], args["q"], s, 1, 1, 1, 8, args["M0"], 2, None, None, None, None, None, None,
-                         None, args["P"], 1, 1.0, 0, 0.0, 1.0, None, s, None, None, None, None, 0, None)
+                         sb, None, None, args["P"], 1, 1.0, 0, 0.0, 1.0, None, s, None, None, None, None, 0, None)
     assert rc == 1
     msg = _lib.last_error()
     assert msg.startswith("avq_forward")
     if call == "bad_budget":
         assert "exceeds number of parents" in msg
+    if call == "state_batch":
+        assert "state_batch" in msg
+
+
+def test_group_count_overflow_is_rejected() -> None:
+    """B*H beyond INT_MAX is refused before any size is derived from it."""
+    lib = _lib.load()
+    s = (ctypes.c_longlong * 3)(1, 1, 1)
+    assert lib.avq_quantize_workspace_size(1 << 16, 1 << 16, 8, 8) == 0
+    rc = lib.avq_quantize_noalloc(1, None, s, None, s, 1 << 16, 1 << 16, 8, 8, 8, 2, None, None, None, None, None,
+                                  None, None, None, None, None, None, None, None, None, None)
+    assert rc == 1 and "exceeds INT_MAX" in _lib.last_error()
 
 
 def test_workspace_queries() -> None:

@@ -86,3 +86,27 @@ def test_decode_with_cache_matches_oracle(paged: bool) -> None:
     assert cache.size == S0 + 40
     ck, cv = cache.lookup()
     np.testing.assert_array_equal(ck.float().cpu().numpy(), torch.from_numpy(kk).view(B, -1, H, D).transpose(1, 2))
+
+
+@pytest.mark.parametrize("B", [1, 2])
+def test_forward_chunked_equals_separate_calls(B: int) -> None:
+    """Query chunks over keys quantized once (the long-context path): batch 1
+    runs all whole chunks in one call against a shared key state, batch 2
+    chunk by chunk; either way each chunk equals its own reference call."""
+    torch.manual_seed(4)
+    dt, T, S, E, H, chunk = "bf16", 3 * 64 + 37, 512, 128, 2, 64
+    cfg = _cfg(E, H, 32, 4, 6)
+    q, k, v = (torch.randn(B, n, E) for n in (T, S, S))
+    qn, kn, vn = (O.rnd(x.numpy(), dt) for x in (q, k, v))
+    kh0 = torch.from_numpy(kn).view(B, S, H, E // H).transpose(1, 2)[0]
+    cb = codebook_from_keys(kh0, 32, 4, seed=9)
+    m = AVQAttention(cfg, in_proj=False, out_proj=False)
+    m.codebook.parents, m.codebook.children = cb.parents.clone(), cb.children.clone()
+    qd, kd, vd = (torch.from_numpy(x).to("cuda", torch.bfloat16) for x in (qn, kn, vn))
+    out = m.forward_chunked(qd, kd, vd, chunk).cpu().numpy()
+    pd, cd = O.cast_codebook(cb.parents.numpy(), cb.children.numpy(), dt)
+    for t0 in range(0, T, chunk):
+        sep = m(qd[:, t0:t0 + chunk], kd, vd).cpu().numpy()
+        np.testing.assert_array_equal(out[:, t0:t0 + chunk], sep)
+        res = O.forward(qn[:, t0:t0 + chunk], kn, vn, pd, cd, O.ForwardConfig(H, 32, 4, 6, dt))
+        assert normrel(out[:, t0:t0 + chunk], res["out_bte"]) <= 1e-2, t0

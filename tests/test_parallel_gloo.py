@@ -57,13 +57,18 @@ class OracleShard:
         mv = int((st.parent_counts > 0).sum(-1).min())
         return (st, h), torch.tensor([mv], dtype=torch.int32)
 
-    def forward(self, q, state, min_valid):
+    def forward(self, q, state, min_valid, chunk_size=0, ready=None):
         st, h = state
         Bq, _, Tq, Dq = q.shape
         cfg = O.ForwardConfig(h, M0, C, P, "f32")
-        res = O.forward_heads(q.reshape(Bq * h, Tq, Dq).numpy(), None, None, self.p, self.c, cfg, quant=st,
-                              budget_floor=int(min_valid.item()))
-        return torch.from_numpy(res["out"]).view(Bq, h, Tq, Dq)
+        step = chunk_size if chunk_size > 0 else Tq
+        outs = []
+        for t0 in range(0, Tq, step):  # each chunk a separate call over the same quantized keys
+            qc = q[:, :, t0:t0 + step]
+            res = O.forward_heads(qc.reshape(Bq * h, qc.shape[2], Dq).numpy(), None, None, self.p, self.c, cfg,
+                                  quant=st, budget_floor=int(min_valid.item()))
+            outs.append(torch.from_numpy(res["out"]).view(Bq, h, qc.shape[2], Dq))
+        return torch.cat(outs, dim=2)
 
 
 def _worker(rank: int, world: int, port: int, out_q):
@@ -77,7 +82,8 @@ def _worker(rank: int, world: int, port: int, out_q):
                         routing=RoutingConfig(refinement_budget=P))
         mod = ShardedAVQAttention(cfg, parents, children, compute_factory=OracleShard)
         out = mod(q, k, v)
-        out_q.put((rank, out.numpy()))
+        out_c = mod(q, k, v, chunk_size=4)  # chunks of 4, 4 and 2 queries
+        out_q.put((rank, (out.numpy(), out_c.numpy())))
     finally:
         dist.destroy_process_group()
 
@@ -106,5 +112,9 @@ def test_two_gloo_ranks_match_unsharded_oracle() -> None:
     for p in procs:
         p.join(timeout=30)
         assert p.exitcode == 0
+    chunked = [O.forward(q[:, t0:t0 + 4].numpy(), k.numpy(), v.numpy(), parents.numpy(), children.numpy(),
+                         O.ForwardConfig(H, M0, C, P, "f32"))["out_bte"] for t0 in range(0, T, 4)]
+    chunked = np.concatenate(chunked, axis=1)
     for r in range(2):
-        np.testing.assert_allclose(outs[r], full["out_bte"], rtol=0, atol=1e-6)
+        np.testing.assert_allclose(outs[r][0], full["out_bte"], rtol=0, atol=1e-6)
+        np.testing.assert_allclose(outs[r][1], chunked, rtol=0, atol=1e-6)
