@@ -691,24 +691,33 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
   if constexpr (DT != DT_F32) {
     if (mma) {
       const int nqt = (a.T + PM_ROWS_PUBLIC - 1) / PM_ROWS_PUBLIC;
-      PAArgs pa{a.q, a.qs, a.B, a.H, a.T, a.D, a.M0, sqrtD, a.parents_dt, a.pagg, a.pcnt, 0, hv ? 1 : 0, w.slog,
-                false, w.m, w.l, w.z, w.a, (float*)w.part0, sel, sel_stride, pcnt_out, a.hvaq, a.beta0, a.alpha,
-                w.beta, sG};
-      // tcgen05 kernel for the plain first pass; the HVAQ variant keeps its
-      // logits for the rescaling pass and runs on the mma.sync kernel
-      const bool pa_tc = !hv && parent_attn_tc_ok(DT, a.D, a.M0), corr_tc = correct_tc_ok(DT, a.D, a.C);
+      // both parent passes on tcgen05 when they fit (the HVAQ rescaling pass
+      // gathers the first budget's parents into one 64-row tile); otherwise
+      // both on the mma.sync kernels, whose plain pass then keeps its logits
+      // in the scratch slices for the rescaling pass
+      const bool tc_ok = parent_attn_tc_ok(DT, a.D, a.M0);
+      bool pa_tc = tc_ok && (!hv || parent_attn_tc_hvaq_ok(DT, a.D, a.M0, a.P));
+      const bool corr_tc = correct_tc_ok(DT, a.D, a.C);
+      PAArgs pa{a.q, a.qs, a.B, a.H, a.T, a.D, a.M0, sqrtD, a.parents_dt, a.pagg, a.pcnt, 0, (hv && !pa_tc) ? 1 : 0,
+                w.slog, false, w.m, w.l, w.z, w.a, (float*)w.part0, sel, sel_stride, pcnt_out, a.hvaq, a.beta0,
+                a.alpha, w.beta, sG};
       if (DT == DT_BF16 && (pa_tc || corr_tc)) launch_exp_table(w.exptab, st);
-      int rc = pa_tc ? launch_parent_attn_tc<DT>(pa, w.exptab, st) : AVQ_ERR_UNSUPPORTED;
-      if (rc == AVQ_ERR_UNSUPPORTED) rc = launch_parent_attn_mma<DT>(pa, st);
+      int rc = AVQ_ERR_UNSUPPORTED;
+      if (pa_tc && (rc = launch_parent_attn_tc<DT>(pa, w.exptab, st)) == AVQ_ERR_UNSUPPORTED) {
+        pa_tc = false;  // an operand the tensor maps cannot describe: the mma.sync kernels
+        pa.keep_logits = hv ? 1 : 0;
+      }
+      if (!pa_tc) rc = launch_parent_attn_mma<DT>(pa, st);
       if (rc != AVQ_OK) return rc;
-      RouteExact rx0{(const float*)w.part0, w.slog, hv ? 1 : 0, w.m, w.z, a.T};
+      // the routing fallback reads exponentials, or the mma.sync HVAQ path's kept logits
+      RouteExact rx0{(const float*)w.part0, w.slog, pa.keep_logits, w.m, w.z, a.T};
       route(w.part0, nqt, a.pcnt, a.M0, a.min_valid, a.P, a.passes, a.pass_decay, 0, (!hv && a.passes > 1) ? 1 : 0,
             lay, sel, sel_stride, pcnt_out, imp_out, rx0);
       if (hv) {
         pa.mode = 1;
         pa.keep_logits = 0;
         pa.colpart = (float*)w.part1;
-        rc = launch_parent_attn_mma<DT>(pa, st);
+        rc = pa_tc ? launch_parent_attn_tc<DT>(pa, w.exptab, st) : launch_parent_attn_mma<DT>(pa, st);
         if (rc != AVQ_OK) return rc;
         RouteExact rx1{(const float*)w.part1, w.slog, 0, w.m, w.z, a.T};
         if (a.passes > 1)
@@ -719,7 +728,7 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
                   a.pcnt, a.ccnt, w.m, w.l, w.z, hv ? w.beta : nullptr, w.a, sel, sel_stride, pcnt_out, a.passes,
                   {0, 0, 0, 0, 0, 0, 0, 0}, a.passes > 1 ? 1 : 0, a.out, a.os, sG};
       for (int k = 0; k < a.passes; ++k) ca.pass_off[k] = lay.off[k];
-      rc = (corr_tc && w.cdesc) ? launch_correct_tc(ca, w.exptab, w.cdesc, st) : AVQ_ERR_UNSUPPORTED;
+      rc = (corr_tc && w.cdesc) ? launch_correct_tc<DT>(ca, w.exptab, w.cdesc, st) : AVQ_ERR_UNSUPPORTED;
       if (rc == AVQ_ERR_UNSUPPORTED) rc = launch_correct_mma<DT>(ca, st);
       if (rc != AVQ_OK) return rc;
       return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;

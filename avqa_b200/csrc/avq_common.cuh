@@ -47,37 +47,41 @@ template <int DT> __device__ __forceinline__ float count_dt(int n) {
   return (float)(n < sat ? n : sat);
 }
 
-__device__ __forceinline__ float step_down(float y, int k) {
-  for (int i = 0; i < k; ++i) y = nextafterf(y, -INFINITY);
-  return y;
-}
-__device__ __forceinline__ float step_up(float y, int k) {
-  for (int i = 0; i < k; ++i) y = nextafterf(y, INFINITY);
-  return y;
+// True when every fp32 value within k ulps of the finite nonzero y narrows to
+// the same DT value, which is then stored in *r.  Stepping the bit pattern by
+// k moves |y| by k ulps in either direction (the sign bit is untouched for
+// |y| above k ulps of zero, which the caller ensures).
+template <int DT>
+__device__ __forceinline__ bool narrow_certain(float y, uint32_t k, float* r) {
+  const uint32_t u = __float_as_uint(y);
+  const float a = rnd<DT>(__uint_as_float(u - k)), b = rnd<DT>(__uint_as_float(u + k));
+  *r = a;
+  return a == b;
 }
 
 // rnd<DT>(correctly rounded fp32 exp(x)).  CUDA's expf is within 2 ulp; when
-// every fp32 value in that window narrows to the same DT value the answer is
-// known, otherwise the exponential is recomputed in double.
+// every fp32 value within 3 ulp of it narrows to the same DT value the answer
+// is known, otherwise the exponential is recomputed in double.  A result
+// below 2^-140 (far below half of the smallest fp16 / bf16 step) narrows to 0.
 template <int DT> __device__ __forceinline__ float exp_rn(float x) {
   if (DT != DT_F32) {
     const float y = expf(x);
-    if (isfinite(y) && y > 0.f) {
-      const float a = rnd<DT>(step_down(y, 3)), b = rnd<DT>(step_up(y, 3));
-      if (a == b) return a;
+    float r;
+    if (isfinite(y)) {
+      if (y < 7.0e-43f) return 0.f;
+      if (narrow_certain<DT>(y, 3u, &r)) return r;
     }
   }
   return rnd<DT>(__double2float_rn(exp((double)x)));
 }
 
-// Same for the natural logarithm (HVAQ entropy), x > 0.
+// Same for the natural logarithm (HVAQ entropy), x > 0 (log(1) = 0 exactly).
 template <int DT> __device__ __forceinline__ float log_rn(float x) {
   if (DT != DT_F32) {
     const float y = logf(x);
-    if (isfinite(y)) {
-      const float a = rnd<DT>(step_down(y, 3)), b = rnd<DT>(step_up(y, 3));
-      if (a == b) return a;
-    }
+    float r;
+    if (y == 0.f && x == 1.f) return 0.f;
+    if (isfinite(y) && fabsf(y) > 1e-30f && narrow_certain<DT>(y, 3u, &r)) return r;
   }
   return rnd<DT>(__double2float_rn(log((double)x)));
 }
@@ -94,12 +98,20 @@ __device__ __forceinline__ bool near_midpoint(float y) {
 }
 
 // DT(correctly rounded fp32 exp(x)): expf is within 2 ulp, so only results
-// near a rounding midpoint need the double-precision recomputation.
+// near a rounding midpoint need the double-precision recomputation.  fp16
+// results in the subnormal range (steps of 2^-24, where the midpoint test on
+// the fp32 mantissa does not apply) are certified by bracketing 3 fp32 ulps;
+// below 2^-140 they narrow to 0.
 template <int DT>
 __device__ __forceinline__ float exp_dt_fast(float x) {
   if (DT != DT_F32) {
     const float y = expf(x);
     if (!near_midpoint<DT>(y)) return rnd<DT>(y);
+    if (DT == DT_F16 && y < 6.2e-5f) {
+      float r;
+      if (y < 7.0e-43f) return 0.f;
+      if (narrow_certain<DT>(y, 3u, &r)) return r;
+    }
   }
   return rnd<DT>(__double2float_rn(exp((double)x)));
 }

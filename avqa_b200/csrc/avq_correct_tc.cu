@@ -1,4 +1,4 @@
-// Child correction on the sm_100a tensor cores for bf16 and D in {64, 128}
+// Child correction on the sm_100a tensor cores for bf16 / fp16 and D in {64, 128}
 // (reference refinement.py:82-304, attention.py:100-163, multipass.py:207-262,
 // attention_module.py:532-535).
 //
@@ -21,6 +21,11 @@
 // The weights are fp32 quantities of the reference's fp32 correction; they use
 // the fast exponential (relative error a few 1e-7), far inside the bf16
 // output tolerance, and never feed a routing decision.
+//
+// fp16: the logit MMA runs on fp16 operands; the weights stay three bf16 parts
+// (one MMA kind takes one operand type), so each gathered fp16 value row is
+// split exactly into two bf16 planes, v = hi + lo (11 significant bits = 8 +
+// at most 3), by the thread that gathered it, and O += W V takes six MMAs.
 #include <cuda.h>
 
 #include <algorithm>
@@ -54,10 +59,11 @@ constexpr int CTHREADS2 = 288;  // 8 row warps (two threads per query) + the MMA
 constexpr int MW = 8;           // the MMA / TMA warp
 
 struct CorrLayout {
-  int q, l[NBUF], v[NBUF], meta[NBUF], exptab, bars, misc, total;
+  int q, l[NBUF], v[NBUF], vlo[NBUF], meta[NBUF], exptab, bars, misc, total;
 };
 
-__host__ __device__ inline CorrLayout corr_layout(int D) {
+// split_v: fp16 value rows, stored as two bf16 planes (v and vlo).
+__host__ __device__ inline CorrLayout corr_layout(int D, bool split_v = false) {
   CorrLayout L;
   int o = 0;
   L.q = o;
@@ -69,6 +75,10 @@ __host__ __device__ inline CorrLayout corr_layout(int D) {
   for (int i = 0; i < NBUF; ++i) {
     L.v[i] = o;
     o += NS * D * 2;
+  }
+  for (int i = 0; i < NBUF; ++i) {
+    L.vlo[i] = o;
+    if (split_v) o += NS * D * 2;
   }
   for (int i = 0; i < NBUF; ++i) {
     L.meta[i] = o;
@@ -120,7 +130,7 @@ struct SlotDesc {
   float n, mk;
 };
 
-template <int C>
+template <int DT, int C>
 __global__ void corr_desc_kernel(const int* __restrict__ sel, int sel_stride, const int* __restrict__ pass_cnt,
                                  int npass, PassOffsets po, int multipass, int H, int M0,
                                  const int* __restrict__ pcnt, const int* __restrict__ ccnt, int maxgroups,
@@ -142,7 +152,7 @@ __global__ void corr_desc_kernel(const int* __restrict__ sel, int sel_stride, co
             const int p = sg[po.off[ps] + j];
             d.lrow = h * M0 + p;
             d.vrow = gs * M0 + p;
-            d.n = count_dt<DT_BF16>(pcnt[(long)gs * M0 + p]);
+            d.n = count_dt<DT>(pcnt[(long)gs * M0 + p]);
             d.mk = d.n > 0.f ? 1.f : 0.f;
           }
         } else if (r < NREAL) {
@@ -152,7 +162,7 @@ __global__ void corr_desc_kernel(const int* __restrict__ sel, int sel_stride, co
             const int pl = quirk ? j : p;
             d.lrow = -2 - ((h * M0 + pl) * C + c);
             d.vrow = -2 - ((gs * M0 + p) * C + c);
-            d.n = count_dt<DT_BF16>(ccnt[((long)gs * M0 + p) * C + c]);
+            d.n = count_dt<DT>(ccnt[((long)gs * M0 + p) * C + c]);
             d.mk = ccnt[((long)gs * M0 + pl) * C + c] > 0 ? 1.f : 0.f;
           }
         }
@@ -162,21 +172,23 @@ __global__ void corr_desc_kernel(const int* __restrict__ sel, int sel_stride, co
   }
 }
 
-template <int D, int C>
+template <int DT, int D, int C>
 __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, int4 qpos, int H, int Tq, float sqrtD,
-    const __nv_bfloat16* __restrict__ parents, const __nv_bfloat16* __restrict__ children,
-    const __nv_bfloat16* __restrict__ pagg, const __nv_bfloat16* __restrict__ cagg, const float* __restrict__ m_in,
-    const float* __restrict__ l_in, const float* __restrict__ z_in, const float* __restrict__ beta_in,
-    const __nv_bfloat16* __restrict__ a_in, const int* __restrict__ pass_cnt, int npass, int maxgroups,
-    const SlotDesc* __restrict__ desc, const uint16_t* __restrict__ exptab_g, float* __restrict__ out, Strides3 os) {
-  constexpr int DT = DT_BF16;
+    const typename Storage<DT>::T* __restrict__ parents, const typename Storage<DT>::T* __restrict__ children,
+    const typename Storage<DT>::T* __restrict__ pagg, const typename Storage<DT>::T* __restrict__ cagg,
+    const float* __restrict__ m_in, const float* __restrict__ l_in, const float* __restrict__ z_in,
+    const float* __restrict__ beta_in, const typename Storage<DT>::T* __restrict__ a_in,
+    const int* __restrict__ pass_cnt, int npass, int maxgroups, const SlotDesc* __restrict__ desc,
+    const uint16_t* __restrict__ exptab_g, float* __restrict__ out, Strides3 os) {
+  using T = typename Storage<DT>::T;
+  constexpr bool SPLIT = DT == DT_F16;  // fp16 value rows become two bf16 planes
   constexpr int J = NS / (1 + C), NREAL = J * (1 + C), CPR = D / 8;
   constexpr int OCOL = 0, SCOL = D, WCOL = D + NS;  // TMEM columns
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_addr(smem_raw);
   unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  const CorrLayout L = corr_layout(D);
+  const CorrLayout L = corr_layout(D, SPLIT);
   const int g = blockIdx.y, b = g / H, h = g % H, t0 = blockIdx.x * CR;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.bars);
@@ -205,7 +217,7 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
     tc::fence_mbar_init();
   }
   if (warp == MW) tc::tmem_alloc(tslot, C_TMEM_COLS);
-  if (tid < 2 * CR) {
+  if (DT == DT_BF16 && tid < 2 * CR) {
     const uint32_t* src = reinterpret_cast<const uint32_t*>(exptab_g);
     uint32_t* dst = reinterpret_cast<uint32_t*>(sm + L.exptab);
     for (int i = tid; i < (EXPN + 1) / 2; i += 2 * CR) dst[i] = src[i];
@@ -228,13 +240,14 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
         c[qpos.z] = b;
         tc::tma_load_4d(sm + L.q + kb * CR * 128, &tm_q, c[0], c[1], c[2], c[3], &bars[CB_Q]);
       }
-      const uint32_t idS = tc::idesc_f16(1, CR, NS, false);
-      const uint32_t idO = tc::idesc_f16(1, CR, D, true);
+      const uint32_t idS = tc::idesc_f16(DT == DT_BF16 ? 1 : 0, CR, NS, false);
+      const uint32_t idO = tc::idesc_f16(1, CR, D, true);  // bf16 weights x bf16 value planes
       const uint32_t qa = tc::smem_addr(sm + L.q);
-      uint32_t la[NBUF], va[NBUF];
+      uint32_t la[NBUF], va[NBUF], vla[NBUF];
       for (int i = 0; i < NBUF; ++i) {
         la[i] = tc::smem_addr(sm + L.l[i]);
         va[i] = tc::smem_addr(sm + L.v[i]);
+        vla[i] = tc::smem_addr(sm + L.vlo[i]);
       }
       auto issue_S = [&](int kg) -> bool {
         const int bf = kg % NBUF;
@@ -260,12 +273,14 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
         if (!(ok = tc::mbar_wait(&bars[CB_WFULL], kg & 1, abort))) break;
         tc::tc_after_sync();
 #pragma unroll
-        for (int part = 0; part < 3; ++part)
+        for (int vp = 0; vp < (SPLIT ? 2 : 1); ++vp)
 #pragma unroll
-          for (int kk = 0; kk < NS / 16; ++kk) {
-            const uint64_t bd = tc::sdesc_sw128(va[bf] + kk * 16 * 128, NS * 128, 1024);
-            tc::mma_ts(tbase + OCOL, tbase + WCOL + part * (NS / 2) + kk * 8, bd, idO, true);
-          }
+          for (int part = 0; part < 3; ++part)
+#pragma unroll
+            for (int kk = 0; kk < NS / 16; ++kk) {
+              const uint64_t bd = tc::sdesc_sw128((vp ? vla[bf] : va[bf]) + kk * 16 * 128, NS * 128, 1024);
+              tc::mma_ts(tbase + OCOL, tbase + WCOL + part * (NS / 2) + kk * 8, bd, idO, true);
+            }
         tc::mma_commit(&bars[CB_WFREE]);
         tc::mma_commit(&bars[CB_EMPTY + bf]);
       }
@@ -298,8 +313,8 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
       const int bf = kg % NBUF;
       if (gathers) {
         const int x = isv ? d.vrow : d.lrow;
-        const __nv_bfloat16* src = x >= 0 ? (isv ? pagg : parents) + (long)x * D
-                                          : (isv ? cagg : children) + (long)(x <= -2 ? -2 - x : 0) * D;
+        const T* src = x >= 0 ? (isv ? pagg : parents) + (long)x * D
+                              : (isv ? cagg : children) + (long)(x <= -2 ? -2 - x : 0) * D;
         unsigned char* dst = sm + (isv ? L.v[bf] : L.l[bf]) + gslot * 128;
 #pragma unroll
         for (int ch = 0; ch < CPR; ++ch)
@@ -313,6 +328,32 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
       cp_async_commit();
     };
     auto publish = [&](int kg) {  // copies of group kg have landed (this thread's part)
+      if constexpr (SPLIT) {
+        // the value row this thread gathered: fp16 -> bf16 hi (in place) + bf16 lo
+        if (gathers && isv) {
+          const int bf = kg % NBUF;
+#pragma unroll
+          for (int ch = 0; ch < CPR; ++ch) {
+            const int off = (ch >> 3) * NS * 128 + gslot * 128 + (((ch & 7) ^ (gslot & 7)) << 4);
+            uint4* vh = reinterpret_cast<uint4*>(sm + L.v[bf] + off);
+            uint4* vl = reinterpret_cast<uint4*>(sm + L.vlo[bf] + off);
+            const uint4 u = *vh;
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float a0 = half_lo<DT_F16>(w[e]), a1 = half_hi<DT_F16>(w[e]);
+              hi[e] = pack2<DT_BF16>(a0, a1);
+              // exact remainders; an infinite sum keeps lo = 0 so that w * v stays infinite
+              const float r0 = isinf(a0) ? 0.f : a0 - half_lo<DT_BF16>(hi[e]);
+              const float r1 = isinf(a1) ? 0.f : a1 - half_hi<DT_BF16>(hi[e]);
+              lo[e] = pack2<DT_BF16>(r0, r1);
+            }
+            *vh = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *vl = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          }
+        }
+      }
       tc::fence_async_smem();
       tc::mbar_arrive(&bars[CB_FULL + kg % NBUF]);
     };
@@ -431,7 +472,9 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
                 float s = kv[e] > 0.f ? sl[i] : -INFINITY;
                 if (k < J) {
                   if (beta_in) s = rnd<DT>(__fmul_rn(bt, rnd<DT>(__fmul_rn(s, sqrtD))));
-                  const float ex = exp_bf16_tab(rnd<DT>(s - m), exptab);
+                  float ex;
+                  if constexpr (DT == DT_BF16) ex = exp_bf16_tab(rnd<DT>(s - m), exptab);
+                  else ex = fmaxf(exp_dt_fast<DT>(rnd<DT>(s - m)), 0.f);  // NaN -> 0
                   // pi = DT(e / z): e / z lies between RD(e zl) and RU(e zh)
                   // (e >= 0); ends that round apart are redone exactly below
                   const float pi = rnd<DT>(__fmul_rd(ex, zl));
@@ -581,7 +624,7 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
 bool correct_tc_ok(int dt, int D, int C) {
   const char* e = std::getenv("AVQ_DISABLE_TCGEN05");
   const bool off = e && *e && *e != '0';
-  return !off && dt == DT_BF16 && (D == 64 || D == 128) && (C == 4 || C == 8);
+  return !off && (dt == DT_BF16 || dt == DT_F16) && (D == 64 || D == 128) && (C == 4 || C == 8);
 }
 
 int correct_tc_groups(int sel_stride, int C) {
@@ -593,17 +636,19 @@ size_t correct_tc_desc_bytes(int G, int sel_stride, int C) {
   return (size_t)G * correct_tc_groups(sel_stride, C) * NS * sizeof(SlotDesc);
 }
 
+template <int DT>
 int launch_correct_tc(const CorrArgs& a, const void* exptab, void* desc, cudaStream_t st) {
+  using T = typename Storage<DT>::T;
   const int G = a.B * a.H, D = a.D;
   CUtensorMap tq;
   int4 qpos;
-  if (!tc::map_rows4(&tq, DT_BF16, a.q, a.qs, a.B, a.H, a.T, D, CR, &qpos)) return AVQ_ERR_UNSUPPORTED;
+  if (!tc::map_rows4(&tq, DT, a.q, a.qs, a.B, a.H, a.T, D, CR, &qpos)) return AVQ_ERR_UNSUPPORTED;
   if (((uintptr_t)a.out % 16) || a.os.s % 4 || a.os.h % 4 || a.os.b % 4) return AVQ_ERR_UNSUPPORTED;
   PassOffsets po;
   for (int k = 0; k < 8; ++k) po.off[k] = a.pass_off[k];
   const int maxgroups = correct_tc_groups(a.sel_stride, a.C);
   SlotDesc* sd = static_cast<SlotDesc*>(desc);
-  const CorrLayout L = corr_layout(D);
+  const CorrLayout L = corr_layout(D, DT == DT_F16);
   const size_t smem = std::max<size_t>((size_t)L.total + 1024, 80 * 1024);  // <= 2 CTAs (2 x 256 TMEM columns) per SM
   auto go = [&](auto dfn, auto kfn) {
     AVQ_TIMED("correct_tc", st);
@@ -611,19 +656,23 @@ int launch_correct_tc(const CorrArgs& a, const void* exptab, void* desc, cudaStr
                           maxgroups, sd, a.sG > 0 ? a.sG : G);
     cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     kfn<<<dim3((a.T + CR - 1) / CR, G), CTHREADS2, smem, st>>>(
-        tq, qpos, a.H, a.T, a.sqrtD, static_cast<const __nv_bfloat16*>(a.parents),
-        static_cast<const __nv_bfloat16*>(a.children), static_cast<const __nv_bfloat16*>(a.pagg),
-        static_cast<const __nv_bfloat16*>(a.cagg), a.m, a.l, a.z, a.beta, static_cast<const __nv_bfloat16*>(a.a),
-        a.pass_cnt, a.npass, maxgroups, sd, static_cast<const uint16_t*>(exptab), a.out, a.os);
+        tq, qpos, a.H, a.T, a.sqrtD, static_cast<const T*>(a.parents), static_cast<const T*>(a.children),
+        static_cast<const T*>(a.pagg), static_cast<const T*>(a.cagg), a.m, a.l, a.z, a.beta,
+        static_cast<const T*>(a.a), a.pass_cnt, a.npass, maxgroups, sd, static_cast<const uint16_t*>(exptab), a.out,
+        a.os);
   };
   if (a.C == 4) {
-    if (D == 64) go(corr_desc_kernel<4>, correct_tc_kernel<64, 4>); else go(corr_desc_kernel<4>, correct_tc_kernel<128, 4>);
+    if (D == 64) go(corr_desc_kernel<DT, 4>, correct_tc_kernel<DT, 64, 4>);
+    else go(corr_desc_kernel<DT, 4>, correct_tc_kernel<DT, 128, 4>);
   } else {
-    if (D == 64) go(corr_desc_kernel<8>, correct_tc_kernel<64, 8>); else go(corr_desc_kernel<8>, correct_tc_kernel<128, 8>);
+    if (D == 64) go(corr_desc_kernel<DT, 8>, correct_tc_kernel<DT, 64, 8>);
+    else go(corr_desc_kernel<DT, 8>, correct_tc_kernel<DT, 128, 8>);
   }
   return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
 }
 
+template int launch_correct_tc<DT_BF16>(const CorrArgs&, const void*, void*, cudaStream_t);
+template int launch_correct_tc<DT_F16>(const CorrArgs&, const void*, void*, cudaStream_t);
 
 // Reads and clears this file's fault word (device code without relocatable
 // linking keeps one copy per file, so every kernel file has its own).

@@ -174,15 +174,19 @@ constexpr int PM_ROWS_PUBLIC = 64;
 // tcgen05 parent attention (first pass without HVAQ): same outputs, scratch
 // slices and 64-query importance partials as launch_parent_attn_mma.
 bool parent_attn_tc_ok(int dt, int D, int M0);
+// The HVAQ rescaling pass on tcgen05 (mode 1): the first pass's budget P
+// must fit one gathered 64-row tile.
+bool parent_attn_tc_hvaq_ok(int dt, int D, int M0, int P);
 size_t parent_attn_tc_table_bytes();
 template <int DT>
 int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st);
 // The bf16 exponential table of the tcgen05 kernels (DT(exp(-x)) for every
 // bf16 x in [2^-9, 128], then 0), parent_attn_tc_table_bytes() bytes.
 void launch_exp_table(void* tab, cudaStream_t st);
-// tcgen05 child correction (bf16): same output as launch_correct_mma.
+// tcgen05 child correction (bf16, fp16): same output as launch_correct_mma.
 bool correct_tc_ok(int dt, int D, int C);
 size_t correct_tc_desc_bytes(int G, int sel_stride, int C);
+template <int DT>
 int launch_correct_tc(const CorrArgs& a, const void* exptab, void* desc, cudaStream_t st);
 // tcgen05 key assignment (parent argmin + child argmin), same outputs as the
 // assign kernels of avq_quantize.cu.

@@ -84,6 +84,7 @@ __device__ __forceinline__ float clamp_min_nan(float x, float lo) { return isnan
 AVQ_F32X2_OP(add_f32x2, "add.rn.f32x2")
 AVQ_F32X2_OP(mul_f32x2_rd, "mul.rm.f32x2")
 AVQ_F32X2_OP(mul_f32x2_ru, "mul.rp.f32x2")
+AVQ_F32X2_OP(mul_f32x2_rn, "mul.rn.f32x2")
 #undef AVQ_F32X2_OP
 
 // The neighbouring fp32 values of a positive finite nonzero x.

@@ -64,7 +64,10 @@ constexpr int TC_MAX_M0 = 8192;  // above 2048 the shared memory allows one CTA 
 
 // Barrier slots: the tile ring's full and empty barriers, the logit slots'
 // full (MMA done) and consumed (row threads done) barriers.
-constexpr int B_Q = 0, B_RFULL = 1, B_REMPTY = 5, B_SFULL = 9, B_EFULL = 13, B_SFREE = 17, B_OFULL = 18, N_BARS = 19;
+// HVAQ mode adds the gathered selected-parent tile (B_SEL: its 32 gathering
+// lanes) and the row threads' temperatures (B_BETA: all 256 row threads).
+constexpr int B_Q = 0, B_RFULL = 1, B_REMPTY = 5, B_SFULL = 9, B_EFULL = 13, B_SFREE = 17, B_OFULL = 18, B_SEL = 19,
+              B_BETA = 20, N_BARS = 21;
 constexpr int NRING = 4;  // tile ring buffers (the layout's p[0], p[1], v[0], v[1], contiguous)
 
 // TMEM column of logit slot k; slots 2 and 3 only in pass 1.
@@ -74,10 +77,12 @@ __device__ __forceinline__ uint32_t s_col(int k) {
 }
 
 struct TcLayout {
-  int q, p[2], v[2], exptab, pm2, n2, srow, scomb, xch, bars, misc, total;
+  int q, p[2], v[2], sel, exptab, pm2, n2, srow, scomb, xch, bars, misc, total;
 };
 
-__host__ __device__ inline TcLayout tc_layout(int D, int M0) {
+// hv: the HVAQ rescaling pass, which also holds one tile of gathered parent
+// rows (the first routing pass's selection).
+__host__ __device__ inline TcLayout tc_layout(int D, int M0, bool hv = false) {
   TcLayout L;
   const int nch = (M0 + TCH - 1) / TCH;
   int o = 0;
@@ -91,6 +96,8 @@ __host__ __device__ inline TcLayout tc_layout(int D, int M0) {
     L.v[i] = o;
     o += TCH * D * 2;
   }
+  L.sel = o;
+  if (hv) o += TCH * D * 2;
   L.exptab = o;
   o += EXP_WORDS * 4;
   o = (o + 15) & ~15;
@@ -183,18 +190,25 @@ __device__ __forceinline__ bool rows_all(bool p) {
   return r != 0;
 }
 
-template <int DT, int D>
+// HV: the HVAQ rescaling pass (pipeline.py:192-258, hopfield.py:55-144).  It
+// reads the plain pass's row max and normaliser from m_out / z_out (the same
+// rows it then overwrites), the plain pass's selection sel0 (at most 64
+// parents), and writes the per-query temperature beta_out; the logits of every
+// later step are DT(beta * DT(s * sqrt(D))).
+template <int DT, int D, bool HV>
 __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_p,
     const __grid_constant__ CUtensorMap tm_v, int4 qpos, int H, int Tq, int M0, float sqrtD,
     const int* __restrict__ pcnt, const uint16_t* __restrict__ exptab_g, typename Storage<DT>::T* __restrict__ scratch,
     float* __restrict__ m_out, float* __restrict__ l_out, float* __restrict__ z_out,
-    typename Storage<DT>::T* __restrict__ a_out, float* __restrict__ colpart, int sG) {
+    typename Storage<DT>::T* __restrict__ a_out, float* __restrict__ colpart, int sG,
+    const typename Storage<DT>::T* __restrict__ parents_g, const int* __restrict__ sel0, int sel_stride,
+    const int* __restrict__ pass_cnt, int hvaq, float beta0, float alpha, float* __restrict__ beta_out) {
   using T = typename Storage<DT>::T;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_addr(smem_raw);
   unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  const TcLayout L = tc_layout(D, M0);
+  const TcLayout L = tc_layout(D, M0, HV);
   const int g = blockIdx.y, b = g / H, h = g % H, qt = blockIdx.x, t0 = qt * TR, gs = g % sG;
   const int nch = (M0 + TCH - 1) / TCH, nv = 2 * nch;
   const int ntiles = (Tq + 63) / 64, LDL = exp_slice_pitch(M0);
@@ -228,7 +242,8 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
   // The producer thread initialises the barriers and issues Q and the first
   // ring tiles at once, so the copies overlap the table fill.
   if (warp == W_TMA && lane == 0) {
-    for (int i = 0; i < N_BARS; ++i) tc::mbar_init(&bars[i], (i >= B_EFULL && i < B_EFULL + 4) ? TROW : 1);
+    for (int i = 0; i < N_BARS; ++i)
+      tc::mbar_init(&bars[i], ((i >= B_EFULL && i < B_EFULL + 4) || i == B_BETA) ? TROW : (i == B_SEL ? 32 : 1));
     *abort = 0;
     tc::fence_mbar_init();
     tc::tma_prefetch_desc(&tm_q);
@@ -263,6 +278,26 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
   const uint32_t tbase = *tslot;
 
   if (warp == W_TMA) {
+    if constexpr (HV) {
+      // the plain pass's selected parents (head h rows), gathered in the
+      // 128-byte-swizzled K-major layout of a TMA box: row j, 16-byte chunk c
+      // of 64-column block kb at kb*TCH*128 + j*128 + ((c ^ j) & 7)*16; rows
+      // past the selection are zero-filled
+      const int nsel = min(pass_cnt[0], TCH);
+      const int* sl = sel0 + (long)g * sel_stride;
+      unsigned char* sb = sm + L.sel;
+      for (int i = lane; i < TCH * (D / 8); i += 32) {
+        const int j = i / (D / 8), c = i % (D / 8);
+        const bool in = j < nsel;
+        const int p = in ? sl[j] : 0;
+        cp_async16(sb + (c >> 3) * TCH * 128 + j * 128 + (((c & 7) ^ (j & 7)) << 4),
+                   parents_g + ((long)h * M0 + p) * D + c * 8, in);
+      }
+      cp_async_commit();
+      cp_async_wait<0>();
+      tc::fence_async_smem();
+      tc::mbar_arrive(&bars[B_SEL]);
+    }
     // ---- TMA producer: the rest of the ring, each buffer once its last tile is consumed ----
     if (lane == 0) {
       int issued = ntl < NRING ? ntl : NRING;
@@ -308,6 +343,23 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
         return k < 2 && w < nv ? w : -1;
       };
       bool ok = tc::mbar_wait(&bars[B_Q], 0, abort);
+      if constexpr (HV) {
+        // logits of the selected parents into slot 0; the first chunk takes the
+        // slot again once every row thread has its temperature
+        if (ok && (ok = tc::mbar_wait(&bars[B_SEL], 0, abort))) {
+          tc::tc_after_sync();
+          const uint32_t sa = tc::smem_addr(sm + L.sel);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t ad = tc::sdesc_sw128(qa + (kk >> 2) * TR * 128 + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = tc::sdesc_sw128(sa + (kk >> 2) * TCH * 128 + (kk & 3) * 32, 16, 1024);
+            tc::mma_ss(tbase + s_col<D>(0), ad, bd, idS, kk > 0);
+          }
+          tc::mma_commit(&bars[B_SFULL]);
+          ok = tc::mbar_wait(&bars[B_BETA], 0, abort);
+          tc::tc_after_sync();
+        }
+      }
       // the chunks whose slot has no earlier user: the first four, and the
       // second pass's chunk 1 when there is one parent chunk
       for (int w = 0; ok && w < 4 && w < nch; ++w) {
@@ -367,11 +419,75 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     T* srow_g = scratch + (((long)g * ntiles + (t >> 6)) * 64 + (t & 63)) * LDL;
     const bool sector_stores = (reinterpret_cast<uintptr_t>(scratch) & 31u) == 0u;
     bool ok = true;
+    float beta = 0.f;
+    if constexpr (HV) {
+      // pass 0: each query's temperature from its plain-pass probabilities of
+      // the selected parents: p = DT(e / max(z, eps)) with the plain pass's m
+      // and z, renormalised over the selection, entropy H = -sum p log p,
+      // beta = DT(beta0 * schedule(H)) (pipeline.py:222-258, hopfield.py:55-102)
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_SFULL], 0u, abort));
+      uint32_t ra[32];
+      if (ok) {
+        tc::tc_after_sync();
+        tc::tmem_ld32(tbase + lane_off + s_col<D>(0) + 32 * hf, ra);
+        tc::tmem_wait_ld();
+      }
+      // every row thread takes the same branch (one vote), so the barriers match
+      if (rows_all(ok)) {
+        const int nsel = min(pass_cnt[0], TCH);
+        const int* sl = sel0 + (long)g * sel_stride;
+        const float m0 = live ? m_out[row] : 0.f;
+        const float zc0 = clamp_min_nan(live ? z_out[row] : 1.f, eps_dt<DT>());
+        float pis[32];
+        double gsp = 0.0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int j = 32 * hf + i;
+          float pi = 0.f;
+          if (j < nsel) {
+            const bool keep = pcnt[(long)gs * M0 + sl[j]] > 0;
+            const float s = keep ? scale_logit<DT>(rnd<DT>(__uint_as_float(ra[i])), sqrtD, inv_sqrtD) : -INFINITY;
+            float e = exp_rn<DT>(rnd<DT>(__fsub_rn(s, m0)));
+            if (isnan(e)) e = 0.f;  // pipeline.py:143-145
+            pi = rnd<DT>(__fdiv_rn(e, zc0));
+            gsp += (double)pi;
+          }
+          pis[i] = pi;
+        }
+        // the halves' sums meet in srow (free until pass 3), half 0's part first
+        double* xd = reinterpret_cast<double*>(srow);
+        xd[hf * TR + r] = gsp;
+        rows_sync();
+        const float gsc = clamp_min_nan(rnd64<DT>(xd[r] + xd[TR + r]), eps_dt<DT>());
+        double ent = 0.0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (32 * hf + i < nsel) {
+            const float top = rnd<DT>(__fdiv_rn(pis[i], gsc));  // pipeline.py:238
+            const float lp = top > 0.f ? log_rn<DT>(top) : 0.f;
+            ent += (double)rnd<DT>(__fmul_rn(top, lp));  // hopfield.py:100
+          }
+        }
+        rows_sync();
+        xd[hf * TR + r] = ent;
+        rows_sync();
+        const float hq = -rnd64<DT>(xd[r] + xd[TR + r]);
+        const float sched = hvaq == 1 ? rnd<DT>(__fadd_rn(1.f, rnd<DT>(__fdiv_rn(1.f, rnd<DT>(__fadd_rn(1.f, hq))))))
+                                      : rnd<DT>(__fadd_rn(1.f, rnd<DT>(__fmul_rn(alpha, hq))));
+        beta = rnd<DT>(__fmul_rn(beta0, sched));  // hopfield.py:102
+        if (live && hf == 0) beta_out[row] = beta;
+      }
+      tc::tc_before_sync();
+      tc::mbar_arrive(&bars[B_BETA]);
+    }
+    const float2 sqd2 = make_float2(sqrtD, sqrtD);
+    const uint32_t beta2 = dup2<DT>(beta);
     // pass 1: the row max of the logits (pipeline.py:107,137).  Narrowing and
-    // scaling are monotone, so it is the logit of the largest raw accumulator
-    // over the non-empty parents (NaN-propagating, as torch.max).
+    // scaling are monotone (so is the HVAQ rescaling, beta > 0), so it is the
+    // logit of the largest raw accumulator over the non-empty parents
+    // (NaN-propagating, as torch.max).
     float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-    uint32_t sph = 0u;  // phase bit per logit slot's full barrier
+    uint32_t sph = HV ? 1u : 0u;  // phase bit per logit slot's full barrier (HVAQ: slot 0 served pass 0)
     for (int v = 0; v < nch; ++v) {
       const int sl = v & 3;
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B_SFULL + sl], (sph >> sl) & 1u, abort));
@@ -405,7 +521,8 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     xch[hf * TR + r] = fmax_nan(fmax_nan(mxa[0], mxa[1]), fmax_nan(mxa[2], mxa[3]));
     rows_sync();
     const float amax = fmax_nan(xch[r], xch[TR + r]);
-    const float rm = rnd<DT>(__fdiv_rn(rnd<DT>(amax), sqrtD));
+    float rm = rnd<DT>(__fdiv_rn(rnd<DT>(amax), sqrtD));
+    if constexpr (HV) rm = rnd<DT>(__fmul_rn(beta, rnd<DT>(__fmul_rn(rm, sqrtD))));  // pipeline.py:256, hopfield.py:144
     const float safe = rm == -INFINITY ? 0.f : rm;  // pipeline.py:137-141
     const uint32_t m2 = dup2<DT>(safe);
     // pass 2: exponentials, sums, e @ V
@@ -450,6 +567,15 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
         if (near) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) s2[j] = logit2<DT>(ra[2 * j], ra[2 * j + 1], sqrtD, inv_sqrtD, 0xFFFFFFFFu);
+        }
+        if constexpr (HV) {
+          // DT(beta * DT(s * sqrt(D))): the fp32 product narrowed, then the exact
+          // DT product rounded once
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float2 sc = mul_f32x2_rn(make_float2(half_lo<DT>(s2[j]), half_hi<DT>(s2[j])), sqd2);
+            s2[j] = hmul2_dt<DT>(pack2<DT>(sc.x, sc.y), beta2);
+          }
         }
         const int pw = c * 32 + hf * 16 + hh * 8;  // first parent pair of the block
         const uint4* pm4 = reinterpret_cast<const uint4*>(pm2 + pw);
@@ -696,6 +822,8 @@ bool parent_attn_tc_ok(int dt, int D, int M0) {
   return !tc_disabled() && dt != DT_F32 && (D == 64 || D == 128) && M0 % 8 == 0 && M0 <= TC_MAX_M0;
 }
 
+bool parent_attn_tc_hvaq_ok(int dt, int D, int M0, int P) { return parent_attn_tc_ok(dt, D, M0) && P <= TCH; }
+
 size_t parent_attn_tc_table_bytes() { return (size_t)EXP_WORDS * 4; }
 
 void launch_exp_table(void* tab, cudaStream_t st) { exp_table_kernel<<<1, 256, 0, st>>>(static_cast<uint16_t*>(tab)); }
@@ -704,6 +832,8 @@ template <int DT>
 int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st) {
   using T = typename Storage<DT>::T;
   const int G = a.B * a.H, D = a.D, M0 = a.M0, sG = a.sG > 0 ? a.sG : G;
+  const bool hv = a.mode == 1;
+  if (hv && (!a.sel0 || !a.pass_cnt || !a.beta)) return AVQ_ERR_UNSUPPORTED;
   // Q [B,H,T,D] strided, P [H, M0, D], V [sG, M0, D]; 128-byte swizzled boxes
   CUtensorMap tq, tp, tv;
   int4 qpos;
@@ -711,18 +841,24 @@ int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st) {
       !tc::map_rows3(&tp, DT, a.parents, a.H, M0, D, TCH) || !tc::map_rows3(&tv, DT, a.pagg, sG, M0, D, TCH))
     return AVQ_ERR_UNSUPPORTED;
   if (exp_slice_pitch(M0) < ((M0 + 15) & ~15)) return AVQ_ERR_UNSUPPORTED;  // whole 16-column stores
-  const TcLayout L = tc_layout(D, M0);
+  const TcLayout L = tc_layout(D, M0, hv);
   // at least 80 KB so that no more than two CTAs (2 x 256 TMEM columns) share an SM
   const size_t smem = std::max<size_t>((size_t)L.total + 1024, 80 * 1024);
   auto go = [&](auto kfn) {
-    AVQ_TIMED("parent_attn_tc", st);
+    AVQ_TIMED(hv ? "parent_attn_hvaq_tc" : "parent_attn_tc", st);
     cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     kfn<<<dim3((a.T + TR - 1) / TR, G), TTHREADS, smem, st>>>(
         tq, tp, tv, qpos, a.H, a.T, M0, a.sqrtD, a.pcnt, static_cast<const uint16_t*>(exptab),
-        static_cast<T*>(a.sglobal), a.m, a.l, a.z, static_cast<T*>(a.a), a.colpart, sG);
+        static_cast<T*>(a.sglobal), a.m, a.l, a.z, static_cast<T*>(a.a), a.colpart, sG,
+        static_cast<const T*>(a.parents), a.sel0, a.sel_stride, a.pass_cnt, a.hvaq, a.beta0, a.alpha, a.beta);
   };
-  if (D == 64) go(parent_attn_tc_kernel<DT, 64>);
-  else go(parent_attn_tc_kernel<DT, 128>);
+  if (hv) {
+    if (D == 64) go(parent_attn_tc_kernel<DT, 64, true>);
+    else go(parent_attn_tc_kernel<DT, 128, true>);
+  } else {
+    if (D == 64) go(parent_attn_tc_kernel<DT, 64, false>);
+    else go(parent_attn_tc_kernel<DT, 128, false>);
+  }
   return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
 }
 

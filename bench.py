@@ -500,10 +500,15 @@ def check_slice(w, qg, kg, vg, out_g, parents32, children32, budget_floor: int, 
     t0 = time.perf_counter()
     res = O.forward_heads(qg.numpy(), kg.numpy(), vg.numpy(), pd, cd, cfg, budget_floor=budget_floor)
     dt = time.perf_counter() - t0
-    ref, got = res["out"], out_g.numpy()
-    err = float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
+    ref, got = res["out"].astype(np.float64), out_g.numpy().astype(np.float64)
+    # the reference's own non-finite outputs (fp16 overflow) must sit in the same places
+    bad_g, bad_r = ~np.isfinite(got), ~np.isfinite(ref)
+    same_nonfinite = bool(np.array_equal(bad_g, bad_r))
+    keep = ~(bad_g | bad_r)
+    err = float(np.linalg.norm(got[keep] - ref[keep]) / max(np.linalg.norm(ref[keep]), 1e-30))
     tol = 2e-5 if w.dtype == "f32" else 1e-2
-    return {"slice": f"b=0 h={hh}", "normwise_error": err, "tolerance": tol, "ok": bool(err <= tol),
+    return {"slice": f"b=0 h={hh}", "normwise_error": err, "tolerance": tol,
+            "nonfinite_rows": int(bad_r.any(-1).sum()), "ok": bool(err <= tol and same_nonfinite),
             "oracle_s": round(dt, 2)}
 
 

@@ -196,9 +196,17 @@ def quantize(keys, values, parents, children, dt: str) -> Quantization:
                             np.zeros((G, M0, C, D), np.float32), np.zeros((G, M0), np.float32),
                             np.zeros((G, M0, C), np.float32), np.zeros((G, M0), np.int64),
                             np.zeros((G, M0, C), np.int64))
-    passign = first_argmin(parent_distances(keys, pg, dt))  # quantizer.py:211
-    csel = children[hidx[:, None], passign]  # [G,S,C,D] (quantizer.py:217-222)
-    cassign = first_argmin(child_distances(keys, csel, dt))  # quantizer.py:227
+    # quantizer.py:211 and :217-227, in blocks of keys so that the [G, block, M0]
+    # distances stay small (every key's argmin depends on that key alone)
+    blk = max(1, (1 << 24) // max(1, G * M0))
+    passign = np.empty((G, S), np.int64)
+    cassign = np.empty((G, S), np.int64)
+    for s0 in range(0, S, blk):
+        kb = keys[:, s0:s0 + blk]
+        pa = first_argmin(parent_distances(kb, pg, dt))
+        csel = children[hidx[:, None], pa]  # [G,blk,C,D]
+        passign[:, s0:s0 + blk] = pa
+        cassign[:, s0:s0 + blk] = first_argmin(child_distances(kb, csel, dt))
     pagg = sequential_bucket_sums(values, passign, M0, dt)  # quantizer.py:242-244
     flat_child = passign * C + cassign  # quantizer.py:256
     cagg = sequential_bucket_sums(values, flat_child, M0 * C, dt).reshape(G, M0, C, D)

@@ -25,6 +25,19 @@ def normrel(a: np.ndarray, b: np.ndarray) -> float:
     return float(np.linalg.norm(a - b) / den) if den > 0 else float(np.linalg.norm(a - b))
 
 
+def finite_normrel(got: np.ndarray, want: np.ndarray, tag: str = "") -> tuple[float, int]:
+    """Normwise error over the finite entries, after checking that both sides
+    have their non-finite entries (the reference's own NaN/inf outputs, e.g.
+    fp16 overflow) in the same places; returns (error, non-finite rows)."""
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    bad_g, bad_w = ~np.isfinite(got), ~np.isfinite(want)
+    assert np.array_equal(bad_g, bad_w), (f"{tag}: non-finite outputs differ: {int(bad_g.sum())} on the GPU, "
+                                          f"{int(bad_w.sum())} in the oracle")
+    keep = ~bad_g
+    return normrel(got[keep], want[keep]), int(bad_g.reshape(-1, got.shape[-1]).any(-1).sum())
+
+
 def to_dev(x: np.ndarray, dt: str, device="cuda") -> torch.Tensor:
     return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(device=device, dtype=TD[dt])
 

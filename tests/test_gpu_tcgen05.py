@@ -44,9 +44,25 @@ CASES = [
              seed=49),
     Workload("m440_d64_bf16", B=1, T=130, S=2048, H=2, D=64, M0=440, C=4, P=16, dtype="bf16", keys="aniso",
              seed=50),
-    # the largest parent count of the tcgen05 parent attention (32 chunks, one CTA per SM)
+    # one CTA per SM: 32 and 64 parent chunks
     Workload("m2048_bf16", B=1, T=160, S=4096, H=1, D=128, M0=2048, C=4, P=64, dtype="bf16", keys="mixture",
              seed=48),
+    Workload("m4096_bf16", B=1, T=130, S=8192, H=1, D=128, M0=4096, C=8, P=128, dtype="bf16", keys="mixture",
+             seed=59),
+    # the HVAQ rescaling pass on tcgen05: fp16 with three routing passes (the
+    # long-context multi-pass shape, reduced), D = 128 (one CTA per SM), a
+    # budget filling the gathered 64-row tile, and one above it (both passes
+    # then run on the mma.sync kernels)
+    Workload("mp_hvaq_f16", B=2, T=300, S=2048, H=2, D=64, M0=256, C=4, P=48, dtype="f16", keys="student_t",
+             seed=60, passes=3, pass_decay=0.5, hvaq=True),
+    Workload("hvaq_d128_bf16", B=1, T=200, S=1500, H=2, D=128, M0=192, C=4, P=24, dtype="bf16", keys="mixture",
+             seed=61, hvaq=True),
+    Workload("hvaq_p64_f16", B=1, T=129, S=1200, H=2, D=64, M0=128, C=8, P=64, dtype="f16", keys="aniso", seed=62,
+             hvaq=True, passes=2, pass_decay=0.5),
+    Workload("hvaq_p80_bf16", B=1, T=100, S=1200, H=2, D=64, M0=128, C=4, P=80, dtype="bf16", keys="mixture",
+             seed=63, hvaq=True),
+    # the fp16 correction with eight children and D = 128 (two bf16 value planes)
+    Workload("f16_c8_d128", B=2, T=257, S=2000, H=2, D=128, M0=160, C=8, P=20, dtype="f16", keys="aniso", seed=64),
 ]
 
 
