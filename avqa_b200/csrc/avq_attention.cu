@@ -579,6 +579,7 @@ struct FwdWorkspace {
   void* slog;  // tensor-core path: logits scratch when not in shared memory (or kept for HVAQ)
   void* exptab;  // tcgen05 path: the bf16 exponential table
   void* cdesc;   // tcgen05 correction: slot descriptors
+  void* dlog;    // decode path: the [G, M0] dtype logits of the step's queries
   size_t bytes;
 };
 
@@ -589,7 +590,24 @@ bool forward_uses_mma(int dtype, int D, int M0, int C) {
 // Layout of the caller's workspace.  The exact path keeps fp32 logits
 // [G,T,M0]; the tensor-core path keeps dtype logits only when they do not fit
 // in shared memory or must survive for the HVAQ pass.
-static FwdWorkspace carve(void* base, int dtype, int G, int T, int D, int M0, int C, int sel_stride, int hvaq) {
+static FwdWorkspace carve(void* base, int dtype, int G, int T, int D, int M0, int C, int P, int passes,
+                          int sel_stride, int hvaq) {
+  if (decode_forward_ok(dtype, T, D, M0, C, P, passes, hvaq)) {
+    // one query per (b,h): logits, the exponential table, the selection
+    char* p = (char*)base;
+    FwdWorkspace w{};
+    auto take = [&](size_t n) {
+      char* r = p;
+      p += align_up(n);
+      return (void*)r;
+    };
+    w.dlog = take(decode_logits_bytes(G, M0));
+    w.exptab = take(parent_attn_tc_table_bytes());
+    w.sel = (int*)take(sizeof(int) * (long)G * sel_stride);
+    w.pass_cnt = (int*)take(sizeof(int) * MAX_PASSES);
+    w.bytes = (size_t)(p - (char*)base);
+    return w;
+  }
   const bool mma = forward_uses_mma(dtype, D, M0, C);
   const int rows = mma ? PM_ROWS_PUBLIC : PA_ROWS;
   const int nqt = (T + rows - 1) / rows;
@@ -616,13 +634,14 @@ static FwdWorkspace carve(void* base, int dtype, int G, int T, int D, int M0, in
   w.pass_cnt = (int*)take(sizeof(int) * MAX_PASSES);
   w.exptab = mma ? take(parent_attn_tc_table_bytes()) : nullptr;
   w.cdesc = (mma && (C == 4 || C == 8)) ? take(correct_tc_desc_bytes(G, sel_stride, C)) : nullptr;
+  w.dlog = nullptr;
   w.bytes = (size_t)(p - (char*)base);
   return w;
 }
 
 size_t forward_workspace_bytes(int dtype, int G, int T, int D, int M0, int C, int P, int passes, float decay,
                                int hvaq) {
-  return carve(nullptr, dtype, G, T, D, M0, C, selection_stride(P, passes, decay), hvaq).bytes;
+  return carve(nullptr, dtype, G, T, D, M0, C, P, passes, selection_stride(P, passes, decay), hvaq).bytes;
 }
 
 // Groups of the quantized state (see ForwardArgs::state_groups).
@@ -658,8 +677,15 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
   const bool qaligned = ((uintptr_t)a.q % 16 == 0) && a.qs.s % 8 == 0 && a.qs.h % 8 == 0 && a.qs.b % 8 == 0;
   const bool mma = forward_uses_mma(DT, a.D, a.M0, a.C);
   if (mma && !qaligned) return AVQ_ERR_UNSUPPORTED;
-  FwdWorkspace w = carve(a.workspace, DT, G, a.T, a.D, a.M0, a.C, sel_stride, a.hvaq);
+  FwdWorkspace w = carve(a.workspace, DT, G, a.T, a.D, a.M0, a.C, a.P, a.passes, sel_stride, a.hvaq);
   if (a.workspace_bytes < w.bytes) return AVQ_ERR_WORKSPACE;
+  if constexpr (DT != DT_F32) {
+    if (w.dlog) {  // a decode step: one query per (b,h)
+      if (DT == DT_BF16) launch_exp_table(w.exptab, st);
+      return launch_decode_forward<DT>(a, w.dlog, w.exptab, a.selected_out, sel_stride, a.pass_counts_out,
+                                       a.importance_out, st);
+    }
+  }
   PassLayout lay;
   lay.n = a.passes;
   pass_budget_caps(a.P, a.passes, a.pass_decay, lay.cap);

@@ -29,7 +29,8 @@ from avqa_b200 import ops
 from avqa_b200.codebook import codebook_from_keys
 from avqa_b200.workloads import TORCH_DTYPE, WORKLOADS, Workload, make_decode_tokens, make_inputs
 from oracle import avq_oracle as O
-from parity import OUT_TOL, check_quantization, check_routing, finite_normrel, quant_from_arrays
+from parity import (OUT_TOL, check_quantization, check_routing, check_routing_single_query, finite_normrel,
+                    quant_from_arrays)
 
 pytestmark = pytest.mark.gpu
 
@@ -188,7 +189,7 @@ def test_c3_decode_full_size() -> None:
                          ("pcnt", exact.parent_counts), ("ccnt", exact.child_counts)):
             np.testing.assert_array_equal(sq[key], ref, err_msg=f"c3 step {step} {key}")
         res = O.forward_heads(qn, kg, vg, pd, cd, _cfg(w), quant=exact, budget_floor=floor)
-        check_routing(_slice_diag(diag, hh), res, w.dtype, tag=f"c3 step {step}")
+        check_routing_single_query(_slice_diag(diag, hh), res, qn, pd, 1, w.dtype, tag=f"c3 step {step}")
         err, _ = finite_normrel(_np(out[:, hh]), res["out"], f"c3 step {step}")
         _report(f"c3 h={hh} step={step}", prior_assignment_flips=flips, keys=int(kg.shape[1]),
                 output_normwise=err, budget_floor=floor)
