@@ -32,8 +32,9 @@ _SIGS = {
     "avq_forward_workspace_size": ([_I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I], _Z),
     "avq_forward": ([_I, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I, _I, _F, _I, _F, _F,
                      _P, _P, _P, _P, _P, _P, _Z, _P], _I),
+    "avq_append_workspace_size": ([_I, _I, _I], _Z),
     "avq_append": ([_I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                    _P, _I, _P], _I),
+                    _P, _I, _P, _Z, _P], _I),
     "avq_reduce_min": ([_P, _I, _P, _P], _I),
     "avq_device_fault": ([_P, _P], _I),
     "avq_quantize_noalloc": ([_I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,

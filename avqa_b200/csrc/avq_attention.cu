@@ -601,7 +601,7 @@ static FwdWorkspace carve(void* base, int dtype, int G, int T, int D, int M0, in
       p += align_up(n);
       return (void*)r;
     };
-    w.dlog = take(decode_logits_bytes(G, M0));
+    w.dlog = take(decode_work_bytes(G, M0, P));
     w.exptab = take(parent_attn_tc_table_bytes());
     w.sel = (int*)take(sizeof(int) * (long)G * sel_stride);
     w.pass_cnt = (int*)take(sizeof(int) * MAX_PASSES);

@@ -194,11 +194,16 @@ int avq_forward(int dtype, const void* q, const long long* q_strides, int B, int
   return finish(rc, "avq_forward");
 }
 
+size_t avq_append_workspace_size(int B, int H, int Tn) {
+  if (B < 0 || H <= 0 || Tn < 0 || too_many_groups(B, H)) return 0;
+  return avq::append_workspace_bytes(B, H, Tn);
+}
+
 int avq_append(int dtype, const void* k, const long long* k_strides, const void* v, const long long* v_strides,
                int B, int H, int Tn, int D, int M0, int C, const void* parents_dt, const float* p_sq,
                const void* children_dt, const float* c_sq, float* pacc, float* cacc, void* pagg, void* cagg,
                int* pcnt, int* ccnt, int* nvalid, void* kpage, void* vpage, const long long* page_strides, int slot0,
-               void* stream) {
+               void* workspace, size_t workspace_bytes, void* stream) {
   if (bad_dtype(dtype)) return fail(AVQ_ERR_ARG, "avq_append: bad dtype %d", dtype);
   if (B < 0 || H <= 0 || Tn < 0 || D <= 0 || M0 <= 0 || C <= 0) return fail(AVQ_ERR_ARG, "avq_append: bad sizes");
   if (!k || !v || !k_strides || !v_strides || !parents_dt || !p_sq || !children_dt || !c_sq || !pacc || !cacc ||
@@ -207,9 +212,12 @@ int avq_append(int dtype, const void* k, const long long* k_strides, const void*
   if ((kpage == nullptr) != (vpage == nullptr) || (kpage && !page_strides))
     return fail(AVQ_ERR_ARG, "avq_append: kpage, vpage and page_strides go together");
   if (too_many_groups(B, H)) return fail(AVQ_ERR_ARG, "avq_append: B*H = %lld exceeds INT_MAX", (long long)B * H);
+  if (workspace_bytes < avq::append_workspace_bytes(B, H, Tn) || !workspace)
+    return fail(AVQ_ERR_WORKSPACE, "avq_append: workspace %zu < %zu bytes", workspace_bytes,
+                avq::append_workspace_bytes(B, H, Tn));
   avq::AppendArgs a{k, st3(k_strides), v, st3(v_strides), B, H, Tn, D, M0, C, parents_dt, p_sq, children_dt, c_sq,
                     pacc, cacc, pagg, cagg, pcnt, ccnt, nvalid, kpage, vpage,
-                    kpage ? st3(page_strides) : avq::Strides3{0, 0, 0}, slot0};
+                    kpage ? st3(page_strides) : avq::Strides3{0, 0, 0}, slot0, workspace, workspace_bytes};
   cudaStream_t st = (cudaStream_t)stream;
   int rc;
   switch (dtype) {

@@ -126,54 +126,42 @@ __global__ void __launch_bounds__(256) decode_logits_kernel(const typename Stora
   }
 }
 
-// Shared memory of decode_attn_kernel, in bytes.
-__host__ __device__ inline size_t decode_attn_smem(int D, int M0, int P) {
+// Shared memory of decode_route_kernel, in bytes.
+__host__ __device__ inline size_t decode_route_smem(int M0) {
   int npow2 = 1;
   while (npow2 < M0) npow2 <<= 1;
-  return (size_t)npow2 * 8                 // keys
-         + (size_t)M0 * 4                  // e
-         + (size_t)DA_WARPS * D * 4 * 2    // warp partials (two sets)
-         + (size_t)D * 4 * 2               // q, a
-         + (size_t)P * 4                   // selection
-         + (size_t)DA_WARPS * 2 * 8 + 64;  // scalar partials
+  return (size_t)npow2 * 8 + (size_t)M0 * 4 + 64;
 }
 
-template <int DT, int D>
-__global__ void __launch_bounds__(DA_THREADS, 4) decode_attn_kernel(
-    const typename Storage<DT>::T* __restrict__ logits, const typename Storage<DT>::T* __restrict__ q, Strides3 qs,
-    int H, int M0, int C, float sqrtD, const typename Storage<DT>::T* __restrict__ children,
-    const typename Storage<DT>::T* __restrict__ pagg, const typename Storage<DT>::T* __restrict__ cagg,
-    const int* __restrict__ pcnt, const int* __restrict__ ccnt, int sG, const int* __restrict__ min_valid, int P,
-    const uint16_t* __restrict__ exptab, float* __restrict__ out, Strides3 os, float* __restrict__ importance_out,
+// Per (b,h): row max, e = DT(exp(DT(s - m))), l, z, p = DT(e / max(z, eps)),
+// w = DT(n p) and the stable top-P.  Writes e [G, M0] fp32, the row's
+// (m, l, max(z, eps)) and the selection for decode_value_kernel.
+template <int DT>
+__global__ void __launch_bounds__(DA_THREADS) decode_route_kernel(
+    const typename Storage<DT>::T* __restrict__ logits, int M0, const int* __restrict__ pcnt, int sG,
+    const int* __restrict__ min_valid, int P, const uint16_t* __restrict__ exptab, float* __restrict__ ework,
+    float* __restrict__ rowstat, int* __restrict__ selwork, float* __restrict__ importance_out,
     int* __restrict__ sel_out, int sel_stride, int* __restrict__ pass_cnt_out) {
-  using T = typename Storage<DT>::T;
-  constexpr int EPL = D / 32;  // elements per lane of a D-row
   extern __shared__ __align__(128) unsigned char smem_raw[];
   int npow2 = 1;
   while (npow2 < M0) npow2 <<= 1;
   unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw);  // [npow2]
   float* ev = reinterpret_cast<float*>(keys + npow2);                          // [M0]
-  float* red0 = ev + M0;                                                       // [DA_WARPS][D]
-  float* red1 = red0 + DA_WARPS * D;                                           // [DA_WARPS][D]
-  float* qv = red1 + DA_WARPS * D;                                             // [D]
-  float* av = qv + D;                                                          // [D]
-  int* sel = reinterpret_cast<int*>(av + D);                                   // [P]
-  double* dred = reinterpret_cast<double*>(((uintptr_t)(sel + P) + 7) & ~(uintptr_t)7);  // [2][DA_WARPS]
   __shared__ float fred[DA_WARPS];
+  __shared__ double dred[2][DA_WARPS];
   __shared__ int sbudget;
-  const int g = blockIdx.x, b = g / H, h = g % H, gs = g % sG;
+  const int g = blockIdx.x, gs = g % sG;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const T* lrow = logits + (long)g * M0;
+  const auto* lrow = logits + (long)g * M0;
   const int* cnt_p = pcnt + (long)gs * M0;
 
-  // ---- logits, row max (pipeline.py:137-141) ----
+  // row max (pipeline.py:137-141)
   float mx = -INFINITY;
   for (int p = tid; p < M0; p += DA_THREADS) {
     const float s = to_f(lrow[p]);
     ev[p] = s;
     mx = fmax_nan_f(mx, s);
   }
-  for (int d = tid; d < D; d += DA_THREADS) qv[d] = to_f(q[(long)b * qs.b + (long)h * qs.h + d]);
   for (int o = 16; o > 0; o >>= 1) mx = fmax_nan_f(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if (lane == 0) fred[warp] = mx;
   __syncthreads();
@@ -181,68 +169,33 @@ __global__ void __launch_bounds__(DA_THREADS, 4) decode_attn_kernel(
   for (int w = 1; w < DA_WARPS; ++w) mx = fmax_nan_f(mx, fred[w]);
   const float safe = mx == -INFINITY ? 0.f : mx;
 
-  // ---- e = DT(exp(DT(s - m))), l = sum DT(e n), z = sum e (pipeline.py:142-150) ----
+  // e = DT(exp(DT(s - m))), l = sum DT(e n), z = sum e (pipeline.py:142-150)
   double lz = 0.0, zz = 0.0;
   for (int p = tid; p < M0; p += DA_THREADS) {
     const float e = exp_of_diff<DT>(rnd<DT>(__fsub_rn(ev[p], safe)), exptab);
     lz += (double)rnd<DT>(__fmul_rn(e, count_dt<DT>(cnt_p[p])));
     zz += (double)e;
     ev[p] = e;
+    ework[(long)g * M0 + p] = e;
   }
   for (int o = 16; o > 0; o >>= 1) {
     lz += __shfl_xor_sync(0xffffffffu, lz, o);
     zz += __shfl_xor_sync(0xffffffffu, zz, o);
   }
   if (lane == 0) {
-    dred[warp] = lz;
-    dred[DA_WARPS + warp] = zz;
+    dred[0][warp] = lz;
+    dred[1][warp] = zz;
   }
-  __syncthreads();  // also: every e is in ev
+  __syncthreads();
   double lt = 0.0, zt = 0.0;
   for (int w = 0; w < DA_WARPS; ++w) {
-    lt += dred[w];
-    zt += dred[DA_WARPS + w];
+    lt += dred[0][w];
+    zt += dred[1][w];
   }
-  const float l0 = rnd64<DT>(lt), z0 = rnd64<DT>(zt);
-  const float zc = clamp_min_nan(z0, eps_dt<DT>());
+  const float zc = clamp_min_nan(rnd64<DT>(zt), eps_dt<DT>());
 
-  // ---- a = DT(e @ V) (pipeline.py:147): every parent row once, fp32 sums ----
-  {
-    float acc[EPL];
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
-    // each lane holds EPL consecutive elements (EPL/2 packed pairs) of a row;
-    // U rows per warp are loaded before they are used
-    const T* vb = pagg + (long)gs * M0 * D + lane * EPL;
-    constexpr int U = 8, NW = EPL / 2;
-    for (int p0 = warp; p0 < M0; p0 += DA_WARPS * U) {
-      uint32_t vr[U][NW];
-      float ew[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int p = p0 + u * DA_WARPS;
-        ew[u] = p < M0 ? ev[p] : 0.f;
-        if constexpr (NW == 2) {
-          const uint2 x = p < M0 ? __ldcs(reinterpret_cast<const uint2*>(vb + (long)p * D)) : make_uint2(0u, 0u);
-          vr[u][0] = x.x;
-          vr[u][1] = x.y;
-        } else {
-          vr[u][0] = p < M0 ? __ldcs(reinterpret_cast<const unsigned int*>(vb + (long)p * D)) : 0u;
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-#pragma unroll
-        for (int e = 0; e < NW; ++e) {
-          acc[2 * e] = fmaf(ew[u], half_lo<DT>(vr[u][e]), acc[2 * e]);
-          acc[2 * e + 1] = fmaf(ew[u], half_hi<DT>(vr[u][e]), acc[2 * e + 1]);
-        }
-    }
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) red0[warp * D + lane * EPL + e] = acc[e];
-  }
-
-  // ---- importance w = DT(n * p), p = DT(e / max(z, eps)) (routing.py:61-63) ----
+  // importance w = DT(n * p), p = DT(e / max(z, eps)) (routing.py:61-63; one
+  // query, so its sum over queries is p itself)
   for (int p = tid; p < npow2; p += DA_THREADS) {
     if (p < M0) {
       const float pr = rnd<DT>(__fdiv_rn(ev[p], zc));
@@ -257,14 +210,14 @@ __global__ void __launch_bounds__(DA_THREADS, 4) decode_attn_kernel(
     const int bud = min(P, *min_valid);  // pipeline.py:340-343
     sbudget = bud;
     if (g == 0 && pass_cnt_out) pass_cnt_out[0] = bud;
+    float* rs = rowstat + (long)g * 4;
+    rs[0] = safe;
+    rs[1] = rnd64<DT>(lt);
+    rs[2] = zc;
+    rs[3] = __int_as_float(bud);
   }
   __syncthreads();
-  for (int d = tid; d < D; d += DA_THREADS) {
-    float s = 0.f;
-    for (int w = 0; w < DA_WARPS; ++w) s += red0[w * D + d];
-    av[d] = rnd<DT>(s);
-  }
-  // ---- stable descending top-k (routing.py:152-170): bitonic sort ----
+  // stable descending top-k (routing.py:152-170): bitonic sort of packed keys
   for (int k = 2; k <= npow2; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
       for (int i = tid; i < npow2; i += DA_THREADS) {
@@ -284,107 +237,199 @@ __global__ void __launch_bounds__(DA_THREADS, 4) decode_attn_kernel(
   const int budget = sbudget;
   for (int j = tid; j < P; j += DA_THREADS) {
     const int p = j < budget ? (int)(keys[j] & 0xffffffffu) : -1;
-    if (j < budget) sel[j] = p;
+    selwork[(long)g * P + j] = p;
     if (sel_out) sel_out[(long)g * sel_stride + j] = p;
   }
-  __syncthreads();
+}
 
-  // ---- correction (refinement.py:165-304, attention.py:149-158) ----
-  // slot s = j (1 + C) + k: k = 0 the selected parent j (removed), k > 0 its
-  // child k - 1 (added); a warp per slot
+// Loads EPL consecutive 16-bit elements (8 or 4 bytes) of a row as floats.
+template <int DT, int EPL>
+__device__ __forceinline__ void load_row_part(const typename Storage<DT>::T* p, float (&x)[EPL]) {
+  if constexpr (EPL == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    x[0] = half_lo<DT>(u.x);
+    x[1] = half_hi<DT>(u.x);
+    x[2] = half_lo<DT>(u.y);
+    x[3] = half_hi<DT>(u.y);
+  } else {
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(p);
+    x[0] = half_lo<DT>(u);
+    x[1] = half_hi<DT>(u);
+  }
+}
+
+// Per (b,h): a = DT(e @ V) streamed from HBM (pipeline.py:147), then the child
+// correction of the selected parents (refinement.py:165-304,
+// attention.py:149-158) and out = a' / max(l', 1e-12).  Slot s of the
+// correction is j (1 + C) + k: k = 0 the selected parent j (removed with
+// weight exp(p - m) n), k > 0 its child k - 1 (added with exp(u - m) n_c).
+template <int DT, int D>
+__global__ void __launch_bounds__(DA_THREADS, 3) decode_value_kernel(
+    const typename Storage<DT>::T* __restrict__ q, Strides3 qs, int H, int M0, int C, float sqrtD,
+    const typename Storage<DT>::T* __restrict__ children, const typename Storage<DT>::T* __restrict__ pagg,
+    const typename Storage<DT>::T* __restrict__ cagg, const int* __restrict__ pcnt, const int* __restrict__ ccnt,
+    int sG, const float* __restrict__ ework, const float* __restrict__ rowstat, const int* __restrict__ selwork,
+    int P, float* __restrict__ out, Strides3 os) {
+  using T = typename Storage<DT>::T;
+  constexpr int EPL = D / 32;  // elements per lane of a D-row
+  __shared__ float red0[DA_WARPS][D], red1[DA_WARPS][D];
+  __shared__ float sl[DA_WARPS][2];
+  const int g = blockIdx.x, b = g / H, h = g % H, gs = g % sG;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float* er = ework + (long)g * M0;
+  const float safe = rowstat[(long)g * 4], l0 = rowstat[(long)g * 4 + 1], zc = rowstat[(long)g * 4 + 2];
+  const int budget = __float_as_int(rowstat[(long)g * 4 + 3]);
+
+  // ---- a = sum_p e_p V_p: eight rows per warp in flight ----
+  float acc[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+  {
+    const T* vb = pagg + (long)gs * M0 * D + lane * EPL;
+    constexpr int U = 8;
+    for (int p0 = warp; p0 < M0; p0 += DA_WARPS * U) {
+      float x[U][EPL], ew[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int p = p0 + u * DA_WARPS;
+        ew[u] = p < M0 ? er[p] : 0.f;
+        if (p < M0) {
+          load_row_part<DT, EPL>(vb + (long)p * D, x[u]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) x[u][e] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[e] = fmaf(ew[u], x[u][e], acc[e]);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) red0[warp][lane * EPL + e] = acc[e];
+
+  // ---- correction ----
+  const float inv_sqrtD = 1.f / sqrtD;
+  float ql[EPL];
+  load_row_part<DT, EPL>(q + (long)b * qs.b + (long)h * qs.h + lane * EPL, ql);
+  const int* sg = selwork + (long)g * P;
   float rl = 0.f, al = 0.f, ra[EPL], aa[EPL];
 #pragma unroll
   for (int e = 0; e < EPL; ++e) ra[e] = aa[e] = 0.f;
-  const float inv_sqrtD = 1.f / sqrtD;
-  const int nslots = budget * (1 + C);
-  float ql[EPL];
+  // a warp per selected parent: its parent-sum row, its C child codeword rows
+  // and child-sum rows are all loaded (packed, EPL/2 words per lane) before
+  // any is used
+  constexpr int NW = EPL / 2, CM = 8;
+  for (int j = warp; j < budget; j += DA_WARPS) {
+    const int p = sg[j];
+    uint32_t pv[NW], cr[CM][NW], cv[CM][NW];
+    const long prow = (long)gs * M0 + p;
+    const int np = pcnt[prow];
+    const int nc = lane < C ? ccnt[prow * C + lane] : 0;
+    const T* pr_ = pagg + prow * D + lane * EPL;
+    if constexpr (NW == 2) {
+      const uint2 u = *reinterpret_cast<const uint2*>(pr_);
+      pv[0] = u.x;
+      pv[1] = u.y;
+    } else {
+      pv[0] = *reinterpret_cast<const uint32_t*>(pr_);
+    }
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) ql[e] = qv[lane * EPL + e];
-  constexpr int SU = 4;  // slots per warp in flight
-  for (int s0 = warp; s0 < nslots; s0 += DA_WARPS * SU) {
-    float lr[SU][EPL], vr[SU][EPL];  // logit row (a child), value row
-    int kind[SU], pp[SU], n[SU];     // kind: -1 none, 0 parent, 1 child
-#pragma unroll
-    for (int u = 0; u < SU; ++u) {
-      const int s = s0 + u * DA_WARPS;
-      kind[u] = -1;
-      if (s < nslots) {
-        const int j = s / (1 + C), k = s % (1 + C), p = sel[j];
-        pp[u] = p;
-        const T* vrow_p;
-        if (k == 0) {
-          kind[u] = 0;
-          n[u] = cnt_p[p];
-          vrow_p = pagg + ((long)gs * M0 + p) * D;
+    for (int c = 0; c < CM; ++c) {
+      if (c < C) {
+        const T* a_ = children + (((long)h * M0 + p) * C + c) * D + lane * EPL;
+        const T* b_ = cagg + (prow * C + c) * D + lane * EPL;
+        if constexpr (NW == 2) {
+          const uint2 u = *reinterpret_cast<const uint2*>(a_), w = *reinterpret_cast<const uint2*>(b_);
+          cr[c][0] = u.x;
+          cr[c][1] = u.y;
+          cv[c][0] = w.x;
+          cv[c][1] = w.y;
         } else {
-          kind[u] = 1;
-          const long crow = ((long)h * M0 + p) * C + (k - 1), vrow = ((long)gs * M0 + p) * C + (k - 1);
-          n[u] = ccnt[vrow];
-          vrow_p = cagg + vrow * D;
-          const T* cr = children + crow * D + lane * EPL;
-#pragma unroll
-          for (int e = 0; e < EPL; ++e) lr[u][e] = to_f(cr[e]);
+          cr[c][0] = *reinterpret_cast<const uint32_t*>(a_);
+          cv[c][0] = *reinterpret_cast<const uint32_t*>(b_);
         }
-        const T* vrl = vrow_p + lane * EPL;
+      } else {
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) vr[u][e] = to_f(vrl[e]);
+        for (int e = 0; e < NW; ++e) cr[c][e] = cv[c][e] = 0u;
       }
     }
-    float dot[SU];
+    float dot[CM];
 #pragma unroll
-    for (int u = 0; u < SU; ++u) {
-      dot[u] = 0.f;
-      if (kind[u] == 1) {
+    for (int c = 0; c < CM; ++c) {
+      dot[c] = 0.f;
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) dot[u] = fmaf(ql[e], lr[u][e], dot[u]);
+      for (int e = 0; e < NW; ++e) {
+        dot[c] = fmaf(ql[2 * e], half_lo<DT>(cr[c][e]), dot[c]);
+        dot[c] = fmaf(ql[2 * e + 1], half_hi<DT>(cr[c][e]), dot[c]);
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-      for (int u = 0; u < SU; ++u) dot[u] += __shfl_xor_sync(0xffffffffu, dot[u], o);
+      for (int c = 0; c < CM; ++c)
+        if (c < C) dot[c] += __shfl_xor_sync(0xffffffffu, dot[c], o);
+    // the removed parent: exp(p - m) n with p its probability (refinement.py:233,335)
+    const float prb = rnd<DT>(__fdiv_rn(er[p], zc));
+    const float wp = __fmul_rn(expf(__fsub_rn(prb, safe)), count_dt<DT>(np));
+    rl += wp;
 #pragma unroll
-    for (int u = 0; u < SU; ++u) {
-      if (kind[u] == 0) {
-        const float pr = rnd<DT>(__fdiv_rn(ev[pp[u]], zc));
-        const float w = __fmul_rn(expf(__fsub_rn(pr, safe)), count_dt<DT>(n[u]));  // refinement.py:335
-        rl += w;
+    for (int e = 0; e < NW; ++e) {
+      ra[2 * e] = fmaf(wp, half_lo<DT>(pv[e]), ra[2 * e]);
+      ra[2 * e + 1] = fmaf(wp, half_hi<DT>(pv[e]), ra[2 * e + 1]);
+    }
+    // its children: u = DT(DT(q.c) / sqrt(D)), -inf for an empty child
+    // (pipeline.py:184-189), weight exp(u - m) n_c (refinement.py:341-343)
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) ra[e] = fmaf(w, vr[u][e], ra[e]);
-      } else if (kind[u] == 1) {
-        // pipeline.py:184-189: u = DT(DT(q.c) / sqrt(D)), -inf for an empty child
-        const float lg = n[u] > 0 ? scale_logit<DT>(rnd<DT>(dot[u]), sqrtD, inv_sqrtD) : -INFINITY;
-        const float w = __fmul_rn(expf(__fsub_rn(lg, safe)), count_dt<DT>(n[u]));  // refinement.py:341-343
+    for (int c = 0; c < CM; ++c) {
+      if (c < C) {
+        const int n = __shfl_sync(0xffffffffu, nc, c);
+        const float lg = n > 0 ? scale_logit<DT>(rnd<DT>(dot[c]), sqrtD, inv_sqrtD) : -INFINITY;
+        const float w = __fmul_rn(expf(__fsub_rn(lg, safe)), count_dt<DT>(n));
         al += w;
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) aa[e] = fmaf(w, vr[u][e], aa[e]);
+        for (int e = 0; e < NW; ++e) {
+          aa[2 * e] = fmaf(w, half_lo<DT>(cv[c][e]), aa[2 * e]);
+          aa[2 * e + 1] = fmaf(w, half_hi<DT>(cv[c][e]), aa[2 * e + 1]);
+        }
       }
     }
   }
+  __syncthreads();  // red0 holds the value sums
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) {
-    red0[warp * D + lane * EPL + e] = ra[e];
-    red1[warp * D + lane * EPL + e] = aa[e];
-  }
+  for (int e = 0; e < EPL; ++e) red1[warp][lane * EPL + e] = ra[e];
   if (lane == 0) {
-    dred[warp] = (double)rl;
-    dred[DA_WARPS + warp] = (double)al;
+    sl[warp][0] = rl;
+    sl[warp][1] = al;
   }
   __syncthreads();
   float rlt = 0.f, alt = 0.f;
   for (int w = 0; w < DA_WARPS; ++w) {
-    rlt += (float)dred[w];
-    alt += (float)dred[DA_WARPS + w];
+    rlt += sl[w][0];
+    alt += sl[w][1];
   }
   const float l1 = __fadd_rn(__fsub_rn(l0, rlt), alt);  // OnlineSoftmaxState.replace, unit scales
   const float den = clamp_min_nan(l1, 1e-12f);           // attention_module.py:532-535
+  // a = DT(e @ V) and the removed parents' sums per column (each column is
+  // read and rewritten by one thread); then the children's sums go through red1
   for (int d = tid; d < D; d += DA_THREADS) {
-    float rs = 0.f, as = 0.f;
+    float s = 0.f, rs = 0.f;
     for (int w = 0; w < DA_WARPS; ++w) {
-      rs += red0[w * D + d];
-      as += red1[w * D + d];
+      s += red0[w][d];
+      rs += red1[w][d];
     }
-    const float a1 = __fadd_rn(__fsub_rn(av[d], rs), as);
+    red0[0][d] = rnd<DT>(s);
+    red0[1][d] = rs;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) red1[warp][lane * EPL + e] = aa[e];
+  __syncthreads();
+  for (int d = tid; d < D; d += DA_THREADS) {
+    float as = 0.f;
+    for (int w = 0; w < DA_WARPS; ++w) as += red1[w][d];
+    const float a1 = __fadd_rn(__fsub_rn(red0[0][d], red0[1][d]), as);
     out[(long)b * os.b + (long)h * os.h + d] = __fdiv_rn(a1, den);
   }
 }
@@ -400,36 +445,53 @@ bool decode_forward_ok(int dt, int T, int D, int M0, int C, int P, int passes, i
          M0 <= 4096 && P <= 1024;
 }
 
-size_t decode_logits_bytes(int G, int M0) { return (size_t)G * M0 * 2; }
+size_t decode_work_bytes(int G, int M0, int P) {
+  return align_up((size_t)G * M0 * 2) + align_up((size_t)G * M0 * 4) + align_up((size_t)G * 16) +
+         align_up((size_t)G * P * 4);
+}
 
 template <int DT>
-int launch_decode_forward(const ForwardArgs& a, void* dlog, const void* exptab, int* sel, int sel_stride,
+int launch_decode_forward(const ForwardArgs& a, void* work, const void* exptab, int* sel, int sel_stride,
                           int* pass_cnt, float* importance, cudaStream_t st) {
   using T = typename Storage<DT>::T;
   const int G = a.B * a.H, D = a.D, sG = a.state_groups > 0 ? a.state_groups : G;
   if (((uintptr_t)a.q % 16) || a.qs.b % 8 || a.qs.h % 8) return AVQ_ERR_UNSUPPORTED;
+  // the workspace: logits [G, M0] dtype, e [G, M0] fp32, row statistics [G, 4], selection [G, P]
+  char* wp = static_cast<char*>(work);
+  T* dlog = reinterpret_cast<T*>(wp);
+  wp += align_up((size_t)G * a.M0 * 2);
+  float* ework = reinterpret_cast<float*>(wp);
+  wp += align_up((size_t)G * a.M0 * 4);
+  float* rowstat = reinterpret_cast<float*>(wp);
+  wp += align_up((size_t)G * 16);
+  int* selwork = reinterpret_cast<int*>(wp);
   const float sqrtD = (float)std::sqrt((double)D);
   const size_t lsm = (size_t)(DL_ROWS + DL_COLS) * (D + 8) * sizeof(T);
-  const size_t asm_ = decode_attn_smem(D, a.M0, a.P);
-  auto go = [&](auto lk, auto ak) {
+  const size_t rsm = decode_route_smem(a.M0);
+  auto go = [&](auto lk, auto vk) {
     {
       AVQ_TIMED("decode_logits", st);
       cudaFuncSetAttribute(lk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsm);
       lk<<<dim3(a.H, (a.M0 + DL_COLS - 1) / DL_COLS, (a.B + DL_ROWS - 1) / DL_ROWS), 256, lsm, st>>>(
           static_cast<const T*>(a.q), a.qs, a.B, a.H, a.M0, sqrtD, static_cast<const T*>(a.parents_dt), a.pcnt, sG,
-          static_cast<T*>(dlog));
+          dlog);
     }
     if (a.min_valid_ready) cudaStreamWaitEvent(st, static_cast<cudaEvent_t>(a.min_valid_ready), 0);
-    AVQ_TIMED("decode_attn", st);
-    cudaFuncSetAttribute(ak, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asm_);
-    ak<<<G, DA_THREADS, asm_, st>>>(static_cast<const T*>(dlog), static_cast<const T*>(a.q), a.qs, a.H, a.M0, a.C,
-                                    sqrtD, static_cast<const T*>(a.children_dt), static_cast<const T*>(a.pagg),
-                                    static_cast<const T*>(a.cagg), a.pcnt, a.ccnt, sG, a.min_valid, a.P,
-                                    static_cast<const uint16_t*>(exptab), a.out, a.os, importance, sel, sel_stride,
-                                    pass_cnt);
+    {
+      AVQ_TIMED("decode_route", st);
+      auto rk = decode_route_kernel<DT>;
+      cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
+      rk<<<G, DA_THREADS, rsm, st>>>(dlog, a.M0, a.pcnt, sG, a.min_valid, a.P, static_cast<const uint16_t*>(exptab),
+                                     ework, rowstat, selwork, importance, sel, sel_stride, pass_cnt);
+    }
+    AVQ_TIMED("decode_value", st);
+    vk<<<G, DA_THREADS, 0, st>>>(static_cast<const T*>(a.q), a.qs, a.H, a.M0, a.C, sqrtD,
+                                 static_cast<const T*>(a.children_dt), static_cast<const T*>(a.pagg),
+                                 static_cast<const T*>(a.cagg), a.pcnt, a.ccnt, sG, ework, rowstat, selwork, a.P,
+                                 a.out, a.os);
   };
-  if (D == 64) go(decode_logits_kernel<DT, 64>, decode_attn_kernel<DT, 64>);
-  else go(decode_logits_kernel<DT, 128>, decode_attn_kernel<DT, 128>);
+  if (D == 64) go(decode_logits_kernel<DT, 64>, decode_value_kernel<DT, 64>);
+  else go(decode_logits_kernel<DT, 128>, decode_value_kernel<DT, 128>);
   return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
 }
 

@@ -95,6 +95,8 @@ struct AppendArgs {
   void* vpage;
   Strides3 pgs;
   int slot0;
+  void* workspace = nullptr;  // append_workspace_bytes(B, H, Tn): the new keys' parents
+  size_t workspace_bytes = 0;
 };
 
 // Parent-attention pass of the tensor-core path (avq_attention_mma.cu).
@@ -201,13 +203,14 @@ int read_fault_correct(int* code, cudaStream_t st);
 
 template <int DT>
 int launch_append(const AppendArgs& a, cudaStream_t st);
+size_t append_workspace_bytes(int B, int H, int Tn);
 // Decode step (one query per (b,h), one routing pass, no HVAQ): per-head
 // logits on mma.sync, then one CTA per (b,h) for softmax, routing and the
 // child correction (avq_decode_attn.cu).
 bool decode_forward_ok(int dt, int T, int D, int M0, int C, int P, int passes, int hvaq);
-size_t decode_logits_bytes(int G, int M0);
+size_t decode_work_bytes(int G, int M0, int P);
 template <int DT>
-int launch_decode_forward(const ForwardArgs& a, void* dlog, const void* exptab, int* sel, int sel_stride,
+int launch_decode_forward(const ForwardArgs& a, void* work, const void* exptab, int* sel, int sel_stride,
                           int* pass_cnt, float* importance, cudaStream_t st);
 int launch_reduce_min(const int* v, int n, int* out, cudaStream_t st);
 

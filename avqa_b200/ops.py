@@ -129,12 +129,14 @@ def append(state: QuantState, k: torch.Tensor, v: torch.Tensor, cb: PreparedCode
     B, H, Tn, D = k.shape
     _, M0, C, _ = cb.dims
     dev = k.device
+    ws_bytes = lib.avq_append_workspace_size(B, H, Tn)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     rc = lib.avq_append(_lib.dtype_code(k.dtype), k.data_ptr(), _lib.strides3(k), v.data_ptr(), _lib.strides3(v),
                         B, H, Tn, D, M0, C, cb.parents.data_ptr(), cb.p_sq.data_ptr(), cb.children.data_ptr(),
                         cb.c_sq.data_ptr(), state.pacc.data_ptr(), state.cacc.data_ptr(), state.pagg.data_ptr(),
                         state.cagg.data_ptr(), state.pcnt.data_ptr(), state.ccnt.data_ptr(), state.nvalid.data_ptr(),
                         _lib.ptr(kpage), _lib.ptr(vpage), _lib.strides3(kpage) if kpage is not None else None,
-                        slot0, _lib.stream_of(dev))
+                        slot0, ws.data_ptr(), ws_bytes, _lib.stream_of(dev))
     _lib.check(rc, "avq_append")
     state.S += Tn
     state.passign = None  # per-key assignments are not tracked across appends

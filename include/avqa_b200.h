@@ -147,15 +147,19 @@ int avq_forward(int dtype, const void* q, const long long* q_strides, int B, int
                 float alpha, float* out, const long long* out_strides, float* importance_out, int* selected_out,
                 int* pass_counts_out, void* workspace, size_t workspace_bytes, void* stream);
 
+size_t avq_append_workspace_size(int B, int H, int Tn);
+
 /* Append Tn new tokens per (b,h) to a quantized key set, in order:
  * assign each new key, add its value to the fp32 bucket sums pacc/cacc,
  * refresh pagg/cagg, bump pcnt/ccnt/nvalid.  When kpage/vpage are not NULL
- * the raw k/v are also written to page slots slot0.. (page_strides). */
+ * the raw k/v are also written to page slots slot0.. (page_strides).
+ * workspace: avq_append_workspace_size(B, H, Tn) bytes (the new keys'
+ * parents, found on the tensor cores as the prefill quantizer finds them). */
 int avq_append(int dtype, const void* k, const long long* k_strides, const void* v, const long long* v_strides,
                int B, int H, int Tn, int D, int M0, int C, const void* parents_dt, const float* p_sq,
                const void* children_dt, const float* c_sq, float* pacc, float* cacc, void* pagg, void* cagg,
                int* pcnt, int* ccnt, int* nvalid, void* kpage, void* vpage, const long long* page_strides, int slot0,
-               void* stream);
+               void* workspace, size_t workspace_bytes, void* stream);
 
 /* *out = min(v[0..n)). */
 int avq_reduce_min(const int* v, int n, int* out, void* stream);

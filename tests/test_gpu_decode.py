@@ -66,7 +66,7 @@ def test_decode_matches_prefill_kernels_and_oracle(w: Workload) -> None:
     assert torch.equal(d_d.importance, d_p.importance)
     assert torch.equal(d_d.selected, d_p.selected)
     assert torch.equal(d_d.pass_counts, d_p.pass_counts)
-    assert normrel(out_d.cpu().numpy(), out_p.cpu().numpy()) < 1e-5
+    assert normrel(out_d.cpu().numpy(), out_p.cpu().numpy()) < 1e-4  # fp32 sums in different orders
     pd, cd = O.cast_codebook(cbk.parents.numpy(), cbk.children.numpy(), dt)
     cfg = oracle_config(dict(w.__dict__), "entropy", 1.0)
     res = O.forward(qn, kn, vn, pd, cd, cfg)

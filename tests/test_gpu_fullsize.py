@@ -29,8 +29,8 @@ from avqa_b200 import ops
 from avqa_b200.codebook import codebook_from_keys
 from avqa_b200.workloads import TORCH_DTYPE, WORKLOADS, Workload, make_decode_tokens, make_inputs
 from oracle import avq_oracle as O
-from parity import (OUT_TOL, check_quantization, check_routing, check_routing_single_query, finite_normrel,
-                    quant_from_arrays)
+from parity import (OUT_TOL, certify_assignment_flips, check_quantization, check_routing,
+                    check_routing_single_query, finite_normrel, quant_from_arrays)
 
 pytestmark = pytest.mark.gpu
 
@@ -173,16 +173,23 @@ def test_c3_decode_full_size() -> None:
     pa, ca = exact.parent_assignments, exact.child_assignments
     for step, (qt, kt, vt) in enumerate(make_decode_tokens(w, 4, B=1)):
         qt, kt, vt = (x.to("cuda", dt) for x in (qt, kt, vt))
+        pc0, cc0 = st.pcnt[hh].clone(), st.ccnt[hh].clone()
         ops.append(st, _heads(kt, w.H), _heads(vt, w.H), cb)
         out, diag = ops.forward(_heads(qt, w.H), cb, st, w.P, diagnostics=True)
         torch.cuda.synchronize()
         floor = int(st.gmin.item())
         kn, vn, qn = (_np(x[:, :, hh * D:(hh + 1) * D]) for x in (kt, vt, qt))
         kg, vg = np.concatenate([kg, kn], 1), np.concatenate([vg, vn], 1)
-        # the new key's assignment (the append kernel is exact: no near-tie allowance)
+        # the new key's buckets on the GPU (the counts that grew) against the
+        # oracle's assignment; a different parent must be a certified near-tie
+        p_gpu = int(torch.nonzero(st.pcnt[hh] - pc0)[0, 0])
+        c_gpu = int(torch.nonzero(st.ccnt[hh, p_gpu] - cc0[p_gpu])[0, 0])
         one = O.quantize(kn, vn, pd, cd, w.dtype)
-        pa = np.concatenate([pa, one.parent_assignments], 1)
-        ca = np.concatenate([ca, one.child_assignments], 1)
+        certify_assignment_flips(kn, pd, 1, np.array([[p_gpu]]), one.parent_assignments, w.dtype, f"c3 step {step}")
+        if p_gpu == int(one.parent_assignments[0, 0]):
+            assert c_gpu == int(one.child_assignments[0, 0]), f"c3 step {step}: child"
+        pa = np.concatenate([pa, np.array([[p_gpu]])], 1)
+        ca = np.concatenate([ca, np.array([[c_gpu]])], 1)
         exact = quant_from_arrays({"passign": pa, "cassign": ca}, vg, w.M0, w.C, w.dtype)
         sq = _slice_quant(st, hh, w.dtype)
         for key, ref in (("pagg", exact.parent_aggregates), ("cagg", exact.child_aggregates),
