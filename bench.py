@@ -228,7 +228,12 @@ def algorithmic_work(w, B: int, T: int | None = None, decode: bool = False, sel_
         sel = G * nsel * (1 + C) * D * es + G * nsel * C * 4   # selected parent / child sums + child counts
         return {
             "parent_attn_tc": ("hbm", pagg), "parent_attn": ("hbm", pagg), "parent_attn_exact": ("hbm", pagg),
-            "decode_attn": ("hbm", pagg + sel + G * T * D * (es + 4)),
+            # every parent-sum row, the selected rows, the exponentials (fp32) and the output
+            "decode_value": ("hbm", pagg + sel + G * M0 * 4 + G * T * D * 4),
+            # the logits read, the exponentials and the importance written, the counts
+            "decode_route": ("hbm", G * M0 * (es + 4 + 4)),
+            "decode_logits": ("tensor", 2.0 * G * T * M0 * D),
+            "append_assign": ("tensor", 2.0 * G * T * M0 * D),
             "correct_tc": ("hbm", sel), "correct": ("hbm", sel), "correct_exact": ("hbm", sel),
             # new token k/v read, the fp32 sums of its parent and child rows
             # (read + write) and their dtype copies written, the page slots
