@@ -12,10 +12,12 @@ reduction executed by the CUDA library:
     [HVAQ] -> child correction (1..passes) -> merge heads -> out_proj
 
 The output is fp32 for every input dtype, as in the reference (its online
-softmax state is fp32, ``attention.py:37-68``).  Features the reference
-offers but no benchmark configuration uses -- user or causal masks, BCAR
-codebook adaptation, the threshold router, the adaptive budget scheduler,
-learnable HVAQ parameters and the dense "reference" execution mode -- raise
+softmax state is fp32, ``attention.py:37-68``).  User and causal masks
+follow ``pipeline.py:82-106`` and ``attention_module.py:369-390``: a parent
+is masked for a query when none of its keys is visible.  Features the
+reference offers but no benchmark configuration uses -- BCAR codebook
+adaptation, the threshold router, the adaptive budget scheduler, learnable
+HVAQ parameters and the dense "reference" execution mode -- raise
 :class:`BackendError` instead of silently running elsewhere.
 """
 from __future__ import annotations
@@ -179,8 +181,8 @@ def cuda_run_pipeline(m, query: torch.Tensor, key: torch.Tensor, value: torch.Te
     reference's own one, once its ``run_pipeline`` is routed here.
     """
     c = m.config
-    if mask is not None or c.causal:
-        raise BackendError("attention masks (user or causal) are not supported by the cuda backend")
+    if mask is not None and chunk_size > 0:
+        raise BackendError("a user mask with query chunks is not supported; pass each chunk's mask to forward")
     m.validate_inputs(query, key, value)
     if not query.is_cuda:
         raise DeviceError("the cuda backend needs CUDA tensors", expected="cuda", actual=str(query.device))
@@ -204,9 +206,30 @@ def cuda_run_pipeline(m, query: torch.Tensor, key: torch.Tensor, value: torch.Te
     args = (min(c.routing.refinement_budget, cb.dims[1]), c.refinement.passes, c.refinement.pass_decay, hvaq_mode(c),
             beta0, c.hopfield.alpha)
     for q_part, out_part in query_chunks(q, out, H, chunk_size):
-        backend.forward(q_part, cb, state, *args, out=out_part, min_valid=min_valid, min_valid_ready=ready)
+        Bq, _, Tq, _ = q_part.shape
+        present = codeword_mask(c, state, Tq, mask, Bq if Bq != state.B else None)
+        backend.forward(q_part, cb, state, *args, out=out_part, min_valid=min_valid, min_valid_ready=ready,
+                        present=present)
         ready = None  # later chunks are ordered after the first one's wait
     return m.dropout(m.out_proj(out))
+
+
+def codeword_mask(config: AVQConfig, state: ops.QuantState, T: int, mask: torch.Tensor | None,
+                  query_batch: int | None = None) -> torch.Tensor | None:
+    """The codeword visibility bits of one call (pipeline.py:82-106), or None.
+
+    A user mask is used as given; otherwise, with ``config.causal``, the
+    causal mask of ``resolve_mask`` (attention_module.py:369-390): query t
+    sees keys ``0 .. t + S - T``, so a single query (decode) sees every key
+    and needs no mask."""
+    if mask is None and not config.causal:
+        return None
+    if mask is None and T == 1:
+        return None
+    if state.passign is None:
+        raise BackendError("a mask over a KV cache with more than one new query is not supported by the cuda "
+                           "backend: its decode state keeps no per-key assignments")
+    return ops.codeword_presence(state, T, mask, None, query_batch)
 
 
 def query_chunks(q: torch.Tensor, out: torch.Tensor, H: int, chunk: int):
@@ -309,5 +332,5 @@ def resolve_quantization(m, k: torch.Tensor, v: torch.Tensor, cb: ops.PreparedCo
     return st
 
 
-__all__ = ["AVQAttention", "cuda_run_pipeline", "global_min_valid", "hvaq_mode", "query_chunks",
+__all__ = ["AVQAttention", "codeword_mask", "cuda_run_pipeline", "global_min_valid", "hvaq_mode", "query_chunks",
            "resolve_quantization"]

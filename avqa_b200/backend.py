@@ -135,9 +135,9 @@ class CUDABackend(Backend):
     def forward(self, q: torch.Tensor, cb: ops.PreparedCodebook, state: ops.QuantState, budget: int,
                 passes: int = 1, pass_decay: float = 1.0, hvaq: int = 0, beta0: float = 0.0, alpha: float = 1.0,
                 out: torch.Tensor | None = None, min_valid: torch.Tensor | None = None, diagnostics: bool = False,
-                min_valid_ready: torch.cuda.Event | None = None):
+                min_valid_ready: torch.cuda.Event | None = None, present: torch.Tensor | None = None):
         return ops.forward(q, cb, state, budget, passes, pass_decay, hvaq, beta0, alpha, out, min_valid, diagnostics,
-                           min_valid_ready)
+                           min_valid_ready, present)
 
 
 __all__ = ["Backend", "CUDABackend", "QuantizationResult"]

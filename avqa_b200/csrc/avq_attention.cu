@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(256) parent_attn_kernel(
     const int* __restrict__ pcnt, int mode, float* __restrict__ sbuf, float* __restrict__ m_io,
     float* __restrict__ l_out, float* __restrict__ z_io, float* __restrict__ a_out, double* __restrict__ imp_part,
     const int* __restrict__ sel0, int sel_stride, const int* __restrict__ pass_cnt, int hvaq, float beta0,
-    float alpha, float* __restrict__ beta_out, int sG) {
+    float alpha, float* __restrict__ beta_out, int sG, const unsigned int* __restrict__ present) {
   constexpr int NK = DMAX / 8;
   extern __shared__ float smem[];
   const int ld = D + 1;
@@ -84,7 +84,9 @@ __global__ void __launch_bounds__(256) parent_attn_kernel(
         const int p = p0 + l8 + 8 * i;
         if (p < M0) {
           // pipeline.py:81 (matmul, / sqrt(D)) and :107 (invalid -> -inf)
-          float s = pcnt[(long)gs * M0 + p] > 0 ? rnd<DT>(__fdiv_rn(rnd64<DT>(acc[i]), sqrtD)) : -INFINITY;
+          // pipeline.py:106 (user / causal mask) and :107 (empty parent)
+          const bool vis = !live || present_bit(present, (M0 + 31) >> 5, (long)g * T + t, p);
+          float s = pcnt[(long)gs * M0 + p] > 0 && vis ? rnd<DT>(__fdiv_rn(rnd64<DT>(acc[i]), sqrtD)) : -INFINITY;
           if (live) sbuf[srow + p] = s;
           rowmax = nanmax(rowmax, s);
         }
@@ -726,7 +728,7 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
       const bool corr_tc = correct_tc_ok(DT, a.D, a.C);
       PAArgs pa{a.q, a.qs, a.B, a.H, a.T, a.D, a.M0, sqrtD, a.parents_dt, a.pagg, a.pcnt, 0, (hv && !pa_tc) ? 1 : 0,
                 w.slog, false, w.m, w.l, w.z, w.a, (float*)w.part0, sel, sel_stride, pcnt_out, a.hvaq, a.beta0,
-                a.alpha, w.beta, sG};
+                a.alpha, w.beta, sG, a.present};
       if (DT == DT_BF16 && (pa_tc || corr_tc)) launch_exp_table(w.exptab, st);
       int rc = AVQ_ERR_UNSUPPORTED;
       if (pa_tc && (rc = launch_parent_attn_tc<DT>(pa, w.exptab, st)) == AVQ_ERR_UNSUPPORTED) {
@@ -752,7 +754,7 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
       }
       CorrArgs ca{a.q, a.qs, a.B, a.H, a.T, a.D, a.M0, a.C, sqrtD, a.parents_dt, a.children_dt, a.pagg, a.cagg,
                   a.pcnt, a.ccnt, w.m, w.l, w.z, hv ? w.beta : nullptr, w.a, sel, sel_stride, pcnt_out, a.passes,
-                  {0, 0, 0, 0, 0, 0, 0, 0}, a.passes > 1 ? 1 : 0, a.out, a.os, sG};
+                  {0, 0, 0, 0, 0, 0, 0, 0}, a.passes > 1 ? 1 : 0, a.out, a.os, sG, a.present};
       for (int k = 0; k < a.passes; ++k) ca.pass_off[k] = lay.off[k];
       rc = (corr_tc && w.cdesc) ? launch_correct_tc<DT>(ca, w.exptab, w.cdesc, st) : AVQ_ERR_UNSUPPORTED;
       if (rc == AVQ_ERR_UNSUPPORTED) rc = launch_correct_mma<DT>(ca, st);
@@ -770,7 +772,7 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pa_smem);                              \
     k<<<dim3(nqt, G), 256, pa_smem, st>>>((const T*)a.q, a.qs, a.H, a.T, a.D, a.M0, sqrtD, (const T*)a.parents_dt,   \
                                           (const T*)a.pagg, a.pcnt, MODE, w.sbuf, w.m, w.l, w.z, w.a, PART, sel,     \
-                                          sel_stride, pcnt_out, a.hvaq, a.beta0, a.alpha, w.beta, sG);               \
+                                          sel_stride, pcnt_out, a.hvaq, a.beta0, a.alpha, w.beta, sG, a.present);    \
   } while (0)
 #define AVQ_PA_D(MODE, PART)                                   \
   do {                                                         \

@@ -40,7 +40,7 @@ __global__ void __launch_bounds__(128, 4) parent_attn_mma_kernel(
     float* __restrict__ m_io, float* __restrict__ l_out, float* __restrict__ z_io,
     typename Storage<DT>::T* __restrict__ a_out, float* __restrict__ colpart, const int* __restrict__ sel0,
     int sel_stride, const int* __restrict__ pass_cnt, int hvaq, float beta0, float alpha,
-    float* __restrict__ beta_out, int sG) {
+    float* __restrict__ beta_out, int sG, const unsigned int* __restrict__ present) {
   using T = typename Storage<DT>::T;
   constexpr int LDS = D + 8, KS = D / 16, CPR = D / 8, NT = D / 8;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -115,7 +115,9 @@ __global__ void __launch_bounds__(128, 4) parent_attn_mma_kernel(
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float x = rnd<DT>(acc[j][e]);
-          s[e] = nb[cl + (e & 1)] > 0.f ? scale_logit<DT>(x, sqrtD, inv_sqrtD) : -INFINITY;
+          const int tq = t0 + (e >= 2 ? r1 : r0);  // pipeline.py:106 (user / causal mask), :107 (empty)
+          const bool vis = !present || (tq < Tq && p < M0 && present_bit(present, (M0 + 31) >> 5, (long)g * Tq + tq, p));
+          s[e] = nb[cl + (e & 1)] > 0.f && vis ? scale_logit<DT>(x, sqrtD, inv_sqrtD) : -INFINITY;
         }
         const uint32_t s01 = pack2<DT>(s[0], s[1]), s23 = pack2<DT>(s[2], s[3]);
         if (p < M0) {
@@ -399,7 +401,7 @@ __global__ void __launch_bounds__(128) correct_mma_kernel(
     const float* __restrict__ l_in, const float* __restrict__ z_in, const float* __restrict__ beta_in,
     const typename Storage<DT>::T* __restrict__ a_in, const int* __restrict__ sel, int sel_stride,
     const int* __restrict__ pass_cnt, int npass, PassOffsets po, int multipass, float* __restrict__ out,
-    Strides3 os, int sG) {
+    Strides3 os, int sG, const unsigned int* __restrict__ present) {
   using T = typename Storage<DT>::T;
   constexpr bool TC = DT == DT_BF16;  // tensor-core value sums
   constexpr int LDS = D + 8, KS = D / 16, CPR = D / 8, NT = D / 8, NCH = CM_J * C;
@@ -413,6 +415,7 @@ __global__ void __launch_bounds__(128) correct_mma_kernel(
   float* snc = snp + CM_J;                 // [NCH] child counts (dtype)
   float* smk = snc + NCH;                  // [NCH] 1: logit child non-empty
   float* sw = smk + NCH;                   // fp16 path: [64][16] weights of one group
+  int* spi = reinterpret_cast<int*>(sw + CM_ROWS * 16);  // [CM_J] the selected parents (-1: empty slot)
   const int g = blockIdx.y, b = g / H, h = g % H, t0 = blockIdx.x * CM_ROWS, gs = g % sG;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r0 = warp * 16 + (lane >> 2), r1 = r0 + 8, cq = (lane & 3) * 2;
@@ -525,6 +528,7 @@ __global__ void __launch_bounds__(128) correct_mma_kernel(
       if (tid < CM_J) {
         const int j = j0 + tid;
         snp[tid] = j < cnt ? count_dt<DT>(pcnt[(long)gs * M0 + sg[po.off[pass] + j]]) : -1.f;
+        spi[tid] = j < cnt ? sg[po.off[pass] + j] : -1;
       }
       for (int jc = tid; jc < NCH; jc += blockDim.x) {
         const int jj = jc / C, ch = jc % C, j = j0 + jj;
@@ -561,7 +565,10 @@ __global__ void __launch_bounds__(128) correct_mma_kernel(
             const float n = snp[nt * 8 + cq + (e & 1)];
             float w = 0.f;
             if (n >= 0.f) {
-              float s = n > 0.f ? scale_logit<DT>(rnd<DT>(px[nt][e]), sqrtD, inv_sqrtD) : -INFINITY;
+              // a parent masked for this query (pipeline.py:106) has probability 0
+              const int tq = t0 + (hi ? r1 : r0), pp = spi[nt * 8 + cq + (e & 1)];
+              const bool vis = !present || tq >= Tq || present_bit(present, (M0 + 31) >> 5, (long)g * Tq + tq, pp);
+              float s = n > 0.f && vis ? scale_logit<DT>(rnd<DT>(px[nt][e]), sqrtD, inv_sqrtD) : -INFINITY;
               if (beta_in) s = rnd<DT>(__fmul_rn(hi ? bt1 : bt0, rnd<DT>(__fmul_rn(s, sqrtD))));
               const float ex = fmaxf(exp_dt_fast<DT>(rnd<DT>(s - (hi ? m1 : m0))), 0.f);
               const float pi = div_dt_fast<DT>(ex, hi ? rz1 : rz0, hi ? zc1 : zc0);
@@ -629,7 +636,8 @@ __global__ void __launch_bounds__(128) correct_mma_kernel(
 
 size_t correct_mma_smem(int D, int C, int dt) {
   const int LDS = D + 8, NCH = 16 * C;
-  return (size_t)(64 + 16 + NCH + 16 + NCH) * LDS * 2 + (16 + 2 * NCH) * sizeof(float) + 64 * 16 * sizeof(float);
+  return (size_t)(64 + 16 + NCH + 16 + NCH) * LDS * 2 + (16 + 2 * NCH) * sizeof(float) + 64 * 16 * sizeof(float) +
+         16 * sizeof(int);
 }
 
 template <int DT>
@@ -645,7 +653,7 @@ int launch_correct_mma(const CorrArgs& a, cudaStream_t st) {
     kfn<<<dim3(nqt, G), 128, smem, st>>>((const T*)a.q, a.qs, a.H, a.T, a.M0, a.sqrtD, (const T*)a.parents,
                                           (const T*)a.children, (const T*)a.pagg, (const T*)a.cagg, a.pcnt, a.ccnt,
                                           a.m, a.l, a.z, a.beta, (const T*)a.a, a.sel, a.sel_stride, a.pass_cnt,
-                                          a.npass, po, a.multipass, a.out, a.os, a.sG > 0 ? a.sG : G);
+                                          a.npass, po, a.multipass, a.out, a.os, a.sG > 0 ? a.sG : G, a.present);
   };
   if (a.C == 4) {
     if (a.D == 64) go(correct_mma_kernel<DT, 64, 4>); else go(correct_mma_kernel<DT, 128, 4>);
@@ -690,7 +698,7 @@ int launch_parent_attn_mma(const PAArgs& a, cudaStream_t st) {
     kfn<<<dim3(nqt, G), 128, smem, st>>>((const T*)a.q, a.qs, a.H, a.T, a.M0, a.sqrtD, (const T*)a.parents,
                                           (const T*)a.pagg, a.pcnt, a.mode, a.keep_logits, (T*)a.sglobal, a.m, a.l,
                                           a.z, (T*)a.a, a.colpart, a.sel0, a.sel_stride, a.pass_cnt, a.hvaq, a.beta0,
-                                          a.alpha, a.beta, a.sG > 0 ? a.sG : G);
+                                          a.alpha, a.beta, a.sG > 0 ? a.sG : G, a.present);
   };
   if (a.D == 64) go(parent_attn_mma_kernel<DT, 64>);
   else go(parent_attn_mma_kernel<DT, 128>);

@@ -157,10 +157,27 @@ size_t avq_forward_workspace_size(int dtype, int B, int H, int T, int D, int M0,
   return avq::forward_workspace_bytes(dtype, B * H, T, D, M0, C, P, passes, pass_decay, hvaq);
 }
 
+int avq_presence_words(int M0) { return M0 > 0 ? avq::presence_words(M0) : 0; }
+
+int avq_codeword_presence(const int* passign, int B, int H, int S, int M0, int T, int state_batch,
+                          const unsigned char* mask, const long long* mask_strides, int causal_offset,
+                          unsigned int* present, void* stream) {
+  if (B < 0 || H <= 0 || S < 0 || M0 <= 0 || T < 0 || M0 > 8192)
+    return fail(AVQ_ERR_ARG, "avq_codeword_presence: bad sizes");
+  if (too_many_groups(B, H)) return fail(AVQ_ERR_ARG, "avq_codeword_presence: B*H exceeds INT_MAX");
+  if (state_batch != B && state_batch != 1)
+    return fail(AVQ_ERR_ARG, "avq_codeword_presence: state_batch must be B (%d) or 1, got %d", B, state_batch);
+  if (!present || (S > 0 && !passign) || (mask && !mask_strides))
+    return fail(AVQ_ERR_ARG, "avq_codeword_presence: null pointer");
+  return finish(avq::launch_presence(passign, B, H, S, M0, T, mask, mask_strides, causal_offset, state_batch * H,
+                                     present, (cudaStream_t)stream),
+                "avq_codeword_presence");
+}
+
 int avq_forward(int dtype, const void* q, const long long* q_strides, int B, int H, int T, int D, int M0, int C,
                 const void* parents_dt, const void* children_dt, const void* pagg, const void* cagg, const int* pcnt,
-                const int* ccnt, int state_batch, const int* min_valid, void* min_valid_ready, int P, int passes,
-                float pass_decay, int hvaq, float beta0,
+                const int* ccnt, int state_batch, const int* min_valid, void* min_valid_ready,
+                const unsigned int* present, int P, int passes, float pass_decay, int hvaq, float beta0,
                 float alpha, float* out, const long long* out_strides, float* importance_out, int* selected_out,
                 int* pass_counts_out, void* workspace, size_t workspace_bytes, void* stream) {
   if (bad_dtype(dtype)) return fail(AVQ_ERR_ARG, "avq_forward: bad dtype %d", dtype);
@@ -183,7 +200,7 @@ int avq_forward(int dtype, const void* q, const long long* q_strides, int B, int
     return fail(AVQ_ERR_WORKSPACE, "avq_forward: workspace %zu < %zu bytes", workspace_bytes, need);
   avq::ForwardArgs a{q, st3(q_strides), B, H, T, D, M0, C, parents_dt, children_dt, pagg, cagg, pcnt, ccnt, min_valid,
                      P, passes, pass_decay, hvaq, beta0, alpha, out, st3(out_strides), importance_out, selected_out,
-                     pass_counts_out, workspace, workspace_bytes, state_batch * H, min_valid_ready};
+                     pass_counts_out, workspace, workspace_bytes, state_batch * H, min_valid_ready, present};
   cudaStream_t st = (cudaStream_t)stream;
   int rc;
   switch (dtype) {

@@ -82,7 +82,7 @@ __host__ __device__ inline CorrLayout corr_layout(int D, bool split_v = false) {
   }
   for (int i = 0; i < NBUF; ++i) {
     L.meta[i] = o;
-    o += 2 * NS * 4;  // n [48] then logit mask [48]
+    o += 3 * NS * 4;  // n [48], logit mask [48], parent index of a parent slot or -1 [48]
   }
   L.exptab = o;
   o += ((EXPN + 1) / 2) * 4;
@@ -180,7 +180,8 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
     const float* __restrict__ m_in, const float* __restrict__ l_in, const float* __restrict__ z_in,
     const float* __restrict__ beta_in, const typename Storage<DT>::T* __restrict__ a_in,
     const int* __restrict__ pass_cnt, int npass, int maxgroups, const SlotDesc* __restrict__ desc,
-    const uint16_t* __restrict__ exptab_g, float* __restrict__ out, Strides3 os) {
+    const uint16_t* __restrict__ exptab_g, float* __restrict__ out, Strides3 os, int M0,
+    const unsigned int* __restrict__ present) {
   using T = typename Storage<DT>::T;
   constexpr bool SPLIT = DT == DT_F16;  // fp16 value rows become two bf16 planes
   constexpr int J = NS / (1 + C), NREAL = J * (1 + C), CPR = D / 8;
@@ -305,6 +306,8 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
     const float zc = clamp_min_nan(live ? z_in[row] : 1.f, eps_dt<DT>()), rz = 1.f / zc;
     const float zl = next_down(rz), zh = next_up(rz);  // bracket 1 / zc
     const float bt = beta_in && live ? beta_in[row] : 0.f;
+    // the row's mask words (pipeline.py:82-106): a masked parent has probability 0
+    const unsigned int* prow = (present && live) ? present + row * ((M0 + 31) >> 5) : nullptr;
     float l = live ? l_in[row] : 1.f;
     const int gslot = r;
     const bool gathers = r < NS, isv = hf == 1;
@@ -323,6 +326,7 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
           float* meta = reinterpret_cast<float*>(sm + L.meta[bf]);
           meta[gslot] = d.n;
           meta[NS + gslot] = d.mk;
+          reinterpret_cast<int*>(meta)[2 * NS + gslot] = (gslot < J && d.lrow >= 0) ? d.lrow - h * M0 : -1;
         }
       }
       cp_async_commit();
@@ -470,6 +474,10 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
               float w = 0.f;
               if (k < NREAL) {
                 float s = kv[e] > 0.f ? sl[i] : -INFINITY;
+                if (k < J && prow) {
+                  const int pp = reinterpret_cast<const int*>(meta)[2 * NS + k];
+                  if (pp >= 0 && !((prow[pp >> 5] >> (pp & 31)) & 1u)) s = -INFINITY;
+                }
                 if (k < J) {
                   if (beta_in) s = rnd<DT>(__fmul_rn(bt, rnd<DT>(__fmul_rn(s, sqrtD))));
                   float ex;
@@ -659,7 +667,7 @@ int launch_correct_tc(const CorrArgs& a, const void* exptab, void* desc, cudaStr
         tq, qpos, a.H, a.T, a.sqrtD, static_cast<const T*>(a.parents), static_cast<const T*>(a.children),
         static_cast<const T*>(a.pagg), static_cast<const T*>(a.cagg), a.m, a.l, a.z, a.beta,
         static_cast<const T*>(a.a), a.pass_cnt, a.npass, maxgroups, sd, static_cast<const uint16_t*>(exptab), a.out,
-        a.os);
+        a.os, a.M0, a.present);
   };
   if (a.C == 4) {
     if (D == 64) go(corr_desc_kernel<DT, 4>, correct_tc_kernel<DT, 64, 4>);

@@ -73,6 +73,7 @@ __global__ void __launch_bounds__(256) decode_logits_kernel(const typename Stora
                                                             Strides3 qs, int B, int H, int M0, float sqrtD,
                                                             const typename Storage<DT>::T* __restrict__ parents,
                                                             const int* __restrict__ pcnt, int sG,
+                                                            const unsigned int* __restrict__ present,
                                                             typename Storage<DT>::T* __restrict__ logits) {
   using T = typename Storage<DT>::T;
   constexpr int LDS = D + 8, KS = D / 16, CPR = D / 8;
@@ -119,7 +120,8 @@ __global__ void __launch_bounds__(256) decode_logits_kernel(const typename Stora
       if (b < B && p < M0) {
         const int g = b * H + h;
         const float x = rnd<DT>(acc[j][e]);
-        const float s = pcnt[(long)(g % sG) * M0 + p] > 0 ? scale_logit<DT>(x, sqrtD, inv_sqrtD) : -INFINITY;
+        const bool vis = present_bit(present, (M0 + 31) >> 5, g, p);  // one query: row g
+        const float s = pcnt[(long)(g % sG) * M0 + p] > 0 && vis ? scale_logit<DT>(x, sqrtD, inv_sqrtD) : -INFINITY;
         logits[(long)g * M0 + p] = from_f<DT>(s);
       }
     }
@@ -474,7 +476,7 @@ int launch_decode_forward(const ForwardArgs& a, void* work, const void* exptab, 
       cudaFuncSetAttribute(lk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsm);
       lk<<<dim3(a.H, (a.M0 + DL_COLS - 1) / DL_COLS, (a.B + DL_ROWS - 1) / DL_ROWS), 256, lsm, st>>>(
           static_cast<const T*>(a.q), a.qs, a.B, a.H, a.M0, sqrtD, static_cast<const T*>(a.parents_dt), a.pcnt, sG,
-          dlog);
+          a.present, dlog);
     }
     if (a.min_valid_ready) cudaStreamWaitEvent(st, static_cast<cudaEvent_t>(a.min_valid_ready), 0);
     {

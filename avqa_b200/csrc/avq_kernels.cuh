@@ -72,6 +72,9 @@ struct ForwardArgs {
   // state of query group g is g % state_groups.  0 means B*H.
   int state_groups = 0;
   void* min_valid_ready = nullptr;  // optional cudaEvent_t awaited before routing
+  // optional codeword visibility under a mask: bit p % 32 of word
+  // present[(g T + t) W + p / 32], W = presence_words(M0), for query group g
+  const unsigned int* present = nullptr;
 };
 
 struct AppendArgs {
@@ -122,6 +125,7 @@ struct PAArgs {
   float beta0, alpha;
   float* beta;         // [G,T]
   int sG = 0;          // state groups: the state of query group g is g % sG
+  const unsigned int* present = nullptr;  // optional mask bits (see ForwardArgs)
 };
 
 // Importance from fp32 per-tile column partials, with the exact fallback
@@ -161,6 +165,7 @@ struct CorrArgs {
   float* out;
   Strides3 os;
   int sG = 0;  // state groups: the state of query group g is g % sG
+  const unsigned int* present = nullptr;  // optional mask bits (see ForwardArgs)
 };
 
 template <int DT>
@@ -200,6 +205,17 @@ int launch_assign_tc(const QuantizeArgs& a, cudaStream_t st);
 int read_device_fault(int* code, cudaStream_t st);
 int read_fault_assign(int* code, cudaStream_t st);
 int read_fault_correct(int* code, cudaStream_t st);
+
+// Codeword visibility bits under a causal (mask == nullptr) or user mask
+// (avq_mask.cu).
+int presence_words(int M0);
+int launch_presence(const int* passign, int B, int H, int S, int M0, int T, const unsigned char* mask,
+                    const long long* mask_strides, int causal_offset, int sG, unsigned int* present, cudaStream_t st);
+
+// The mask bit of parent p for row (g, t) (all present when there is no mask).
+__device__ __forceinline__ bool present_bit(const unsigned int* present, int W, long gt, int p) {
+  return !present || ((present[gt * W + (p >> 5)] >> (p & 31)) & 1u);
+}
 
 template <int DT>
 int launch_append(const AppendArgs& a, cudaStream_t st);

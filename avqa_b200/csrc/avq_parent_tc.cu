@@ -203,7 +203,8 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     float* __restrict__ m_out, float* __restrict__ l_out, float* __restrict__ z_out,
     typename Storage<DT>::T* __restrict__ a_out, float* __restrict__ colpart, int sG,
     const typename Storage<DT>::T* __restrict__ parents_g, const int* __restrict__ sel0, int sel_stride,
-    const int* __restrict__ pass_cnt, int hvaq, float beta0, float alpha, float* __restrict__ beta_out) {
+    const int* __restrict__ pass_cnt, int hvaq, float beta0, float alpha, float* __restrict__ beta_out,
+    const unsigned int* __restrict__ present) {
   using T = typename Storage<DT>::T;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_addr(smem_raw);
@@ -417,6 +418,10 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     const uint32_t ninf2 = DT == DT_BF16 ? 0xFF80FF80u : 0xFC00FC00u;
     const long row = (long)g * Tq + t;
     T* srow_g = scratch + (((long)g * ntiles + (t >> 6)) * 64 + (t & 63)) * LDL;
+    // the row's mask words (pipeline.py:82-106); none for rows past T
+    const int PW = (M0 + 31) >> 5;
+    const unsigned int* prow = (present && live) ? present + row * PW : nullptr;
+    auto pword = [&](int wi) -> uint32_t { return prow ? (wi < PW ? prow[wi] : 0u) : 0xFFFFFFFFu; };
     const bool sector_stores = (reinterpret_cast<uintptr_t>(scratch) & 31u) == 0u;
     bool ok = true;
     float beta = 0.f;
@@ -445,7 +450,8 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
           const int j = 32 * hf + i;
           float pi = 0.f;
           if (j < nsel) {
-            const bool keep = pcnt[(long)gs * M0 + sl[j]] > 0;
+            const int pj = sl[j];
+            const bool keep = pcnt[(long)gs * M0 + pj] > 0 && (!prow || ((prow[pj >> 5] >> (pj & 31)) & 1u));
             const float s = keep ? scale_logit<DT>(rnd<DT>(__uint_as_float(ra[i])), sqrtD, inv_sqrtD) : -INFINITY;
             float e = exp_rn<DT>(rnd<DT>(__fsub_rn(s, m0)));
             if (isnan(e)) e = 0.f;  // pipeline.py:143-145
@@ -501,7 +507,8 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       tc::mbar_arrive(&bars[B_EFULL + sl]);
       const uint32_t* pm = pm2 + v * 32 + 16 * hf;
       const uint4* pm4 = reinterpret_cast<const uint4*>(pm);
-      uint32_t all = 0xFFFFFFFFu;
+      const uint32_t pb = pword(2 * v + hf);  // parent 64 v + 32 hf + i is bit i
+      uint32_t all = pb;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const uint4 u = pm4[q];
@@ -513,7 +520,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const bool keep = (pm[i >> 1] >> ((i & 1) * 16)) & 1u;
+          const bool keep = ((pm[i >> 1] >> ((i & 1) * 16)) & 1u) && ((pb >> i) & 1u);
           mxa[i & 3] = fmax_nan(mxa[i & 3], keep ? __uint_as_float(ra[i]) : -INFINITY);
         }
       }
@@ -535,6 +542,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       if (!ok) break;
       tc::tc_after_sync();
       const uint32_t col = tbase + lane_off + D + 64 * s + 32 * hf;
+      const uint32_t pb = pword(2 * c + hf);
       float zh[2];
       // 16 parents at a time; the second block's TMEM load is in flight while
       // the first is computed (its exponentials go to columns 0-7, the load
@@ -589,7 +597,12 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const int j = 4 * q + k;
-            const uint32_t sm2 = (s2[j] & pmv[k]) | (ninf2 & ~pmv[k]);  // -inf for empty parents (pipeline.py:107)
+            uint32_t keepm = pmv[k];
+            if (prow) {  // the pair's two mask bits, widened to its halves (pipeline.py:106)
+              const uint32_t two = (pb >> (hh * 16 + 2 * j)) & 3u;
+              keepm &= ((two & 1u) ? 0xFFFFu : 0u) | ((two & 2u) ? 0xFFFF0000u : 0u);
+            }
+            const uint32_t sm2 = (s2[j] & keepm) | (ninf2 & ~keepm);  // -inf for empty parents (pipeline.py:107)
             const uint32_t ee = exp2_dt<DT>(hsub2_dt<DT>(sm2, m2), exptab);
             e2[j] = ee;
             const uint32_t w2 = hmul2_dt<DT>(ee, nnv[k]);  // DT(e * n), pipeline.py:146
@@ -850,7 +863,8 @@ int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st) {
     kfn<<<dim3((a.T + TR - 1) / TR, G), TTHREADS, smem, st>>>(
         tq, tp, tv, qpos, a.H, a.T, M0, a.sqrtD, a.pcnt, static_cast<const uint16_t*>(exptab),
         static_cast<T*>(a.sglobal), a.m, a.l, a.z, static_cast<T*>(a.a), a.colpart, sG,
-        static_cast<const T*>(a.parents), a.sel0, a.sel_stride, a.pass_cnt, a.hvaq, a.beta0, a.alpha, a.beta);
+        static_cast<const T*>(a.parents), a.sel0, a.sel_stride, a.pass_cnt, a.hvaq, a.beta0, a.alpha, a.beta,
+        a.present);
   };
   if (hv) {
     if (D == 64) go(parent_attn_tc_kernel<DT, 64, true>);

@@ -11,6 +11,8 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import ctypes
+
 import torch
 
 from avqa_b200 import _lib
@@ -146,6 +148,54 @@ def append(state: QuantState, k: torch.Tensor, v: torch.Tensor, cb: PreparedCode
     _lib.check(rc, "avq_reduce_min")
 
 
+def codeword_presence(state: QuantState, T: int, mask: torch.Tensor | None = None, causal_offset: int | None = None,
+                      query_batch: int | None = None) -> torch.Tensor:
+    """Codeword visibility bits ``[Bq*H, T, ceil(M0/32)]`` int32 for ``T``
+    queries per (b,h) (pipeline.py:82-106): a parent is visible to a query
+    when one of its keys is allowed by the mask.
+
+    ``mask``: bool/uint8 ``[T, S]`` or ``[B, H, T, S]`` (True = attend; size-1
+    leading dims broadcast); without it the causal mask, query t seeing keys
+    ``0 .. t + causal_offset`` (the reference uses ``S - T``).  ``query_batch``
+    is the query batch when the state (batch 1) serves several."""
+    from avqa_b200.exceptions import ConfigurationError, NotInitializedError, ShapeError
+    lib = _lib.load()
+    if state.passign is None:
+        raise NotInitializedError("the codeword mask needs the key assignments of this state (not kept after a "
+                                  "decode append)")
+    dev = state.pcnt.device
+    Bq = state.B if query_batch is None else query_batch
+    H, S, M0 = state.H, state.S, state.pcnt.shape[-1]
+    W = lib.avq_presence_words(M0)
+    out = torch.empty(Bq * H, T, W, dtype=torch.int32, device=dev)
+    strides = None
+    mptr = None
+    if mask is not None:
+        if mask.ndim not in (2, 4):
+            raise ConfigurationError("mask must be rank 2 [T_q, T_k] or rank 4 [B, H, T_q, T_k]",
+                                     {"got_rank": mask.ndim})
+        if tuple(mask.shape[-2:]) != (T, S):
+            raise ShapeError("mask shape does not match the queries and keys", expected=(T, S),
+                             actual=tuple(mask.shape[-2:]))
+        m = mask.to(device=dev, dtype=torch.uint8)
+        if m.stride(-1) != 1:
+            m = m.contiguous()
+        if m.ndim == 2:
+            st = (0, 0, m.stride(0))
+        else:
+            if m.shape[0] not in (1, Bq) or m.shape[1] not in (1, H):
+                raise ShapeError("rank-4 mask does not broadcast to [B, H, T, S]", expected=(Bq, H, T, S),
+                                 actual=tuple(m.shape))
+            st = (m.stride(0) if m.shape[0] > 1 else 0, m.stride(1) if m.shape[1] > 1 else 0, m.stride(2))
+        strides = (ctypes.c_longlong * 3)(*st)
+        mptr = m.data_ptr()  # m stays referenced until the kernel is enqueued
+    offset = (S - T) if causal_offset is None else causal_offset
+    rc = lib.avq_codeword_presence(_lib.ptr(state.passign), Bq, H, S, M0, T, state.B, mptr, strides, offset,
+                                   out.data_ptr(), _lib.stream_of(dev))
+    _lib.check(rc, "avq_codeword_presence")
+    return out
+
+
 @dataclass
 class ForwardDiagnostics:
     importance: torch.Tensor  # [G, M0] fp32 (pre-HVAQ importance, dtype values)
@@ -172,7 +222,7 @@ def pass_caps(P: int, passes: int, decay: float) -> list[int]:
 def forward(q: torch.Tensor, cb: PreparedCodebook, st: QuantState, P: int, passes: int = 1, pass_decay: float = 1.0,
             hvaq: int = 0, beta0: float = 0.0, alpha: float = 1.0, out: torch.Tensor | None = None,
             min_valid: torch.Tensor | None = None, diagnostics: bool = False,
-            min_valid_ready: torch.cuda.Event | None = None):
+            min_valid_ready: torch.cuda.Event | None = None, present: torch.Tensor | None = None):
     """AVQ attention of ``q`` ``[B, H, T, D]`` over ``st``.
 
     ``st`` holds either B batches of keys, or one batch that every query
@@ -180,7 +230,8 @@ def forward(q: torch.Tensor, cb: PreparedCodebook, st: QuantState, P: int, passe
     each batch entry is routed on its own, exactly as separate calls over the
     same keys).  ``min_valid_ready``: an event recorded after ``min_valid``
     was produced on another stream; the library waits on it only right
-    before routing.
+    before routing.  ``present``: codeword visibility bits of a mask
+    (:func:`codeword_presence`) for these queries.
 
     Returns ``out`` as a ``[B, H, T, D]`` fp32 view (module layout when
     ``out`` is given as a ``[B, T, H, D]``-strided tensor) and optional
@@ -210,12 +261,13 @@ def forward(q: torch.Tensor, cb: PreparedCodebook, st: QuantState, P: int, passe
     rc = lib.avq_forward(_lib.dtype_code(q.dtype), q.data_ptr(), _lib.strides3(q), B, H, T, D, M0, C,
                          cb.parents.data_ptr(), cb.children.data_ptr(), st.pagg.data_ptr(), st.cagg.data_ptr(),
                          st.pcnt.data_ptr(), st.ccnt.data_ptr(), st.B, mv.data_ptr(),
-                         None if min_valid_ready is None else min_valid_ready.cuda_event, P, passes, pass_decay,
+                         None if min_valid_ready is None else min_valid_ready.cuda_event, _lib.ptr(present), P,
+                         passes, pass_decay,
                          hvaq, beta0, alpha, out.data_ptr(), _lib.strides3(out), _lib.ptr(imp), _lib.ptr(sel),
                          _lib.ptr(pc), ws.data_ptr(), ws_bytes, _lib.stream_of(dev))
     _lib.check(rc, "avq_forward")
     return out, diag
 
 
-__all__ = ["ForwardDiagnostics", "PreparedCodebook", "QuantState", "append", "forward", "pass_caps",
-           "prepare_codebook", "quantize"]
+__all__ = ["ForwardDiagnostics", "PreparedCodebook", "QuantState", "append", "codeword_presence", "forward",
+           "pass_caps", "prepare_codebook", "quantize"]

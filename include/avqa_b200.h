@@ -117,6 +117,24 @@ int avq_quantize_noalloc(int dtype, const void* keys, const long long* key_strid
                          int* passign, int* cassign, void* pagg, void* cagg, float* pacc, float* cacc, int* pcnt,
                          int* ccnt, int* nvalid, int* gmin_valid, void* stream);
 
+/* Words per (b,h, query) row of the codeword visibility bits: ceil(M0 / 32). */
+int avq_presence_words(int M0);
+
+/* Codeword visibility under a mask (pipeline.py:82-106 with the causal mask
+ * of attention_module.py:210-223, 369-390): parent p is visible to query t of
+ * (b,h) when at least one key assigned to it is allowed by the mask.  Bit
+ * p % 32 of present[((b*H + h)*T + t)*W + p/32] (W = avq_presence_words(M0),
+ * present holds B*H*T*W words) is set for a visible parent.
+ * mask NULL: the causal mask, query t sees keys 0 .. t + causal_offset (the
+ * reference uses causal_offset = S - T: the cached prefix is visible to every
+ * query).  Otherwise mask is uint8 (nonzero = attend) with element strides
+ * mask_strides {b, h, t} (the key stride is 1; zero strides broadcast, so a
+ * [T, S] mask passes {0, 0, S}).  passign [state_batch*H, S] are the parent
+ * assignments of avq_quantize; state_batch is B or 1 as in avq_forward. */
+int avq_codeword_presence(const int* passign, int B, int H, int S, int M0, int T, int state_batch,
+                          const unsigned char* mask, const long long* mask_strides, int causal_offset,
+                          unsigned int* present, void* stream);
+
 /* Number of int32 slots per (b,h) in the `selected` output of avq_forward:
  * the sum of the per-pass budget caps for base budget P. */
 int avq_selection_stride(int P, int passes, float pass_decay);
@@ -135,15 +153,17 @@ size_t avq_forward_workspace_size(int dtype, int B, int H, int T, int D, int M0,
  * min(P, *min_valid).  min_valid_ready: NULL, or a cudaEvent_t recorded by
  * whatever produces *min_valid (e.g. a cross-rank all-reduce on another
  * stream): `stream` waits on it only before the routing kernel, so the
- * parent-attention kernel overlaps the reduction.  hvaq: 0 off, 1 entropy schedule,
+ * parent-attention kernel overlaps the reduction.  present: NULL, or the
+ * codeword visibility bits of avq_codeword_presence for these B*H*T query
+ * rows (a masked parent's logit is -inf for that query).  hvaq: 0 off, 1 entropy schedule,
  * 2 linear schedule; beta0 the base temperature (1/sqrt(D) when the config
  * says 0), alpha the linear slope.  importance_out [G,M0] fp32, selected_out
  * [G, avq_selection_stride()] int32 and pass_counts_out [passes] int32 are
  * optional diagnostics (NULL to skip). */
 int avq_forward(int dtype, const void* q, const long long* q_strides, int B, int H, int T, int D, int M0, int C,
                 const void* parents_dt, const void* children_dt, const void* pagg, const void* cagg, const int* pcnt,
-                const int* ccnt, int state_batch, const int* min_valid, void* min_valid_ready, int P, int passes,
-                float pass_decay, int hvaq, float beta0,
+                const int* ccnt, int state_batch, const int* min_valid, void* min_valid_ready,
+                const unsigned int* present, int P, int passes, float pass_decay, int hvaq, float beta0,
                 float alpha, float* out, const long long* out_strides, float* importance_out, int* selected_out,
                 int* pass_counts_out, void* workspace, size_t workspace_bytes, void* stream);
 

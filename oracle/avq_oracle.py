@@ -230,11 +230,47 @@ def scaled_logits(q, keys_g, D: int, dt: str) -> np.ndarray:
     return rnd(_f64(raw) / opmath_scalar(math.sqrt(D)), dt)
 
 
-def parent_logits(q, parents, pcnt, H: int, dt: str) -> np.ndarray:
-    """pipeline.py:46-108 (no user mask): logits, -inf where count == 0."""
+def causal_mask(t_q: int, t_k: int) -> np.ndarray:
+    """attention_module.py:210-223: ``[T_q, T_k]``, query i sees keys
+    ``0 .. i + (t_k - t_q)`` (the cached prefix is visible to every query)."""
+    i = np.arange(t_q)[:, None]
+    j = np.arange(t_k)[None, :]
+    return j <= i + (t_k - t_q)
+
+
+def codeword_present(mask_g: np.ndarray, passign: np.ndarray, M0: int) -> np.ndarray:
+    """pipeline.py:98-105: parent p is visible to query t when at least one
+    key assigned to p is allowed by the mask.  ``mask_g`` [G, T, S] bool,
+    ``passign`` [G, S]; returns [G, T, M0] bool."""
+    G, T, S = mask_g.shape
+    out = np.zeros((G, T, M0), bool)
+    for g in range(G):
+        onehot = np.zeros((S, M0), np.float32)
+        onehot[np.arange(S), passign[g]] = 1.0
+        out[g] = (mask_g[g].astype(np.float32) @ onehot) > 0
+    return out
+
+
+def expand_mask(mask: np.ndarray, B: int, H: int) -> np.ndarray:
+    """A rank-2 ``[T, S]`` or rank-4 ``[B, H, T, S]`` mask as ``[G, T, S]``
+    (pipeline.py:93-97)."""
+    mask = np.asarray(mask, bool)
+    if mask.ndim == 2:
+        return np.broadcast_to(mask, (B * H,) + mask.shape)
+    if mask.ndim == 4:
+        return np.broadcast_to(mask, (B, H) + mask.shape[2:]).reshape((B * H,) + mask.shape[2:])
+    raise ValueError("mask must be rank 2 [T_q, T_k] or rank 4 [B, H, T_q, T_k]")
+
+
+def parent_logits(q, parents, pcnt, H: int, dt: str, present: np.ndarray | None = None) -> np.ndarray:
+    """pipeline.py:46-108: logits, -inf where the codeword has no key visible
+    to the query (``present``, from a user or causal mask) and where
+    count == 0."""
     G = q.shape[0]
     D = q.shape[-1]
     s = scaled_logits(q, parents[np.arange(G) % H], D, dt)
+    if present is not None:
+        s = np.where(present, s, np.float32(-np.inf))
     return np.where((pcnt > 0)[:, None, :], s, np.float32(-np.inf)).astype(np.float32)
 
 
@@ -412,7 +448,7 @@ def merge_heads(x: np.ndarray, B: int, H: int) -> np.ndarray:
 
 
 def forward_heads(qg, kg, vg, parents, children, cfg: ForwardConfig, quant: Quantization | None = None,
-                  budget_floor: int | None = None) -> dict:
+                  budget_floor: int | None = None, mask_g: np.ndarray | None = None) -> dict:
     """Run the AVQ forward on head-split tensors ``[G,T,D]`` / ``[G,S,D]``.
 
     ``parents``/``children`` must already be cast to ``cfg.dtype``
@@ -429,7 +465,11 @@ def forward_heads(qg, kg, vg, parents, children, cfg: ForwardConfig, quant: Quan
         quant = quantize(kg, vg, parents, children, dt)
     res["quant"] = quant
     pc = quant.parent_counts
-    s = parent_logits(qg, parents, pc, H, dt)
+    present = None
+    if mask_g is not None:  # pipeline.py:82-106; the child logits ignore the mask
+        present = codeword_present(mask_g, quant.parent_assignments, parents.shape[1])
+        res["present"] = present
+    s = parent_logits(qg, parents, pc, H, dt, present)
     st = online_softmax(s, quant.parent_aggregates, pc, dt)
     res["logits"], res["state0"] = s, st
     w = importance(st.probs, pc, dt)
@@ -497,10 +537,13 @@ def forward_heads(qg, kg, vg, parents, children, cfg: ForwardConfig, quant: Quan
     return res
 
 
-def forward(q, k, v, parents, children, cfg: ForwardConfig, **kw) -> dict:
-    """Module-layout forward: ``[B,T,E]`` inputs, ``[B,T,E]`` fp32 output."""
+def forward(q, k, v, parents, children, cfg: ForwardConfig, mask: np.ndarray | None = None, **kw) -> dict:
+    """Module-layout forward: ``[B,T,E]`` inputs, ``[B,T,E]`` fp32 output;
+    ``mask`` rank 2 ``[T, S]`` or rank 4 ``[B, H, T, S]`` (True = attend)."""
     B = q.shape[0]
     H = cfg.num_heads
+    if mask is not None:
+        kw["mask_g"] = expand_mask(mask, B, H)
     res = forward_heads(split_heads(q, H), split_heads(k, H), split_heads(v, H), parents, children, cfg, **kw)
     res["out_bte"] = merge_heads(res["out"], B, H)
     return res
@@ -512,7 +555,8 @@ def cast_codebook(parents32: np.ndarray, children32: np.ndarray, dt: str):
 
 
 __all__ = [
-    "DTYPES", "EPS", "ForwardConfig", "Quantization", "SoftmaxState", "cast_codebook",
+    "DTYPES", "EPS", "ForwardConfig", "Quantization", "SoftmaxState", "cast_codebook", "causal_mask",
+    "codeword_present", "expand_mask",
     "child_logits_sel", "compute_pass_budgets", "correction", "count_saturation", "first_argmin",
     "forward", "forward_heads", "hvaq_logits", "importance", "merge_heads", "online_softmax",
     "parent_distances", "parent_logits", "quantize", "rnd", "sequential_bucket_sums",

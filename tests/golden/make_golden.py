@@ -63,7 +63,32 @@ CASES: dict[str, dict] = {
                                        keys="mixture", seed=9)),
     "ties_bf16": dict(w=Workload("ties", B=1, T=4, S=16, H=1, D=8, M0=4, C=2, P=4, dtype="bf16",
                                  keys="mixture", seed=10), ties=True),
+    # masks (pipeline.py:82-106): the causal mask of config.causal, a rank-2
+    # user mask with one fully masked query, a rank-4 user mask, and the causal
+    # mask with multi-pass refinement + HVAQ and with query chunks
+    "causal_bf16": dict(w=Workload("causal", B=2, T=96, S=96, H=2, D=64, M0=16, C=4, P=6, dtype="bf16",
+                                   keys="mixture", seed=12), mask="causal"),
+    "mask2_f32": dict(w=Workload("mask2", B=1, T=40, S=64, H=2, D=32, M0=12, C=2, P=4, dtype="f32",
+                                 keys="mixture", seed=13), mask="user2"),
+    "mask4_bf16": dict(w=Workload("mask4", B=2, T=32, S=80, H=2, D=64, M0=16, C=4, P=5, dtype="bf16",
+                                  keys="mixture", seed=14), mask="user4"),
+    "causal_mp_hvaq_f16": dict(w=Workload("cmh", B=1, T=128, S=128, H=2, D=64, M0=24, C=4, P=8, dtype="f16",
+                                          keys="student_t", seed=15, passes=2, pass_decay=0.5, hvaq=True),
+                               mask="causal"),
+    "causal_chunks_bf16": dict(w=Workload("cch", B=1, T=64, S=64, H=2, D=64, M0=16, C=4, P=6, dtype="bf16",
+                                          keys="mixture", seed=16, q_chunk=32), mask="causal"),
 }
+
+
+def user_mask(w: Workload, rank: int) -> torch.Tensor:
+    """A seeded boolean mask (True = attend, density 0.3); rank 2 ``[T, S]``
+    with query 0 fully masked, or rank 4 ``[B, H, T, S]``."""
+    g = torch.Generator().manual_seed(w.seed + 99)
+    if rank == 2:
+        m = torch.rand(w.T, w.S, generator=g) < 0.3
+        m[0] = False
+        return m
+    return torch.rand(w.B, w.H, w.T, w.S, generator=g) < 0.3
 
 
 def bits(t: torch.Tensor) -> np.ndarray:
@@ -120,7 +145,11 @@ def run_case(name: str, spec: dict, ref_root: Path) -> dict:
         children[:, 1] = children[:, 0]  # duplicated parent -> exact distance ties
         parents = children.mean(2)
 
+    mask = None
+    if spec.get("mask") in ("user2", "user4"):
+        mask = user_mask(w, 2 if spec["mask"] == "user2" else 4)
     cfg = AVQConfig(
+        causal=spec.get("mask") == "causal",
         attention=AttentionShapeConfig(embed_dim=w.E, num_heads=H),
         codebook=CodebookConfig(num_codewords=w.M0, children_per_codeword=w.C),
         routing=RoutingConfig(strategy=spec.get("strategy", "topp"), refinement_budget=w.P),
@@ -194,7 +223,7 @@ def run_case(name: str, spec: dict, ref_root: Path) -> dict:
                 for c0 in range(0, w.T, w.q_chunk):
                     rec["out"].append(mod(q[:, c0:c0 + w.q_chunk], k, v))
             else:
-                rec["out"].append(mod(q, k, v))
+                rec["out"].append(mod(q, k, v, mask=mask))
     finally:
         apl.online_softmax = orig_os
         apl.compute_importance, amp.compute_importance = orig_ci_p, orig_ci_m
@@ -206,6 +235,9 @@ def run_case(name: str, spec: dict, ref_root: Path) -> dict:
                 n_calls=len(rec["out"]), n_select=len(rec["selected"]), n_softmax=len(rec["softmax"]),
                 n_importance=len(rec["importance"]), n_beta=len(rec["beta"]))
     arrs: dict[str, np.ndarray] = {"parents32": parents.numpy(), "children32": children.numpy()}
+    meta["mask"] = spec.get("mask")
+    if mask is not None:
+        arrs["mask"] = mask.numpy().astype(np.uint8)
     if w.keys == "readme":
         # regenerated at test time from torch.manual_seed; the digest pins them
         meta["qkv_sha256"] = hashlib.sha256(b"".join(t.numpy().tobytes() for t in (q, k, v))).hexdigest()
@@ -238,8 +270,11 @@ def run_case(name: str, spec: dict, ref_root: Path) -> dict:
 
 def main() -> None:
     ref_root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    only = set(sys.argv[2:])  # optional case names: regenerate just those
     torch.set_num_threads(1)
     for name, spec in CASES.items():
+        if only and name not in only:
+            continue
         arrs = run_case(name, spec, ref_root)
         np.savez_compressed(HERE / f"{name}.npz", **arrs)
         print(name, "saved", sum(a.nbytes for a in arrs.values()), "bytes")

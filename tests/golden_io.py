@@ -48,6 +48,17 @@ class Golden:
     def f(self, key: str) -> np.ndarray:
         return from_bits(self.arrs[key], self.dt)
 
+    def mask_for(self, t_q: int, t_k: int):
+        """The call's mask (True = attend): the recorded user mask, the causal
+        mask of config.causal for a ``t_q`` x ``t_k`` call, or None."""
+        kind = self.meta.get("mask")
+        if kind == "causal":
+            i = np.arange(t_q)[:, None]
+            return np.arange(t_k)[None, :] <= i + (t_k - t_q)
+        if kind in ("user2", "user4"):
+            return self.arrs["mask"].astype(bool)
+        return None
+
     def inputs(self):
         """fp32-valued numpy ``(q, k, v)`` in module layout ``[B, T/S, E]``."""
         if "q" in self.arrs:

@@ -49,14 +49,14 @@ def oracle_config(w: dict, adaptive: str = "entropy", alpha: float = 1.0, beta_i
                            hvaq_beta_init=beta_init, hvaq_alpha=alpha)
 
 
-def cuda_forward_heads(qg_bhtd: torch.Tensor, state, cb, cfg: O.ForwardConfig):
+def cuda_forward_heads(qg_bhtd: torch.Tensor, state, cb, cfg: O.ForwardConfig, present=None):
     """Run ops.forward with diagnostics; returns (out [B,H,T,D] numpy, diag)."""
     from avqa_b200 import ops
     D = qg_bhtd.shape[-1]
     hv = 0 if not cfg.hvaq or cfg.hvaq_adaptive == "none" else {"entropy": 1, "linear": 2}[cfg.hvaq_adaptive]
     beta0 = cfg.hvaq_beta_init if cfg.hvaq_beta_init > 0 else 1.0 / np.sqrt(D)
     out, diag = ops.forward(qg_bhtd, cb, state, min(cfg.refinement_budget, cfg.num_codewords), cfg.passes,
-                            cfg.pass_decay, hv, float(beta0), cfg.hvaq_alpha, diagnostics=True)
+                            cfg.pass_decay, hv, float(beta0), cfg.hvaq_alpha, diagnostics=True, present=present)
     torch.cuda.synchronize()
     return out.float().cpu().numpy(), diag
 

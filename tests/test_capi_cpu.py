@@ -48,7 +48,7 @@ def test_forward_rejects_bad_arguments(call: str) -> None:
         args["P"] = 9
     sb = 3 if call == "state_batch" else 1
     rc = lib.avq_forward(args["dtype"], args["q"], s, 1, 1, 1, 8, args["M0"], 2, None, None, None, None, None, None,
-                         sb, None, None, args["P"], 1, 1.0, 0, 0.0, 1.0, None, s, None, None, None, None, 0, None)
+                         sb, None, None, None, args["P"], 1, 1.0, 0, 0.0, 1.0, None, s, None, None, None, None, 0, None)
     assert rc == 1
     msg = _lib.last_error()
     assert msg.startswith("avq_forward")

@@ -13,8 +13,8 @@ import torch
 
 import golden_io as G
 from oracle import avq_oracle as O
-from parity import (OUT_TOL, assert_quant_equal, check_quantization, check_routing, cuda_forward_heads, heads_view,
-                    normrel, oracle_config, quant_arrays, to_dev)
+from parity import (OUT_TOL, assert_quant_equal, check_quantization, check_routing, cuda_forward_heads,
+                    finite_normrel, heads_view, normrel, oracle_config, quant_arrays, to_dev)
 
 pytestmark = pytest.mark.gpu
 
@@ -75,13 +75,14 @@ def test_golden_case(name: str) -> None:
             yield qd, k, v, st, q
     sel_i = 0
     for ci, (qdev, kfull, vfull, st, qnp) in enumerate(calls()):
-        res = O.forward(qnp, kfull, vfull, pd, cd, cfg)
+        mask = g.mask_for(qnp.shape[1], kfull.shape[1])
+        res = O.forward(qnp, kfull, vfull, pd, cd, cfg, mask=mask)
         got_q = quant_arrays(st, B, H)
         if got_q["passign"] is not None:
             quant = check_quantization(got_q, O.split_heads(kfull, H), O.split_heads(vfull, H), pd, cd, dt,
                                        res["quant"], tag=f"{name} call{ci} vs oracle")
             if quant is not res["quant"]:
-                res = O.forward(qnp, kfull, vfull, pd, cd, cfg, quant=quant)
+                res = O.forward(qnp, kfull, vfull, pd, cd, cfg, quant=quant, mask=mask)
         else:
             assert_quant_equal(got_q, res["quant"], tag=f"{name} call{ci} vs oracle")
         want = _golden_quant(g, ci, (B * H, C, D))
@@ -92,7 +93,13 @@ def test_golden_case(name: str) -> None:
             np.testing.assert_array_equal(got_q[key], want[key], err_msg=f"{name} call{ci} {key} vs reference")
         if res.get("naive"):
             continue
-        out, diag = cuda_forward_heads(heads_view(qdev, H), st, cb, cfg)
+        present = None
+        if mask is not None:  # the codeword visibility bits, compared with the oracle's
+            present = ops.codeword_presence(st, qnp.shape[1], torch.from_numpy(np.ascontiguousarray(mask)))
+            bits = present.cpu().numpy().view(np.uint32)
+            got_p = ((bits[..., :, None] >> np.arange(32, dtype=np.uint32)) & 1).reshape(*bits.shape[:2], -1)
+            np.testing.assert_array_equal(got_p[..., :M0].astype(bool), res["present"], err_msg=f"{name} present")
+        out, diag = cuda_forward_heads(heads_view(qdev, H), st, cb, cfg, present)
         check_routing(diag, res, dt, tag=f"{name} call{ci}")
         for s in diag.selections():
             gs = g.get(f"sel{sel_i}").reshape(B * H, -1)
@@ -100,5 +107,6 @@ def test_golden_case(name: str) -> None:
             sel_i += 1
         out_bte = out.transpose(0, 2, 1, 3).reshape(B, -1, H * D)
         ref_out = g.get(f"out{ci}").reshape(out_bte.shape)
-        assert normrel(out_bte, ref_out) <= tol, f"{name} call{ci}: {normrel(out_bte, ref_out)} vs reference"
-        assert normrel(out_bte, res["out_bte"]) <= tol
+        err_ref, _ = finite_normrel(out_bte, ref_out, f"{name} call{ci} vs reference")
+        err_orc, _ = finite_normrel(out_bte, res["out_bte"], f"{name} call{ci} vs oracle")
+        assert err_ref <= tol and err_orc <= tol, f"{name} call{ci}: {err_ref} vs reference, {err_orc} vs oracle"
