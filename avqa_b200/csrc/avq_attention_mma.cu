@@ -115,8 +115,10 @@ __global__ void __launch_bounds__(128, 4) parent_attn_mma_kernel(
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float x = rnd<DT>(acc[j][e]);
-          const int tq = t0 + (e >= 2 ? r1 : r0);  // pipeline.py:106 (user / causal mask), :107 (empty)
-          const bool vis = !present || (tq < Tq && p < M0 && present_bit(present, (M0 + 31) >> 5, (long)g * Tq + tq, p));
+          // pipeline.py:106 (user / causal mask), :107 (empty); element e is column cl + (e & 1)
+          const int tq = t0 + (e >= 2 ? r1 : r0), pe = p + (e & 1);
+          const bool vis =
+              !present || (tq < Tq && pe < M0 && present_bit(present, (M0 + 31) >> 5, (long)g * Tq + tq, pe));
           s[e] = nb[cl + (e & 1)] > 0.f && vis ? scale_logit<DT>(x, sqrtD, inv_sqrtD) : -INFINITY;
         }
         const uint32_t s01 = pack2<DT>(s[0], s[1]), s23 = pack2<DT>(s[2], s[3]);
