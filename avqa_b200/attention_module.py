@@ -70,8 +70,6 @@ class AVQAttention(nn.Module):
     def _check_supported(self) -> None:
         c = self.config
         unsupported = []
-        if c.codebook.bcar_enabled:
-            unsupported.append("codebook.bcar_enabled")
         if c.routing.strategy == "threshold":
             unsupported.append("routing.strategy='threshold'")
         if c.refinement.adaptive_budget:
@@ -195,6 +193,16 @@ def cuda_run_pipeline(m, query: torch.Tensor, key: torch.Tensor, value: torch.Te
     backend: CUDABackend = m.backend  # type: ignore[assignment]
     cb = backend.prepared_codebook(m.codebook.parents, m.codebook.children, q.dtype, q.device)
     state = resolve_quantization(m, k, v, cb, kv_cache)
+    if c.codebook.bcar_enabled and state.S > 0:
+        # run_vq_precompute (attention_module.py:420-428): the codebook adapts
+        # to this call's keys after their quantization; the attention below
+        # uses the adapted codebook over the unadapted quantization
+        if state.passign is None:
+            raise BackendError("BCAR over a KV cache after a decode step is not supported by the cuda backend: "
+                               "its decode state keeps no per-key assignments")
+        kf = k if kv_cache is None else _full_keys(kv_cache, k)
+        ops.bcar_update(kf, state, m.codebook.parents, m.codebook.children, c.codebook.bcar_decay)
+        cb = backend.prepared_codebook(m.codebook.parents, m.codebook.children, q.dtype, q.device)
     B, _, T, D = q.shape
     if state.S == 0:
         # pipeline.py:344-345: budget 0 -> naive attention over zero keys
@@ -283,6 +291,13 @@ def global_min_valid(state: ops.QuantState, group=None) -> tuple[torch.Tensor, t
         ready.record(side)
     g.record_stream(side)
     return g, ready
+
+
+def _full_keys(kv_cache, k: torch.Tensor) -> torch.Tensor:
+    """The cached keys followed by none: after the first call with a cache,
+    the cache holds every key the state quantized (resolve_kv_cache)."""
+    ck, _ = kv_cache.lookup()
+    return ck.to(device=k.device, dtype=k.dtype)
 
 
 def _cache_states(kv_cache) -> dict:

@@ -157,6 +157,36 @@ size_t avq_forward_workspace_size(int dtype, int B, int H, int T, int D, int M0,
   return avq::forward_workspace_bytes(dtype, B * H, T, D, M0, C, P, passes, pass_decay, hvaq);
 }
 
+size_t avq_bcar_workspace_size(int B, int H, int M0, int C, int D) {
+  if (B < 0 || H <= 0 || M0 <= 0 || C <= 0 || D <= 0 || too_many_groups(B, H)) return 0;
+  return avq::bcar_workspace_bytes(B * H, M0, C, D);
+}
+
+int avq_bcar_update(int dtype, const void* keys, const long long* key_strides, const int* passign, const int* cassign,
+                    int B, int H, int S, int D, int M0, int C, float decay, const void* children_in, void* children_out,
+                    void* parents_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (bad_dtype(dtype)) return fail(AVQ_ERR_ARG, "avq_bcar_update: bad dtype %d", dtype);
+  if (B <= 0 || H <= 0 || S < 0 || D <= 0 || M0 <= 0 || C <= 0) return fail(AVQ_ERR_ARG, "avq_bcar_update: bad sizes");
+  if (too_many_groups(B, H)) return fail(AVQ_ERR_ARG, "avq_bcar_update: B*H exceeds INT_MAX");
+  if (!(decay >= 0.f && decay < 1.f))
+    return fail(AVQ_ERR_ARG, "avq_bcar_update: decay must be in [0, 1), got %g", (double)decay);
+  if (!key_strides || !children_in || !children_out || !parents_out || (S > 0 && (!keys || !passign || !cassign)))
+    return fail(AVQ_ERR_ARG, "avq_bcar_update: null pointer");
+  if (children_out == children_in)
+    return fail(AVQ_ERR_ARG, "avq_bcar_update: children_out must not alias children_in");
+  const size_t need = avq::bcar_workspace_bytes(B * H, M0, C, D);
+  if (workspace_bytes < need || !workspace)
+    return fail(AVQ_ERR_WORKSPACE, "avq_bcar_update: workspace %zu < %zu bytes", workspace_bytes, need);
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc;
+  switch (dtype) {
+    case 0: rc = avq::launch_bcar<avq::DT_F32>(keys, st3(key_strides), passign, cassign, B, H, S, D, M0, C, decay, children_in, children_out, parents_out, workspace, st); break;
+    case 1: rc = avq::launch_bcar<avq::DT_BF16>(keys, st3(key_strides), passign, cassign, B, H, S, D, M0, C, decay, children_in, children_out, parents_out, workspace, st); break;
+    default: rc = avq::launch_bcar<avq::DT_F16>(keys, st3(key_strides), passign, cassign, B, H, S, D, M0, C, decay, children_in, children_out, parents_out, workspace, st); break;
+  }
+  return finish(rc, "avq_bcar_update");
+}
+
 int avq_presence_words(int M0) { return M0 > 0 ? avq::presence_words(M0) : 0; }
 
 int avq_codeword_presence(const int* passign, int B, int H, int S, int M0, int T, int state_batch,

@@ -206,6 +206,13 @@ int read_device_fault(int* code, cudaStream_t st);
 int read_fault_assign(int* code, cudaStream_t st);
 int read_fault_correct(int* code, cudaStream_t st);
 
+// BCAR online codebook adaptation (avq_bcar.cu).
+size_t bcar_workspace_bytes(int G, int M0, int C, int D);
+template <int DT>
+int launch_bcar(const void* keys, Strides3 ks, const int* passign, const int* cassign, int B, int H, int S, int D,
+                int M0, int C, float decay, const void* ch_in, void* ch_out, void* parents_out, void* workspace,
+                cudaStream_t st);
+
 // Codeword visibility bits under a causal (mask == nullptr) or user mask
 // (avq_mask.cu).
 int presence_words(int M0);

@@ -196,6 +196,32 @@ def codeword_presence(state: QuantState, T: int, mask: torch.Tensor | None = Non
     return out
 
 
+def bcar_update(keys: torch.Tensor, state: QuantState, parents: torch.Tensor, children: torch.Tensor,
+                decay: float) -> None:
+    """BCAR (online_adaptation.py:37-127): adapt ``children`` [H, M0, C, D]
+    toward the means of the keys ``[B, H, S, D]`` that ``state`` assigned to
+    each child cell and re-derive ``parents`` [H, M0, D] as their children's
+    means, in place, in the codebook dtype (= the keys' dtype)."""
+    from avqa_b200.exceptions import NotInitializedError
+    lib = _lib.load()
+    if state.passign is None:
+        raise NotInitializedError("BCAR needs the key assignments of this state (not kept after a decode append)")
+    B, H, S, D = keys.shape
+    _, M0, C, _ = children.shape
+    dev = keys.device
+    new_c = torch.empty_like(children)
+    new_p = torch.empty_like(parents)
+    ws_bytes = lib.avq_bcar_workspace_size(B, H, M0, C, D)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    rc = lib.avq_bcar_update(_lib.dtype_code(keys.dtype), keys.data_ptr(), _lib.strides3(keys),
+                             _lib.ptr(state.passign), _lib.ptr(state.cassign), B, H, S, D, M0, C, float(decay),
+                             children.data_ptr(), new_c.data_ptr(), new_p.data_ptr(), ws.data_ptr(), ws_bytes,
+                             _lib.stream_of(dev))
+    _lib.check(rc, "avq_bcar_update")
+    children.copy_(new_c)
+    parents.copy_(new_p)
+
+
 @dataclass
 class ForwardDiagnostics:
     importance: torch.Tensor  # [G, M0] fp32 (pre-HVAQ importance, dtype values)
@@ -269,5 +295,5 @@ def forward(q: torch.Tensor, cb: PreparedCodebook, st: QuantState, P: int, passe
     return out, diag
 
 
-__all__ = ["ForwardDiagnostics", "PreparedCodebook", "QuantState", "append", "codeword_presence", "forward",
-           "pass_caps", "prepare_codebook", "quantize"]
+__all__ = ["ForwardDiagnostics", "PreparedCodebook", "QuantState", "append", "bcar_update", "codeword_presence",
+           "forward", "pass_caps", "prepare_codebook", "quantize"]

@@ -25,6 +25,9 @@
  *                         cache.py:246-260, plus the re-quantization of the grown key
  *                         set (quantizer.py:166-278) done incrementally
  *   avq_reduce_min        the budget's min over (b,h) of valid parents, pipeline.py:341-342
+ *   avq_codeword_presence the user / causal mask's codeword visibility, pipeline.py:82-106,
+ *                         attention_module.py:210-223, 369-390
+ *   avq_bcar_update       online_codebook_adaptation, online_adaptation.py:37-127
  *   avq_device_fault      no counterpart: device-side fault record of the bounded waits
  *   avq_quantize_noalloc  no counterpart: avq_quantize with its scratch in a fixed
  *                         device array, for hosts that cannot allocate
@@ -116,6 +119,22 @@ int avq_quantize_noalloc(int dtype, const void* keys, const long long* key_strid
                          const void* parents_dt, const float* p_sq, const void* children_dt, const float* c_sq,
                          int* passign, int* cassign, void* pagg, void* cagg, float* pacc, float* cacc, int* pcnt,
                          int* ccnt, int* nvalid, int* gmin_valid, void* stream);
+
+size_t avq_bcar_workspace_size(int B, int H, int M0, int C, int D);
+
+/* BCAR online codebook adaptation (online_adaptation.py:37-127, run by
+ * run_vq_precompute, attention_module.py:420-428): one EMA step of the child
+ * codebook toward the mean of the keys assigned to each child cell,
+ * children' = c + DT(w * DT(mean - c)) with w = DT(1 - decay) where the cell
+ * got keys, averaged over the batch (the reference tiles the codebook with
+ * repeat_interleave(B) while groups are ordered b*H + h; that pairing is
+ * kept), then parents' = mean of their children.  keys [B,H,S,D] (strides as
+ * avq_quantize), passign/cassign [B*H, S] from avq_quantize; children_in
+ * [H,M0,C,D] in dtype; writes children_out (must not alias children_in) and
+ * parents_out [H,M0,D].  workspace: avq_bcar_workspace_size bytes. */
+int avq_bcar_update(int dtype, const void* keys, const long long* key_strides, const int* passign, const int* cassign,
+                    int B, int H, int S, int D, int M0, int C, float decay, const void* children_in, void* children_out,
+                    void* parents_out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Words per (b,h, query) row of the codeword visibility bits: ceil(M0 / 32). */
 int avq_presence_words(int M0);

@@ -220,6 +220,62 @@ def quantize(keys, values, parents, children, dt: str) -> Quantization:
 
 
 # ---------------------------------------------------------------------------
+# BCAR online codebook adaptation: online_adaptation.py:37-127
+# ---------------------------------------------------------------------------
+
+
+def bcar_update(keys_g: np.ndarray, passign: np.ndarray, cassign: np.ndarray, parents: np.ndarray,
+                children: np.ndarray, B: int, decay: float, dt: str) -> tuple[np.ndarray, np.ndarray]:
+    """One EMA step of the child codebook, parents re-derived as the mean of
+    their children; returns the new ``(parents, children)`` in ``dt``.
+
+    ``keys_g`` [G, S, D], assignments [G, S] (G = B*H, g = b*H + h),
+    ``parents`` [H, M0, D], ``children`` [H, M0, C, D] holding dt values.
+    Follows the reference op by op in the codebook dtype:
+
+    * per group and cell: the key sum (an einsum with a one-hot matrix:
+      the exact sum rounded through fp32), the count (a sum, rounded), its
+      reciprocal, the mean ``DT(sum * DT(1 / count))`` (online_adaptation.py:99-108);
+    * ``new = DT(c + DT(w * DT(mean - c)))`` with ``w = DT(fp32(1 - decay))``
+      where the cell received keys, else 0 (:113-115);
+    * the tiled codebook is ``children.repeat_interleave(B, dim=0)`` while
+      the groups are ordered b-major, so group ``i = b*H + h`` updates the
+      children of head ``i // B`` and the results are averaged over ``b``
+      as ``view(B, H, ...)`` reads them (:95, :116) -- for B > 1 the head
+      pairing is the reference's own;
+    * cells that received no key in any b keep their children (:117-123);
+      then ``parents = DT(mean over c)`` (:126).
+    """
+    G, S, D = keys_g.shape
+    H, M0, C, _ = children.shape
+    MC = M0 * C
+    f64 = np.float64
+    sums = np.zeros((G, MC, D), f64)
+    cnts = np.zeros((G, MC), np.int64)
+    cell = passign.astype(np.int64) * C + cassign.astype(np.int64)
+    for g in range(G):
+        np.add.at(sums[g], cell[g], keys_g[g].astype(f64))
+        cnts[g] = np.bincount(cell[g], minlength=MC)
+    sum_dt = rnd(sums, dt)
+    cnt_dt = rnd(cnts.astype(f64), dt)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        inv = np.where(cnt_dt > 0, rnd(1.0 / np.where(cnt_dt > 0, cnt_dt, 1.0).astype(f64), dt), np.float32(0))
+    mean = rnd(sum_dt.astype(f64) * inv[..., None].astype(f64), dt)
+    has = cnts > 0
+    w = np.where(has, np.float32(rnd(np.array([np.float32(1.0 - decay)], f64), dt)[0]), np.float32(0))
+    src = children.reshape(H, MC, D)[np.arange(G) // B]  # repeat_interleave(B, dim=0)
+    with np.errstate(invalid="ignore", over="ignore"):
+        diff = rnd(mean.astype(f64) - src, dt)
+        upd = rnd(w[..., None].astype(f64) * diff, dt)
+        new_bh = rnd(src.astype(f64) + upd, dt)
+        per_h = rnd(new_bh.reshape(B, H, MC, D).astype(f64).sum(0).astype(np.float32).astype(f64) / B, dt)
+    any_b = has.reshape(B, H, MC).any(0)
+    new_children = np.where(any_b[..., None], per_h, children.reshape(H, MC, D)).reshape(H, M0, C, D)
+    new_parents = rnd(new_children.astype(f64).sum(2).astype(np.float32).astype(f64) / C, dt)
+    return new_parents.astype(np.float32), new_children.astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
 # Parent attention: pipeline.py:46-151
 # ---------------------------------------------------------------------------
 
@@ -555,7 +611,8 @@ def cast_codebook(parents32: np.ndarray, children32: np.ndarray, dt: str):
 
 
 __all__ = [
-    "DTYPES", "EPS", "ForwardConfig", "Quantization", "SoftmaxState", "cast_codebook", "causal_mask",
+    "DTYPES", "EPS", "ForwardConfig", "Quantization", "SoftmaxState", "bcar_update", "cast_codebook",
+    "causal_mask",
     "codeword_present", "expand_mask",
     "child_logits_sel", "compute_pass_budgets", "correction", "count_saturation", "first_argmin",
     "forward", "forward_heads", "hvaq_logits", "importance", "merge_heads", "online_softmax",

@@ -77,6 +77,15 @@ CASES: dict[str, dict] = {
                                mask="causal"),
     "causal_chunks_bf16": dict(w=Workload("cch", B=1, T=64, S=64, H=2, D=64, M0=16, C=4, P=6, dtype="bf16",
                                           keys="mixture", seed=16, q_chunk=32), mask="causal"),
+    # BCAR online codebook adaptation (online_adaptation.py:37-127), two calls
+    # in a row so that the second quantizes against the adapted codebook; B > 1
+    # exercises the reference's tiling of the codebook over the batch
+    "bcar_bf16": dict(w=Workload("bcar", B=1, T=64, S=200, H=2, D=64, M0=16, C=4, P=6, dtype="bf16",
+                                 keys="mixture", seed=17), bcar=0.9, calls=2),
+    "bcar_b2_f32": dict(w=Workload("bcar2", B=2, T=32, S=96, H=3, D=32, M0=12, C=2, P=4, dtype="f32",
+                                   keys="mixture", seed=18), bcar=0.8, calls=2),
+    "bcar_b3_f16": dict(w=Workload("bcar3", B=3, T=40, S=120, H=2, D=64, M0=16, C=4, P=5, dtype="f16",
+                                   keys="aniso", seed=19), bcar=0.95, calls=2),
 }
 
 
@@ -151,7 +160,8 @@ def run_case(name: str, spec: dict, ref_root: Path) -> dict:
     cfg = AVQConfig(
         causal=spec.get("mask") == "causal",
         attention=AttentionShapeConfig(embed_dim=w.E, num_heads=H),
-        codebook=CodebookConfig(num_codewords=w.M0, children_per_codeword=w.C),
+        codebook=CodebookConfig(num_codewords=w.M0, children_per_codeword=w.C,
+                                bcar_enabled="bcar" in spec, bcar_decay=spec.get("bcar", 0.99)),
         routing=RoutingConfig(strategy=spec.get("strategy", "topp"), refinement_budget=w.P),
         refinement=RefinementConfig(passes=w.passes, pass_decay=w.pass_decay),
         backend=BackendConfig(hopfield=w.hvaq),
@@ -223,7 +233,9 @@ def run_case(name: str, spec: dict, ref_root: Path) -> dict:
                 for c0 in range(0, w.T, w.q_chunk):
                     rec["out"].append(mod(q[:, c0:c0 + w.q_chunk], k, v))
             else:
-                rec["out"].append(mod(q, k, v, mask=mask))
+                for _ in range(spec.get("calls", 1)):
+                    rec["out"].append(mod(q, k, v, mask=mask))
+                    rec.setdefault("cb", []).append((mod.codebook.parents.clone(), mod.codebook.children.clone()))
     finally:
         apl.online_softmax = orig_os
         apl.compute_importance, amp.compute_importance = orig_ci_p, orig_ci_m
@@ -259,6 +271,9 @@ def run_case(name: str, spec: dict, ref_root: Path) -> dict:
         arrs[f"sel{i}"] = t.numpy().astype(np.int32)
     for i, t in enumerate(rec["beta"]):
         arrs[f"beta{i}"] = bits(t)
+    for i, (pp, cc) in enumerate(rec.get("cb", []) if "bcar" in spec else []):
+        arrs[f"cb{i}_parents"], arrs[f"cb{i}_children"] = bits(pp), bits(cc)
+    meta["bcar_decay"] = spec.get("bcar")
     for i, t in enumerate(rec["out"]):
         arrs[f"out{i}"] = t.float().numpy()
         meta[f"out{i}_dtype"] = str(t.dtype)

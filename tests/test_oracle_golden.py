@@ -28,6 +28,19 @@ def _calls(g: G.Golden):
             qt, kt, vt = (O.rnd(x.numpy(), dt) for x in (qt, kt, vt))
             kk, vv = np.concatenate([kk, kt], 1), np.concatenate([vv, vt], 1)
             yield O.forward(qt, kk, vv, pd, cd, cfg)
+    elif g.meta.get("bcar_decay"):
+        # each call quantizes with the current codebook, adapts it (BCAR) and
+        # attends with the adapted codebook over the unadapted quantization
+        H, D = w["H"], w["D"]
+        kg, vg = O.split_heads(k, H), O.split_heads(v, H)
+        n_calls = g.meta["n_calls"]
+        for _ in range(n_calls):
+            quant = O.quantize(kg, vg, pd, cd, dt)
+            pd, cd = O.bcar_update(kg, quant.parent_assignments, quant.child_assignments, pd, cd, w["B"],
+                                   g.meta["bcar_decay"], dt)
+            res = O.forward(q, k, v, pd, cd, cfg, quant=quant)
+            res["codebook"] = (pd, cd)
+            yield res
     elif w["q_chunk"]:
         for c0 in range(0, w["T"], w["q_chunk"]):
             qc = q[:, c0:c0 + w["q_chunk"]]
@@ -67,11 +80,21 @@ def test_oracle_matches_reference(name: str) -> None:
         # the reference's own non-finite outputs (fp16) must sit in the same places
         err, _ = finite_normrel(res["out_bte"], g.get(f"out{ci}").reshape(res["out_bte"].shape), name)
         assert err <= OUT_TOL[dt], err
+        if "codebook" in res:
+            # the adapted codebook: bit for bit in bf16 / fp16, where the
+            # reference's one-hot einsum sums the keys exactly in fp32; in fp32
+            # that einsum rounds in its own order, so within a few ulp
+            for got, key in zip(res["codebook"], ("parents", "children")):
+                want = g.f(f"cb{ci}_{key}").reshape(got.shape)
+                if dt == "f32":
+                    np.testing.assert_allclose(got, want, rtol=4 * 2.0 ** -23, atol=1e-7, err_msg=f"{name} {key}")
+                else:
+                    np.testing.assert_array_equal(got, want, err_msg=f"{name} {key}")
         assert err <= 1e-5, f"oracle drifted from the reference: {err}"
 
 
 def test_fixtures_cover_every_config_family() -> None:
     names = set(G.case_names())
     for must in ("c1_readme_f32", "mix_bf16", "mp_hvaq_f16", "decode_bf16", "rope_bf16", "empty_keys_bf16",
-                 "ties_bf16", "mp_quirk_f32", "causal_bf16", "mask2_f32", "mask4_bf16"):
+                 "ties_bf16", "mp_quirk_f32", "causal_bf16", "mask2_f32", "mask4_bf16", "bcar_bf16", "bcar_b2_f32"):
         assert must in names
