@@ -30,6 +30,7 @@ _SIGS = {
                       _P, _P, _P, _Z, _P], _I),
     "avq_selection_stride": ([_I, _I, _F], _I),
     "avq_forward_workspace_size": ([_I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I], _Z),
+    "avq_dense_attention": ([_I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P], _I),
     "avq_bcar_workspace_size": ([_I, _I, _I, _I, _I], _Z),
     "avq_bcar_update": ([_I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _Z, _P], _I),
     "avq_presence_words": ([_I], _I),

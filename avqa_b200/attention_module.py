@@ -76,8 +76,6 @@ class AVQAttention(nn.Module):
             unsupported.append("refinement.adaptive_budget")
         if c.hopfield.learnable_parent_beta or c.hopfield.learnable_alpha:
             unsupported.append("hopfield.learnable_*")
-        if not c.refinement.enabled or c.execution.mode == "reference":
-            unsupported.append("dense (naive) attention path")
         if c.execution.compile_enabled:
             unsupported.append("execution.compile_enabled")
         if unsupported:
@@ -191,6 +189,10 @@ def cuda_run_pipeline(m, query: torch.Tensor, key: torch.Tensor, value: torch.Te
     v = AVQAttention.split_heads(vp, H)
     m.sync_codebook_device(q)
     backend: CUDABackend = m.backend  # type: ignore[assignment]
+    if not c.refinement.enabled or c.execution.mode == "reference":
+        # pipeline.py:310-312: no scheduler, or the reference mode: dense
+        # attention over the (cached) keys with the resolved mask
+        return dense_path(m, q, k, v, mask, kv_cache, chunk_size)
     cb = backend.prepared_codebook(m.codebook.parents, m.codebook.children, q.dtype, q.device)
     state = resolve_quantization(m, k, v, cb, kv_cache)
     if c.codebook.bcar_enabled and state.S > 0:
@@ -220,6 +222,34 @@ def cuda_run_pipeline(m, query: torch.Tensor, key: torch.Tensor, value: torch.Te
                         present=present)
         ready = None  # later chunks are ordered after the first one's wait
     return m.dropout(m.out_proj(out))
+
+
+def dense_path(m, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.Tensor | None, kv_cache,
+               chunk_size: int = 0) -> torch.Tensor:
+    """naive_fallback (pipeline.py:261-273) after resolve_kv_cache and
+    resolve_mask (attention_module.py:350-390): dense attention, merge heads,
+    output projection, dropout; the output keeps the input dtype.  Query
+    chunks are separate calls (each with its own causal offset)."""
+    if kv_cache is not None:
+        ck, cv = kv_cache.lookup()
+        new_k, new_v = k, v
+        if ck.shape[-2] > 0:
+            k = torch.cat([ck.to(device=k.device, dtype=k.dtype), k], dim=-2)
+            v = torch.cat([cv.to(device=v.device, dtype=v.dtype), v], dim=-2)
+        kv_cache.append(new_k, new_v)
+        _cache_states(kv_cache).clear()  # quantized states no longer cover the cache
+    B, H, T, D = q.shape
+    S = k.shape[-2]
+    out = torch.empty(B, H, T, D, dtype=q.dtype, device=q.device)
+    step = chunk_size if chunk_size > 0 else max(T, 1)
+    for t0 in range(0, T, step):
+        qc = q[:, :, t0:t0 + step]
+        Tq = qc.shape[2]
+        mk = mask
+        if mk is None and m.config.causal:
+            mk = torch.arange(S, device=q.device)[None, :] <= torch.arange(Tq, device=q.device)[:, None] + (S - Tq)
+        out[:, :, t0:t0 + Tq] = m.backend.naive_attention(qc, k, v, mk)
+    return m.dropout(m.out_proj(AVQAttention.merge_heads(out)))
 
 
 def codeword_mask(config: AVQConfig, state: ops.QuantState, T: int, mask: torch.Tensor | None,

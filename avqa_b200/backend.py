@@ -125,10 +125,20 @@ class CUDABackend(Backend):
 
     def naive_attention(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
                         mask: torch.Tensor | None = None) -> torch.Tensor:
+        """Dense softmax attention (backend.py:190-203) on the GPU, in the input dtype."""
         if key.shape[-2] == 0:
             # softmax over zero keys times zero values: the reference yields zeros
             return torch.zeros(*query.shape[:-1], value.shape[-1], dtype=query.dtype, device=query.device)
-        raise BackendError("naive (dense) attention is not provided by the cuda backend")
+        if value.shape[-1] != query.shape[-1]:
+            raise ShapeError("value head_dim must equal the query's", expected=query.shape[-1],
+                             actual=value.shape[-1])
+        return ops.dense_attention(query, key, value, mask)
+
+    def online_softmax_attention(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                                 block_size: int = 64, mask: torch.Tensor | None = None) -> torch.Tensor:
+        """The tiled online-softmax form (backend.py:105-156); the kernel tiles
+        by 64 keys whatever ``block_size`` says (the result is the same)."""
+        return online_softmax_attention(query, key, value, block_size, mask)
 
     # -- fused forward -------------------------------------------------------
 
@@ -140,4 +150,12 @@ class CUDABackend(Backend):
                            min_valid_ready, present)
 
 
-__all__ = ["Backend", "CUDABackend", "QuantizationResult"]
+def online_softmax_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, block_size: int = 64,
+                             mask: torch.Tensor | None = None) -> torch.Tensor:
+    """Tiled online-softmax attention (backend.py:105-156) on the GPU."""
+    if key.shape[-2] == 0:
+        return torch.zeros(*query.shape[:-1], value.shape[-1], dtype=query.dtype, device=query.device)
+    return ops.dense_attention(query, key, value, mask)
+
+
+__all__ = ["Backend", "CUDABackend", "QuantizationResult", "online_softmax_attention"]

@@ -157,6 +157,26 @@ size_t avq_forward_workspace_size(int dtype, int B, int H, int T, int D, int M0,
   return avq::forward_workspace_bytes(dtype, B * H, T, D, M0, C, P, passes, pass_decay, hvaq);
 }
 
+int avq_dense_attention(int dtype, const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+                        const void* v, const long long* v_strides, int B, int H, int T, int N, int D,
+                        const unsigned char* mask, const long long* mask_strides, void* out,
+                        const long long* out_strides, void* stream) {
+  if (bad_dtype(dtype)) return fail(AVQ_ERR_ARG, "avq_dense_attention: bad dtype %d", dtype);
+  if (B < 0 || H <= 0 || T < 0 || N < 0 || D <= 0) return fail(AVQ_ERR_ARG, "avq_dense_attention: bad sizes");
+  if (too_many_groups(B, H)) return fail(AVQ_ERR_ARG, "avq_dense_attention: B*H exceeds INT_MAX");
+  if (!q_strides || !k_strides || !v_strides || !out_strides || (mask && !mask_strides) ||
+      ((long long)B * T > 0 && (!q || !out)) || ((long long)B * N > 0 && (!k || !v)))
+    return fail(AVQ_ERR_ARG, "avq_dense_attention: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc;
+  switch (dtype) {
+    case 0: rc = avq::launch_dense_attention<avq::DT_F32>(q, st3(q_strides), k, st3(k_strides), v, st3(v_strides), B, H, T, N, D, mask, mask_strides, out, st3(out_strides), st); break;
+    case 1: rc = avq::launch_dense_attention<avq::DT_BF16>(q, st3(q_strides), k, st3(k_strides), v, st3(v_strides), B, H, T, N, D, mask, mask_strides, out, st3(out_strides), st); break;
+    default: rc = avq::launch_dense_attention<avq::DT_F16>(q, st3(q_strides), k, st3(k_strides), v, st3(v_strides), B, H, T, N, D, mask, mask_strides, out, st3(out_strides), st); break;
+  }
+  return finish(rc, "avq_dense_attention");
+}
+
 size_t avq_bcar_workspace_size(int B, int H, int M0, int C, int D) {
   if (B < 0 || H <= 0 || M0 <= 0 || C <= 0 || D <= 0 || too_many_groups(B, H)) return 0;
   return avq::bcar_workspace_bytes(B * H, M0, C, D);

@@ -206,6 +206,12 @@ int read_device_fault(int* code, cudaStream_t st);
 int read_fault_assign(int* code, cudaStream_t st);
 int read_fault_correct(int* code, cudaStream_t st);
 
+// Dense softmax attention (avq_dense.cu): the reference's naive path.
+template <int DT>
+int launch_dense_attention(const void* q, Strides3 qs, const void* k, Strides3 ks, const void* v, Strides3 vs, int B,
+                           int H, int T, int N, int D, const unsigned char* mask, const long long* mask_strides,
+                           void* out, Strides3 os, cudaStream_t st);
+
 // BCAR online codebook adaptation (avq_bcar.cu).
 size_t bcar_workspace_bytes(int G, int M0, int C, int D);
 template <int DT>

@@ -158,7 +158,7 @@ def codeword_presence(state: QuantState, T: int, mask: torch.Tensor | None = Non
     leading dims broadcast); without it the causal mask, query t seeing keys
     ``0 .. t + causal_offset`` (the reference uses ``S - T``).  ``query_batch``
     is the query batch when the state (batch 1) serves several."""
-    from avqa_b200.exceptions import ConfigurationError, NotInitializedError, ShapeError
+    from avqa_b200.exceptions import NotInitializedError
     lib = _lib.load()
     if state.passign is None:
         raise NotInitializedError("the codeword mask needs the key assignments of this state (not kept after a "
@@ -168,31 +168,53 @@ def codeword_presence(state: QuantState, T: int, mask: torch.Tensor | None = Non
     H, S, M0 = state.H, state.S, state.pcnt.shape[-1]
     W = lib.avq_presence_words(M0)
     out = torch.empty(Bq * H, T, W, dtype=torch.int32, device=dev)
-    strides = None
-    mptr = None
-    if mask is not None:
-        if mask.ndim not in (2, 4):
-            raise ConfigurationError("mask must be rank 2 [T_q, T_k] or rank 4 [B, H, T_q, T_k]",
-                                     {"got_rank": mask.ndim})
-        if tuple(mask.shape[-2:]) != (T, S):
-            raise ShapeError("mask shape does not match the queries and keys", expected=(T, S),
-                             actual=tuple(mask.shape[-2:]))
-        m = mask.to(device=dev, dtype=torch.uint8)
-        if m.stride(-1) != 1:
-            m = m.contiguous()
-        if m.ndim == 2:
-            st = (0, 0, m.stride(0))
-        else:
-            if m.shape[0] not in (1, Bq) or m.shape[1] not in (1, H):
-                raise ShapeError("rank-4 mask does not broadcast to [B, H, T, S]", expected=(Bq, H, T, S),
-                                 actual=tuple(m.shape))
-            st = (m.stride(0) if m.shape[0] > 1 else 0, m.stride(1) if m.shape[1] > 1 else 0, m.stride(2))
-        strides = (ctypes.c_longlong * 3)(*st)
-        mptr = m.data_ptr()  # m stays referenced until the kernel is enqueued
+    m, strides = _mask_operand(mask, Bq, H, T, S, dev)  # m stays referenced until the kernel is enqueued
     offset = (S - T) if causal_offset is None else causal_offset
-    rc = lib.avq_codeword_presence(_lib.ptr(state.passign), Bq, H, S, M0, T, state.B, mptr, strides, offset,
+    rc = lib.avq_codeword_presence(_lib.ptr(state.passign), Bq, H, S, M0, T, state.B, _lib.ptr(m), strides, offset,
                                    out.data_ptr(), _lib.stream_of(dev))
     _lib.check(rc, "avq_codeword_presence")
+    return out
+
+
+def _mask_operand(mask: torch.Tensor | None, B: int, H: int, T: int, S: int, dev):
+    """(uint8 mask tensor or None, ctypes strides {b, h, t} or None) of a
+    rank-2 [T, S] or rank-4 [B|1, H|1, T, S] mask (True = attend)."""
+    from avqa_b200.exceptions import ConfigurationError, ShapeError
+    if mask is None:
+        return None, None
+    if mask.ndim not in (2, 4):
+        raise ConfigurationError("mask must be rank 2 [T_q, T_k] or rank 4 [B, H, T_q, T_k]", {"got_rank": mask.ndim})
+    if tuple(mask.shape[-2:]) != (T, S):
+        raise ShapeError("mask shape does not match the queries and keys", expected=(T, S),
+                         actual=tuple(mask.shape[-2:]))
+    m = mask.to(device=dev, dtype=torch.uint8)
+    if m.stride(-1) != 1:
+        m = m.contiguous()
+    if m.ndim == 2:
+        st = (0, 0, m.stride(0))
+    else:
+        if m.shape[0] not in (1, B) or m.shape[1] not in (1, H):
+            raise ShapeError("rank-4 mask does not broadcast to [B, H, T, S]", expected=(B, H, T, S),
+                             actual=tuple(m.shape))
+        st = (m.stride(0) if m.shape[0] > 1 else 0, m.stride(1) if m.shape[1] > 1 else 0, m.stride(2))
+    return m, (ctypes.c_longlong * 3)(*st)
+
+
+def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                    mask: torch.Tensor | None = None) -> torch.Tensor:
+    """softmax(mask(q k^T / sqrt(D))) v for ``[B, H, T|N, D]`` views, in the
+    input dtype (backend.py:190-203); returns a ``[B, H, T, D]`` view."""
+    lib = _lib.load()
+    _cuda(q, "query")
+    B, H, T, D = q.shape
+    N = k.shape[2]
+    dev = q.device
+    out = torch.empty(B, T, H, D, dtype=q.dtype, device=dev).permute(0, 2, 1, 3)
+    m, mst = _mask_operand(mask, B, H, T, N, dev)
+    rc = lib.avq_dense_attention(_lib.dtype_code(q.dtype), q.data_ptr(), _lib.strides3(q), k.data_ptr(),
+                                 _lib.strides3(k), v.data_ptr(), _lib.strides3(v), B, H, T, N, D, _lib.ptr(m), mst,
+                                 out.data_ptr(), _lib.strides3(out), _lib.stream_of(dev))
+    _lib.check(rc, "avq_dense_attention")
     return out
 
 
@@ -296,4 +318,4 @@ def forward(q: torch.Tensor, cb: PreparedCodebook, st: QuantState, P: int, passe
 
 
 __all__ = ["ForwardDiagnostics", "PreparedCodebook", "QuantState", "append", "bcar_update", "codeword_presence",
-           "forward", "pass_caps", "prepare_codebook", "quantize"]
+           "dense_attention", "forward", "pass_caps", "prepare_codebook", "quantize"]

@@ -28,6 +28,8 @@
  *   avq_codeword_presence the user / causal mask's codeword visibility, pipeline.py:82-106,
  *                         attention_module.py:210-223, 369-390
  *   avq_bcar_update       online_codebook_adaptation, online_adaptation.py:37-127
+ *   avq_dense_attention   TorchBackend.naive_attention / online_softmax_attention,
+ *                         backend.py:105-156, 190-203
  *   avq_device_fault      no counterpart: device-side fault record of the bounded waits
  *   avq_quantize_noalloc  no counterpart: avq_quantize with its scratch in a fixed
  *                         device array, for hosts that cannot allocate
@@ -119,6 +121,19 @@ int avq_quantize_noalloc(int dtype, const void* keys, const long long* key_strid
                          const void* parents_dt, const float* p_sq, const void* children_dt, const float* c_sq,
                          int* passign, int* cassign, void* pagg, void* cagg, float* pacc, float* cacc, int* pcnt,
                          int* ccnt, int* nvalid, int* gmin_valid, void* stream);
+
+/* Dense softmax attention, the reference's naive path (backend.py:190-203,
+ * the online-softmax form of :105-156; used by execution.mode="reference",
+ * by refinement disabled and by the budget-0 fallback, pipeline.py:261-273,
+ * 310-345): out = softmax(mask(DT(DT(q k^T) * D^-1/2))) v in the input dtype.
+ * q [B,H,T,D], k and v [B,H,N,D] (strides as avq_quantize), out [B,H,T,D]
+ * (out_strides).  mask NULL, or uint8 (nonzero = attend) with element strides
+ * {b, h, t} and unit key stride (zero strides broadcast).  A query with every
+ * key masked gets NaN, as softmax over -inf does. */
+int avq_dense_attention(int dtype, const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+                        const void* v, const long long* v_strides, int B, int H, int T, int N, int D,
+                        const unsigned char* mask, const long long* mask_strides, void* out,
+                        const long long* out_strides, void* stream);
 
 size_t avq_bcar_workspace_size(int B, int H, int M0, int C, int D);
 

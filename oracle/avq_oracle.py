@@ -220,6 +220,28 @@ def quantize(keys, values, parents, children, dt: str) -> Quantization:
 
 
 # ---------------------------------------------------------------------------
+# Dense attention: backend.py:190-203 (TorchBackend.naive_attention)
+# ---------------------------------------------------------------------------
+
+
+def naive_attention(qg, kg, vg, dt: str, mask_g: np.ndarray | None = None) -> np.ndarray:
+    """``softmax(mask(DT(DT(q k^T) * D^-1/2))) v`` in the dtype: the logits
+    and the probabilities rounded to the dtype, the product rounded once.
+    ``[G, T|N, D]`` inputs, ``mask_g`` [G, T, N] (True = attend); a fully
+    masked query is NaN (softmax over -inf)."""
+    D = qg.shape[-1]
+    scale = opmath_scalar(float(D ** -0.5))
+    with np.errstate(invalid="ignore", over="ignore", divide="ignore"):
+        s = rnd(rnd(np.matmul(_f64(qg), _f64(kg).swapaxes(-1, -2)), dt).astype(np.float64) * scale, dt)
+        if mask_g is not None:
+            s = np.where(mask_g, s, np.float32(-np.inf))
+        mx = s.max(-1, keepdims=True)
+        e = np.exp(_f64(s) - mx)
+        probs = rnd(e / e.sum(-1, keepdims=True), dt)
+        return rnd(np.matmul(_f64(probs), _f64(vg)), dt)
+
+
+# ---------------------------------------------------------------------------
 # BCAR online codebook adaptation: online_adaptation.py:37-127
 # ---------------------------------------------------------------------------
 
@@ -612,6 +634,7 @@ def cast_codebook(parents32: np.ndarray, children32: np.ndarray, dt: str):
 
 __all__ = [
     "DTYPES", "EPS", "ForwardConfig", "Quantization", "SoftmaxState", "bcar_update", "cast_codebook",
+    "naive_attention",
     "causal_mask",
     "codeword_present", "expand_mask",
     "child_logits_sel", "compute_pass_budgets", "correction", "count_saturation", "first_argmin",

@@ -86,6 +86,12 @@ CASES: dict[str, dict] = {
                                    keys="mixture", seed=18), bcar=0.8, calls=2),
     "bcar_b3_f16": dict(w=Workload("bcar3", B=3, T=40, S=120, H=2, D=64, M0=16, C=4, P=5, dtype="f16",
                                    keys="aniso", seed=19), bcar=0.95, calls=2),
+    # the dense path (backend.py:190-203): execution.mode = "reference" with the
+    # causal mask, and refinement disabled with a rank-2 user mask
+    "dense_ref_bf16": dict(w=Workload("dense", B=2, T=48, S=80, H=2, D=64, M0=16, C=4, P=6, dtype="bf16",
+                                      keys="mixture", seed=20), mode="reference", mask="causal"),
+    "dense_norefine_f32": dict(w=Workload("dense2", B=1, T=40, S=64, H=2, D=32, M0=12, C=2, P=4, dtype="f32",
+                                          keys="mixture", seed=21), refine=False, mask="user2"),
 }
 
 
@@ -157,13 +163,15 @@ def run_case(name: str, spec: dict, ref_root: Path) -> dict:
     mask = None
     if spec.get("mask") in ("user2", "user4"):
         mask = user_mask(w, 2 if spec["mask"] == "user2" else 4)
+    from avqa.config import ExecutionConfig
     cfg = AVQConfig(
         causal=spec.get("mask") == "causal",
+        execution=ExecutionConfig(mode=spec.get("mode", "optimized")),
         attention=AttentionShapeConfig(embed_dim=w.E, num_heads=H),
         codebook=CodebookConfig(num_codewords=w.M0, children_per_codeword=w.C,
                                 bcar_enabled="bcar" in spec, bcar_decay=spec.get("bcar", 0.99)),
         routing=RoutingConfig(strategy=spec.get("strategy", "topp"), refinement_budget=w.P),
-        refinement=RefinementConfig(passes=w.passes, pass_decay=w.pass_decay),
+        refinement=RefinementConfig(enabled=spec.get("refine", True), passes=w.passes, pass_decay=w.pass_decay),
         backend=BackendConfig(hopfield=w.hvaq),
         hopfield=HopfieldConfig(adaptive=spec.get("adaptive", "entropy") if w.hvaq else "none",
                                 alpha=spec.get("alpha", 1.0)),
@@ -274,6 +282,7 @@ def run_case(name: str, spec: dict, ref_root: Path) -> dict:
     for i, (pp, cc) in enumerate(rec.get("cb", []) if "bcar" in spec else []):
         arrs[f"cb{i}_parents"], arrs[f"cb{i}_children"] = bits(pp), bits(cc)
     meta["bcar_decay"] = spec.get("bcar")
+    meta["dense"] = spec.get("mode") == "reference" or spec.get("refine", True) is False
     for i, t in enumerate(rec["out"]):
         arrs[f"out{i}"] = t.float().numpy()
         meta[f"out{i}_dtype"] = str(t.dtype)

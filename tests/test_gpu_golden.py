@@ -41,6 +41,8 @@ def test_golden_case(name: str) -> None:
     g = G.load(name)
     if g.meta.get("bcar_decay"):
         pytest.skip("BCAR adapts the codebook between quantization and attention: tests/test_gpu_bcar.py")
+    if g.meta.get("dense"):
+        pytest.skip("the dense path has no quantization: tests/test_gpu_dense.py")
     w, dt = g.w, g.dt
     cfg = _cfg(g)
     B, H, D, M0, C = w["B"], w["H"], w["D"], w["M0"], w["C"]

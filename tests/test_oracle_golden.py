@@ -49,10 +49,26 @@ def _calls(g: G.Golden):
         yield O.forward(q, k, v, pd, cd, cfg, mask=g.mask_for(q.shape[1], k.shape[1]))
 
 
+def _dense_out(g: G.Golden) -> np.ndarray:
+    """The dense path (backend.py:190-203) on the fixture's inputs, [B, T, E]."""
+    w, dt = g.w, g.dt
+    H = w["H"]
+    q, k, v = g.inputs()
+    mask = g.mask_for(q.shape[1], k.shape[1])
+    mg = None if mask is None else O.expand_mask(mask, w["B"], H)
+    out = O.naive_attention(O.split_heads(q, H), O.split_heads(k, H), O.split_heads(v, H), dt, mg)
+    return O.merge_heads(out, w["B"], H)
+
+
 @pytest.mark.parametrize("name", G.case_names())
 def test_oracle_matches_reference(name: str) -> None:
     g = G.load(name)
     w, dt = g.w, g.dt
+    if g.meta.get("dense"):
+        got, want = _dense_out(g), g.get("out0").reshape(w["B"], w["T"], -1)
+        err, nonfinite = finite_normrel(got, want, name)
+        assert err <= OUT_TOL[dt] and err <= 5e-3 * (dt != "f32") + 1e-6, err
+        return
     G_ = w["B"] * w["H"]
     sel_i = imp_i = 0
     for ci, res in enumerate(_calls(g)):
@@ -96,5 +112,6 @@ def test_oracle_matches_reference(name: str) -> None:
 def test_fixtures_cover_every_config_family() -> None:
     names = set(G.case_names())
     for must in ("c1_readme_f32", "mix_bf16", "mp_hvaq_f16", "decode_bf16", "rope_bf16", "empty_keys_bf16",
-                 "ties_bf16", "mp_quirk_f32", "causal_bf16", "mask2_f32", "mask4_bf16", "bcar_bf16", "bcar_b2_f32"):
+                 "ties_bf16", "mp_quirk_f32", "causal_bf16", "mask2_f32", "mask4_bf16", "bcar_bf16", "bcar_b2_f32",
+                 "dense_ref_bf16", "dense_norefine_f32"):
         assert must in names
