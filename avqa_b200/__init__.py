@@ -7,6 +7,7 @@ Public API mirrors the reference package ``avqa``:
 - :class:`AVQConfig` and its sub-configs
 - :class:`Backend`, :class:`CUDABackend`, :class:`QuantizationResult`
 - :class:`HierarchicalCodebook`, KV caches, the error hierarchy
+- :class:`StreamingVQBuffer`       causal incremental VQ (``avqa.streaming_vq``)
 
 The compute runs in ``libavqa_b200.so`` (C ABI: ``include/avqa_b200.h``),
 built in-tree by ``python -m avqa_b200.build_ext``.
@@ -20,6 +21,7 @@ from avqa_b200.codebook import HierarchicalCodebook, codebook_from_keys
 from avqa_b200.config import AVQConfig
 from avqa_b200.exceptions import (AVQAError, BackendError, CodebookError, ConfigurationError, DeviceError, DtypeError,
                                   MergeError, NotInitializedError, RoutingError, ShapeError)
+from avqa_b200.streaming_vq import StreamingVQBuffer
 
 __version__ = "0.1.0"
 Codebook = HierarchicalCodebook
@@ -27,6 +29,6 @@ Codebook = HierarchicalCodebook
 __all__ = [
     "AVQAError", "AVQAttention", "AVQConfig", "Backend", "BackendError", "CUDABackend", "Codebook", "CodebookError",
     "ConfigurationError", "DeviceError", "DtypeError", "HierarchicalCodebook", "InMemoryKVCache", "KVCache",
-    "MergeError", "NotInitializedError", "PagedKVCache", "QuantizationResult", "RoutingError", "ShapeError",
+    "MergeError", "NotInitializedError", "PagedKVCache", "QuantizationResult", "RoutingError", "ShapeError", "StreamingVQBuffer",
     "__version__", "codebook_from_keys",
 ]

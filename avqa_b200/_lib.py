@@ -20,6 +20,7 @@ _P = ctypes.c_void_p
 _I = ctypes.c_int
 _F = ctypes.c_float
 _Z = ctypes.c_size_t
+_L = ctypes.c_longlong
 
 _SIGS = {
     "avq_version": ([], ctypes.c_char_p),
@@ -33,6 +34,9 @@ _SIGS = {
     "avq_dense_attention": ([_I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P], _I),
     "avq_bcar_workspace_size": ([_I, _I, _I, _I, _I], _Z),
     "avq_bcar_update": ([_I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _Z, _P], _I),
+    "avq_stream_workspace_size": ([_I, _I, _I, _I], _Z),
+    "avq_stream_extend": ([_I, _P, _L, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _L, _L, _P, _P, _P, _P, _P, _Z,
+                           _P], _I),
     "avq_presence_words": ([_I], _I),
     "avq_codeword_presence": ([_P, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P], _I),
     "avq_forward": ([_I, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _I, _I, _F, _I, _F,

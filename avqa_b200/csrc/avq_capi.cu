@@ -207,6 +207,49 @@ int avq_bcar_update(int dtype, const void* keys, const long long* key_strides, c
   return finish(rc, "avq_bcar_update");
 }
 
+size_t avq_stream_workspace_size(int B, int H, int M0, int C) {
+  if (B < 0 || H <= 0 || M0 <= 0 || C <= 0 || too_many_groups(B, H) || (long long)H * M0 * C > INT_MAX) return 0;
+  return avq::stream_workspace_bytes(B, H, M0, C);
+}
+
+int avq_stream_extend(int dtype, const void* keys, long long key_row_stride, int B, int H, int M0, int C, int D,
+                      const void* parents, const void* children, long long* parent_out, long long* child_out,
+                      long long* parent_record, long long* child_record, long long record_stride,
+                      long long record_size, long long* parent_counts, long long* child_counts,
+                      void* parent_aggregates, void* child_aggregates, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  if (bad_dtype(dtype)) return fail(AVQ_ERR_ARG, "avq_stream_extend: bad dtype %d", dtype);
+  if (B < 0 || H <= 0 || M0 <= 0 || C <= 0 || D <= 0) return fail(AVQ_ERR_ARG, "avq_stream_extend: bad sizes");
+  if (too_many_groups(B, H) || (long long)H * M0 * C > INT_MAX)
+    return fail(AVQ_ERR_ARG, "avq_stream_extend: B*H or H*M0*C exceeds INT_MAX");
+  if (D > avq::stream_max_head_dim())
+    return fail(AVQ_ERR_UNSUPPORTED, "avq_stream_extend: head_dim %d > %d", D, avq::stream_max_head_dim());
+  if (B == 0) return AVQ_OK;
+  if (!keys || !parents || !children || !parent_out || !child_out || !parent_counts || !child_counts ||
+      !parent_aggregates || !child_aggregates || (!parent_record) != (!child_record))
+    return fail(AVQ_ERR_ARG, "avq_stream_extend: null pointer");
+  if (key_row_stride < D) return fail(AVQ_ERR_ARG, "avq_stream_extend: key row stride %lld < D", key_row_stride);
+  if (parent_record && (record_size < 0 || record_stride < record_size + B))
+    return fail(AVQ_ERR_ARG, "avq_stream_extend: record stride %lld < size %lld + B %d", record_stride,
+                record_size, B);
+  const size_t need = avq::stream_workspace_bytes(B, H, M0, C);
+  if (workspace_bytes < need || !workspace)
+    return fail(AVQ_ERR_WORKSPACE, "avq_stream_extend: workspace %zu < %zu bytes", workspace_bytes, need);
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc;
+#define AVQ_STREAM_CALL(DT)                                                                                      \
+  avq::launch_stream_extend<DT>(keys, key_row_stride, B, H, M0, C, D, parents, children, parent_out, child_out, \
+                                parent_record, child_record, record_stride, record_size, parent_counts,          \
+                                child_counts, parent_aggregates, child_aggregates, workspace, st)
+  switch (dtype) {
+    case 0: rc = AVQ_STREAM_CALL(avq::DT_F32); break;
+    case 1: rc = AVQ_STREAM_CALL(avq::DT_BF16); break;
+    default: rc = AVQ_STREAM_CALL(avq::DT_F16); break;
+  }
+#undef AVQ_STREAM_CALL
+  return finish(rc, "avq_stream_extend");
+}
+
 int avq_presence_words(int M0) { return M0 > 0 ? avq::presence_words(M0) : 0; }
 
 int avq_codeword_presence(const int* passign, int B, int H, int S, int M0, int T, int state_batch,

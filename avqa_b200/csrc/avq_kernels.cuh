@@ -214,6 +214,15 @@ int launch_dense_attention(const void* q, Strides3 qs, const void* k, Strides3 k
 
 // BCAR online codebook adaptation (avq_bcar.cu).
 size_t bcar_workspace_bytes(int G, int M0, int C, int D);
+
+// Streaming VQ extend (avq_stream.cu).
+int stream_max_head_dim();
+size_t stream_workspace_bytes(int B, int H, int M0, int C);
+template <int DT>
+int launch_stream_extend(const void* keys, long long kstride, int B, int H, int M0, int C, int D, const void* parents,
+                         const void* children, long long* pout, long long* cout_, long long* prec, long long* crec,
+                         long long rec_stride, long long rec_size, long long* pcnt, long long* ccnt, void* pagg,
+                         void* cagg, void* workspace, cudaStream_t st);
 template <int DT>
 int launch_bcar(const void* keys, Strides3 ks, const int* passign, const int* cassign, int B, int H, int S, int D,
                 int M0, int C, float decay, const void* ch_in, void* ch_out, void* parents_out, void* workspace,

@@ -28,6 +28,7 @@
  *   avq_codeword_presence the user / causal mask's codeword visibility, pipeline.py:82-106,
  *                         attention_module.py:210-223, 369-390
  *   avq_bcar_update       online_codebook_adaptation, online_adaptation.py:37-127
+ *   avq_stream_extend     StreamingVQBuffer.extend, streaming_vq.py:109-229
  *   avq_dense_attention   TorchBackend.naive_attention / online_softmax_attention,
  *                         backend.py:105-156, 190-203
  *   avq_device_fault      no counterpart: device-side fault record of the bounded waits
@@ -150,6 +151,32 @@ size_t avq_bcar_workspace_size(int B, int H, int M0, int C, int D);
 int avq_bcar_update(int dtype, const void* keys, const long long* key_strides, const int* passign, const int* cassign,
                     int B, int H, int S, int D, int M0, int C, float decay, const void* children_in, void* children_out,
                     void* parents_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Scratch bytes for avq_stream_extend with B new keys (0 for bad sizes). */
+size_t avq_stream_workspace_size(int B, int H, int M0, int C);
+
+/* Streaming VQ extend (StreamingVQBuffer.extend, streaming_vq.py:109-229):
+ * B new keys [B, D] (row stride key_row_stride elements, unit inner stride),
+ * the same keys for every head, are assigned against parents [H,M0,D] by the
+ * distance DT(DT(k_sq - 2 k.p) + p_sq) and against the assigned parent's
+ * children [H,M0,C,D] by sum DT((k - c)^2) (first argmin, a NaN wins).
+ * Writes parent_out / child_out [B,H] int64; when parent_record is not NULL
+ * also appends them to the running records [H, record_stride] laid out as the
+ * reference's assign.reshape(1, H, B): flat result i at row i / B, column
+ * record_size + i % B.  Then adds the keys into the running sums
+ * parent_aggregates [H,M0,D] / child_aggregates [H,M0,C,D] (dtype) and the
+ * int64 counts [H,M0] / [H,M0,C] as the reference's index_add_ does: flat
+ * row i adds key i / H to head i / B; the rows of one call accumulate in
+ * fp32 in row order from the stored value and narrow once.  D <= 512.
+ * All buffers are contiguous device memory; keys, codebook and aggregates
+ * share `dtype`.  workspace: avq_stream_workspace_size bytes.  B = 0 is a
+ * no-op. */
+int avq_stream_extend(int dtype, const void* keys, long long key_row_stride, int B, int H, int M0, int C, int D,
+                      const void* parents, const void* children, long long* parent_out, long long* child_out,
+                      long long* parent_record, long long* child_record, long long record_stride,
+                      long long record_size, long long* parent_counts, long long* child_counts,
+                      void* parent_aggregates, void* child_aggregates, void* workspace, size_t workspace_bytes,
+                      void* stream);
 
 /* Words per (b,h, query) row of the codeword visibility bits: ceil(M0 / 32). */
 int avq_presence_words(int M0);

@@ -220,6 +220,76 @@ def quantize(keys, values, parents, children, dt: str) -> Quantization:
 
 
 # ---------------------------------------------------------------------------
+# Streaming VQ: streaming_vq.py:34-255 (StreamingVQBuffer)
+# ---------------------------------------------------------------------------
+
+
+@dataclass
+class StreamState:
+    """StreamingVQBuffer's buffers: counts exact, aggregates in the dtype."""
+
+    pcnt: np.ndarray  # [H, M0] int64
+    ccnt: np.ndarray  # [H, M0, C] int64
+    pagg: np.ndarray  # [H, M0, D] f32 (dt values)
+    cagg: np.ndarray  # [H, M0, C, D]
+    passign: list = field(default_factory=list)  # per extend: [H, B] (the reference's reshape(1, H, B))
+    cassign: list = field(default_factory=list)
+
+
+def stream_init(H: int, M0: int, C: int, D: int) -> StreamState:
+    return StreamState(np.zeros((H, M0), np.int64), np.zeros((H, M0, C), np.int64),
+                       np.zeros((H, M0, D), np.float32), np.zeros((H, M0, C, D), np.float32))
+
+
+def stream_extend(st: StreamState, keys: np.ndarray, parents: np.ndarray, children: np.ndarray,
+                  dt: str) -> tuple[np.ndarray, np.ndarray]:
+    """StreamingVQBuffer.extend (streaming_vq.py:109-229) for ``keys`` [B, D]
+    (the same keys for every head); returns ``(parent, child)`` [B, H].
+
+    * distance ``DT(DT(k_sq - DT(2 DT(k.p))) + p_sq)`` (:172-177, that order);
+    * child ``DT(sum DT(DT(k - c)^2))`` over the assigned parent's children (:185-187);
+    * the aggregates gain the keys by ``index_add_`` with row i of the flat
+      ``[B*H]`` order: destination head ``i // B`` (``repeat_interleave``),
+      parent ``assign.reshape(-1)[i]`` and key ``i // H`` (:191-209); each
+      destination row adds its keys to the stored dtype value in fp32, in row
+      order, and narrows once per call;
+    * the record appends ``assign.reshape(1, H, B)`` (:212-223).
+    """
+    H, M0, D = parents.shape
+    C = children.shape[2]
+    B = keys.shape[0]
+    f64 = np.float64
+    k_sq = sq_norms(keys, dt)  # [B]
+    p_sq = sq_norms(parents, dt)  # [H, M0]
+    cross = rnd(np.einsum("bd,hmd->bhm", _f64(keys), _f64(parents)), dt)
+    with np.errstate(invalid="ignore", over="ignore"):
+        dist = rnd(_f64(rnd(_f64(k_sq)[:, None, None] - _f64(rnd(2.0 * _f64(cross), dt)), dt)) + p_sq[None], dt)
+    pa = first_argmin(dist)  # [B, H]
+    chosen = children[np.arange(H)[None, :], pa]  # [B, H, C, D]
+    diff = rnd(_f64(keys)[:, None, None, :] - chosen, dt)
+    cd = rnd(rnd(_f64(diff) * diff, dt).astype(f64).sum(-1), dt)
+    ca = first_argmin(cd)  # [B, H]
+    rows = np.arange(B * H)
+    head = rows // B
+    fp, fc = pa.reshape(-1), (pa * C + ca).reshape(-1)
+    kf = keys[rows // H]
+    for flat_dst, agg, cnt, width in ((head * M0 + fp, st.pagg.reshape(-1, D), st.pcnt.reshape(-1), M0),
+                                      (head * M0 * C + fc, st.cagg.reshape(-1, D), st.ccnt.reshape(-1), M0 * C)):
+        acc = {}
+        for i in range(B * H):
+            d = int(flat_dst[i])
+            if d not in acc:
+                acc[d] = agg[d].astype(np.float32).copy()
+            acc[d] = (acc[d] + kf[i].astype(np.float32)).astype(np.float32)
+            cnt[d] += 1
+        for d, a in acc.items():
+            agg[d] = rnd(a, dt)
+    st.passign.append(pa.reshape(H, B))
+    st.cassign.append(ca.reshape(H, B))
+    return pa, ca
+
+
+# ---------------------------------------------------------------------------
 # Dense attention: backend.py:190-203 (TorchBackend.naive_attention)
 # ---------------------------------------------------------------------------
 
@@ -634,7 +704,7 @@ def cast_codebook(parents32: np.ndarray, children32: np.ndarray, dt: str):
 
 __all__ = [
     "DTYPES", "EPS", "ForwardConfig", "Quantization", "SoftmaxState", "bcar_update", "cast_codebook",
-    "naive_attention",
+    "naive_attention", "stream_extend", "stream_init", "StreamState",
     "causal_mask",
     "codeword_present", "expand_mask",
     "child_logits_sel", "compute_pass_budgets", "correction", "count_saturation", "first_argmin",

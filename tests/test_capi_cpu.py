@@ -76,3 +76,37 @@ def test_workspace_queries() -> None:
     mma = lib.avq_forward_workspace_size(1, 4, 32, 8192, 128, 512, 4, 32, 1, 1.0, 0)
     exact = lib.avq_forward_workspace_size(0, 4, 32, 8192, 128, 512, 4, 32, 1, 1.0, 0)
     assert 0 < mma < exact
+
+
+@pytest.mark.parametrize("case", ["bad_dtype", "bad_sizes", "head_dim", "null", "record", "workspace"])
+def test_stream_extend_rejects_bad_arguments(case: str) -> None:
+    """avq_stream_extend validates before touching device memory."""
+    lib = _lib.load()
+    dummy = 16  # any non-null address: every case fails before a dereference
+    a = dict(dtype=1, B=2, H=2, M0=4, C=2, D=8, ptr=dummy, rec=dummy, stride=8, size=0, ws=1 << 20)
+    if case == "bad_dtype":
+        a["dtype"] = 9
+    elif case == "bad_sizes":
+        a["M0"] = 0
+    elif case == "head_dim":
+        a["D"] = 1024
+    elif case == "null":
+        a["ptr"] = None
+    elif case == "record":
+        a["stride"] = 1  # record row narrower than size + B
+    elif case == "workspace":
+        a["ws"] = 8
+    p, r = a["ptr"], a["rec"]
+    rc = lib.avq_stream_extend(a["dtype"], dummy, a["D"], a["B"], a["H"], a["M0"], a["C"], a["D"], p, p, p, p, r, r,
+                               a["stride"], a["size"], p, p, p, p, dummy, a["ws"], None)
+    assert rc == {"head_dim": 3, "workspace": 4}.get(case, 1), _lib.last_error()
+    assert _lib.last_error().startswith("avq_stream_extend")
+
+
+def test_stream_workspace_query() -> None:
+    lib = _lib.load()
+    assert lib.avq_stream_workspace_size(1, 8, 256, 8) >= 8 * 8 + 8 * 256 * 4 + 8 * 256 * 8 * 4
+    assert lib.avq_stream_workspace_size(1 << 16, 1 << 16, 8, 8) == 0
+    # zero keys: a no-op that needs no pointers
+    assert lib.avq_stream_extend(1, None, 8, 0, 2, 4, 2, 8, None, None, None, None, None, None, 0, 0, None, None,
+                                 None, None, None, 0, None) == 0
