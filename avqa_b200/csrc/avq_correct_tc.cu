@@ -63,7 +63,9 @@ struct CorrLayout {
 };
 
 // split_v: fp16 value rows, stored as two bf16 planes (v and vlo).
-__host__ __device__ inline CorrLayout corr_layout(int D, bool split_v = false) {
+// masked: a third meta array holds each parent slot's parent index (for the
+// mask bits); unmasked calls keep the two-array layout.
+__host__ __device__ inline CorrLayout corr_layout(int D, bool split_v, bool masked) {
   CorrLayout L;
   int o = 0;
   L.q = o;
@@ -82,7 +84,7 @@ __host__ __device__ inline CorrLayout corr_layout(int D, bool split_v = false) {
   }
   for (int i = 0; i < NBUF; ++i) {
     L.meta[i] = o;
-    o += 3 * NS * 4;  // n [48], logit mask [48], parent index of a parent slot or -1 [48]
+    o += (masked ? 3 : 2) * NS * 4;  // n [48], logit mask [48], (masked) parent index of a parent slot or -1 [48]
   }
   L.exptab = o;
   o += ((EXPN + 1) / 2) * 4;
@@ -172,7 +174,8 @@ __global__ void corr_desc_kernel(const int* __restrict__ sel, int sel_stride, co
   }
 }
 
-template <int DT, int D, int C>
+// MK: a user / causal mask is applied (present != nullptr); compiled out otherwise.
+template <int DT, int D, int C, bool MK>
 __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, int4 qpos, int H, int Tq, float sqrtD,
     const typename Storage<DT>::T* __restrict__ parents, const typename Storage<DT>::T* __restrict__ children,
@@ -189,7 +192,7 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_addr(smem_raw);
   unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  const CorrLayout L = corr_layout(D, SPLIT);
+  const CorrLayout L = corr_layout(D, SPLIT, MK);
   const int g = blockIdx.y, b = g / H, h = g % H, t0 = blockIdx.x * CR;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.bars);
@@ -307,7 +310,7 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
     const float zl = next_down(rz), zh = next_up(rz);  // bracket 1 / zc
     const float bt = beta_in && live ? beta_in[row] : 0.f;
     // the row's mask words (pipeline.py:82-106): a masked parent has probability 0
-    const unsigned int* prow = (present && live) ? present + row * ((M0 + 31) >> 5) : nullptr;
+    const unsigned int* prow = (MK && live) ? present + row * ((M0 + 31) >> 5) : nullptr;
     float l = live ? l_in[row] : 1.f;
     const int gslot = r;
     const bool gathers = r < NS, isv = hf == 1;
@@ -326,7 +329,8 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
           float* meta = reinterpret_cast<float*>(sm + L.meta[bf]);
           meta[gslot] = d.n;
           meta[NS + gslot] = d.mk;
-          reinterpret_cast<int*>(meta)[2 * NS + gslot] = (gslot < J && d.lrow >= 0) ? d.lrow - h * M0 : -1;
+          if constexpr (MK)
+            reinterpret_cast<int*>(meta)[2 * NS + gslot] = (gslot < J && d.lrow >= 0) ? d.lrow - h * M0 : -1;
         }
       }
       cp_async_commit();
@@ -474,9 +478,11 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
               float w = 0.f;
               if (k < NREAL) {
                 float s = kv[e] > 0.f ? sl[i] : -INFINITY;
-                if (k < J && prow) {
-                  const int pp = reinterpret_cast<const int*>(meta)[2 * NS + k];
-                  if (pp >= 0 && !((prow[pp >> 5] >> (pp & 31)) & 1u)) s = -INFINITY;
+                if constexpr (MK) {
+                  if (k < J && prow) {
+                    const int pp = reinterpret_cast<const int*>(meta)[2 * NS + k];
+                    if (pp >= 0 && !((prow[pp >> 5] >> (pp & 31)) & 1u)) s = -INFINITY;
+                  }
                 }
                 if (k < J) {
                   if (beta_in) s = rnd<DT>(__fmul_rn(bt, rnd<DT>(__fmul_rn(s, sqrtD))));
@@ -656,7 +662,8 @@ int launch_correct_tc(const CorrArgs& a, const void* exptab, void* desc, cudaStr
   for (int k = 0; k < 8; ++k) po.off[k] = a.pass_off[k];
   const int maxgroups = correct_tc_groups(a.sel_stride, a.C);
   SlotDesc* sd = static_cast<SlotDesc*>(desc);
-  const CorrLayout L = corr_layout(D, DT == DT_F16);
+  const bool mk = a.present != nullptr;
+  const CorrLayout L = corr_layout(D, DT == DT_F16, mk);
   const size_t smem = std::max<size_t>((size_t)L.total + 1024, 80 * 1024);  // <= 2 CTAs (2 x 256 TMEM columns) per SM
   auto go = [&](auto dfn, auto kfn) {
     AVQ_TIMED("correct_tc", st);
@@ -669,12 +676,13 @@ int launch_correct_tc(const CorrArgs& a, const void* exptab, void* desc, cudaStr
         static_cast<const T*>(a.a), a.pass_cnt, a.npass, maxgroups, sd, static_cast<const uint16_t*>(exptab), a.out,
         a.os, a.M0, a.present);
   };
+  auto pick = [&](auto dfn, auto k_plain, auto k_masked) { mk ? go(dfn, k_masked) : go(dfn, k_plain); };
   if (a.C == 4) {
-    if (D == 64) go(corr_desc_kernel<DT, 4>, correct_tc_kernel<DT, 64, 4>);
-    else go(corr_desc_kernel<DT, 4>, correct_tc_kernel<DT, 128, 4>);
+    if (D == 64) pick(corr_desc_kernel<DT, 4>, correct_tc_kernel<DT, 64, 4, false>, correct_tc_kernel<DT, 64, 4, true>);
+    else pick(corr_desc_kernel<DT, 4>, correct_tc_kernel<DT, 128, 4, false>, correct_tc_kernel<DT, 128, 4, true>);
   } else {
-    if (D == 64) go(corr_desc_kernel<DT, 8>, correct_tc_kernel<DT, 64, 8>);
-    else go(corr_desc_kernel<DT, 8>, correct_tc_kernel<DT, 128, 8>);
+    if (D == 64) pick(corr_desc_kernel<DT, 8>, correct_tc_kernel<DT, 64, 8, false>, correct_tc_kernel<DT, 64, 8, true>);
+    else pick(corr_desc_kernel<DT, 8>, correct_tc_kernel<DT, 128, 8, false>, correct_tc_kernel<DT, 128, 8, true>);
   }
   return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
 }

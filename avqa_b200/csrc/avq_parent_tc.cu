@@ -195,7 +195,10 @@ __device__ __forceinline__ bool rows_all(bool p) {
 // rows it then overwrites), the plain pass's selection sel0 (at most 64
 // parents), and writes the per-query temperature beta_out; the logits of every
 // later step are DT(beta * DT(s * sqrt(D))).
-template <int DT, int D, bool HV>
+// MK: a user / causal mask is applied (present != nullptr); without it the
+// mask code is compiled out, so unmasked calls run the same instructions as a
+// kernel without mask support.
+template <int DT, int D, bool HV, bool MK>
 __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_p,
     const __grid_constant__ CUtensorMap tm_v, int4 qpos, int H, int Tq, int M0, float sqrtD,
@@ -420,8 +423,11 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     T* srow_g = scratch + (((long)g * ntiles + (t >> 6)) * 64 + (t & 63)) * LDL;
     // the row's mask words (pipeline.py:82-106); none for rows past T
     const int PW = (M0 + 31) >> 5;
-    const unsigned int* prow = (present && live) ? present + row * PW : nullptr;
-    auto pword = [&](int wi) -> uint32_t { return prow ? (wi < PW ? prow[wi] : 0u) : 0xFFFFFFFFu; };
+    const unsigned int* prow = (MK && live) ? present + row * PW : nullptr;
+    auto pword = [&](int wi) -> uint32_t {
+      if constexpr (!MK) return 0xFFFFFFFFu;
+      return prow ? (wi < PW ? prow[wi] : 0u) : 0xFFFFFFFFu;
+    };
     const bool sector_stores = (reinterpret_cast<uintptr_t>(scratch) & 31u) == 0u;
     bool ok = true;
     float beta = 0.f;
@@ -451,7 +457,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
           float pi = 0.f;
           if (j < nsel) {
             const int pj = sl[j];
-            const bool keep = pcnt[(long)gs * M0 + pj] > 0 && (!prow || ((prow[pj >> 5] >> (pj & 31)) & 1u));
+            const bool keep = pcnt[(long)gs * M0 + pj] > 0 && (!MK || !prow || ((prow[pj >> 5] >> (pj & 31)) & 1u));
             const float s = keep ? scale_logit<DT>(rnd<DT>(__uint_as_float(ra[i])), sqrtD, inv_sqrtD) : -INFINITY;
             float e = exp_rn<DT>(rnd<DT>(__fsub_rn(s, m0)));
             if (isnan(e)) e = 0.f;  // pipeline.py:143-145
@@ -598,7 +604,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
           for (int k = 0; k < 4; ++k) {
             const int j = 4 * q + k;
             uint32_t keepm = pmv[k];
-            if (prow) {  // the pair's two mask bits, widened to its halves (pipeline.py:106)
+            if constexpr (MK) {  // the pair's two mask bits, widened to its halves (pipeline.py:106)
               const uint32_t two = (pb >> (hh * 16 + 2 * j)) & 3u;
               keepm &= ((two & 1u) ? 0xFFFFu : 0u) | ((two & 2u) ? 0xFFFF0000u : 0u);
             }
@@ -866,12 +872,13 @@ int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st) {
         static_cast<const T*>(a.parents), a.sel0, a.sel_stride, a.pass_cnt, a.hvaq, a.beta0, a.alpha, a.beta,
         a.present);
   };
+  const bool mk = a.present != nullptr;
   if (hv) {
-    if (D == 64) go(parent_attn_tc_kernel<DT, 64, true>);
-    else go(parent_attn_tc_kernel<DT, 128, true>);
+    if (D == 64) mk ? go(parent_attn_tc_kernel<DT, 64, true, true>) : go(parent_attn_tc_kernel<DT, 64, true, false>);
+    else mk ? go(parent_attn_tc_kernel<DT, 128, true, true>) : go(parent_attn_tc_kernel<DT, 128, true, false>);
   } else {
-    if (D == 64) go(parent_attn_tc_kernel<DT, 64, false>);
-    else go(parent_attn_tc_kernel<DT, 128, false>);
+    if (D == 64) mk ? go(parent_attn_tc_kernel<DT, 64, false, true>) : go(parent_attn_tc_kernel<DT, 64, false, false>);
+    else mk ? go(parent_attn_tc_kernel<DT, 128, false, true>) : go(parent_attn_tc_kernel<DT, 128, false, false>);
   }
   return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
 }
