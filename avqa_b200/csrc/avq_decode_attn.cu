@@ -5,7 +5,7 @@
 //
 // A decode step's work is dominated by reading every (b,h)'s parent sums
 // V = pagg[g] once ([M0, D] in the dtype), plus the selected parents'
-// children sums; the arithmetic is small.  Two kernels:
+// children sums; the arithmetic is small.  Three kernels:
 //
 //   decode_logits_kernel  per head, the logits of all B queries against a
 //       128-parent chunk: S = Q_h P_h^T on mma.sync tensor cores (fp32
@@ -13,12 +13,12 @@
 //       scaled by 1/sqrt(D) (pipeline.py:81) and masked where the parent is
 //       empty (:107).  The codebook tile is read once per head, not once per
 //       (b,h).
-//   decode_attn_kernel    per (b,h): row max, exponentials, l and z, the
+//   decode_route_kernel   per (b,h): row max, exponentials, l and z, the
 //       probabilities and the importance n * p (with one query, its sum over
 //       queries is p itself), the stable top-P over M0 (bitonic sort of
-//       packed keys: descending value, NaN first, ascending index), a = e @ V
-//       streamed from HBM, then the child correction of the selected parents
-//       and out = a' / max(l', 1e-12).
+//       packed keys: descending value, NaN first, ascending index).
+//   decode_value_kernel   per (b,h): a = e @ V streamed from HBM, then the
+//       child correction of the selected parents and out = a' / max(l', 1e-12).
 //
 // Rounding points are those of the prefill path: DT(exp(DT(s - m))), z and l
 // as exactly rounded sums, p = DT(e / max(z, eps)), w = DT(n p); the
