@@ -38,7 +38,8 @@ _SIGS = {
     "avq_stream_extend": ([_I, _P, _L, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _L, _L, _P, _P, _P, _P, _P, _Z,
                            _P], _I),
     "avq_presence_words": ([_I], _I),
-    "avq_codeword_presence": ([_P, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P], _I),
+    "avq_codeword_presence": ([_P, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _Z, _P], _I),
+    "avq_presence_workspace_size": ([_I, _I, _I], _Z),
     "avq_forward": ([_I, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _I, _I, _F, _I, _F,
                      _F, _P, _P, _P, _P, _P, _P, _Z, _P], _I),
     "avq_append_workspace_size": ([_I, _I, _I], _Z),

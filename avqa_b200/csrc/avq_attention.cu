@@ -13,6 +13,7 @@
 //   correct: per query, subtract each selected parent's term and add its
 //       children's terms (fp32), pass after pass, then out = a / max(l, eps).
 #include "avq_kernels.cuh"
+#include "avq_select.cuh"
 
 namespace avq {
 
@@ -247,6 +248,18 @@ __device__ __forceinline__ unsigned long long route_key(float w, int p) {
   return ((unsigned long long)(~float_order_key(w)) << 32) | (unsigned)p;
 }
 
+// route_kernel's shared memory: keys [npow2] u64, ambiguous columns [M0]
+// int32, refined flags [M0] bytes, then (16-byte aligned) the selection
+// scratch and the selected keys [SEL_MAX] u64.
+__host__ __device__ inline size_t route_sel_offset(int M0) {
+  int npow2 = 1;
+  while (npow2 < M0) npow2 <<= 1;
+  return ((size_t)npow2 * 8 + (size_t)M0 * 4 + (size_t)M0 + 15) & ~(size_t)15;
+}
+__host__ __device__ inline size_t route_smem(int M0) {
+  return route_sel_offset(M0) + (size_t)select_scratch_words(M0, SEL_MAX) * 4 + (size_t)SEL_MAX * 8;
+}
+
 template <int DT>
 __global__ void __launch_bounds__(1024) route_kernel(const double* __restrict__ imp_part, int nqt,
                                                      const int* __restrict__ pcnt, int M0,
@@ -358,6 +371,22 @@ __global__ void __launch_bounds__(1024) route_kernel(const double* __restrict__ 
     }
     __syncthreads();
   }
+  // stable descending order (routing.py:152-170).  Pass k takes the next
+  // cnt[k] parents of the order not refined before, so the order is needed
+  // only as far as the passes' total: a radix select of that many keys when
+  // it is small, else a bitonic sort of all of them.
+  int need = 0;
+  for (int k = 0; k < passes; ++k) need += cnt[k];
+  need = min(need, M0);
+  const unsigned long long* order = keys;
+  int span = M0;
+  if (need <= SEL_MAX) {
+    uint32_t* scr = reinterpret_cast<uint32_t*>(reinterpret_cast<unsigned char*>(keys) + route_sel_offset(M0));
+    unsigned long long* chosen = reinterpret_cast<unsigned long long*>(scr + select_scratch_words(M0, SEL_MAX));
+    select_smallest<1024>(keys, M0, need, chosen, scr);
+    order = chosen;
+    span = need;
+  } else {
   for (int k = 2; k <= npow2; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
       for (int i = threadIdx.x; i < npow2; i += blockDim.x) {
@@ -374,19 +403,20 @@ __global__ void __launch_bounds__(1024) route_kernel(const double* __restrict__ 
       __syncthreads();
     }
   }
+  }
   int* sg = sel + (long)g * sel_stride;
   if (phase == 0) {
-    for (int j = threadIdx.x; j < lay.cap[0]; j += blockDim.x) sg[lay.off[0] + j] = j < cnt[0] ? (int)(keys[j] & 0xffffffffu) : -1;
+    for (int j = threadIdx.x; j < lay.cap[0]; j += blockDim.x) sg[lay.off[0] + j] = j < cnt[0] ? (int)(order[j] & 0xffffffffu) : -1;
   }
   if (phase == 1 || (phase == 0 && all_passes)) {
     __syncthreads();
     if (threadIdx.x == 0) {
-      for (int j = 0; j < cnt[0]; ++j) refined[phase == 0 ? (int)(keys[j] & 0xffffffffu) : sg[lay.off[0] + j]] = 1;
+      for (int j = 0; j < cnt[0]; ++j) refined[phase == 0 ? (int)(order[j] & 0xffffffffu) : sg[lay.off[0] + j]] = 1;
       int pos = 0;
       for (int k = 1; k < passes; ++k) {
         int taken = 0;
-        while (taken < cnt[k] && pos < M0) {
-          const int p = (int)(keys[pos++] & 0xffffffffu);
+        while (taken < cnt[k] && pos < span) {
+          const int p = (int)(order[pos++] & 0xffffffffu);
           if (!refined[p]) sg[lay.off[k] + taken++] = p;
         }
         for (int j = 0; j < cnt[k]; ++j) refined[sg[lay.off[k] + j]] = 1;
@@ -698,9 +728,7 @@ int launch_forward(const ForwardArgs& a, cudaStream_t st) {
   int* sel = a.selected_out ? a.selected_out : w.sel;
   int* pcnt_out = a.pass_counts_out ? a.pass_counts_out : w.pass_cnt;
   const float sqrtD = (float)std::sqrt((double)a.D);
-  int npow2 = 1;
-  while (npow2 < a.M0) npow2 <<= 1;
-  const size_t rt_smem = sizeof(unsigned long long) * npow2 + sizeof(int) * a.M0 + a.M0;
+  const size_t rt_smem = route_smem(a.M0);
   auto rk = route_kernel<DT>;
   cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rt_smem);
   const int sG = state_groups(a);

@@ -22,8 +22,6 @@ namespace avq {
 
 constexpr int PM_ROWS = 64;
 constexpr int PM_CH = 64;
-constexpr int PM_MAX_SMEM_M0 = 1024;
-
 
 // ---------------------------------------------------------------------------
 // Parent attention kernel.  CTA = 64 queries = 4 warps x 16 rows; a lane quad

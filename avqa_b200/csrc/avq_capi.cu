@@ -252,9 +252,14 @@ int avq_stream_extend(int dtype, const void* keys, long long key_row_stride, int
 
 int avq_presence_words(int M0) { return M0 > 0 ? avq::presence_words(M0) : 0; }
 
+size_t avq_presence_workspace_size(int H, int M0, int state_batch) {
+  if (H <= 0 || M0 <= 0 || state_batch <= 0 || too_many_groups(state_batch, H)) return 0;
+  return avq::presence_workspace_bytes(state_batch * H, M0);
+}
+
 int avq_codeword_presence(const int* passign, int B, int H, int S, int M0, int T, int state_batch,
                           const unsigned char* mask, const long long* mask_strides, int causal_offset,
-                          unsigned int* present, void* stream) {
+                          unsigned int* present, void* workspace, size_t workspace_bytes, void* stream) {
   if (B < 0 || H <= 0 || S < 0 || M0 <= 0 || T < 0 || M0 > 8192)
     return fail(AVQ_ERR_ARG, "avq_codeword_presence: bad sizes");
   if (too_many_groups(B, H)) return fail(AVQ_ERR_ARG, "avq_codeword_presence: B*H exceeds INT_MAX");
@@ -262,8 +267,11 @@ int avq_codeword_presence(const int* passign, int B, int H, int S, int M0, int T
     return fail(AVQ_ERR_ARG, "avq_codeword_presence: state_batch must be B (%d) or 1, got %d", B, state_batch);
   if (!present || (S > 0 && !passign) || (mask && !mask_strides))
     return fail(AVQ_ERR_ARG, "avq_codeword_presence: null pointer");
+  const size_t need = avq::presence_workspace_bytes(state_batch * H, M0);
+  if (!mask && (workspace_bytes < need || !workspace))
+    return fail(AVQ_ERR_WORKSPACE, "avq_codeword_presence: workspace %zu < %zu bytes", workspace_bytes, need);
   return finish(avq::launch_presence(passign, B, H, S, M0, T, mask, mask_strides, causal_offset, state_batch * H,
-                                     present, (cudaStream_t)stream),
+                                     present, workspace, (cudaStream_t)stream),
                 "avq_codeword_presence");
 }
 

@@ -30,6 +30,7 @@
 
 #include "avq_kernels.cuh"
 #include "avq_mma.cuh"
+#include "avq_select.cuh"
 
 namespace avq {
 
@@ -129,10 +130,15 @@ __global__ void __launch_bounds__(256) decode_logits_kernel(const typename Stora
 }
 
 // Shared memory of decode_route_kernel, in bytes.
-__host__ __device__ inline size_t decode_route_smem(int M0) {
+// keys [npow2] u64, e [M0] fp32, then (16-byte aligned) the selection
+// scratch and the selected keys [SEL_MAX] u64.
+__host__ __device__ inline size_t decode_route_sel_offset(int M0) {
   int npow2 = 1;
   while (npow2 < M0) npow2 <<= 1;
-  return (size_t)npow2 * 8 + (size_t)M0 * 4 + 64;
+  return ((size_t)npow2 * 8 + (size_t)M0 * 4 + 15) & ~(size_t)15;
+}
+__host__ __device__ inline size_t decode_route_smem(int M0) {
+  return decode_route_sel_offset(M0) + (size_t)select_scratch_words(M0, SEL_MAX) * 4 + (size_t)SEL_MAX * 8;
 }
 
 // Per (b,h): row max, e = DT(exp(DT(s - m))), l, z, p = DT(e / max(z, eps)),
@@ -219,7 +225,16 @@ __global__ void __launch_bounds__(DA_THREADS) decode_route_kernel(
     rs[3] = __int_as_float(bud);
   }
   __syncthreads();
-  // stable descending top-k (routing.py:152-170): bitonic sort of packed keys
+  const int budget = sbudget;
+  // stable descending top-k (routing.py:152-170): a radix select of the
+  // budget's keys when it is small, else a bitonic sort of all packed keys
+  const unsigned long long* order = keys;
+  if (budget <= SEL_MAX) {
+    uint32_t* scr = reinterpret_cast<uint32_t*>(smem_raw + decode_route_sel_offset(M0));
+    unsigned long long* chosen = reinterpret_cast<unsigned long long*>(scr + select_scratch_words(M0, SEL_MAX));
+    select_smallest<DA_THREADS>(keys, M0, budget, chosen, scr);
+    order = chosen;
+  } else {
   for (int k = 2; k <= npow2; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
       for (int i = tid; i < npow2; i += DA_THREADS) {
@@ -236,9 +251,9 @@ __global__ void __launch_bounds__(DA_THREADS) decode_route_kernel(
       __syncthreads();
     }
   }
-  const int budget = sbudget;
+  }
   for (int j = tid; j < P; j += DA_THREADS) {
-    const int p = j < budget ? (int)(keys[j] & 0xffffffffu) : -1;
+    const int p = j < budget ? (int)(order[j] & 0xffffffffu) : -1;
     selwork[(long)g * P + j] = p;
     if (sel_out) sel_out[(long)g * sel_stride + j] = p;
   }

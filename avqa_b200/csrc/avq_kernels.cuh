@@ -231,8 +231,10 @@ int launch_bcar(const void* keys, Strides3 ks, const int* passign, const int* ca
 // Codeword visibility bits under a causal (mask == nullptr) or user mask
 // (avq_mask.cu).
 int presence_words(int M0);
+size_t presence_workspace_bytes(int sG, int M0);
 int launch_presence(const int* passign, int B, int H, int S, int M0, int T, const unsigned char* mask,
-                    const long long* mask_strides, int causal_offset, int sG, unsigned int* present, cudaStream_t st);
+                    const long long* mask_strides, int causal_offset, int sG, unsigned int* present, void* scratch,
+                    cudaStream_t st);
 
 // The mask bit of parent p for row (g, t) (all present when there is no mask).
 __device__ __forceinline__ bool present_bit(const unsigned int* present, int W, long gt, int p) {

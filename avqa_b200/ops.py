@@ -170,8 +170,10 @@ def codeword_presence(state: QuantState, T: int, mask: torch.Tensor | None = Non
     out = torch.empty(Bq * H, T, W, dtype=torch.int32, device=dev)
     m, strides = _mask_operand(mask, Bq, H, T, S, dev)  # m stays referenced until the kernel is enqueued
     offset = (S - T) if causal_offset is None else causal_offset
+    ws_bytes = lib.avq_presence_workspace_size(H, M0, state.B) if m is None else 0
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     rc = lib.avq_codeword_presence(_lib.ptr(state.passign), Bq, H, S, M0, T, state.B, _lib.ptr(m), strides, offset,
-                                   out.data_ptr(), _lib.stream_of(dev))
+                                   out.data_ptr(), ws.data_ptr(), ws_bytes, _lib.stream_of(dev))
     _lib.check(rc, "avq_codeword_presence")
     return out
 

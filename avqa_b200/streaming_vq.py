@@ -52,6 +52,7 @@ class StreamingVQBuffer:
         self._crec = torch.zeros(1, H, 0, dtype=torch.long, device=device)
         self.size = 0
         self._started = False  # an extend (even of zero keys) has run since the last reset
+        self._ws = None  # (stream handle, scratch): reused by later extends on the same stream
 
     def __len__(self) -> int:
         return self.size
@@ -126,14 +127,16 @@ class StreamingVQBuffer:
         cout = torch.empty(B, H, dtype=torch.long, device=self.device)
         self._reserve(B)
         ws_bytes = lib.avq_stream_workspace_size(B, H, M0, C)
-        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=self.device)
+        stream = _lib.stream_of(self.device)
+        if self._ws is None or self._ws[0] != stream or self._ws[1].numel() < ws_bytes:
+            self._ws = (stream, torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=self.device))
+        ws = self._ws[1]
         rc = lib.avq_stream_extend(_lib.dtype_code(self.dtype), keys.data_ptr(), keys.stride(0) if B > 1 else D, B, H,
                                    M0, C, D, parents.data_ptr(), children.data_ptr(), pout.data_ptr(),
                                    cout.data_ptr(), self._prec.data_ptr(), self._crec.data_ptr(),
                                    self._prec.shape[-1], self.size, self.parent_counts.data_ptr(),
                                    self.child_counts.data_ptr(), self.parent_aggregates.data_ptr(),
-                                   self.child_aggregates.data_ptr(), ws.data_ptr(), ws_bytes,
-                                   _lib.stream_of(self.device))
+                                   self.child_aggregates.data_ptr(), ws.data_ptr(), ws_bytes, stream)
         _lib.check(rc, "avq_stream_extend")
         self.size += B
         self._started = True

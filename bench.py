@@ -24,7 +24,10 @@ The other configurations are measured in the same run and reported under
 shares): the README fp32 example (latency), decode over a paged KV cache,
 multi-pass refinement with the HVAQ temperature (fp16), and the long-context
 chunked attention -- the last three head-sharded over the ranks with one
-NCCL all-gather of the output (strong scaling).
+NCCL all-gather of the output (strong scaling) -- and, under ``fx``, the
+rows beside the hot path at the headline's shapes with one batch entry: a
+causal forward, a BCAR codebook update, the dense attention path and a
+streaming-VQ token stream.
 
 ``--impl reference`` times the CPU restatement of the reference algorithm
 (oracle/, numpy with all host threads) on a bounded sample (one (b,h) slice
@@ -47,7 +50,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "query tokens/s/GPU at 1/2/4/8 B200; % of HBM/tensor roofline per kernel"
 UNIT = "query tokens/s"
-SUB_DEFAULT = "c1,c3,c4,c5"
+SUB_DEFAULT = "c1,c3,c4,c5,fx"
 
 
 def parse_args():
@@ -840,7 +843,85 @@ def sub_c3(ctx: Ctx, clk) -> dict:
     return rec
 
 
-SUBS = {"c1": sub_c1, "c3": sub_c3, "c4": sub_c4, "c5": sub_c5}
+def sub_fx(ctx: Ctx, clk) -> dict:
+    """The rows beside the hot path at the c2 shapes (B=1 per GPU, replicated):
+    a causal forward (mask bits + the masked kernel variants), one BCAR
+    codebook update after a quantization, the dense attention path, and a
+    streaming-VQ token stream (one key per extend call)."""
+    import torch
+
+    from avqa_b200 import AVQAttention, AVQConfig, StreamingVQBuffer, ops
+    from avqa_b200.backend import CUDABackend
+    from avqa_b200.config import AttentionShapeConfig, CodebookConfig, RoutingConfig
+    from avqa_b200.workloads import TORCH_DTYPE, WORKLOADS, Workload, make_inputs
+    w = Workload(**{**WORKLOADS["c2"].__dict__, "B": 1})
+    dt, dev = TORCH_DTYPE[w.dtype], ctx.dev
+    G, H, T, S, D, M0, C = w.H, w.H, w.T, w.S, w.D, w.M0, w.C
+    es = 2
+    q, k, v = (x.to(dt) for x in make_inputs(w, device=dev))
+    cb = _codebook(w, k, dt)
+    heads = lambda x: x.view(1, -1, H, D).transpose(1, 2)
+    out = {}
+    # causal forward
+    cfg = AVQConfig(causal=True, attention=AttentionShapeConfig(embed_dim=w.E, num_heads=H),
+                    codebook=CodebookConfig(num_codewords=M0, children_per_codeword=C),
+                    routing=RoutingConfig(refinement_budget=w.P))
+    mod = AVQAttention(cfg, in_proj=False, out_proj=False)
+    mod.codebook.parents, mod.codebook.children = cb.parents.to(dev), cb.children.to(dev)
+    work = algorithmic_work(w, 1) | {"presence": ("hbm", G * S * 4 + G * T * ((M0 + 31) // 32) * 4)}
+    with torch.no_grad():
+        rec = measure(ctx, lambda i: mod(q, k, v), 3, 10, work, T, clk)
+    rec.update(workload=f"causal forward, c2 shapes B=1: Tq=S={T} H={H} D={D} M0={M0} C={C} P={w.P} bf16",
+               parallelism="replicated (one forward per GPU)")
+    rec["value"] /= ctx.world
+    out["causal"] = rec
+    # BCAR: one EMA step of the codebook toward this call's keys
+    pc = cb.parents.to(dev, dt).contiguous()
+    cc = cb.children.to(dev, dt).contiguous()
+    pcb = ops.prepare_codebook(cb.parents, cb.children, dt, dev)
+    kh = heads(k)
+    st = ops.quantize(kh, heads(v), pcb)
+    work = {"bcar": ("hbm", G * S * (D * es + 8) + 2 * H * M0 * C * D * es + H * M0 * D * es)}
+    rec = measure(ctx, lambda i: ops.bcar_update(kh, st, pc, cc, 0.99), 3, 20, work, S, clk)
+    rec.update(unit="keys/s", workload=f"BCAR update after quantizing S={S} keys, H={H} M0={M0} C={C} D={D} bf16",
+               parallelism="replicated")
+    rec["value"] /= ctx.world
+    out["bcar"] = rec
+    # dense path (execution.mode = "reference" / refinement off)
+    be = CUDABackend()
+    qh, vh = heads(q), heads(v)
+    work = {"dense_attn": ("tensor", 4.0 * G * T * S * D)}
+    with torch.no_grad():
+        rec = measure(ctx, lambda i: be.naive_attention(qh, kh, vh), 2, 5, work, T, clk)
+    rec.update(workload=f"dense attention Tq=S={T} H={H} D={D} bf16 (mma.sync)", parallelism="replicated")
+    rec["value"] /= ctx.world
+    out["dense"] = rec
+    # streaming VQ: one key per extend, shared by every head
+    buf = StreamingVQBuffer(H, M0, C, D, device=dev, dtype=dt)
+    keys1 = kh[0, 0]  # [S, D] head 0's keys as the stream
+    work = {"stream_parent": ("hbm", H * M0 * D * es), "stream_child": ("hbm", H * C * D * es),
+            "stream_aggregate": ("hbm", 2 * H * (2 * D * es + 16))}
+    rec = measure(ctx, lambda i: buf.extend(keys1[i % S:i % S + 1], pc, cc), 20, 200, work, 1, clk)
+    rec.update(unit="keys/s", workload=f"StreamingVQBuffer.extend of one key, H={H} M0={M0} C={C} D={D} bf16 "
+                                       "(timed through the Python API: host launch overhead included)",
+               parallelism="replicated")
+    rec["value"] /= ctx.world
+    out["stream"] = rec
+    # the same stream fed 256 keys per extend call (a prefill chunk)
+    nb = 256
+    work = {"stream_parent": ("hbm", H * M0 * D * es + nb * D * es), "stream_child": ("hbm", nb * H * C * D * es),
+            "stream_aggregate": ("hbm", 2 * nb * H * (2 * D * es + 16))}
+    buf = StreamingVQBuffer(H, M0, C, D, device=dev, dtype=dt)
+    rec = measure(ctx, lambda i: buf.extend(keys1[(i * nb) % (S - nb):(i * nb) % (S - nb) + nb], pc, cc), 5, 50,
+                  work, nb, clk)
+    rec.update(unit="keys/s", workload=f"StreamingVQBuffer.extend of {nb} keys per call, H={H} M0={M0} C={C} D={D} "
+                                       "bf16", parallelism="replicated")
+    rec["value"] /= ctx.world
+    out["stream_b256"] = rec
+    return out
+
+
+SUBS = {"c1": sub_c1, "c3": sub_c3, "c4": sub_c4, "c5": sub_c5, "fx": sub_fx}
 
 
 def run_ours(args) -> None:

@@ -191,10 +191,16 @@ int avq_presence_words(int M0);
  * query).  Otherwise mask is uint8 (nonzero = attend) with element strides
  * mask_strides {b, h, t} (the key stride is 1; zero strides broadcast, so a
  * [T, S] mask passes {0, 0, S}).  passign [state_batch*H, S] are the parent
- * assignments of avq_quantize; state_batch is B or 1 as in avq_forward. */
+ * assignments of avq_quantize; state_batch is B or 1 as in avq_forward.
+ * workspace: avq_presence_workspace_size bytes for the causal path (may be
+ * NULL with a user mask). */
 int avq_codeword_presence(const int* passign, int B, int H, int S, int M0, int T, int state_batch,
                           const unsigned char* mask, const long long* mask_strides, int causal_offset,
-                          unsigned int* present, void* stream);
+                          unsigned int* present, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Scratch bytes of avq_codeword_presence's causal path (mask NULL): the first
+ * key position of every (key set, parent).  A user mask needs none. */
+size_t avq_presence_workspace_size(int H, int M0, int state_batch);
 
 /* Number of int32 slots per (b,h) in the `selected` output of avq_forward:
  * the sum of the per-pass budget caps for base budget P. */
