@@ -7,14 +7,16 @@
 //                   order (:172-177); the dot products accumulate in double,
 //                   so each term is the exactly rounded value; first argmin
 //                   over parents (a NaN wins) via a 64-bit atomicMin of
-//                   (order key, index) per (b, h).  Grid: parent tiles x heads
-//                   x key tiles, so a single key still spreads the codebook
-//                   read over the SMs.
+//                   (order key, index) per (b, h).  A thread per parent, a CTA
+//                   per (128 parents, head, 8 keys), so a single key still
+//                   spreads the codebook read over the SMs.
 //   stream_child  : DT(sum DT(DT(k - c)^2)) over the assigned parent's
 //                   children (:183-188), first argmin; writes the [B, H]
 //                   int64 results and appends them to the running record,
 //                   which the reference lays out as assign.reshape(1, H, B):
 //                   flat result i goes to record row i / B, column size + i % B.
+//                   With one key per call it also does the aggregation below
+//                   (each head then has exactly one row).
 //   stream_aggregate : index_add_ of the keys (:191-213).  Row i of the flat
 //                   [B*H] order adds key i / H to head i / B
 //                   (arange(H).repeat_interleave(B)) at codeword
@@ -31,7 +33,8 @@ namespace avq {
 namespace {
 
 constexpr int SP_KEYS = 8;      // keys per CTA
-constexpr int SP_PARENTS = 64;  // parents per CTA (8 per warp)
+constexpr int SP_THREADS = 128;  // parents per CTA: one thread per parent
+constexpr int SP_CHUNK = 32;     // dimensions per register chunk of a parent row
 constexpr int ST_MAX_D = 512;
 
 // (order key, index) for a 64-bit atomicMin: the smallest distance, then the
@@ -41,14 +44,21 @@ __device__ __forceinline__ unsigned long long argmin_key(float d, int i) {
   return ((unsigned long long)k << 32) | (uint32_t)i;
 }
 
+// One thread per parent: the parent row streams through registers in
+// 32-element chunks (16-byte loads, all issued before use), the dot products
+// with the CTA's keys (shared memory, read as broadcasts) accumulate in
+// double, so no cross-lane reduction is needed per parent; the per-key
+// minimum goes through one warp reduction and one atomicMin per warp.
 template <int DT>
-__global__ void __launch_bounds__(256) stream_parent_kernel(const typename Storage<DT>::T* __restrict__ keys,
-                                                            long long kstride, int B, int M0, int D,
-                                                            const typename Storage<DT>::T* __restrict__ parents,
-                                                            unsigned long long* __restrict__ best, int H) {
+__global__ void __launch_bounds__(SP_THREADS) stream_parent_kernel(const typename Storage<DT>::T* __restrict__ keys,
+                                                                   long long kstride, int B, int M0, int D,
+                                                                   const typename Storage<DT>::T* __restrict__ parents,
+                                                                   unsigned long long* __restrict__ best, int H) {
+  using T = typename Storage<DT>::T;
+  constexpr int EW = 16 / sizeof(T);  // elements per 16-byte load
   __shared__ float kk[SP_KEYS][ST_MAX_D];
   __shared__ float ksq[SP_KEYS];
-  const int h = blockIdx.y, p0 = blockIdx.x * SP_PARENTS, b0 = blockIdx.z * SP_KEYS;
+  const int h = blockIdx.y, p = blockIdx.x * SP_THREADS + threadIdx.x, b0 = blockIdx.z * SP_KEYS;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nk = min(SP_KEYS, B - b0);
   for (int e = tid; e < SP_KEYS * D; e += blockDim.x) {
@@ -56,80 +66,132 @@ __global__ void __launch_bounds__(256) stream_parent_kernel(const typename Stora
     kk[r][d] = r < nk ? to_f(keys[(long long)(b0 + r) * kstride + d]) : 0.f;
   }
   __syncthreads();
-  if (warp < nk) {  // k_sq = (keys * keys).sum(1): products in DT, fp32 sum narrowed once
+  for (int r = warp; r < nk; r += SP_THREADS / 32) {  // k_sq = (keys * keys).sum(1), narrowed once
     double acc = 0.0;
-    for (int d = lane; d < D; d += 32) acc += (double)rnd<DT>(__fmul_rn(kk[warp][d], kk[warp][d]));
+    for (int d = lane; d < D; d += 32) acc += (double)rnd<DT>(__fmul_rn(kk[r][d], kk[r][d]));
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) ksq[warp] = rnd64<DT>(acc);
+    if (lane == 0) ksq[r] = rnd64<DT>(acc);
   }
   __syncthreads();
-  unsigned long long mine = ~0ull;  // lane r < nk: best of key r over this warp's parents
-  for (int j = 0; j < SP_PARENTS / 8; ++j) {
-    const int p = p0 + warp * (SP_PARENTS / 8) + j;
-    if (p >= M0) break;
-    const typename Storage<DT>::T* prow = parents + ((long long)h * M0 + p) * D;
-    double psq = 0.0, acc[SP_KEYS];
+  const bool live = p < M0;
+  double psq = 0.0, acc[SP_KEYS];
 #pragma unroll
-    for (int r = 0; r < SP_KEYS; ++r) acc[r] = 0.0;
-    for (int d = lane; d < D; d += 32) {
-      const float pv = to_f(prow[d]);
-      psq += (double)rnd<DT>(__fmul_rn(pv, pv));
+  for (int r = 0; r < SP_KEYS; ++r) acc[r] = 0.0;
+  const T* prow = parents + ((long long)h * M0 + (live ? p : 0)) * D;
+  // 16-byte loads when every row starts on a 16-byte boundary
+  const bool vec = D % EW == 0 && (reinterpret_cast<uintptr_t>(parents) & 15u) == 0u;
+  for (int d0 = 0; d0 < D; d0 += SP_CHUNK) {
+    T pc[SP_CHUNK];
+    if (vec) {
+      uint4 raw[SP_CHUNK / EW];
 #pragma unroll
-      for (int r = 0; r < SP_KEYS; ++r)
-        if (r < nk) acc[r] = fma((double)kk[r][d], (double)pv, acc[r]);
+      for (int i = 0; i < SP_CHUNK / EW; ++i)
+        raw[i] = (live && d0 + i * EW < D) ? *reinterpret_cast<const uint4*>(prow + d0 + i * EW)
+                                           : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int i = 0; i < SP_CHUNK / EW; ++i)
+#pragma unroll
+        for (int e = 0; e < EW; ++e) pc[i * EW + e] = reinterpret_cast<const T*>(&raw[i])[e];
+    } else {
+#pragma unroll
+      for (int e = 0; e < SP_CHUNK; ++e) pc[e] = (live && d0 + e < D) ? prow[d0 + e] : prow[0];
     }
-    for (int o = 16; o > 0; o >>= 1) {
-      psq += __shfl_xor_sync(0xffffffffu, psq, o);
 #pragma unroll
-      for (int r = 0; r < SP_KEYS; ++r)
-        if (r < nk) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
-    }
-    const float p_sq = rnd64<DT>(psq);
+    for (int e = 0; e < SP_CHUNK; ++e) {
+      const int d = d0 + e;
+      if (d < D) {
+        const float pv = to_f(pc[e]);
+        psq += (double)rnd<DT>(__fmul_rn(pv, pv));
 #pragma unroll
-    for (int r = 0; r < SP_KEYS; ++r) {
-      if (lane == r && r < nk) {
-        const float cross = rnd64<DT>(acc[r]);
-        const float two = rnd<DT>(__fmul_rn(2.f, cross));
-        const float t1 = rnd<DT>(__fsub_rn(ksq[r], two));
-        const float dd = rnd<DT>(__fadd_rn(t1, p_sq));
-        const unsigned long long key = argmin_key(dd, p);
-        mine = key < mine ? key : mine;
+        for (int r = 0; r < SP_KEYS; ++r)
+          if (r < nk) acc[r] = fma((double)kk[r][d], (double)pv, acc[r]);
       }
     }
   }
-  if (lane < nk && mine != ~0ull) atomicMin(best + (long long)(b0 + lane) * H + h, mine);
+  const float p_sq = rnd64<DT>(psq);
+#pragma unroll
+  for (int r = 0; r < SP_KEYS; ++r) {
+    if (r < nk) {
+      unsigned long long key = ~0ull;
+      if (live) {
+        const float cross = rnd64<DT>(acc[r]);
+        const float two = rnd<DT>(__fmul_rn(2.f, cross));
+        const float t1 = rnd<DT>(__fsub_rn(ksq[r], two));
+        key = argmin_key(rnd<DT>(__fadd_rn(t1, p_sq)), p);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other < key ? other : key;
+      }
+      if (lane == 0 && key != ~0ull) atomicMin(best + (long long)(b0 + r) * H + h, key);
+    }
+  }
 }
 
-template <int DT>
+// A warp per flat result i = b H + h: the child argmin over the assigned
+// parent's children (their rows loaded before any is used), the [B, H]
+// outputs and the record.  FUSED (one key per call): row i = h is then the
+// only row of head h, so the warp also adds the key to its parent and child
+// sums (fp32 sum of the stored value and the key, narrowed once) and counts.
+// PER: key elements per lane (D <= 32 PER).
+template <int DT, bool FUSED, int PER>
 __global__ void __launch_bounds__(256) stream_child_kernel(const typename Storage<DT>::T* __restrict__ keys,
                                                            long long kstride, int B, int H, int M0, int C, int D,
                                                            const typename Storage<DT>::T* __restrict__ children,
                                                            const unsigned long long* __restrict__ best,
                                                            long long* __restrict__ pout, long long* __restrict__ cout_,
                                                            long long* __restrict__ prec, long long* __restrict__ crec,
-                                                           long long rec_stride, long long rec_size) {
+                                                           long long rec_stride, long long rec_size,
+                                                           typename Storage<DT>::T* __restrict__ pagg,
+                                                           typename Storage<DT>::T* __restrict__ cagg,
+                                                           long long* __restrict__ pcnt, long long* __restrict__ ccnt) {
+  constexpr int CMAX = 4;  // children per batch of row loads
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long i = (long long)blockIdx.x * 8 + warp;  // flat [B, H] index
   if (i >= (long long)B * H) return;
   const int b = (int)(i / H), h = (int)(i % H);
   const int p = (int)(uint32_t)(best[i] & 0xffffffffu);
   const typename Storage<DT>::T* krow = keys + (long long)b * kstride;
+  float kv[PER];
+#pragma unroll
+  for (int e = 0; e < PER; ++e) kv[e] = lane + 32 * e < D ? to_f(krow[lane + 32 * e]) : 0.f;
   float bv = 0.f;
   int bi = -1;
-  for (int c = 0; c < C; ++c) {
-    const typename Storage<DT>::T* crow = children + (((long long)h * M0 + p) * C + c) * D;
-    double acc = 0.0;
-    for (int d = lane; d < D; d += 32) {
-      const float df = rnd<DT>(__fsub_rn(to_f(krow[d]), to_f(crow[d])));
-      acc += (double)rnd<DT>(__fmul_rn(df, df));
+  for (int c0 = 0; c0 < C; c0 += CMAX) {
+    double acc[CMAX];
+    float cv[CMAX][PER];
+#pragma unroll
+    for (int c = 0; c < CMAX; ++c) {
+      const typename Storage<DT>::T* crow = children + (((long long)h * M0 + p) * C + (c0 + c < C ? c0 + c : 0)) * D;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) cv[c][e] = (c0 + c < C && lane + 32 * e < D) ? to_f(crow[lane + 32 * e]) : 0.f;
     }
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    const float v = rnd64<DT>(acc);
-    // first minimum; a NaN wins over every number (and the first NaN stays)
-    const bool take = bi < 0 || (isnan(v) ? !isnan(bv) : (!isnan(bv) && v < bv));
-    if (take) {
-      bv = v;
-      bi = c;
+#pragma unroll
+    for (int c = 0; c < CMAX; ++c) {
+      acc[c] = 0.0;
+#pragma unroll
+      for (int e = 0; e < PER; ++e)
+        if (lane + 32 * e < D) {
+          const float df = rnd<DT>(__fsub_rn(kv[e], cv[c][e]));
+          acc[c] += (double)rnd<DT>(__fmul_rn(df, df));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int c = 0; c < CMAX; ++c) acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], o);
+#pragma unroll
+    for (int c = 0; c < CMAX; ++c) {
+      if (c0 + c < C) {
+        const float v = rnd64<DT>(acc[c]);
+        // first minimum; a NaN wins over every number (and the first NaN stays)
+        const bool take = bi < 0 || (isnan(v) ? !isnan(bv) : (!isnan(bv) && v < bv));
+        if (take) {
+          bv = v;
+          bi = c0 + c;
+        }
+      }
     }
   }
   if (lane == 0) {
@@ -139,6 +201,22 @@ __global__ void __launch_bounds__(256) stream_child_kernel(const typename Storag
       const long long r = i / B, j = i % B;
       prec[r * rec_stride + rec_size + j] = p;
       crec[r * rec_stride + rec_size + j] = bi;
+    }
+  }
+  if constexpr (FUSED) {
+    typename Storage<DT>::T* pa = pagg + ((long long)h * M0 + p) * D;
+    typename Storage<DT>::T* ca = cagg + (((long long)h * M0 + p) * C + bi) * D;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+      const int d = lane + 32 * e;
+      if (d < D) {
+        pa[d] = from_f<DT>(__fadd_rn(to_f(pa[d]), kv[e]));
+        ca[d] = from_f<DT>(__fadd_rn(to_f(ca[d]), kv[e]));
+      }
+    }
+    if (lane == 0) {
+      pcnt[(long long)h * M0 + p] += 1;
+      ccnt[((long long)h * M0 + p) * C + bi] += 1;
     }
   }
 }
@@ -246,17 +324,21 @@ int launch_stream_extend(const void* keys, long long kstride, int B, int H, int 
   const T* k = static_cast<const T*>(keys);
   {
     AVQ_TIMED("stream_parent", st);
-    stream_parent_kernel<DT><<<dim3((M0 + SP_PARENTS - 1) / SP_PARENTS, H, (B + SP_KEYS - 1) / SP_KEYS), 256, 0, st>>>(
+    stream_parent_kernel<DT><<<dim3((M0 + SP_THREADS - 1) / SP_THREADS, H, (B + SP_KEYS - 1) / SP_KEYS), SP_THREADS, 0,
+                               st>>>(
         k, kstride, B, M0, D, static_cast<const T*>(parents), best, H);
   }
   {
     AVQ_TIMED("stream_child", st);
     const long long rows_bh = (long long)B * H;
-    stream_child_kernel<DT><<<(unsigned)((rows_bh + 7) / 8), 256, 0, st>>>(
-        k, kstride, B, H, M0, C, D, static_cast<const T*>(children), best, pout, cout_, prec, crec, rec_stride,
-        rec_size);
+    auto kfn = D <= 128 ? (B == 1 ? stream_child_kernel<DT, true, 4> : stream_child_kernel<DT, false, 4>)
+                        : (B == 1 ? stream_child_kernel<DT, true, ST_MAX_D / 32>
+                                  : stream_child_kernel<DT, false, ST_MAX_D / 32>);
+    kfn<<<(unsigned)((rows_bh + 7) / 8), 256, 0, st>>>(k, kstride, B, H, M0, C, D, static_cast<const T*>(children),
+                                                       best, pout, cout_, prec, crec, rec_stride, rec_size,
+                                                       static_cast<T*>(pagg), static_cast<T*>(cagg), pcnt, ccnt);
   }
-  {
+  if (B > 1) {
     AVQ_TIMED("stream_aggregate", st);
     stream_aggregate_kernel<DT><<<dim3(H, 2), 256, 0, st>>>(k, kstride, B, H, M0, C, D, pout, cout_,
                                                              static_cast<T*>(pagg), static_cast<T*>(cagg), pcnt, ccnt,

@@ -68,6 +68,8 @@ def parse_args():
                     help="(b,h) slices in the CPU-baseline sample; 0 skips the baseline (profiling runs)")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the per-GPU batch B (smaller cases for profiler captures)")
+    ap.add_argument("--sub-batch", type=int, default=0,
+                    help="override the batch of the c3 / c4 records (smaller cases for profiler captures)")
     return ap.parse_args()
 
 
@@ -429,6 +431,7 @@ class Ctx:
         import torch
         import torch.distributed as dist
         self.world, self.rank, self.dev = world, rank, dev
+        self.sub_batch = 0  # batch override of the c3 / c4 records
         self.stream = torch.cuda.current_stream(dev)
         self.group = dist.group.WORLD if world > 1 else None
         self.peaks, self.peak_src = load_peaks()
@@ -719,8 +722,10 @@ def sub_c4(ctx: Ctx, clk) -> dict:
     head-sharded over the ranks."""
     import torch
 
-    from avqa_b200.workloads import TORCH_DTYPE, WORKLOADS, make_inputs
+    from avqa_b200.workloads import TORCH_DTYPE, WORKLOADS, Workload, make_inputs
     w = WORKLOADS["c4"]
+    if ctx.sub_batch:
+        w = Workload(**{**w.__dict__, "B": ctx.sub_batch})
     dt = TORCH_DTYPE[w.dtype]
     q, k, v = make_inputs(w, device=ctx.dev)
     cb = _codebook(w, k[:1], dt)
@@ -737,7 +742,7 @@ def sub_c4(ctx: Ctx, clk) -> dict:
 
     with torch.no_grad():
         rec = measure(ctx, step, 3, 10, work, w.B * w.T, clk)
-    rec.update(workload="c4: B=8 Tq=S=16384 H=16 D=64 M0=256 C=4 fp16, 3 passes (48/24/12), HVAQ entropy, "
+    rec.update(workload=f"c4: B={w.B} Tq=S=16384 H=16 D=64 M0=256 C=4 fp16, 3 passes (48/24/12), HVAQ entropy, "
                         "Student-t keys", parallelism=f"head-sharded x{ctx.world} ({hloc} heads/GPU), output "
                                                       f"all-gather")
     if ctx.rank == 0:
@@ -800,8 +805,10 @@ def sub_c3(ctx: Ctx, clk) -> dict:
     import torch
 
     from avqa_b200 import PagedKVCache
-    from avqa_b200.workloads import TORCH_DTYPE, WORKLOADS, make_decode_tokens, make_inputs
+    from avqa_b200.workloads import TORCH_DTYPE, WORKLOADS, Workload, make_decode_tokens, make_inputs
     w = WORKLOADS["c3"]
+    if ctx.sub_batch:
+        w = Workload(**{**w.__dict__, "B": ctx.sub_batch})
     dt = TORCH_DTYPE[w.dtype]
     dev = ctx.dev
     # the prior, batch by batch (the same cluster centres, each batch its own samples)
@@ -832,7 +839,7 @@ def sub_c3(ctx: Ctx, clk) -> dict:
 
         warm = 3
         rec = measure(ctx, step, warm, w.decode_steps - warm, work, w.B, clk)
-    rec.update(workload=f"c3: decode B=64 H=32 D=128 bf16, prior S=32768 in 256-token pages, M0=1024 C=8 P=64; "
+    rec.update(workload=f"c3: decode B={w.B} H=32 D=128 bf16, prior S=32768 in 256-token pages, M0=1024 C=8 P=64; "
                         f"{w.decode_steps} steps of one token per (b,h): {warm} warm-up, "
                         f"{w.decode_steps - warm} timed", parallelism=f"head-sharded x{ctx.world} ({hloc} heads/GPU), "
                                                                       f"output all-gather",
@@ -932,6 +939,7 @@ def run_ours(args) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     ctx = Ctx(world, rank, dev)
+    ctx.sub_batch = args.sub_batch
     subs = [s for s in args.configs.split(",") if s and s != "none"]
     with ClockSampler(gpu_uuid(dev)) as clk:
         head = run_headline(args, ctx, clk)

@@ -71,6 +71,9 @@ STREAMS = [
     ("f32", 3, 40, 2, 32, [5, 9], 33),
     ("bf16", 2, 8, 4, 64, [700, 300], 34),            # many keys per codeword in one call
     ("bf16", 16, 512, 4, 256, [64], 35),              # several key tiles and parent tiles
+    ("bf16", 3, 24, 3, 20, [1, 5, 1], 37),            # D not a multiple of 8: scalar parent loads; odd C
+    ("f16", 2, 16, 6, 40, [1, 7, 1], 38),             # C > 4: two batches of child rows
+    ("f32", 4, 300, 2, 512, [1, 3], 39),              # the widest head dimension, a partial parent tile
 ]
 
 
