@@ -27,6 +27,7 @@
 // child, u = DT(DT(q.c) / sqrt(D)), -inf for an empty child).
 #include <cmath>
 #include <cstdlib>
+#include <type_traits>
 
 #include "avq_kernels.cuh"
 #include "avq_mma.cuh"
@@ -297,30 +298,33 @@ __global__ void __launch_bounds__(DA_THREADS, 3) decode_value_kernel(
   const float safe = rowstat[(long)g * 4], l0 = rowstat[(long)g * 4 + 1], zc = rowstat[(long)g * 4 + 2];
   const int budget = __float_as_int(rowstat[(long)g * 4 + 3]);
 
-  // ---- a = sum_p e_p V_p: eight rows per warp in flight ----
+  // ---- a = sum_p e_p V_p: sixteen rows per warp in flight, kept packed ----
   float acc[EPL];
 #pragma unroll
   for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
   {
+    using Part = typename std::conditional<EPL == 4, uint2, uint32_t>::type;
+    constexpr int NWP = EPL / 2;
     const T* vb = pagg + (long)gs * M0 * D + lane * EPL;
-    constexpr int U = 8;
+    constexpr int U = 16;
     for (int p0 = warp; p0 < M0; p0 += DA_WARPS * U) {
-      float x[U][EPL], ew[U];
+      Part x[U];
+      float ew[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int p = p0 + u * DA_WARPS;
         ew[u] = p < M0 ? er[p] : 0.f;
-        if (p < M0) {
-          load_row_part<DT, EPL>(vb + (long)p * D, x[u]);
-        } else {
-#pragma unroll
-          for (int e = 0; e < EPL; ++e) x[u][e] = 0.f;
-        }
+        x[u] = p < M0 ? *reinterpret_cast<const Part*>(vb + (long)p * D) : Part{};
       }
 #pragma unroll
-      for (int u = 0; u < U; ++u)
+      for (int u = 0; u < U; ++u) {
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(&x[u]);
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) acc[e] = fmaf(ew[u], x[u][e], acc[e]);
+        for (int e = 0; e < NWP; ++e) {
+          acc[2 * e] = fmaf(ew[u], half_lo<DT>(w[e]), acc[2 * e]);
+          acc[2 * e + 1] = fmaf(ew[u], half_hi<DT>(w[e]), acc[2 * e + 1]);
+        }
+      }
     }
   }
 #pragma unroll
