@@ -272,7 +272,8 @@ __global__ void __launch_bounds__(1024) route_kernel(const double* __restrict__ 
   extern __shared__ unsigned long long keys[];  // [npow2]
   __shared__ int cnt[MAX_PASSES];
   __shared__ int namb;
-  __shared__ double red[32];
+  constexpr int AMB_BATCH = 8;  // ambiguous columns recounted per sweep over the rows
+  __shared__ double red[AMB_BATCH][32];
   const int g = blockIdx.x, gs = g % sG;
   int npow2 = 1;
   while (npow2 < M0) npow2 <<= 1;
@@ -345,26 +346,47 @@ __global__ void __launch_bounds__(1024) route_kernel(const double* __restrict__ 
   }
   }
   __syncthreads();
-  // exact column sums for the ambiguous entries, from the stored tiles
+  // exact column sums for the ambiguous entries, from the stored tiles: up to
+  // eight columns per sweep over the rows, so a row's row statistics are read
+  // once per sweep and its columns come from the same cached lines
   const int LDL = exp_slice_pitch(M0);
   using T = typename Storage<DT>::T;
   const T* scr = (const T*)rx.scratch;
-  for (int ia = 0; ia < namb; ++ia) {
-    const int p = amb[ia];
-    double s = 0.0;
+  const int nwarps = (int)(blockDim.x >> 5);
+  for (int a0 = 0; a0 < namb; a0 += AMB_BATCH) {
+    const int na = min(AMB_BATCH, namb - a0);
+    int cols[AMB_BATCH];
+    double s[AMB_BATCH];
+#pragma unroll
+    for (int k = 0; k < AMB_BATCH; ++k) {
+      cols[k] = k < na ? amb[a0 + k] : 0;
+      s[k] = 0.0;
+    }
     for (int t = threadIdx.x; t < rx.T; t += blockDim.x) {
       const long row = (long)g * rx.T + t;
-      const float x = to_f(scr[(((long)g * nqt + (t >> 6)) * 64 + (t & 63)) * LDL + p]);
-      const float e = rx.scr_logits ? fmaxf(exp_dt_fast<DT>(rnd<DT>(x - rx.m[row])), 0.f) : x;
+      const T* srow = scr + (((long)g * nqt + (t >> 6)) * 64 + (t & 63)) * LDL;
+      const float m = rx.m[row];
       const float zc = rx.z[row] < eps_dt<DT>() ? eps_dt<DT>() : rx.z[row];
-      s += (double)div_dt_fast<DT>(e, 1.f / zc, zc);
+      const float rz = 1.f / zc;
+#pragma unroll
+      for (int k = 0; k < AMB_BATCH; ++k) {
+        if (k < na) {
+          const float x = to_f(srow[cols[k]]);
+          const float e = rx.scr_logits ? fmaxf(exp_dt_fast<DT>(rnd<DT>(x - m)), 0.f) : x;
+          s[k] += (double)div_dt_fast<DT>(e, rz, zc);
+        }
+      }
     }
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+#pragma unroll
+    for (int k = 0; k < AMB_BATCH; ++k) {
+      for (int o = 16; o > 0; o >>= 1) s[k] += __shfl_xor_sync(0xffffffffu, s[k], o);
+      if ((threadIdx.x & 31) == 0) red[k][threadIdx.x >> 5] = s[k];
+    }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if ((int)threadIdx.x < na) {
+      const int k = threadIdx.x, p = amb[a0 + k];
       double tot = 0.0;
-      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+      for (int i = 0; i < nwarps; ++i) tot += red[k][i];
       const float w = rnd<DT>(__fmul_rn(count_dt<DT>(pcnt[(long)gs * M0 + p]), rnd64<DT>(tot)));
       if (importance_out) importance_out[(long)g * M0 + p] = w;
       keys[p] = route_key(w, p);
