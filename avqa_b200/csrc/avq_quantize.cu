@@ -613,15 +613,15 @@ __global__ void __launch_bounds__(AG_WARPS * 32) aggregate_vec_kernel(
       float v[VPL];
       load_row_elems<DT, VPL>(&ring[i % AG_RING][lane * VPL], v);
       const int cc = __shfl_sync(0xffffffffu, cur_c, j);
-      // every child sum takes the row or +0: x + (+0) = x for every sum that can
-      // occur (they start at +0 and never become -0), so this equals the
-      // conditional add without a branch
 #pragma unroll
-      for (int q = 0; q < VPL; ++q) {
-        ap[q] = __fadd_rn(ap[q], v[q]);
+      for (int q = 0; q < VPL; ++q) ap[q] = __fadd_rn(ap[q], v[q]);
+      // the row's child, the same in every lane (a shuffled member id), so each
+      // test is a uniform branch and only that child's sums take the row
 #pragma unroll
-        for (int c = 0; c < CMAX; ++c) ac[c][q] = __fadd_rn(ac[c][q], c == cc ? v[q] : 0.f);
-      }
+      for (int c = 0; c < CMAX; ++c)
+        if (c == cc)
+#pragma unroll
+          for (int q = 0; q < VPL; ++q) ac[c][q] = __fadd_rn(ac[c][q], v[q]);
       // refill the slot with row i + AG_RING (after the slot's value was used)
       const int ni = i + AG_RING;
       if (ni < n) {
