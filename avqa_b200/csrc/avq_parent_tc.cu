@@ -449,6 +449,14 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
         const int* sl = sel0 + (long)g * sel_stride;
         const float m0 = live ? m_out[row] : 0.f;
         const float zc0 = clamp_min_nan(live ? z_out[row] : 1.f, eps_dt<DT>());
+        // DT(x / d) for x >= 0: x / d lies between RD(x dl) and RU(x dh), dl, dh
+        // the fp32 neighbours of RN(1 / d); when both round to the same dtype
+        // value so does the correctly rounded quotient, else divide exactly
+        auto div_pos = [](float x, float d, float dl, float dh) -> float {
+          const float lo = rnd<DT>(__fmul_rd(x, dl));
+          return lo == rnd<DT>(__fmul_ru(x, dh)) ? lo : rnd<DT>(__fdiv_rn(x, d));
+        };
+        const float zi0 = 1.f / zc0, zl0 = next_down(zi0), zh0 = next_up(zi0);
         float pis[32];
         double gsp = 0.0;
 #pragma unroll
@@ -459,9 +467,8 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
             const int pj = sl[j];
             const bool keep = pcnt[(long)gs * M0 + pj] > 0 && (!MK || !prow || ((prow[pj >> 5] >> (pj & 31)) & 1u));
             const float s = keep ? scale_logit<DT>(rnd<DT>(__uint_as_float(ra[i])), sqrtD, inv_sqrtD) : -INFINITY;
-            float e = exp_rn<DT>(rnd<DT>(__fsub_rn(s, m0)));
-            if (isnan(e)) e = 0.f;  // pipeline.py:143-145
-            pi = rnd<DT>(__fdiv_rn(e, zc0));
+            const float e = fmaxf(exp_dt_fast<DT>(rnd<DT>(__fsub_rn(s, m0))), 0.f);  // NaN -> 0 (pipeline.py:143-145)
+            pi = div_pos(e, zc0, zl0, zh0);
             gsp += (double)pi;
           }
           pis[i] = pi;
@@ -471,11 +478,12 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
         xd[hf * TR + r] = gsp;
         rows_sync();
         const float gsc = clamp_min_nan(rnd64<DT>(xd[r] + xd[TR + r]), eps_dt<DT>());
+        const float gi = 1.f / gsc, gl = next_down(gi), gh = next_up(gi);
         double ent = 0.0;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           if (32 * hf + i < nsel) {
-            const float top = rnd<DT>(__fdiv_rn(pis[i], gsc));  // pipeline.py:238
+            const float top = div_pos(pis[i], gsc, gl, gh);  // pipeline.py:238
             const float lp = top > 0.f ? log_rn<DT>(top) : 0.f;
             ent += (double)rnd<DT>(__fmul_rn(top, lp));  // hopfield.py:100
           }
