@@ -440,6 +440,17 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
         // the correctly rounded quotient (sign copied back); else exact redo
         float sl[24];
         bool near = false;
+        if constexpr (D == 64) {
+          // sqrt(64) = 8: DT(x / 8) is exact in fp32, one packed multiply by 1/8
+#pragma unroll
+          for (int i2 = 0; i2 < 12; ++i2) {
+            const int i = 2 * i2;
+            const uint32_t s2 = hmul2_dt<DT>(pack2<DT>(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])),
+                                             dup2<DT>(0.125f));
+            sl[i] = half_lo<DT>(s2);
+            sl[i + 1] = half_hi<DT>(s2);
+          }
+        } else {
 #pragma unroll
         for (int i2 = 0; i2 < 12; ++i2) {
           const int i = 2 * i2;
@@ -452,6 +463,7 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
           const uint32_t s2 = qlo | (x2 & 0x80008000u);
           sl[i] = half_lo<DT>(s2);
           sl[i + 1] = half_hi<DT>(s2);
+        }
         }
         if (near) {
 #pragma unroll

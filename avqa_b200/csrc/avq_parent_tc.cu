@@ -575,6 +575,13 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
         // nearest is symmetric, so the sign is copied back.  A block where
         // some pair's ends disagree is redone with correctly rounded quotients.
         uint32_t s2[8];
+        if constexpr (D == 64) {
+          // sqrt(64) = 8: the quotient is exact in fp32, so DT(x / 8) is one
+          // packed multiply by 1/8 (a single rounding, as the reference's)
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            s2[j] = hmul2_dt<DT>(pack2<DT>(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1])), dup2<DT>(0.125f));
+        } else {
         bool near = false;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -589,6 +596,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
         if (near) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) s2[j] = logit2<DT>(ra[2 * j], ra[2 * j + 1], sqrtD, inv_sqrtD, 0xFFFFFFFFu);
+        }
         }
         if constexpr (HV) {
           // DT(beta * DT(s * sqrt(D))): the fp32 product narrowed, then the exact
