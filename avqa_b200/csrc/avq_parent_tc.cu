@@ -603,8 +603,12 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
           // DT product rounded once
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const float2 sc = mul_f32x2_rn(make_float2(half_lo<DT>(s2[j]), half_hi<DT>(s2[j])), sqd2);
-            s2[j] = hmul2_dt<DT>(pack2<DT>(sc.x, sc.y), beta2);
+            if constexpr (D == 64) {  // s * 8 is exact: one packed multiply
+              s2[j] = hmul2_dt<DT>(hmul2_dt<DT>(s2[j], dup2<DT>(8.f)), beta2);
+            } else {
+              const float2 sc = mul_f32x2_rn(make_float2(half_lo<DT>(s2[j]), half_hi<DT>(s2[j])), sqd2);
+              s2[j] = hmul2_dt<DT>(pack2<DT>(sc.x, sc.y), beta2);
+            }
           }
         }
         const int pw = c * 32 + hf * 16 + hh * 8;  // first parent pair of the block
