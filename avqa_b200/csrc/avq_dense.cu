@@ -111,7 +111,9 @@ __global__ void __launch_bounds__(128) dense_attn_mma_kernel(
       tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, o));
     }
     const float n0 = fmaxf(m0, tm0), n1 = fmaxf(m1, tm1);
-    const float c0 = n0 == -INFINITY ? 1.f : expf(m0 - n0), c1 = n1 == -INFINITY ? 1.f : expf(m1 - n1);
+    // the fast exponential (within 2 ulp): the probabilities feed the P V product
+    // in the dtype, far coarser than fp32
+    const float c0 = n0 == -INFINITY ? 1.f : __expf(m0 - n0), c1 = n1 == -INFINITY ? 1.f : __expf(m1 - n1);
     m0 = n0;
     m1 = n1;
     l0 *= c0;
@@ -131,7 +133,7 @@ __global__ void __launch_bounds__(128) dense_attn_mma_kernel(
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float mm = e >= 2 ? m1 : m0;
-        p[e] = s[j][e] == -INFINITY ? 0.f : expf(s[j][e] - mm);
+        p[e] = s[j][e] == -INFINITY ? 0.f : __expf(s[j][e] - mm);
       }
       l0 += p[0] + p[1];
       l1 += p[2] + p[3];

@@ -56,19 +56,22 @@ __global__ void __launch_bounds__(SP_THREADS) stream_parent_kernel(const typenam
                                                                    unsigned long long* __restrict__ best, int H) {
   using T = typename Storage<DT>::T;
   constexpr int EW = 16 / sizeof(T);  // elements per 16-byte load
-  __shared__ float kk[SP_KEYS][ST_MAX_D];
+  __shared__ double kk[SP_KEYS][ST_MAX_D];  // held as double: one conversion per key element, not per product
   __shared__ float ksq[SP_KEYS];
   const int h = blockIdx.y, p = blockIdx.x * SP_THREADS + threadIdx.x, b0 = blockIdx.z * SP_KEYS;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nk = min(SP_KEYS, B - b0);
   for (int e = tid; e < SP_KEYS * D; e += blockDim.x) {
     const int r = e / D, d = e % D;
-    kk[r][d] = r < nk ? to_f(keys[(long long)(b0 + r) * kstride + d]) : 0.f;
+    kk[r][d] = r < nk ? (double)to_f(keys[(long long)(b0 + r) * kstride + d]) : 0.0;
   }
   __syncthreads();
   for (int r = warp; r < nk; r += SP_THREADS / 32) {  // k_sq = (keys * keys).sum(1), narrowed once
     double acc = 0.0;
-    for (int d = lane; d < D; d += 32) acc += (double)rnd<DT>(__fmul_rn(kk[r][d], kk[r][d]));
+    for (int d = lane; d < D; d += 32) {
+      const float kv = (float)kk[r][d];
+      acc += (double)rnd<DT>(__fmul_rn(kv, kv));
+    }
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (lane == 0) ksq[r] = rnd64<DT>(acc);
   }
@@ -101,10 +104,11 @@ __global__ void __launch_bounds__(SP_THREADS) stream_parent_kernel(const typenam
       const int d = d0 + e;
       if (d < D) {
         const float pv = to_f(pc[e]);
+        const double pvd = (double)pv;
         psq += (double)rnd<DT>(__fmul_rn(pv, pv));
 #pragma unroll
         for (int r = 0; r < SP_KEYS; ++r)
-          if (r < nk) acc[r] = fma((double)kk[r][d], (double)pv, acc[r]);
+          if (r < nk) acc[r] = fma(kk[r][d], pvd, acc[r]);
       }
     }
   }
