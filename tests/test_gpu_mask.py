@@ -96,10 +96,12 @@ def test_mask_mma_kernels_match_tcgen05() -> None:
     assert finite_normrel(out_tc, out_mma, "tc vs mma")[0] <= 1e-5
 
 
-def test_causal_presence_bits_match_oracle() -> None:
-    """The causal bits alone, including the cached-prefix offset."""
+@pytest.mark.parametrize("M0", [80, 64, 512])
+def test_causal_presence_bits_match_oracle(M0: int) -> None:
+    """The causal bits alone, including the cached-prefix offset, for word
+    counts of 3, 2 and 16 per query row."""
     g = torch.Generator().manual_seed(86)
-    B, H, S, D, M0, C, T = 2, 3, 500, 64, 80, 4, 120
+    B, H, S, D, C, T = 2, 3, 500, 64, 4, 120
     k = torch.randn(B, S, H * D, generator=g).to(torch.bfloat16)
     kh = k.view(B, S, H, D).transpose(1, 2)
     cb32 = codebook_from_keys(kh[0].float(), M0, C, 1)
