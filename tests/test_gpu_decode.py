@@ -35,6 +35,9 @@ CASES = [
     Workload("dec_sparse_bf16", B=2, T=1, S=20, H=2, D=128, M0=300, C=3, P=32, dtype="bf16", keys="mixture", seed=74),
     Workload("dec_m4096_bf16", B=2, T=1, S=6000, H=1, D=128, M0=4096, C=8, P=128, dtype="bf16", keys="mixture",
              seed=75),
+    # a budget above 256: the routing sorts every key instead of the radix select
+    Workload("dec_wide_budget_bf16", B=3, T=1, S=4096, H=2, D=64, M0=1024, C=2, P=320, dtype="bf16", keys="mixture",
+             seed=76),
 ]
 
 

@@ -34,6 +34,11 @@ CASES = [
              hvaq=True),
     Workload("quirk_f32", B=1, T=12, S=64, H=2, D=16, M0=6, C=2, P=6, dtype="f32", keys="mixture", seed=31, passes=2,
              pass_decay=1.0),
+    # routing orders of more than 256 parents: the bitonic sort instead of the radix select
+    Workload("wide_budget_bf16", B=1, T=128, S=4096, H=2, D=128, M0=512, C=4, P=300, dtype="bf16", keys="mixture",
+             seed=32),
+    Workload("wide_budget_mp_f16", B=1, T=96, S=3072, H=2, D=64, M0=384, C=4, P=200, dtype="f16", keys="mixture",
+             seed=33, passes=2, pass_decay=0.5),
 ]
 
 
