@@ -3,6 +3,10 @@
 // It is the reference's execution.mode = "reference" path, the path with
 // refinement disabled, and the budget-0 fallback (pipeline.py:261-273, 310-345).
 //
+//   without a mask, bf16 / fp16, D in {64, 128}: the tcgen05 parent-attention
+//       kernel in its dense mode (avq_parent_tc.cu): keys and values as its
+//       parent and parent-sum tiles, two passes (row max, then e = DT(exp(
+//       DT(s - m))) and O += e V on the tensor cores), out = DT(O / z);
 //   dense_attn_mma_kernel   bf16 / fp16, D in {64, 128}: one CTA per 64
 //       queries of one (b,h), 64-key tiles double-buffered with cp.async,
 //       S = Q K^T and O += P V on mma.sync (fp32 accumulators), the softmax
@@ -241,6 +245,10 @@ int launch_dense_attention(const void* q, Strides3 qs, const void* k, Strides3 k
              ((uintptr_t)out % 4) == 0 && os.s % 2 == 0 && os.h % 2 == 0 && os.b % 2 == 0;
   AVQ_TIMED("dense_attn", st);
   if constexpr (DT != DT_F32) {
+    if (!mask) {  // the tcgen05 parent-attention kernel in its dense mode
+      const int rc = launch_dense_tc<DT>(q, qs, k, ks, v, vs, B, H, T, N, D, scale, out, os, st);
+      if (rc != AVQ_ERR_UNSUPPORTED) return rc;
+    }
     if (mma) {
       const size_t smem = (size_t)(DQ + 4 * DK) * (D + 8) * sizeof(T_);
       auto go = [&](auto kfn) {

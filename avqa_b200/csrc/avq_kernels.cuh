@@ -215,6 +215,12 @@ int launch_dense_attention(const void* q, Strides3 qs, const void* k, Strides3 k
 // BCAR online codebook adaptation (avq_bcar.cu).
 size_t bcar_workspace_bytes(int G, int M0, int C, int D);
 
+// Dense attention on the tcgen05 parent-attention kernel (no mask; bf16 / fp16,
+// D in {64, 128}, N <= 8192 keys, N % 8 == 0); AVQ_ERR_UNSUPPORTED otherwise.
+template <int DT>
+int launch_dense_tc(const void* q, Strides3 qs, const void* k, Strides3 ks, const void* v, Strides3 vs, int B, int H,
+                    int T, int N, int D, float scale, void* out, Strides3 os, cudaStream_t st);
+
 // Streaming VQ extend (avq_stream.cu).
 int stream_max_head_dim();
 size_t stream_workspace_bytes(int B, int H, int M0, int C);

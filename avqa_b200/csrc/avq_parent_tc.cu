@@ -198,7 +198,13 @@ __device__ __forceinline__ bool rows_all(bool p) {
 // MK: a user / causal mask is applied (present != nullptr); without it the
 // mask code is compiled out, so unmasked calls run the same instructions as a
 // kernel without mask support.
-template <int DT, int D, bool HV, bool MK>
+// DN: dense attention (the reference's naive_attention, backend.py:190-203):
+// the "parents" and "parent sums" are the (b,h)'s own keys and values (4-D
+// maps tm_p / tm_v at kvpos), every key counts once, the logits are
+// DT(DT(acc) * scale) as the reference multiplies by its scale, and instead of
+// the routing state the kernel writes out = DT(O / z) at `dout` (strides os);
+// passes 1 and 2 only (no exponential slices, no importance partials).
+template <int DT, int D, bool HV, bool MK, bool DN = false>
 __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_p,
     const __grid_constant__ CUtensorMap tm_v, int4 qpos, int H, int Tq, int M0, float sqrtD,
@@ -207,7 +213,9 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     typename Storage<DT>::T* __restrict__ a_out, float* __restrict__ colpart, int sG,
     const typename Storage<DT>::T* __restrict__ parents_g, const int* __restrict__ sel0, int sel_stride,
     const int* __restrict__ pass_cnt, int hvaq, float beta0, float alpha, float* __restrict__ beta_out,
-    const unsigned int* __restrict__ present) {
+    const unsigned int* __restrict__ present, int4 kvpos, float dscale, typename Storage<DT>::T* __restrict__ dout,
+    Strides3 os) {
+  static_assert(!DN || (!HV && !MK), "the dense mode has no HVAQ pass and no mask bits");
   using T = typename Storage<DT>::T;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_addr(smem_raw);
@@ -237,8 +245,17 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     const bool par = i < nch || ((i - nch) & 1) == 0;
     const int c = i < nch ? i : (i - nch) >> 1;
     for (int kb = 0; kb < D / 64; ++kb) {
-      if (par) tc::tma_load_3d(buf + kb * TCH * 128, &tm_p, kb * 64, c * TCH, h, &bars[B_RFULL + k]);
-      else tc::tma_load_3d(buf + kb * TCH * 128, &tm_v, kb * 64, c * TCH, gs, &bars[B_RFULL + k]);
+      if constexpr (DN) {  // keys / values of this (b,h): rows c*TCH.. of the 4-D map
+        int cc[4];
+        cc[0] = kb * 64;
+        cc[kvpos.x] = c * TCH;
+        cc[kvpos.y] = h;
+        cc[kvpos.z] = b;
+        tc::tma_load_4d(buf + kb * TCH * 128, par ? &tm_p : &tm_v, cc[0], cc[1], cc[2], cc[3], &bars[B_RFULL + k]);
+      } else {
+        if (par) tc::tma_load_3d(buf + kb * TCH * 128, &tm_p, kb * 64, c * TCH, h, &bars[B_RFULL + k]);
+        else tc::tma_load_3d(buf + kb * TCH * 128, &tm_v, kb * 64, c * TCH, gs, &bars[B_RFULL + k]);
+      }
     }
   };
 
@@ -271,7 +288,14 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     for (int i = tid; i < EXP_WORDS; i += TROW) dst[i] = src[i];
     for (int j = tid; j < nch * 32; j += TROW) {
       const int p = 2 * j;
-      const int c0 = p < M0 ? pcnt[(long)gs * M0 + p] : 0, c1 = p + 1 < M0 ? pcnt[(long)gs * M0 + p + 1] : 0;
+      int c0, c1;
+      if constexpr (DN) {  // every key counts once
+        c0 = p < M0 ? 1 : 0;
+        c1 = p + 1 < M0 ? 1 : 0;
+      } else {
+        c0 = p < M0 ? pcnt[(long)gs * M0 + p] : 0;
+        c1 = p + 1 < M0 ? pcnt[(long)gs * M0 + p + 1] : 0;
+      }
       pm2[j] = (c0 > 0 ? 0xFFFFu : 0u) | (c1 > 0 ? 0xFFFF0000u : 0u);
       n2[j] = pack2<DT>(count_dt<DT>(c0), count_dt<DT>(c1));
     }
@@ -420,7 +444,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     const float2 invh2 = make_float2(next_up(inv_sqrtD), next_up(inv_sqrtD));      // >= 1/sqrt(D)
     const uint32_t ninf2 = DT == DT_BF16 ? 0xFF80FF80u : 0xFC00FC00u;
     const long row = (long)g * Tq + t;
-    T* srow_g = scratch + (((long)g * ntiles + (t >> 6)) * 64 + (t & 63)) * LDL;
+    T* srow_g = DN ? nullptr : scratch + (((long)g * ntiles + (t >> 6)) * 64 + (t & 63)) * LDL;
     // the row's mask words (pipeline.py:82-106); none for rows past T
     const int PW = (M0 + 31) >> 5;
     const unsigned int* prow = (MK && live) ? present + row * PW : nullptr;
@@ -542,7 +566,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     xch[hf * TR + r] = fmax_nan(fmax_nan(mxa[0], mxa[1]), fmax_nan(mxa[2], mxa[3]));
     rows_sync();
     const float amax = fmax_nan(xch[r], xch[TR + r]);
-    float rm = rnd<DT>(__fdiv_rn(rnd<DT>(amax), sqrtD));
+    float rm = DN ? rnd<DT>(__fmul_rn(rnd<DT>(amax), dscale)) : rnd<DT>(__fdiv_rn(rnd<DT>(amax), sqrtD));
     if constexpr (HV) rm = rnd<DT>(__fmul_rn(beta, rnd<DT>(__fmul_rn(rm, sqrtD))));  // pipeline.py:256, hopfield.py:144
     const float safe = rm == -INFINITY ? 0.f : rm;  // pipeline.py:137-141
     const uint32_t m2 = dup2<DT>(safe);
@@ -575,7 +599,16 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
         // nearest is symmetric, so the sign is copied back.  A block where
         // some pair's ends disagree is redone with correctly rounded quotients.
         uint32_t s2[8];
-        if constexpr (D == 64) {
+        if constexpr (DN) {
+          // DT(DT(acc) * scale), the reference's own product (backend.py:197)
+          const float2 sc2 = make_float2(dscale, dscale);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t x2 = pack2<DT>(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1]));
+            const float2 y = mul_f32x2_rn(make_float2(half_lo<DT>(x2), half_hi<DT>(x2)), sc2);
+            s2[j] = pack2<DT>(y.x, y.y);
+          }
+        } else if constexpr (D == 64) {
           // sqrt(64) = 8: the quotient is exact in fp32, so DT(x / 8) is one
           // packed multiply by 1/8 (a single rounding, as the reference's)
 #pragma unroll
@@ -631,8 +664,10 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
             const uint32_t sm2 = (s2[j] & keepm) | (ninf2 & ~keepm);  // -inf for empty parents (pipeline.py:107)
             const uint32_t ee = exp2_dt<DT>(hsub2_dt<DT>(sm2, m2), exptab);
             e2[j] = ee;
-            const uint32_t w2 = hmul2_dt<DT>(ee, nnv[k]);  // DT(e * n), pipeline.py:146
-            la2 = add_f32x2(la2, make_float2(half_lo<DT>(w2), half_hi<DT>(w2)));
+            if constexpr (!DN) {  // every dense key counts once: l is z
+              const uint32_t w2 = hmul2_dt<DT>(ee, nnv[k]);  // DT(e * n), pipeline.py:146
+              la2 = add_f32x2(la2, make_float2(half_lo<DT>(w2), half_hi<DT>(w2)));
+            }
             zs[j] = half_lo<DT>(ee) + half_hi<DT>(ee);
           }
         }
@@ -645,7 +680,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
         // a block of 16 starting below M0 is stored whole: when M0 % 16 == 8 the
         // last block spills 8 columns past M0, into the row pitch's padding
         // (exp_slice_pitch(M0) >= round_up(M0, 16), asserted on the host)
-        if (live && 2 * pw < M0) {
+        if (!DN && live && 2 * pw < M0) {
           // one whole 32-byte sector per store when the slices are 32-byte
           // aligned (the pitch keeps every row so), else two 16-byte halves
           T* dst = srow_g + 2 * pw;
@@ -678,7 +713,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
     // relative of the exact one; when the window straddles a dtype rounding
     // point the row is summed again exactly (by both threads, alike).
     float z = rnd<DT>(zsum);
-    if (ok && live) {
+    if (!DN && ok && live) {
       const float eps = zsum * (float)(nch + 8) * 5.9604645e-8f;
       if (rnd<DT>(zsum - eps) != rnd<DT>(zsum + eps)) {
         double ex = 0.0;
@@ -703,12 +738,17 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       constexpr int SLDB = D * 2 + 16;  // padded row bytes: a warp's 16-byte writes hit distinct banks
       static_assert(TR * SLDB <= TR * D * 2 + 4 * TCH * D * 2, "output staging");
       unsigned char* stga = sm + L.q;
+      const float iz = 1.f / zsum;  // the dense output is O / z
 #pragma unroll
       for (int d0 = 0; d0 < D / 2; d0 += 32) {
         uint32_t oa[32];
         const int dc = hf * (D / 2) + d0;
         tc::tmem_ld32(tbase + lane_off + dc, oa);
         tc::tmem_wait_ld();
+        if constexpr (DN) {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) oa[k] = __float_as_uint(__uint_as_float(oa[k]) * iz);
+        }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const uint32_t* src = oa + 8 * k;
@@ -725,16 +765,18 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
 #pragma unroll 4
       for (int i = 0; i < TR / 8; i += RPI) {
         const int rr = (warp & 7) * (TR / 8) + i + lane / U4, tt = t0 + rr;
-        if (tt < Tq)
-          reinterpret_cast<uint4*>(a_out + ((long)g * Tq + tt) * D)[c16] =
-              *reinterpret_cast<const uint4*>(stga + rr * SLDB + 16 * c16);
+        if (tt < Tq) {
+          T* dst = DN ? dout + (long)b * os.b + (long)h * os.h + (long)tt * os.s : a_out + ((long)g * Tq + tt) * D;
+          reinterpret_cast<uint4*>(dst)[c16] = *reinterpret_cast<const uint4*>(stga + rr * SLDB + 16 * c16);
+        }
       }
-      if (live && hf == 0) {
+      if (!DN && live && hf == 0) {
         m_out[row] = safe;
         l_out[row] = rnd<DT>(lsum);
         z_out[row] = z;
       }
     }
+    if constexpr (!DN) {
     const float zc = clamp_min_nan(z, eps_dt<DT>());
     if (hf == 0) {  // z and the fp32 neighbours of RN(1/z), which bracket 1/z
       const float zi = 1.f / zc;
@@ -835,6 +877,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       }
     }
     cp_async_wait<0>();
+    }  // !DN
   }
 
   // ---- teardown ----
@@ -890,7 +933,7 @@ int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st) {
         tq, tp, tv, qpos, a.H, a.T, M0, a.sqrtD, a.pcnt, static_cast<const uint16_t*>(exptab),
         static_cast<T*>(a.sglobal), a.m, a.l, a.z, static_cast<T*>(a.a), a.colpart, sG,
         static_cast<const T*>(a.parents), a.sel0, a.sel_stride, a.pass_cnt, a.hvaq, a.beta0, a.alpha, a.beta,
-        a.present);
+        a.present, make_int4(0, 0, 0, 0), 0.f, nullptr, Strides3{0, 0, 0});
   };
   const bool mk = a.present != nullptr;
   if (hv) {
@@ -905,6 +948,51 @@ int launch_parent_attn_tc(const PAArgs& a, void* exptab, cudaStream_t st) {
 
 template int launch_parent_attn_tc<DT_BF16>(const PAArgs&, void*, cudaStream_t);
 template int launch_parent_attn_tc<DT_F16>(const PAArgs&, void*, cudaStream_t);
+
+namespace {
+// The bf16 exponential table of the dense path, rewritten by every call (the
+// same 4 KB each time), so the dense entry needs no caller workspace.
+__device__ uint16_t g_dense_exptab[2 * EXP_WORDS];
+}  // namespace
+
+// Dense attention on the parent-attention kernel (DN mode): keys and values
+// are the parent and parent-sum operands, one CTA per 128 queries of a (b,h).
+template <int DT>
+int launch_dense_tc(const void* q, Strides3 qs, const void* k, Strides3 ks, const void* v, Strides3 vs, int B, int H,
+                    int T, int N, int D, float scale, void* out, Strides3 os, cudaStream_t st) {
+  using T_ = typename Storage<DT>::T;
+  if (tc_disabled() || (D != 64 && D != 128) || N < 1 || N > TC_MAX_M0 || N % 8 || T < 1) return AVQ_ERR_UNSUPPORTED;
+  // whole-row 16-byte output stores
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) || os.b % 8 || os.h % 8 || os.s % 8) return AVQ_ERR_UNSUPPORTED;
+  CUtensorMap tq, tk, tv;
+  int4 qpos, kpos, vpos;
+  if (!tc::map_rows4(&tq, DT, q, qs, B, H, T, D, TR, &qpos) || !tc::map_rows4(&tk, DT, k, ks, B, H, N, D, TCH, &kpos) ||
+      !tc::map_rows4(&tv, DT, v, vs, B, H, N, D, TCH, &vpos))
+    return AVQ_ERR_UNSUPPORTED;
+  if (kpos.x != vpos.x || kpos.y != vpos.y || kpos.z != vpos.z) return AVQ_ERR_UNSUPPORTED;
+  // the kernel copies the table into shared memory whatever the dtype (fp16
+  // does not read it), so the address is always a filled device array
+  void* tab = nullptr;
+  if (cudaGetSymbolAddress(&tab, g_dense_exptab) != cudaSuccess) return AVQ_ERR_CUDA;
+  launch_exp_table(tab, st);
+  const TcLayout L = tc_layout(D, N, false);
+  const size_t smem = std::max<size_t>((size_t)L.total + 1024, 80 * 1024);
+  auto go = [&](auto kfn) {
+    cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kfn<<<dim3((T + TR - 1) / TR, B * H), TTHREADS, smem, st>>>(
+        tq, tk, tv, qpos, H, T, N, (float)std::sqrt((double)D), nullptr, static_cast<const uint16_t*>(tab), nullptr,
+        nullptr, nullptr, nullptr, nullptr, nullptr, 1, nullptr, nullptr, 0, nullptr, 0, 0.f, 0.f, nullptr, nullptr,
+        kpos, scale, static_cast<T_*>(out), os);
+  };
+  if (D == 64) go(parent_attn_tc_kernel<DT, 64, false, false, true>);
+  else go(parent_attn_tc_kernel<DT, 128, false, false, true>);
+  return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
+}
+
+template int launch_dense_tc<DT_BF16>(const void*, Strides3, const void*, Strides3, const void*, Strides3, int, int,
+                                      int, int, int, float, void*, Strides3, cudaStream_t);
+template int launch_dense_tc<DT_F16>(const void*, Strides3, const void*, Strides3, const void*, Strides3, int, int,
+                                     int, int, int, float, void*, Strides3, cudaStream_t);
 
 int read_device_fault(int* code, cudaStream_t st) {
   int v = 0, va = 0, vc = 0;

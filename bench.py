@@ -900,7 +900,7 @@ def sub_fx(ctx: Ctx, clk) -> dict:
     work = {"dense_attn": ("tensor", 4.0 * G * T * S * D)}
     with torch.no_grad():
         rec = measure(ctx, lambda i: be.naive_attention(qh, kh, vh), 2, 5, work, T, clk)
-    rec.update(workload=f"dense attention Tq=S={T} H={H} D={D} bf16 (mma.sync)", parallelism="replicated")
+    rec.update(workload=f"dense attention Tq=S={T} H={H} D={D} bf16 (tcgen05 kernel)", parallelism="replicated")
     rec["value"] /= ctx.world
     out["dense"] = rec
     # streaming VQ: one key per extend, shared by every head

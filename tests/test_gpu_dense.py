@@ -4,8 +4,9 @@ outputs and the oracle.
 
 Covers the module in execution.mode = "reference" and with refinement
 disabled (tests/golden/dense_*.npz, causal and user masks), and the kernels
-directly: the mma.sync kernel (bf16 / fp16, D = 64 and 128) and the fp32 /
-other-D kernel, with key and query counts that are not multiples of the 64
+directly: the tcgen05 kernel (unmasked bf16 / fp16, D = 64 and 128, key
+counts a multiple of 8 up to 8192), the mma.sync kernel (masked calls and the
+other key counts) and the fp32 / other-D kernel, with key and query counts that are not multiples of the 64
 tiles, rank-4 masks, fully masked queries (NaN, as torch.softmax gives) and a
 KV cache.
 """
@@ -53,10 +54,15 @@ CASES = [
     ("bf16", 1, 2, 70, 64, 128, "rank2"),
     ("f32", 2, 2, 33, 90, 40, "rank4"),
     ("bf16", 1, 1, 20, 300, 72, None),  # D = 72: the fp32-accumulating kernel
+    # unmasked bf16 / fp16 with D = 64 or 128 and N % 8 == 0: the tcgen05 kernel
+    ("f16", 2, 2, 130, 256, 128, None),   # a partial second query tile
+    ("bf16", 1, 2, 257, 1024, 128, None),  # sixteen key chunks
+    ("f16", 1, 1, 5, 8, 64, None),        # one key row block, mostly padding
+    ("bf16", 1, 1, 4, 8200, 64, None),    # above the tcgen05 kernel's key limit: mma.sync
 ]
 
 
-@pytest.mark.parametrize("case", CASES, ids=lambda c: f"{c[0]}_D{c[5]}_{c[6]}")
+@pytest.mark.parametrize("case", CASES, ids=lambda c: f"{c[0]}_T{c[3]}_N{c[4]}_D{c[5]}_{c[6]}")
 def test_dense_kernels_match_oracle(case) -> None:
     dt, B, H, T, N, D, kind = case
     g = torch.Generator().manual_seed(91 + D + T)
