@@ -36,6 +36,8 @@ of the headline workload per step) and reports the same metric.
 from __future__ import annotations
 
 import argparse
+import contextlib
+import gc
 import json
 import os
 import subprocess
@@ -458,14 +460,30 @@ class Ctx:
         self.barrier()
         torch.cuda.synchronize(self.dev)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
-        ev[0].record(self.stream)
-        for i in range(steps):
-            fn(start + i)
-            ev[i + 1].record(self.stream)
-        torch.cuda.synchronize(self.dev)
+        with no_gc():
+            ev[0].record(self.stream)
+            for i in range(steps):
+                fn(start + i)
+                ev[i + 1].record(self.stream)
+            torch.cuda.synchronize(self.dev)
         self.barrier()
         per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
         return self.max_over_ranks(ev[0].elapsed_time(ev[-1])), per
+
+
+@contextlib.contextmanager
+def no_gc():
+    """Python's cyclic collector paused over a timed region (as ``timeit``
+    does): a full collection stalls the host for tens of milliseconds, which
+    a host-bound loop of short steps would count as device idle time."""
+    gc.collect()
+    was = gc.isenabled()
+    gc.disable()
+    try:
+        yield
+    finally:
+        if was:
+            gc.enable()
 
 
 def _median(xs: list[float]) -> float:
@@ -487,7 +505,7 @@ def measure(ctx: Ctx, fn, warmup: int, steps: int, work: dict, tokens_per_step: 
     prof = _lib.profile_end()
     kernels, roof = kernel_table(prof, work, ctx.peaks, ctx.peak_src, total_ms / 1e3)
     rec = {"steps": steps, "warmup": warmup, "ms_per_step": total_ms / steps, "ms_per_step_median": _median(per),
-           "value": tokens_per_step * steps / (total_ms / 1e3), "unit": UNIT, "roofline": roof, "kernels": kernels,
+           "ms_per_step_max": max(per) if per else 0.0, "value": tokens_per_step * steps / (total_ms / 1e3), "unit": UNIT, "roofline": roof, "kernels": kernels,
            "gpu_launches": sum(n * (3 if k == "bucket_sort" else 1) for k, (_, n) in prof.items())}
     if clk is not None:
         rec["clocks"] = clk.summary(t0, t1)
@@ -630,25 +648,55 @@ def run_e2e(ctx: Ctx, mod, q, k, v, w, steps: int) -> dict:
         ctx.barrier()
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        s_in.wait_event(e0)
-        for i in range(n):
-            e2e_step(i)
-        stream.wait_stream(s_out)
-        stream.wait_stream(s_in)
-        e1.record(stream)
+        with no_gc():
+            e0.record(stream)
+            s_in.wait_event(e0)
+            for i in range(n):
+                e2e_step(i)
+            stream.wait_stream(s_out)
+            stream.wait_stream(s_in)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+        ctx.barrier()
+        return ctx.max_over_ranks(e0.elapsed_time(e1))
+
+    def copies_only(n):
+        """The same copies with no compute: the host link's floor for a step."""
+        ctx.barrier()
         torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        o = torch.empty(hout[0].shape, dtype=hout[0].dtype, device=dev)
+        with no_gc():
+            e0.record(stream)
+            s_in.wait_event(e0)
+            s_out.wait_event(e0)
+            for i in range(n):
+                with torch.cuda.stream(s_in):
+                    for d, hx in zip(dbuf[i % 2], (hq, hk, hv)):
+                        d.copy_(hx, non_blocking=True)
+                with torch.cuda.stream(s_out):
+                    hout[i % 2].copy_(o, non_blocking=True)
+            stream.wait_stream(s_out)
+            stream.wait_stream(s_in)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
         ctx.barrier()
         return ctx.max_over_ranks(e0.elapsed_time(e1))
 
     e2e_timed(2)
-    nb = max(4, steps // 2)
+    # steady state of a serving loop: enough steps that filling and draining
+    # the three-stream pipeline (the first upload, the last download) weigh
+    # little, about 0.3 s at the c2 shapes
+    nb = max(16, steps)
     ms = e2e_timed(nb)
+    link_ms = copies_only(nb)
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
     d2h = hout[0].numel() * hout[0].element_size()
     return {"value": ctx.world * w.B * w.T * nb / (ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "ms_per_step": ms / nb,
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms / nb, "steps": nb,
             "host_copy_gbs_per_gpu": (h2d + d2h) / (ms / nb / 1e3) / 1e9,
+            "copies_only_ms_per_step": link_ms / nb,
+            "frac_of_copy_bound": link_ms / ms,
             "overlap": "H2D, compute and D2H on separate streams, two device buffer sets"}
 
 
