@@ -15,9 +15,8 @@
 // keys: the order-preserving integer form of the 16-bit distance in the high
 // half and the parent index in the low half.  A row with a NaN
 // distance (only possible with non-finite inputs) takes a scalar path.
-// Child stage (quantizer.py:218-226): each row warp then takes its 32 keys
-// one group of four at a time, the keys' child blocks arriving by bulk copy
-// in the idle parent buffers; the cross term is a sum of dtype-rounded
+// Child stage (quantizer.py:218-226): a later kernel, once the keys are sorted
+// by parent (child_bucket_kernel); the cross term is a sum of dtype-rounded
 // elementwise products, rounded once as its exact value would be (fp32 with
 // an error bound, fp64 where the bound cannot decide).
 #include <cuda.h>
@@ -43,13 +42,11 @@ constexpr int ATHREADS = 192;  // 4 row warps + MMA warp + TMA warp
 constexpr int A_TMEM_COLS = 256;
 constexpr int A_MAX_M0 = 4096;
 constexpr int A_MAX_C = 8;           // children per parent on this path
-constexpr int A_KP = 4;              // keys per ring group of the child stage
-constexpr int A_RING_GROUPS = 4;     // most ring groups of a row warp's child stage
 
 constexpr int AB_K = 0, AB_PFULL = 1, AB_PEMPTY = 3, AB_SFULL = 5, AB_SCONS = 7, AB_END = 9, AN_BARS = 10;
 
 struct AssignLayout {
-  int k, p[2], ps2, rbar, bars, misc, total;
+  int k, p[2], ps2, bars, misc, total;
 };
 
 __host__ __device__ inline AssignLayout assign_layout(int D, int M0) {
@@ -64,8 +61,6 @@ __host__ __device__ inline AssignLayout assign_layout(int D, int M0) {
   }
   L.ps2 = o;
   o += nch * (ACH / 2) * 4;
-  L.rbar = o;  // child-stage ring barriers, A_RING_GROUPS per row warp
-  o += 4 * A_RING_GROUPS * 8;
   L.bars = o;
   o += AN_BARS * 8;
   L.misc = o;
@@ -118,14 +113,6 @@ __device__ __forceinline__ void drain(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// Global -> shared bulk copy (TMA engine, no tensor map), completing on `bar`.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   tc::smem_addr(dst)),
-               "l"(src), "r"(bytes), "r"(tc::smem_addr(bar))
-               : "memory");
-}
-
 // Bound on sum_d |DT(k_d c_d)| from the dtype norms: |k_d c_d| <= (k_d^2 +
 // c_d^2) / 2, and k_sq, c_sq are the once-rounded exact sums of the dtype
 // squares, so sum_d k_d^2 <= k_sq (1 + 2.1 u) + D eta (u the dtype's unit
@@ -137,13 +124,18 @@ struct ChildBound {
   static constexpr float slack = DT == DT_F16 ? 0x1p-36f : 0x1p-140f;  // >= 2^-21 * 4 * 128 * eta
 };
 
-// Child stage of one warp's 32 keys (quantizer.py:218-227).  A key's C child
-// rows form one contiguous block; its rows are spread over the warp, G lanes
-// to a row, lane (rsub, vg) holding the 16-byte chunks vg + G*t (t < NV) of
-// row rsub.  The blocks stream through a per-warp ring of NG groups of A_KP
-// keys in shared memory, one bulk copy per key issued by the key's own lane,
-// NG - 1 groups ahead of the one being reduced; each key's C child norms sit
-// in its lane's registers.
+// Child assignment in bucket order (quantizer.py:218-227), after the parent
+// pass and the counting sort by parent: a warp takes 32 consecutive keys of
+// the sorted order of one (b,h), so neighbouring keys mostly share their
+// parent and its C child rows (one contiguous block) are read from L2 once
+// for many keys instead of once per key.  Each key's dtype k_sq comes from
+// the parent pass, parked in the key's cassign word as float bits, and is
+// overwritten by the key's child index here.
+//
+// A key's child rows are spread over the warp R = 32/G rows at a time (NP
+// passes of R rows), G lanes to a row, lane (rsub, vg) holding the 16-byte
+// chunks vg + G*t (t < NV) of row ps*R + rsub in pass ps; the warp takes its
+// keys four at a time.
 //
 // cross = DT(fp32(sum_d DT(k_d c_d))) with the sum exact (what the fp64 sum
 // of the dtype products gives) is evaluated in fp32: each lane sums its 8*NV
@@ -153,168 +145,174 @@ struct ChildBound {
 // rounding are monotone, so when both ends of [S' - b, S' + b] (rounded
 // outwards) round to the same dtype value that value is the exact sum's
 // rounding; otherwise (close to a dtype rounding boundary, or non-finite)
-// the row is summed again in fp64.  The row's lanes reduce-scatter the A_KP
+// the row is summed again in fp64.  The row's lanes reduce-scatter the four
 // keys' sums, so each lane finishes one key: the rounding test, the distance
-// and the argmin run once per lane, not once per key.  torch.argmin over the children (first minimum, a NaN wins) is a
-// signed min over 32-bit keys: the order-preserving integer form of the
-// distance, whose low 13 bits are zero for dtype values, or'ed with the
-// child index.
-template <int DT, int D, int NV, int NG>
-__device__ __forceinline__ int child_stage(unsigned char* ring, uint64_t* rbar, volatile int* abort,
-                                           const unsigned char* ktile, int warp, int lane, uint32_t livemask, int pbest,
-                                           float ksq, const unsigned char* __restrict__ chh,
-                                           const float* __restrict__ csqh, int C) {
-  static_assert(NG <= A_RING_GROUPS, "ring barriers");
-  constexpr int CPR = D / 8, G = CPR / NV, KP = A_KP, NGRP = 32 / KP;
+// and the argmin run once per lane, not once per key.  torch.argmin over the
+// children (first minimum, a NaN wins) is a signed min over 32-bit keys: the
+// order-preserving integer form of the distance, whose low 13 bits are zero
+// for dtype values, or'ed with the child index.
+constexpr int CB_WARPS = 8;  // warps per CTA of the child kernel
+
+template <int DT, int D, int NV, int NP>
+__global__ void __launch_bounds__(CB_WARPS * 32, NP > 1 ? 2 : 3) child_bucket_kernel(
+    const typename Storage<DT>::T* __restrict__ keys, Strides3 ks, int H, int S, int M0, int C,
+    const int* __restrict__ order, const int* __restrict__ passign, const typename Storage<DT>::T* __restrict__ children,
+    const float* __restrict__ c_sq, int* __restrict__ cassign) {
+  using T = typename Storage<DT>::T;
+  constexpr int CPR = D / 8, G = CPR / NV, KP = 4, NGRP = 32 / KP;
   static_assert(G >= KP && G % KP == 0 && 32 % G == 0, "lanes per row");
-  constexpr int RB = D * 2;  // bytes per child row
+  constexpr int R = 32 / G;       // child rows per pass
+  constexpr int CQ = R * NP;      // the largest C this split serves
   const unsigned full = 0xffffffffu;
-  static_assert(KP == 4, "two halving levels");
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = blockIdx.y, b = g / H, h = g % H;
+  const int i0 = (blockIdx.x * CB_WARPS + warp) * 32;
+  if (i0 >= S) return;  // whole warps leave together
   const int vg = lane % G, rsub = lane / G;
   const bool hb1 = (vg & (G / 2)) != 0, hb2 = (vg & (G / 4)) != 0;
   const int kq = (hb1 ? 2 : 0) + (hb2 ? 1 : 0);  // the key of the group this lane finishes
-  const bool rowon = rsub < C;
-  const int blk = C * RB;
-  const int boff_mine = pbest * blk;  // byte offset of this lane's key's child block in the head
-  const int lane_off = rsub * RB + vg * 16;
-  (void)warp;
-  // keys KP*grp .. KP*grp+KP-1 into ring group grp % NG: each live key's
-  // owner lane copies its block with one bulk copy; the group's first owner
-  // arms the barrier.  Every lane's reads of the slot fed the shuffles of the
-  // reductions before, so they are complete when the owner's copy is issued.
-  auto issue = [&](int grp) {
-    const int sg = grp % NG, kk = lane % KP;
-    const uint32_t gl = (livemask >> (grp * KP)) & ((1u << KP) - 1u);
-    if (lane == grp * KP) tc::mbar_expect_tx(&rbar[sg], (uint32_t)__popc(gl) * (uint32_t)blk);
-    __syncwarp();
-    if (lane / KP == grp && ((gl >> kk) & 1u))
-      bulk_g2s(ring + (sg * KP + kk) * blk, chh + boff_mine, (uint32_t)blk, &rbar[sg]);
-  };
-  // this lane's key's child norms, read once; the epilogue takes them from the
-  // key's owner lane
-  // the largest C that this lane split serves (the dispatch picks NV from C)
-  constexpr int CQ = D == 128 ? (NV >= 4 ? 8 : (NV == 2 ? 4 : 2)) : (NV >= 2 ? 8 : 4);
-  float cq[CQ];
-  const bool live_mine = ((livemask >> lane) & 1u) != 0u;
+  // this lane's own key: sorted position i0 + lane
+  const bool live = i0 + lane < S;
+  const int s_mine = live ? order[(long)g * S + i0 + lane] : 0;
+  const int p_mine = live ? passign[(long)g * S + s_mine] : 0;
+  const float ksq_mine = live ? __int_as_float(cassign[(long)g * S + s_mine]) : 0.f;
+  float cq[CQ];  // the lane's key's child norms; the finishing lanes take them by shuffle
 #pragma unroll
-  for (int c = 0; c < CQ; ++c) cq[c] = live_mine && c < C ? csqh[pbest * C + c] : 0.f;
-  uint32_t koff[NV];  // this lane's key chunks in the swizzled key tile, before the row swizzle
+  for (int c = 0; c < CQ; ++c) cq[c] = live && c < C ? c_sq[((long)h * M0 + p_mine) * C + c] : 0.f;
+  const T* kbase = keys + (long)b * ks.b + (long)h * ks.h;
+  const T* cbase = children + (long)h * M0 * C * D;
+  // the warp's 32 key rows, staged in shared memory at once (one gather
+  // latency for the warp instead of one per group of four)
+  extern __shared__ __align__(16) unsigned char cb_smem[];
+  unsigned char* krows = cb_smem + warp * 32 * D * 2;
 #pragma unroll
-  for (int t = 0; t < NV; ++t) {
-    const int v = vg + G * t;
-    koff[t] = (uint32_t)((v >> 3) * AR * 128 + ((v & 7) << 4));
-  }
-  auto key_chunk = [&](int rk, int t) -> uint4 {  // chunk j of slab v/8 sits at j ^ (rk & 7)
-    return *reinterpret_cast<const uint4*>(ktile + rk * 128 + (koff[t] ^ ((rk & 7) << 4)));
+  for (int c = 0; c < CPR; ++c)
+    cp_async16(krows + lane * D * 2 + 16 * c, kbase + (long)s_mine * ks.s + 8 * c, live);
+  cp_async_commit();
+  auto key_chunk = [&](int j, int t) -> uint4 {  // chunk vg + G t of the warp's key j
+    return *reinterpret_cast<const uint4*>(krows + j * D * 2 + 16 * (vg + G * t));
   };
-  auto blk_chunk = [&](int slot, int t) -> uint4 {
-    return rowon ? *reinterpret_cast<const uint4*>(ring + slot * blk + lane_off + G * 16 * t)
-                 : make_uint4(0u, 0u, 0u, 0u);
+  cp_async_wait<0>();
+  __syncwarp();
+  // the child rows of the parent in hand, reloaded only where the sorted keys
+  // move on to the next parent (warp-uniform)
+  auto blk_chunk = [&](int p, int ps, int t) -> uint4 {
+    const int crow = ps * R + rsub;
+    return crow < C ? *reinterpret_cast<const uint4*>(cbase + ((long)p * C + crow) * D + 8 * (vg + G * t))
+                    : make_uint4(0u, 0u, 0u, 0u);
   };
-
-  int mine = -1;
+  int cur_p = -1;
+  uint4 wc[NP][NV];
+  int mine = 0;
 #pragma unroll 1
-  for (int gq = 0; gq < NG; ++gq) issue(gq);
-  int gq = 0;
-#pragma unroll 1
-  for (; gq < NGRP; ++gq) {
-    const int sg = gq % NG;
-    if (!__all_sync(full, tc::mbar_wait(&rbar[sg], (gq / NG) & 1, abort))) break;
-    float sx[KP];
+  for (int gq = 0; gq < NGRP; ++gq) {
+    if (i0 + gq * KP >= S) break;  // warp-uniform
+    int pk[KP];
+#pragma unroll
+    for (int kk = 0; kk < KP; ++kk) pk[kk] = __shfl_sync(full, p_mine, gq * KP + kk);  // 0 past S
+    const float ksk = __shfl_sync(full, ksq_mine, gq * KP + kq);
+    float sxa[NP][KP];
 #pragma unroll
     for (int kk = 0; kk < KP; ++kk) {
-      const int rk = warp * 32 + gq * KP + kk;
-      float2 acc[NV * 4];
+      if (pk[kk] != cur_p) {
+        cur_p = pk[kk];
 #pragma unroll
-      for (int t = 0; t < NV; ++t) {
-        const uint4 u = key_chunk(rk, t), w = blk_chunk(sg * KP + kk, t);
-        const uint32_t ku[4] = {u.x, u.y, u.z, u.w}, cw[4] = {w.x, w.y, w.z, w.w};
+        for (int ps = 0; ps < NP; ++ps)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t pr = hmul2_dt<DT>(ku[e], cw[e]);  // DT(k_d * c_d)
-          acc[4 * t + e] = make_float2(half_lo<DT>(pr), half_hi<DT>(pr));
-        }
+          for (int t = 0; t < NV; ++t) wc[ps][t] = blk_chunk(cur_p, ps, t);
       }
 #pragma unroll
-      for (int st = 1; st < NV * 4; st <<= 1)
-#pragma unroll
-        for (int i = 0; i + st < NV * 4; i += 2 * st) acc[i] = add_f32x2(acc[i], acc[i + st]);
-      sx[kk] = acc[0].x + acc[0].y;
-    }
-    // reduce-scatter of the four keys' row sums over the row's G lanes: the
-    // lanes G/2 apart swap a pair of keys and keep the other, the lanes G/4
-    // apart one key of the pair, and a butterfly over the rest completes the
-    // lane's key kq (every lane of it then holds the same sum)
-    float sv;
-    {
-      const float s0 = hb1 ? sx[0] : sx[2], s1 = hb1 ? sx[1] : sx[3];
-      const float r0 = __shfl_xor_sync(full, s0, G / 2), r1 = __shfl_xor_sync(full, s1, G / 2);
-      const float w0 = (hb1 ? sx[2] : sx[0]) + r0, w1 = (hb1 ? sx[3] : sx[1]) + r1;
-      const float r = __shfl_xor_sync(full, hb2 ? w0 : w1, G / 4);
-      sv = (hb2 ? w1 : w0) + r;
-    }
-#pragma unroll
-    for (int o = 1; o < G / 4; o <<= 1) sv += __shfl_xor_sync(full, sv, o);
-    const float ksk = __shfl_sync(full, ksq, gq * KP + kq);
-    float cs = 0.f;  // c_sq of this lane's (key, child) pair, from the key's owner lane
-#pragma unroll
-    for (int c = 0; c < CQ; ++c) {
-      if (c < C) {
-        const float v = __shfl_sync(full, cq[c], gq * KP + kq);
-        cs = rsub == c ? v : cs;
-      }
-    }
-    const float bnd = __fmaf_ru(__fadd_ru(ksk, cs), ChildBound<DT>::scale, ChildBound<DT>::slack);
-    float cross = rnd<DT>(__fsub_rd(sv, bnd));
-    const bool bad = rowon && !(cross == rnd<DT>(__fadd_ru(sv, bnd)));
-    if (__any_sync(full, bad)) {
-#pragma unroll
-      for (int kk = 0; kk < KP; ++kk) {
-        if (!__any_sync(full, bad && kq == kk)) continue;
-        const int rk = warp * 32 + gq * KP + kk;
-        double e64 = 0.0;
+      for (int ps = 0; ps < NP; ++ps) {
+        float2 acc[NV * 4];
 #pragma unroll
         for (int t = 0; t < NV; ++t) {
-          const uint4 u = key_chunk(rk, t), w = blk_chunk(sg * KP + kk, t);
+          const uint4 u = key_chunk(gq * KP + kk, t), w = wc[ps][t];
           const uint32_t ku[4] = {u.x, u.y, u.z, u.w}, cw[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const uint32_t pr = hmul2_dt<DT>(ku[e], cw[e]);
-            e64 += (double)half_lo<DT>(pr) + (double)half_hi<DT>(pr);
+            const uint32_t pr = hmul2_dt<DT>(ku[e], cw[e]);  // DT(k_d * c_d)
+            acc[4 * t + e] = make_float2(half_lo<DT>(pr), half_hi<DT>(pr));
           }
         }
 #pragma unroll
-        for (int o = 1; o < G; o <<= 1) e64 += __shfl_xor_sync(full, e64, o);
-        if (bad && kq == kk) cross = rnd64<DT>(e64);
+        for (int st = 1; st < NV * 4; st <<= 1)
+#pragma unroll
+          for (int i = 0; i + st < NV * 4; i += 2 * st) acc[i] = add_f32x2(acc[i], acc[i + st]);
+        sxa[ps][kk] = acc[0].x + acc[0].y;
       }
     }
-    // d = DT(DT(k_sq + c_sq) - DT(2 * cross)); + 0 turns a -0 into +0 (torch compares them equal)
-    const float dd = __fadd_rn(rnd<DT>(__fsub_rn(rnd<DT>(__fadd_rn(ksk, cs)), rnd<DT>(__fmul_rn(2.f, cross)))), 0.f);
-    const int bits = __float_as_int(dd);
-    const int ord = bits >= 0 ? bits : (bits ^ 0x7FFFE000);
-    int key = !rowon ? 0x7FFFFFFF : isnan(dd) ? (int)(0x80000000u | (uint32_t)rsub) : (ord & ~0x1FFF) | rsub;
+    int best = 0x7FFFFFFF;  // over the passes: the key of this lane's key kq
 #pragma unroll
-    for (int o = G; o < 32; o <<= 1) key = min(key, __shfl_xor_sync(full, key, o));
+    for (int ps = 0; ps < NP; ++ps) {
+      const int crow = ps * R + rsub;  // the child row of this lane in this pass
+      const bool rowon = crow < C;
+      const float* sx = sxa[ps];
+      // reduce-scatter of the four keys' row sums over the row's G lanes: the
+      // lanes G/2 apart swap a pair of keys and keep the other, the lanes G/4
+      // apart one key of the pair, and a butterfly over the rest completes the
+      // lane's key kq (every lane of it then holds the same sum)
+      float sv;
+      {
+        const float s0 = hb1 ? sx[0] : sx[2], s1 = hb1 ? sx[1] : sx[3];
+        const float r0 = __shfl_xor_sync(full, s0, G / 2), r1 = __shfl_xor_sync(full, s1, G / 2);
+        const float w0 = (hb1 ? sx[2] : sx[0]) + r0, w1 = (hb1 ? sx[3] : sx[1]) + r1;
+        const float r = __shfl_xor_sync(full, hb2 ? w0 : w1, G / 4);
+        sv = (hb2 ? w1 : w0) + r;
+      }
+#pragma unroll
+      for (int o = 1; o < G / 4; o <<= 1) sv += __shfl_xor_sync(full, sv, o);
+      float cs = 0.f;  // c_sq of this lane's (key, child) pair, from the key's owner lane
+#pragma unroll
+      for (int c = ps * R; c < ps * R + R; ++c) {
+        const float v = __shfl_sync(full, cq[c], gq * KP + kq);
+        cs = crow == c ? v : cs;
+      }
+      const float bnd = __fmaf_ru(__fadd_ru(ksk, cs), ChildBound<DT>::scale, ChildBound<DT>::slack);
+      float cross = rnd<DT>(__fsub_rd(sv, bnd));
+      const bool bad = rowon && !(cross == rnd<DT>(__fadd_ru(sv, bnd)));
+      if (__any_sync(full, bad)) {
+#pragma unroll
+        for (int kk = 0; kk < KP; ++kk) {
+          if (!__any_sync(full, bad && kq == kk)) continue;
+          double e64 = 0.0;
+#pragma unroll
+          for (int t = 0; t < NV; ++t) {
+            const uint4 u = key_chunk(gq * KP + kk, t), w = blk_chunk(pk[kk], ps, t);
+            const uint32_t ku[4] = {u.x, u.y, u.z, u.w}, cw[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t pr = hmul2_dt<DT>(ku[e], cw[e]);
+              e64 += (double)half_lo<DT>(pr) + (double)half_hi<DT>(pr);
+            }
+          }
+#pragma unroll
+          for (int o = 1; o < G; o <<= 1) e64 += __shfl_xor_sync(full, e64, o);
+          if (bad && kq == kk) cross = rnd64<DT>(e64);
+        }
+      }
+      // d = DT(DT(k_sq + c_sq) - DT(2 * cross)); + 0 turns a -0 into +0 (torch compares them equal)
+      const float dd =
+          __fadd_rn(rnd<DT>(__fsub_rn(rnd<DT>(__fadd_rn(ksk, cs)), rnd<DT>(__fmul_rn(2.f, cross)))), 0.f);
+      const int bits = __float_as_int(dd);
+      const int ord = bits >= 0 ? bits : (bits ^ 0x7FFFE000);
+      int key = !rowon ? 0x7FFFFFFF : isnan(dd) ? (int)(0x80000000u | (uint32_t)crow) : (ord & ~0x1FFF) | crow;
+#pragma unroll
+      for (int o = G; o < 32; o <<= 1) key = min(key, __shfl_xor_sync(full, key, o));
+      best = min(best, key);  // the child index in the low bits keeps the first minimum
+    }
     // row 0's lane vg = (kk >> 1) G/2 + (kk & 1) G/4 now holds key kk of the group
     const int kk_own = lane % KP;
-    const int res = __shfl_sync(full, key, (kk_own >> 1) * (G / 2) + (kk_own & 1) * (G / 4));
+    const int res = __shfl_sync(full, best, (kk_own >> 1) * (G / 2) + (kk_own & 1) * (G / 4));
     if (lane / KP == gq) mine = res & 0x1FFF;
-    // every value read from this ring group fed the reductions above: refill it
-    if (gq + NG < NGRP) issue(gq + NG);
   }
-  if (gq < NGRP) {  // a wait gave up: let the copies in flight land before the CTA exits
-    for (int g2 = gq; g2 < NGRP && g2 < gq + NG; ++g2) drain(&rbar[g2 % NG], (g2 / NG) & 1);
-    return -1;
-  }
-  return mine;
+  if (live) cassign[(long)g * S + s_mine] = mine;
 }
 
 template <int DT, int D>
 __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_p, int4 kpos, int H, int S,
-    int M0, int C, const typename Storage<DT>::T* __restrict__ parents, const float* __restrict__ p_sq,
-    const typename Storage<DT>::T* __restrict__ children, const float* __restrict__ c_sq, int* __restrict__ passign,
-    int* __restrict__ cassign) {
+    int M0, const typename Storage<DT>::T* __restrict__ parents, const float* __restrict__ p_sq,
+    int* __restrict__ passign, int* __restrict__ cassign) {
   using T = typename Storage<DT>::T;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_addr(smem_raw);
@@ -322,6 +320,12 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
   const AssignLayout L = assign_layout(D, M0);
   const int g = blockIdx.y, b = g / H, h = g % H, s0 = blockIdx.x * AR;
   const int nch = (M0 + ACH - 1) / ACH;
+  // the CTA's i-th chunk is chunk (i + rot) mod nch: the CTAs of a head that
+  // run together start at different chunks, so that they do not all request
+  // the same codebook lines from L2 at once (the argmin keys carry the parent
+  // index, so the order of the chunks does not change the result)
+  const int rot = blockIdx.x % nch;
+  auto chunk_of = [&](int i) { return i + rot < nch ? i + rot : i + rot - nch; };
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.bars);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + L.misc);
@@ -334,7 +338,6 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
     // the producer initialises the barriers and starts the key tile and the
     // first two parent chunks while the other warps set up
     for (int i = 0; i < AN_BARS; ++i) tc::mbar_init(&bars[i], (i == AB_SCONS || i == AB_SCONS + 1) ? AR : 1);
-    for (int i = 0; i < 4 * A_RING_GROUPS; ++i) tc::mbar_init(reinterpret_cast<uint64_t*>(sm + L.rbar) + i, 1);
     *abort = 0;
     tc::fence_mbar_init();
     tc::tma_prefetch_desc(&tm_k);
@@ -351,7 +354,7 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
     for (int ci = 0; ci < 2 && ci < nch; ++ci) {
       tc::mbar_expect_tx(&bars[AB_PFULL + ci], ACH * D * 2);
       for (int kb = 0; kb < D / 64; ++kb)
-        tc::tma_load_3d(sm + L.p[ci] + kb * ACH * 128, &tm_p, kb * 64, ci * ACH, h, &bars[AB_PFULL + ci]);
+        tc::tma_load_3d(sm + L.p[ci] + kb * ACH * 128, &tm_p, kb * 64, chunk_of(ci) * ACH, h, &bars[AB_PFULL + ci]);
       ++np[ci];
     }
   }
@@ -387,7 +390,7 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
         if (!tc::mbar_wait(&bars[AB_PEMPTY + s], ((ci - 2) >> 1) & 1, abort)) break;
         tc::mbar_expect_tx(&bars[AB_PFULL + s], ACH * D * 2);
         for (int kb = 0; kb < D / 64; ++kb)
-          tc::tma_load_3d(sm + L.p[s] + kb * ACH * 128, &tm_p, kb * 64, ci * ACH, h, &bars[AB_PFULL + s]);
+          tc::tma_load_3d(sm + L.p[s] + kb * ACH * 128, &tm_p, kb * 64, chunk_of(ci) * ACH, h, &bars[AB_PFULL + s]);
         ++np[s];
       }
       if (*abort) {
@@ -496,7 +499,8 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
       const uint32_t col = tbase + lane_off + ACH * sb;
       uint32_t qa[32], qb[32];
       auto scan = [&](const uint32_t (&r)[32], int quarter) {
-        const uint4* pp = reinterpret_cast<const uint4*>(ps2 + ci * (ACH / 2) + 16 * quarter);
+        const int cid = chunk_of(ci);
+        const uint4* pp = reinterpret_cast<const uint4*>(ps2 + cid * (ACH / 2) + 16 * quarter);
         if (finite_w) {
           int qbest = 0x7FFFFFFF;  // keys with the index within the quarter
 #pragma unroll
@@ -512,10 +516,10 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
               qbest = min(qbest, min(key_lo(k2, il), key_hi(k2, il)));
             }
           }
-          best = min(best, qbest + (ci * ACH + 32 * quarter));  // the index half has room: M0 <= 4096
+          best = min(best, qbest + (cid * ACH + 32 * quarter));  // the index half has room: M0 <= 4096
           return;
         }
-        const uint32_t base2 = (uint32_t)(ci * ACH + 32 * quarter) * 0x10001u + 0x10000u;
+        const uint32_t base2 = (uint32_t)(cid * ACH + 32 * quarter) * 0x10001u + 0x10000u;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const uint4 pq = pp[q];
@@ -569,28 +573,11 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
         }
       }
     }
-    // child stage: the assigned parent's children (quantizer.py:218-226), a
-    // warp's 32 keys through a cp.async ring in the now idle parent buffers
-    int bi = -1;
-    if (ok) {
-      const uint32_t livemask = __ballot_sync(0xffffffffu, live);
-      unsigned char* ring = sm + L.p[0] + warp * (ACH * D);
-      uint64_t* rbar = reinterpret_cast<uint64_t*>(sm + L.rbar) + warp * A_RING_GROUPS;
-      const unsigned char* chh = reinterpret_cast<const unsigned char*>(children + (long)h * M0 * C * D);
-      const float* csqh = c_sq + (long)h * M0 * C;
-      const unsigned char* kt = sm + L.k;
-      if constexpr (D == 128)
-        bi = C <= 2 ? child_stage<DT, D, 1, 4>(ring, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
-             : C <= 4 ? child_stage<DT, D, 2, 4>(ring, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
-                      : child_stage<DT, D, 4, 2>(ring, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C);
-      else
-        bi = C <= 4 ? child_stage<DT, D, 1, 4>(ring, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C)
-                    : child_stage<DT, D, 2, 2>(ring, rbar, abort, kt, warp, lane, livemask, pbest, ksq, chh, csqh, C);
-    }
+    // the child stage runs later, in bucket order (child_bucket_kernel); it
+    // finds this key's k_sq in the key's cassign word
     if (live) {  // a CTA that gave up on a wait still leaves indices in range for the later kernels
-      const bool good = ok && bi >= 0;
-      passign[(long)g * S + s] = good ? pbest : 0;
-      cassign[(long)g * S + s] = good ? bi : 0;
+      passign[(long)g * S + s] = ok ? pbest : 0;
+      cassign[(long)g * S + s] = __float_as_int(ok ? ksq : 0.f);
     }
   }
 
@@ -628,9 +615,8 @@ int launch_assign_tc(const QuantizeArgs& a, cudaStream_t st) {
   auto go = [&](auto kfn) {
     AVQ_TIMED("assign_tc", st);
     cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kfn<<<dim3((a.S + AR - 1) / AR, G), ATHREADS, smem, st>>>(tk, tp, kpos, a.H, a.S, a.M0, a.C,
+    kfn<<<dim3((a.S + AR - 1) / AR, G), ATHREADS, smem, st>>>(tk, tp, kpos, a.H, a.S, a.M0,
                                                                 static_cast<const T*>(a.parents_dt), a.p_sq,
-                                                                static_cast<const T*>(a.children_dt), a.c_sq,
                                                                 a.passign, a.cassign);
   };
   if (D == 64) go(assign_tc_kernel<DT, 64>);
@@ -640,6 +626,39 @@ int launch_assign_tc(const QuantizeArgs& a, cudaStream_t st) {
 
 template int launch_assign_tc<DT_BF16>(const QuantizeArgs&, cudaStream_t);
 template int launch_assign_tc<DT_F16>(const QuantizeArgs&, cudaStream_t);
+
+// The child stage of a launch_assign_tc pass, once `order` holds each (b,h)'s
+// keys sorted by parent.
+template <int DT>
+int launch_child_bucket(const QuantizeArgs& a, const int* order, cudaStream_t st) {
+  using T = typename Storage<DT>::T;
+  const int G = a.B * a.H;
+  if (a.S <= 0) return AVQ_OK;
+  const dim3 grid((a.S + 32 * CB_WARPS - 1) / (32 * CB_WARPS), G);
+  AVQ_TIMED("child", st);
+#define AVQ_CB(D_, NV, NP)                                                                                          \
+  do {                                                                                                              \
+    cudaFuncSetAttribute(child_bucket_kernel<DT, D_, NV, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize,        \
+                         CB_WARPS * 32 * (D_) * 2);                                                                 \
+    child_bucket_kernel<DT, D_, NV, NP><<<grid, CB_WARPS * 32, CB_WARPS * 32 * (D_) * 2, st>>>(                    \
+        static_cast<const T*>(a.keys), a.ks, a.H, a.S, a.M0, a.C, order, a.passign,                               \
+        static_cast<const T*>(a.children_dt), a.c_sq, a.cassign);                                                 \
+  } while (0)
+  // rows per pass 32 / (D / 8 / NV): 2 or 4 at D = 128, 4 or 8 at D = 64
+  if (a.D == 128) {
+    if (a.C <= 2) AVQ_CB(128, 1, 1);
+    else if (a.C <= 4) AVQ_CB(128, 2, 1);
+    else AVQ_CB(128, 2, 2);
+  } else {
+    if (a.C <= 4) AVQ_CB(64, 1, 1);
+    else AVQ_CB(64, 2, 1);
+  }
+#undef AVQ_CB
+  return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
+}
+
+template int launch_child_bucket<DT_BF16>(const QuantizeArgs&, const int*, cudaStream_t);
+template int launch_child_bucket<DT_F16>(const QuantizeArgs&, const int*, cudaStream_t);
 
 
 // Reads and clears this file's fault word (device code without relocatable

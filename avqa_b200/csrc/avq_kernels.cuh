@@ -200,6 +200,9 @@ int launch_correct_tc(const CorrArgs& a, const void* exptab, void* desc, cudaStr
 bool assign_tc_ok(int dt, int D, int M0);
 template <int DT>
 int launch_assign_tc(const QuantizeArgs& a, cudaStream_t st);
+// the child assignment of a launch_assign_tc pass, after the sort by parent
+template <int DT>
+int launch_child_bucket(const QuantizeArgs& a, const int* order, cudaStream_t st);
 // Reads and clears the device fault record (stream-synchronous): the OR of
 // the fault words of the tcgen05 kernel files.
 int read_device_fault(int* code, cudaStream_t st);

@@ -706,6 +706,7 @@ int launch_quantize(const QuantizeArgs& a, cudaStream_t st) {
   int* poff = (int*)ws;
   ws += align_up((size_t)G * a.M0 * sizeof(int));
   int* agg_next = (int*)ws;  // work counter of the persistent aggregation warps
+  bool child_later = false;  // the tcgen05 parent pass leaves the children to launch_child_bucket
   if (a.S > 0) {
     const bool aligned = ((uintptr_t)a.keys % 16 == 0) && a.ks.s % 8 == 0 && a.ks.h % 8 == 0 && a.ks.b % 8 == 0;
     bool done = false;
@@ -714,6 +715,7 @@ int launch_quantize(const QuantizeArgs& a, cudaStream_t st) {
         const int rc = launch_assign_tc<DT>(a, st);
         if (rc != AVQ_OK && rc != AVQ_ERR_UNSUPPORTED) return rc;
         done = rc == AVQ_OK;
+        child_later = done;
       }
       if (!done && aligned && (a.D == 64 || a.D == 128)) {
         done = true;
@@ -750,6 +752,12 @@ int launch_quantize(const QuantizeArgs& a, cudaStream_t st) {
     if (a.S > 0)
       bucket_scatter_kernel<<<dim3(nseg, G), 32, a.M0 * sizeof(int), st>>>(a.passign, hist, a.S, a.M0, nseg, seg_len,
                                                                            order);
+  }
+  if constexpr (DT != DT_F32) {
+    if (child_later) {
+      const int rc = launch_child_bucket<DT>(a, order, st);
+      if (rc != AVQ_OK) return rc;
+    }
   }
   AVQ_TIMED("aggregate", st);
   const long rows = (long)G * a.M0;
