@@ -219,6 +219,17 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
     }
     *abort = 0;
     tc::fence_mbar_init();
+    // the Q tile, issued at once
+    tc::tma_prefetch_desc(&tm_q);
+    tc::mbar_expect_tx(&bars[CB_Q], CR * D * 2);
+    for (int kb = 0; kb < D / 64; ++kb) {
+      int c[4];
+      c[0] = kb * 64;
+      c[qpos.x] = t0;
+      c[qpos.y] = h;
+      c[qpos.z] = b;
+      tc::tma_load_4d(sm + L.q + kb * CR * 128, &tm_q, c[0], c[1], c[2], c[3], &bars[CB_Q]);
+    }
   }
   if (warp == MW) tc::tmem_alloc(tslot, C_TMEM_COLS);
   if (DT == DT_BF16 && tid < 2 * CR) {
@@ -226,24 +237,111 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
     uint32_t* dst = reinterpret_cast<uint32_t*>(sm + L.exptab);
     for (int i = tid; i < (EXPN + 1) / 2; i += 2 * CR) dst[i] = src[i];
   }
+  // ---- the row threads' prologue, before the CTA barrier so that its loads
+  // (row statistics, the seed a, the first two groups' slot rows) overlap
+  // the set-up: two threads per query.  Warps 0-3 (half 0) and 4-7 (half 1)
+  // both reach TMEM lane r; half h takes slots 24h..24h+23 of every group
+  // and the output columns [h D/2, (h+1) D/2).  Threads r < 48 of half 0
+  // gather the logit row of slot r, those of half 1 its value row.
+  const bool rowt = warp != MW;
+  const int hf = tid >> 7, r = tid & (CR - 1), t = t0 + r;
+  const bool live = rowt && t < Tq;
+  const long row = (long)g * Tq + (live ? t : 0);
+  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+  constexpr int XCOL = WCOL + 3 * (NS / 2);  // 8 free columns: the halves' weight sums
+  static_assert(XCOL + 8 <= C_TMEM_COLS, "TMEM columns");
+  const float inv_sqrtD = 1.f / sqrtD;
+  const float2 invl2 = make_float2(next_down(inv_sqrtD), next_down(inv_sqrtD));  // <= 1/sqrt(D)
+  const float2 invh2 = make_float2(next_up(inv_sqrtD), next_up(inv_sqrtD));      // >= 1/sqrt(D)
+  const float m = live ? m_in[row] : 0.f;
+  const float zc = clamp_min_nan(live ? z_in[row] : 1.f, eps_dt<DT>()), rz = 1.f / zc;
+  const float zl = next_down(rz), zh = next_up(rz);  // bracket 1 / zc
+  const float bt = beta_in && live ? beta_in[row] : 0.f;
+  // the row's mask words (pipeline.py:82-106): a masked parent has probability 0
+  const unsigned int* prow = (MK && live) ? present + row * ((M0 + 31) >> 5) : nullptr;
+  float l = live ? l_in[row] : 1.f;
+  const int gslot = r;
+  const bool gathers = rowt && r < NS, isv = hf == 1;
+  const SlotDesc* dg = desc + (long)g * maxgroups * NS + gslot;
+  auto gather = [&](int kg, const SlotDesc& d) {
+    const int bf = kg % NBUF;
+    if (gathers) {
+      const int x = isv ? d.vrow : d.lrow;
+      const T* src = x >= 0 ? (isv ? pagg : parents) + (long)x * D
+                            : (isv ? cagg : children) + (long)(x <= -2 ? -2 - x : 0) * D;
+      unsigned char* dst = sm + (isv ? L.v[bf] : L.l[bf]) + gslot * 128;
+#pragma unroll
+      for (int ch = 0; ch < CPR; ++ch)
+        cp_async16(dst + (ch >> 3) * NS * 128 + (((ch & 7) ^ (gslot & 7)) << 4), src + ch * 8, x != -1);
+      if (!isv) {
+        float* meta = reinterpret_cast<float*>(sm + L.meta[bf]);
+        meta[gslot] = d.n;
+        meta[NS + gslot] = d.mk;
+        if constexpr (MK)
+          reinterpret_cast<int*>(meta)[2 * NS + gslot] = (gslot < J && d.lrow >= 0) ? d.lrow - h * M0 : -1;
+      }
+    }
+    cp_async_commit();
+  };
+  auto publish = [&](int kg) {  // copies of group kg have landed (this thread's part)
+    if constexpr (SPLIT) {
+      // the value row this thread gathered: fp16 -> bf16 hi (in place) + bf16 lo
+      if (gathers && isv) {
+        const int bf = kg % NBUF;
+#pragma unroll
+        for (int ch = 0; ch < CPR; ++ch) {
+          const int off = (ch >> 3) * NS * 128 + gslot * 128 + (((ch & 7) ^ (gslot & 7)) << 4);
+          uint4* vh = reinterpret_cast<uint4*>(sm + L.v[bf] + off);
+          uint4* vl = reinterpret_cast<uint4*>(sm + L.vlo[bf] + off);
+          const uint4 u = *vh;
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+          uint32_t hi[4], lo[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float a0 = half_lo<DT_F16>(w[e]), a1 = half_hi<DT_F16>(w[e]);
+            hi[e] = pack2<DT_BF16>(a0, a1);
+            // exact remainders; an infinite sum keeps lo = 0 so that w * v stays infinite
+            const float r0 = isinf(a0) ? 0.f : a0 - half_lo<DT_BF16>(hi[e]);
+            const float r1 = isinf(a1) ? 0.f : a1 - half_hi<DT_BF16>(hi[e]);
+            lo[e] = pack2<DT_BF16>(r0, r1);
+          }
+          *vh = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          *vl = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+      }
+    }
+    tc::fence_async_smem();
+    tc::mbar_arrive(&bars[CB_FULL + kg % NBUF]);
+  };
+  // this half's columns of the parent pass's a (attention.py:154-158), loaded
+  // first so that their latency overlaps the first gathers
+  uint4 a_seed[D / 16];
+#pragma unroll
+  for (int k = 0; k < D / 16; ++k)
+    a_seed[k] = live ? reinterpret_cast<const uint4*>(a_in + row * D + hf * (D / 2))[k] : make_uint4(0u, 0u, 0u, 0u);
+  SlotDesc dn1{-1, -1, -1.f, 0.f}, dn2{-1, -1, -1.f, 0.f};  // descriptors of the next groups
+  if (gathers) {
+    // the first descriptors at once, then the first two groups' rows
+    const SlotDesc d0 = ngroups > 0 ? dg[0] : SlotDesc{-1, -1, -1.f, 0.f};
+    if (ngroups > 1) dn1 = dg[NS];
+    if (ngroups > 2) dn2 = dg[2 * NS];
+    if (ngroups > 0) gather(0, d0);
+    else cp_async_commit();
+  } else if (rowt) {
+    cp_async_commit();
+  }
+  if (rowt) {
+    if (ngroups > 1) gather(1, dn1);
+    else cp_async_commit();
+  }
   tc::tc_before_sync();
   __syncthreads();
   tc::tc_after_sync();
   const uint32_t tbase = *tslot;
 
   if (warp == MW) {
-    // ---- Q tile (TMA) and MMA issue ----
+    // ---- MMA issue (thread 0 issued the Q tile) ----
     if (lane == 0) {
-      tc::tma_prefetch_desc(&tm_q);
-      tc::mbar_expect_tx(&bars[CB_Q], CR * D * 2);
-      for (int kb = 0; kb < D / 64; ++kb) {
-        int c[4];
-        c[0] = kb * 64;
-        c[qpos.x] = t0;
-        c[qpos.y] = h;
-        c[qpos.z] = b;
-        tc::tma_load_4d(sm + L.q + kb * CR * 128, &tm_q, c[0], c[1], c[2], c[3], &bars[CB_Q]);
-      }
       const uint32_t idS = tc::idesc_f16(DT == DT_BF16 ? 1 : 0, CR, NS, false);
       const uint32_t idO = tc::idesc_f16(1, CR, D, true);  // bf16 weights x bf16 value planes
       const uint32_t qa = tc::smem_addr(sm + L.q);
@@ -292,100 +390,7 @@ __global__ void __launch_bounds__(CTHREADS2, 2) correct_tc_kernel(
       if (!ok) drain_c(&bars[CB_OFULL], 0);
     }
   } else {
-    // ---- row threads: two per query.  Warps 0-3 (half 0) and 4-7 (half 1)
-    // both reach TMEM lane r; half h takes slots 24h..24h+23 of every group
-    // and the output columns [h D/2, (h+1) D/2).  Threads r < 48 of half 0
-    // gather the logit row of slot r, those of half 1 its value row.
-    const int hf = tid >> 7, r = tid & (CR - 1), t = t0 + r;
-    const bool live = t < Tq;
-    const long row = (long)g * Tq + (live ? t : 0);
-    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    constexpr int XCOL = WCOL + 3 * (NS / 2);  // 8 free columns: the halves' weight sums
-    static_assert(XCOL + 8 <= C_TMEM_COLS, "TMEM columns");
-    const float inv_sqrtD = 1.f / sqrtD;
-    const float2 invl2 = make_float2(next_down(inv_sqrtD), next_down(inv_sqrtD));  // <= 1/sqrt(D)
-    const float2 invh2 = make_float2(next_up(inv_sqrtD), next_up(inv_sqrtD));      // >= 1/sqrt(D)
-    const float m = live ? m_in[row] : 0.f;
-    const float zc = clamp_min_nan(live ? z_in[row] : 1.f, eps_dt<DT>()), rz = 1.f / zc;
-    const float zl = next_down(rz), zh = next_up(rz);  // bracket 1 / zc
-    const float bt = beta_in && live ? beta_in[row] : 0.f;
-    // the row's mask words (pipeline.py:82-106): a masked parent has probability 0
-    const unsigned int* prow = (MK && live) ? present + row * ((M0 + 31) >> 5) : nullptr;
-    float l = live ? l_in[row] : 1.f;
-    const int gslot = r;
-    const bool gathers = r < NS, isv = hf == 1;
-    const SlotDesc* dg = desc + (long)g * maxgroups * NS + gslot;
-    auto gather = [&](int kg, const SlotDesc& d) {
-      const int bf = kg % NBUF;
-      if (gathers) {
-        const int x = isv ? d.vrow : d.lrow;
-        const T* src = x >= 0 ? (isv ? pagg : parents) + (long)x * D
-                              : (isv ? cagg : children) + (long)(x <= -2 ? -2 - x : 0) * D;
-        unsigned char* dst = sm + (isv ? L.v[bf] : L.l[bf]) + gslot * 128;
-#pragma unroll
-        for (int ch = 0; ch < CPR; ++ch)
-          cp_async16(dst + (ch >> 3) * NS * 128 + (((ch & 7) ^ (gslot & 7)) << 4), src + ch * 8, x != -1);
-        if (!isv) {
-          float* meta = reinterpret_cast<float*>(sm + L.meta[bf]);
-          meta[gslot] = d.n;
-          meta[NS + gslot] = d.mk;
-          if constexpr (MK)
-            reinterpret_cast<int*>(meta)[2 * NS + gslot] = (gslot < J && d.lrow >= 0) ? d.lrow - h * M0 : -1;
-        }
-      }
-      cp_async_commit();
-    };
-    auto publish = [&](int kg) {  // copies of group kg have landed (this thread's part)
-      if constexpr (SPLIT) {
-        // the value row this thread gathered: fp16 -> bf16 hi (in place) + bf16 lo
-        if (gathers && isv) {
-          const int bf = kg % NBUF;
-#pragma unroll
-          for (int ch = 0; ch < CPR; ++ch) {
-            const int off = (ch >> 3) * NS * 128 + gslot * 128 + (((ch & 7) ^ (gslot & 7)) << 4);
-            uint4* vh = reinterpret_cast<uint4*>(sm + L.v[bf] + off);
-            uint4* vl = reinterpret_cast<uint4*>(sm + L.vlo[bf] + off);
-            const uint4 u = *vh;
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-            uint32_t hi[4], lo[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float a0 = half_lo<DT_F16>(w[e]), a1 = half_hi<DT_F16>(w[e]);
-              hi[e] = pack2<DT_BF16>(a0, a1);
-              // exact remainders; an infinite sum keeps lo = 0 so that w * v stays infinite
-              const float r0 = isinf(a0) ? 0.f : a0 - half_lo<DT_BF16>(hi[e]);
-              const float r1 = isinf(a1) ? 0.f : a1 - half_hi<DT_BF16>(hi[e]);
-              lo[e] = pack2<DT_BF16>(r0, r1);
-            }
-            *vh = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            *vl = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-          }
-        }
-      }
-      tc::fence_async_smem();
-      tc::mbar_arrive(&bars[CB_FULL + kg % NBUF]);
-    };
-    // this half's columns of the parent pass's a (attention.py:154-158), loaded
-    // first so that their latency overlaps the first gathers
-    uint4 a_seed[D / 16];
-#pragma unroll
-    for (int k = 0; k < D / 16; ++k)
-      a_seed[k] = live ? reinterpret_cast<const uint4*>(a_in + row * D + hf * (D / 2))[k] : make_uint4(0u, 0u, 0u, 0u);
-    SlotDesc dn1{-1, -1, -1.f, 0.f}, dn2{-1, -1, -1.f, 0.f};  // descriptors of the next groups
-    if (gathers) {
-      if (ngroups > 0) {
-        const SlotDesc d0 = dg[0];
-        gather(0, d0);
-      } else {
-        cp_async_commit();
-      }
-      if (ngroups > 1) dn1 = dg[NS];
-      if (ngroups > 2) dn2 = dg[2 * NS];
-    } else {
-      cp_async_commit();
-    }
-    if (ngroups > 1) gather(1, dn1);
-    else cp_async_commit();
+    // ---- row threads ----
     cp_async_wait<1>();
     if (ngroups > 0) publish(0);
     // O = a, this half's columns
