@@ -615,7 +615,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
           for (int j = 0; j < 8; ++j)
             s2[j] = hmul2_dt<DT>(pack2<DT>(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1])), dup2<DT>(0.125f));
         } else {
-        bool near = false;
+        uint32_t near = 0u;  // bits where some pair's ends disagree (one LOP3 per pair)
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint32_t x2 = pack2<DT>(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1]));
@@ -623,10 +623,10 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
           const float2 av = make_float2(half_lo<DT>(a2), half_hi<DT>(a2));
           const float2 ylo = mul_f32x2_rd(av, invl2), yhi = mul_f32x2_ru(av, invh2);
           const uint32_t qlo = pack2<DT>(ylo.x, ylo.y);
-          near |= qlo != pack2<DT>(yhi.x, yhi.y);
+          near |= qlo ^ pack2<DT>(yhi.x, yhi.y);
           s2[j] = qlo | (x2 & 0x80008000u);
         }
-        if (near) {
+        if (near != 0u) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) s2[j] = logit2<DT>(ra[2 * j], ra[2 * j + 1], sqrtD, inv_sqrtD, 0xFFFFFFFFu);
         }
@@ -819,7 +819,7 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
       float2 c2 = make_float2(0.f, 0.f);
 #pragma unroll 1
       for (int g8 = 0; g8 < 2; ++g8) {
-        uint32_t w[8], q[8], bad = 0u;
+        uint32_t w[8], q[8], bad = 0u;  // bits where some pair's ends disagree
         float4 zr[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -836,13 +836,12 @@ __global__ void __launch_bounds__(TTHREADS, 2) parent_attn_tc_kernel(
           const float2 ylo = mul_f32x2_rd(ev, make_float2(zr[i].y, zr[i].y));
           const float2 yhi = mul_f32x2_ru(ev, make_float2(zr[i].z, zr[i].z));
           q[i] = pack2<DT>(ylo.x, ylo.y);
-          bad |= (q[i] != pack2<DT>(yhi.x, yhi.y) ? 1u : 0u) << i;
+          bad |= q[i] ^ pack2<DT>(yhi.x, yhi.y);
         }
-        if (bad) {
+        if (bad) {  // rare: the eight pairs divided exactly (the agreeing ones give the same values)
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            if ((bad >> i) & 1u)
-              q[i] = pack2<DT>(__fdiv_rn(half_lo<DT>(w[i]), zr[i].x), __fdiv_rn(half_hi<DT>(w[i]), zr[i].x));
+            q[i] = pack2<DT>(__fdiv_rn(half_lo<DT>(w[i]), zr[i].x), __fdiv_rn(half_hi<DT>(w[i]), zr[i].x));
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) c2 = add_f32x2(c2, make_float2(half_lo<DT>(q[i]), half_hi<DT>(q[i])));
