@@ -2,9 +2,9 @@
 // fp16 and D in {64, 128} (reference quantizer.py:166-226).
 //
 // CTA = 128 keys of one (b,h); thread r of warps 0-3 owns key r (TMEM lane r);
-// warp 4 issues tcgen05.mma, warp 5 streams the key tile and 128-parent
-// chunks of the head's codebook with TMA.  TMEM holds two 128-column buffers
-// of fp32 cross terms K P_c^T.
+// warp 4 issues tcgen05.mma, warp 5 streams the key tile and 64- or
+// 128-parent chunks of the head's codebook with TMA.  TMEM holds two buffers
+// of fp32 cross terms K P_c^T, one column per parent of a chunk.
 //
 // Parent distance (quantizer.py:207-210), each op rounded to the dtype:
 //   d = DT(DT(k_sq + p_sq) - DT(2 * DT(k . p)))
@@ -37,9 +37,11 @@ __device__ int g_fault;
 namespace {
 
 constexpr int AR = 128;        // keys per CTA
-constexpr int ACH = 128;       // parents per chunk
+// parents per chunk: 64 (two 64-column TMEM buffers, three CTAs per SM) up to
+// A_SMALL_M0 parents, else 128 (two 128-column buffers, two CTAs per SM: half
+// as many chunk hand-overs for a large codebook)
+constexpr int A_SMALL_M0 = 1024;
 constexpr int ATHREADS = 192;  // 4 row warps + MMA warp + TMA warp
-constexpr int A_TMEM_COLS = 256;
 constexpr int A_MAX_M0 = 4096;
 constexpr int A_MAX_C = 8;           // children per parent on this path
 
@@ -49,7 +51,7 @@ struct AssignLayout {
   int k, p[2], ps2, bars, misc, total;
 };
 
-__host__ __device__ inline AssignLayout assign_layout(int D, int M0) {
+__host__ __device__ inline AssignLayout assign_layout(int D, int M0, int ACH) {
   AssignLayout L;
   const int nch = (M0 + ACH - 1) / ACH;
   int o = 0;
@@ -308,8 +310,8 @@ __global__ void __launch_bounds__(CB_WARPS * 32, NP > 1 ? 2 : 3) child_bucket_ke
   if (live) cassign[(long)g * S + s_mine] = mine;
 }
 
-template <int DT, int D>
-__global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
+template <int DT, int D, int ACH>
+__global__ void __launch_bounds__(ATHREADS, ACH == 64 ? 3 : 2) assign_tc_kernel(
     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_p, int4 kpos, int H, int S,
     int M0, const typename Storage<DT>::T* __restrict__ parents, const float* __restrict__ p_sq,
     int* __restrict__ passign, int* __restrict__ cassign) {
@@ -317,7 +319,8 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = tc::smem_addr(smem_raw);
   unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  const AssignLayout L = assign_layout(D, M0);
+  constexpr int A_TMEM_COLS = 2 * ACH;
+  const AssignLayout L = assign_layout(D, M0, ACH);
   const int g = blockIdx.y, b = g / H, h = g % H, s0 = blockIdx.x * AR;
   const int nch = (M0 + ACH - 1) / ACH;
   // the CTA's i-th chunk is chunk (i + rot) mod nch: the CTAs of a head that
@@ -494,8 +497,8 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[AB_SFULL + sb], (ci >> 1) & 1, abort));
       if (!ok) break;
       tc::tc_after_sync();
-      // four 32-column quarters; the next quarter's TMEM load is in flight
-      // while the current one is scanned
+      // two 32-column quarters; the second quarter's TMEM load is in flight
+      // while the first one is scanned
       const uint32_t col = tbase + lane_off + ACH * sb;
       uint32_t qa[32], qb[32];
       auto scan = [&](const uint32_t (&r)[32], int quarter) {
@@ -535,20 +538,23 @@ __global__ void __launch_bounds__(ATHREADS, 2) assign_tc_kernel(
           }
         }
       };
+      static_assert(ACH == 64 || ACH == 128, "chunk size");
       tc::tmem_ld32(col, qa);
       tc::tmem_wait_ld();
       tc::tmem_ld32(col + 32, qb);
       scan(qa, 0);
       tc::tmem_wait_ld();
-      tc::tmem_ld32(col + 64, qa);
-      scan(qb, 1);
-      tc::tmem_wait_ld();
-      tc::tmem_ld32(col + 96, qb);
-      scan(qa, 2);
-      tc::tmem_wait_ld();
+      if constexpr (ACH == 128) {
+        tc::tmem_ld32(col + 64, qa);
+        scan(qb, 1);
+        tc::tmem_wait_ld();
+        tc::tmem_ld32(col + 96, qb);
+        scan(qa, 2);
+        tc::tmem_wait_ld();
+      }
       tc::tc_before_sync();
       tc::mbar_arrive(&bars[AB_SCONS + sb]);
-      scan(qb, 3);
+      scan(qb, ACH / 32 - 1);
     }
     int pbest = best & 0xFFFF;
     const bool has_nan = isnan(half_lo<DT>(nanacc)) || isnan(half_hi<DT>(nanacc));
@@ -605,13 +611,16 @@ int launch_assign_tc(const QuantizeArgs& a, cudaStream_t st) {
   CUtensorMap tk, tp;
   int4 kpos;
   if (!tc::map_rows4(&tk, DT, a.keys, a.ks, a.B, a.H, a.S, D, AR, &kpos) ||
-      !tc::map_rows3(&tp, DT, a.parents_dt, a.H, a.M0, D, ACH))
+      !tc::map_rows3(&tp, DT, a.parents_dt, a.H, a.M0, D, a.M0 <= A_SMALL_M0 ? 64 : 128))
     return AVQ_ERR_UNSUPPORTED;
   // the child blocks move with bulk copies: 16-byte aligned rows
   if (a.C < 1 || a.C > A_MAX_C || (uintptr_t)a.children_dt % 16 != 0 || (uintptr_t)a.c_sq % 4 != 0)
     return AVQ_ERR_UNSUPPORTED;
-  const AssignLayout L = assign_layout(D, a.M0);
-  const size_t smem = std::max<size_t>((size_t)L.total + 1024, 80 * 1024);  // <= 2 CTAs (2 x 256 TMEM columns) per SM
+  const int ach = a.M0 <= A_SMALL_M0 ? 64 : 128;
+  const AssignLayout L = assign_layout(D, a.M0, ach);
+  // 64-parent chunks: at least 60 KB, so at most 3 CTAs (3 x 128 TMEM columns) per SM;
+  // 128-parent chunks: at least 80 KB, at most 2 CTAs (2 x 256 columns): tcgen05.alloc never waits
+  const size_t smem = std::max<size_t>((size_t)L.total + 1024, (ach == 64 ? 60 : 80) * 1024);
   auto go = [&](auto kfn) {
     AVQ_TIMED("assign_tc", st);
     cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -619,8 +628,13 @@ int launch_assign_tc(const QuantizeArgs& a, cudaStream_t st) {
                                                                 static_cast<const T*>(a.parents_dt), a.p_sq,
                                                                 a.passign, a.cassign);
   };
-  if (D == 64) go(assign_tc_kernel<DT, 64>);
-  else go(assign_tc_kernel<DT, 128>);
+  if (ach == 64) {
+    if (D == 64) go(assign_tc_kernel<DT, 64, 64>);
+    else go(assign_tc_kernel<DT, 128, 64>);
+  } else {
+    if (D == 64) go(assign_tc_kernel<DT, 64, 128>);
+    else go(assign_tc_kernel<DT, 128, 128>);
+  }
   return cudaPeekAtLastError() == cudaSuccess ? AVQ_OK : AVQ_ERR_CUDA;
 }
 
