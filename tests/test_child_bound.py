@@ -1,9 +1,12 @@
-"""The child-distance rounding test of the tcgen05 assignment kernel, on CPU.
+"""The child-distance rounding test of the child assignment kernel that runs
+after the tcgen05 parent pass (child_bucket_kernel), on CPU.
 
 The kernel evaluates the child cross term DT(fp32(sum_d DT(k_d c_d))) (the sum
 exact, quantizer.py:224-226) in fp32 along a fixed tree, then accepts the
 result only when both ends of [S' - b, S' + b] round to the same dtype value,
-with b = RU(RU(k_sq + c_sq) * 0.52 * 2^-21 + slack).  This emulates that
+with b = RU(RU(k_sq + c_sq) * 0.52 * 2^-21 + slack).  The tree is the same
+for every pass over the child rows (C = 8 at D = 128 takes two passes of four
+rows with nv = 2).  This emulates that
 tree and test with exact directed rounding and checks, over distributions
 chosen to stress it (near ties, integers, mismatched norms, f16 underflow,
 overflow), that every accepted value equals the oracle's exact rounding.
