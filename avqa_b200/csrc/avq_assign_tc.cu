@@ -613,7 +613,7 @@ int launch_assign_tc(const QuantizeArgs& a, cudaStream_t st) {
   if (!tc::map_rows4(&tk, DT, a.keys, a.ks, a.B, a.H, a.S, D, AR, &kpos) ||
       !tc::map_rows3(&tp, DT, a.parents_dt, a.H, a.M0, D, a.M0 <= A_SMALL_M0 ? 64 : 128))
     return AVQ_ERR_UNSUPPORTED;
-  // the child blocks move with bulk copies: 16-byte aligned rows
+  // the child kernel reads child rows with 16-byte loads: aligned rows, at most A_MAX_C children
   if (a.C < 1 || a.C > A_MAX_C || (uintptr_t)a.children_dt % 16 != 0 || (uintptr_t)a.c_sq % 4 != 0)
     return AVQ_ERR_UNSUPPORTED;
   const int ach = a.M0 <= A_SMALL_M0 ? 64 : 128;
