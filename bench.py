@@ -253,6 +253,7 @@ def algorithmic_work(w, B: int, T: int | None = None, decode: bool = False, sel_
         "parent_attn_hvaq": ("tensor", 4.0 * G * T * M0 * D),     # HVAQ rescaled pass
         "parent_attn_exact": ("tensor", 4.0 * G * T * M0 * D),
         "assign": ("tensor", 2.0 * G * S * M0 * D + 2.0 * G * S * C * D),
+        "assign_exact": ("tensor", 2.0 * G * S * M0 * D + 2.0 * G * S * C * D),  # fp32 path
         "assign_tc": ("tensor", 2.0 * G * S * M0 * D),            # the parent pass; children in "child"
         # child stage in parent order: each key row, its order / parent /
         # cassign words, every parent's child rows and norms once
