@@ -505,20 +505,39 @@ __global__ void __launch_bounds__(ATHREADS, ACH == 64 ? 3 : 2) assign_tc_kernel(
         const int cid = chunk_of(ci);
         const uint4* pp = reinterpret_cast<const uint4*>(ps2 + cid * (ACH / 2) + 16 * quarter);
         if (finite_w) {
-          int qbest = 0x7FFFFFFF;  // keys with the index within the quarter
+          // keys with the index within the quarter.  While no distance of the
+          // warp's quarter has its sign bit set (distances are >= +0 unless a
+          // key nearly equals a parent), the raw dtype bits order as signed
+          // 16-bit integers already, so the order transform is skipped and
+          // only the sign bits are gathered; otherwise the quarter is scanned
+          // again with the transform (the same keys for the >= +0 halves)
+          auto quarter_min = [&](auto ordered) -> int {
+            constexpr bool ORD = decltype(ordered)::value;
+            int qbest = 0x7FFFFFFF;
+            uint32_t sgn = 0u;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint4 pq = pp[q];
-            const uint32_t pv[4] = {pq.x, pq.y, pq.z, pq.w};
+            for (int q = 0; q < 4; ++q) {
+              const uint4 pq = pp[q];
+              const uint32_t pv[4] = {pq.x, pq.y, pq.z, pq.w};
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int j = 4 * q + k;
-              const uint32_t x2 = pack2<DT>(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));  // DT(k . p)
-              const uint32_t d2 = hfma2_dt<DT>(x2, 0xC000C000u, hadd2_dt<DT>(ksq2, pv[k]));
-              const uint32_t k2 = order2(d2), il = (uint32_t)(2 * j) | ((uint32_t)(2 * j + 1) << 16);
-              qbest = min(qbest, min(key_lo(k2, il), key_hi(k2, il)));
+              for (int k = 0; k < 4; ++k) {
+                const int j = 4 * q + k;
+                const uint32_t x2 = pack2<DT>(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));  // DT(k . p)
+                const uint32_t d2 = hfma2_dt<DT>(x2, 0xC000C000u, hadd2_dt<DT>(ksq2, pv[k]));
+                uint32_t k2 = d2;
+                if constexpr (ORD) k2 = order2(d2);
+                else sgn |= d2;
+                const uint32_t il = (uint32_t)(2 * j) | ((uint32_t)(2 * j + 1) << 16);
+                qbest = min(qbest, min(key_lo(k2, il), key_hi(k2, il)));
+              }
             }
-          }
+            if constexpr (!ORD) {
+              if (__any_sync(0xffffffffu, (sgn & 0x80008000u) != 0u)) return -1;
+            }
+            return qbest;
+          };
+          int qbest = quarter_min(std::false_type{});
+          if (qbest < 0) qbest = quarter_min(std::true_type{});  // warp-uniform: the vote above
           best = min(best, qbest + (cid * ACH + 32 * quarter));  // the index half has room: M0 <= 4096
           return;
         }
