@@ -5,9 +5,9 @@ A distance pair is a dtype x2 word.  The kernel's key for parent j is
 (order16(d_j) << 16) | j as a signed 32-bit integer, and the minimum key is
 torch.argmin's choice: the smallest distance, the first index on ties.  (A
 distance is one fma, s - 2x; an exact cancellation rounds to +0 in
-round-to-nearest, so -0 does not occur.)  order16 flips the magnitude bits of negative values.  While no
-distance of a quarter has its sign bit set, the kernel skips order16 and
-uses the raw bits.  This test checks that:
+round-to-nearest, so -0 does not occur.)  order16 flips the magnitude bits
+of negative values.  While no distance of a quarter has its sign bit set, the
+kernel skips order16 and uses the raw bits.  This test checks that:
 - raw and transformed keys then pick the same parent;
 - the sign-bit gather flags every quarter where they could differ;
 - the transformed keys always reproduce numpy's first-minimum argmin.
